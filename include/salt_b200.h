@@ -1,0 +1,200 @@
+/*
+ * salt_b200 — C ABI of the B200 (sm_100a) implementation of SALT's integer event-driven
+ * forward pass and its float chunked affine scan.
+ *
+ * The reference (Salt-Shio/Spiking-Affine-Lazy-Training) is pure Python/JAX; it has no C
+ * interface.  Each entry point below replaces one reference Python call (cited per entry);
+ * a host binding (ctypes here, a jax.ffi custom-call handler or cgo elsewhere) passes plain
+ * device pointers and sizes.  No torch, JAX or C++ types cross this boundary.
+ *
+ * Conventions
+ *   - All array pointers are DEVICE pointers unless a comment says "host".
+ *   - Batch-major layouts: a stream is (batch, capacity) row-major; per-neuron arrays are
+ *     (batch, n_neurons) with neuron = oc * h_out * w_out + oy * w_out + ox for conv layers
+ *     (salt_core/layers/conv.py:189-197).
+ *   - Every call is asynchronous on `stream` (a cudaStream_t) and returns a status; argument
+ *     errors are reported before anything is enqueued.  Capacity overflow is NOT an error: it
+ *     is reported through `fits` / `needed_queue` / `n_real`, as salt_core/capacity.py:60-63.
+ *   - Streams written by this library do not materialise their pad entries: entries at or
+ *     beyond min(n_real, capacity) are pads whose time is 1e12 and source 0
+ *     (salt_core/stream.py:42-45).  `virtual_pads = 1` tells a consumer to read them that way.
+ */
+#ifndef SALT_B200_H
+#define SALT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t salt_status;
+enum {
+  SALT_OK = 0,
+  SALT_BAD_ARG = 1,          /* invalid geometry, bit widths, sizes or null pointers */
+  SALT_CUDA_ERROR = 2,       /* a CUDA runtime call failed; see salt_last_error() */
+  SALT_NO_DEVICE = 3,        /* no sm_100 device is visible */
+  SALT_WORKSPACE_TOO_SMALL = 4
+};
+
+enum { SALT_ROUND = 0, SALT_TRUNCATE = 1 };  /* salt_core/quant/fixed_point.py:20-23 */
+enum { SALT_WRAP = 0, SALT_SATURATE = 1 };   /* salt_core/quant/fixed_point.py:26-29 */
+
+/* Fixed-point settings of one quantised layer (salt_core/quant/params.py:9-21). */
+typedef struct {
+  int32_t f_a, f_V, i_V;   /* f_a <= 15, i_V + f_V <= 30 (fixed_point.py:15-17) */
+  int32_t round_mode;      /* SALT_ROUND / SALT_TRUNCATE (network-wide in the reference) */
+  int32_t overflow_mode;   /* SALT_WRAP / SALT_SATURATE */
+  int32_t lut_len;         /* length of decay_table_int */
+  int32_t has_vth;         /* 0: v_th_int is None, the layer never fires */
+  int32_t q_bits;          /* 8 / 16 when every weight code fits int8 / int16, else 32; lets
+                              the kernels stage narrower weights in shared memory */
+  int32_t needs_tail;      /* 1 when some v_th_int <= 0 or some decay code is outside
+                              [0, 2^f_a): only then can catch-up/identity/pad columns fire, and
+                              the kernels must walk them (salt_core/quant/scan.py:65-80 applies
+                              every column).  Setting it when not needed is always correct. */
+} salt_quant_desc;
+
+/* ConvLayer geometry and capacity (salt_core/layers/conv.py:107-138). */
+typedef struct {
+  int32_t ic, h_in, w_in, oc, k, s, p;
+  int32_t max_queue_len, max_out_spikes, max_extra_steps;
+} salt_conv_desc;
+
+/* FCLayer geometry and capacity (salt_core/layers/fc.py:323-341). */
+typedef struct {
+  int32_t n_in, n_out;
+  int32_t max_out_spikes, max_extra_steps;
+} salt_fc_desc;
+
+/* Input event stream of a layer: (batch, capacity) times/sources plus n_real per sample.
+ * salt_core/stream.py:16-21 EventStream (event_gain is identically 1 on the integer path). */
+typedef struct {
+  const float *times;
+  const int32_t *src;
+  const int32_t *n_real;
+  int32_t capacity;
+  int32_t virtual_pads;
+} salt_stream_in;
+
+/* Output stream of a layer, capacity = the layer's max_out_spikes.  n_real[b] is the total
+ * spike count (not clipped), exactly as stream.py:61 reports it. */
+typedef struct {
+  float *times;
+  int32_t *src;
+  int32_t *n_real;
+} salt_stream_out;
+
+/* Per-sample diagnostics of one layer (batch entries each).  Any pointer may be NULL.
+ *   spike_count  LayerDiag.spike_count (layers/base.py:73-79)
+ *   needed_queue LayerDiag.needed["max_queue_len"] = max n_real + 1 (layers/conv.py:222-224)
+ *   overflowed   any(QuantLayerResult.overflowed) (example/quant_run.py:88-89)
+ *   vmin / vmax  min/max of v_unfitted_min/max over neurons (example/quant_run.py:90-93)
+ *   fits         Capacity.fits (capacity.py:60-63) */
+typedef struct {
+  int32_t *spike_count, *needed_queue, *overflowed, *vmin, *vmax, *fits;
+} salt_layer_stats;
+
+/* ---------------------------------------------------------------- conv layer
+ * Replaces ConvLayer.forward with QuantBackend (salt_core/layers/conv.py:209-234 calling
+ * build_conv_structure connectivity/conv.py:128-172, QuantBackend.scan quant/backend.py:31-53,
+ * extract_output_events_conv stream.py:84-100, _layer_diag layers/base.py:73-79).
+ *   q    (oc, ic, k, k) int32 weight codes      lut (lut_len) int32 decay_table_int
+ *   vth  (oc*h_out*w_out) int32, or NULL when has_vth == 0
+ *   v_final (batch, n_neurons) int32 register values after the queue (QuantLayerResult.v_final)
+ * The workspace must be at least salt_conv_layer_workspace_size() bytes, 256-byte aligned. */
+salt_status salt_conv_layer_workspace_size(const salt_conv_desc *layer, const salt_quant_desc *quant,
+                                           int32_t batch, int32_t in_capacity, size_t *bytes);
+salt_status salt_conv_layer_forward(const salt_conv_desc *layer, const salt_quant_desc *quant,
+                                    const int32_t *q, const int32_t *lut, const int32_t *vth,
+                                    int32_t batch, const salt_stream_in *in, salt_stream_out *out,
+                                    int32_t *v_final, const salt_layer_stats *stats,
+                                    void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------- fc layer
+ * Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:385-402 calling
+ * build_fc_structure connectivity/fc.py:20-33, fc_weight_codes :54-61, QuantBackend.scan,
+ * extract_output_events_fc stream.py:67-81).
+ *   q (n_out, n_in) int32 weight codes; vth (n_out) or NULL; v_final (batch, n_out). */
+salt_status salt_fc_layer_workspace_size(const salt_fc_desc *layer, const salt_quant_desc *quant,
+                                         int32_t batch, int32_t in_capacity, size_t *bytes);
+salt_status salt_fc_layer_forward(const salt_fc_desc *layer, const salt_quant_desc *quant,
+                                  const int32_t *q, const int32_t *lut, const int32_t *vth,
+                                  int32_t batch, const salt_stream_in *in, salt_stream_out *out,
+                                  int32_t *v_final, const salt_layer_stats *stats,
+                                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------- dense scan
+ * Replaces quant.scan.run_layer (salt_core/quant/scan.py:65-80, :97-132) on materialised
+ * (n, L) queues — the Backend.scan plug-in point of salt_core/backend.py:64-74.
+ *   a_int (n, L) int32, is_identity (n, L) uint8, q_int (n, L) int32, vth (n) or NULL
+ *   spike_mask / overflowed (n, L) uint8 (may be NULL); v_final, vmin, vmax (n) int32. */
+salt_status salt_quant_scan_dense(const salt_quant_desc *quant, int32_t n, int32_t L,
+                                  const int32_t *a_int, const uint8_t *is_identity,
+                                  const int32_t *q_int, const int32_t *vth, uint8_t *spike_mask,
+                                  uint8_t *overflowed, int32_t *v_final, int32_t *vmin,
+                                  int32_t *vmax, void *stream);
+
+/* ---------------------------------------------------------------- network plan
+ * A native runtime object that chains layers on the device (salt_core/network.py:193-222
+ * run_network, vmapped over the batch as Network.apply_batched :279-283) with every
+ * intermediate stream kept in the workspace, optionally replayed as one CUDA graph.
+ * Layer parameters are HOST pointers copied to the device at creation. */
+typedef struct {
+  int32_t kind;            /* 0 conv, 1 fc */
+  salt_conv_desc conv;
+  salt_fc_desc fc;
+  salt_quant_desc quant;
+  const int32_t *q_host;   /* weight codes (layout as above) */
+  const int32_t *lut_host;
+  const int32_t *vth_host; /* per-neuron thresholds, NULL when has_vth == 0 */
+} salt_layer_spec;
+
+typedef struct salt_network salt_network;
+
+salt_status salt_network_create(const salt_layer_spec *layers, int32_t n_layers,
+                                salt_network **out);
+salt_status salt_network_destroy(salt_network *net);
+salt_status salt_network_workspace_size(const salt_network *net, int32_t batch,
+                                        int32_t in_capacity, size_t *bytes);
+/* Runs every layer.  Outputs (device, may be NULL except logits):
+ *   logits      (batch, n_last) int32: v_final of the last layer (register values)
+ *   spike_count (n_layers, batch) int32, overflowed (n_layers, batch) int32,
+ *   vmin/vmax   (n_layers, batch) int32, needed_queue (n_layers, batch) int32,
+ *   fits        (batch) int32: AND of Capacity.fits over layers (network.py:216-219). */
+salt_status salt_network_forward(salt_network *net, int32_t batch, const salt_stream_in *in,
+                                 int32_t *logits, int32_t *spike_count, int32_t *overflowed,
+                                 int32_t *vmin, int32_t *vmax, int32_t *needed_queue,
+                                 int32_t *fits, void *workspace, size_t workspace_bytes,
+                                 void *stream);
+/* Number of kernel launches the last salt_network_forward enqueued (for launch accounting). */
+int32_t salt_network_last_launch_count(const salt_network *net);
+
+/* ---------------------------------------------------------------- float chunked scan
+ * Replaces FloatBackend.scan on an FC layer (salt_core/float/backend.py:16-31 ->
+ * fc_float_values connectivity/fc.py:36-51 -> float.scan.run_layer float/scan.py:34-50,
+ * process_chunk float/affine.py:99-126) for the forward value only, with a per-neuron tau.
+ *   times/src (n_events) one stream; w (n_in, n_out) float32 — transposed so one event reads
+ *   one contiguous row; decay_base (n_out) = 1 - 1/tau; v_th scalar.
+ *   v_final (n_out) float32; spikes are written as (event index, neuron) int32 pairs in
+ *   spike_pairs (capacity max_spikes pairs) in (event, neuron) order — the order of
+ *   extract_output_events_fc (stream.py:67-81); *n_spikes (device) gets the total count, which
+ *   may exceed max_spikes (then only the first max_spikes pairs in that order are kept). */
+salt_status salt_float_fc_scan(int32_t n_in, int32_t n_out, int32_t n_events, int32_t n_real,
+                               const float *times, const int32_t *src, const float *w,
+                               const float *decay_base, float v_th, float *v_final,
+                               int32_t *spike_pairs, int32_t max_spikes, int32_t *n_spikes,
+                               void *workspace, size_t workspace_bytes, void *stream);
+salt_status salt_float_fc_scan_workspace_size(int32_t n_out, int32_t n_events, size_t *bytes);
+
+/* Library facts and errors (host). */
+const char *salt_last_error(void);
+const char *salt_version(void);
+/* Kernel launches enqueued by this thread since the last reset (for launch accounting). */
+int64_t salt_launch_counter(int32_t reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SALT_B200_H */

@@ -1,0 +1,523 @@
+/*
+ * CPU oracle for the SALT integer event-driven forward — TEST INFRASTRUCTURE ONLY.
+ * See salt_oracle.h.  Every function cites the reference file:line it restates.
+ * Parity pins: the reference's own known-answer tests, transcribed under tests/golden/.
+ *
+ * JAX semantics that the restatement reproduces on purpose:
+ *   - int32 arithmetic wraps (two's complement); `>>` on int32 is arithmetic.
+ *   - Python/JAX `//` and `%` on ints are floor division / floor modulo.
+ *   - array indexing with a dynamic index first maps a negative index i to i + n and then
+ *     clamps to [0, n-1] (out-of-bounds gathers clamp, they never fault).
+ *   - times are float32; differences are float32 subtractions; `.astype(int32)` truncates.
+ */
+#include "salt_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdatomic.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define SO_PAD_TIME ((float)1e12) /* stream.py:13 _PAD_TIME, stored as float32 */
+
+static inline int32_t wadd(int32_t a, int32_t b) { return (int32_t)((uint32_t)a + (uint32_t)b); }
+static inline int32_t wmul(int32_t a, int32_t b) { return (int32_t)((uint32_t)a * (uint32_t)b); }
+static inline int32_t floordiv(int32_t a, int32_t b) {
+  int32_t q = a / b, r = a % b;
+  return (r != 0 && ((r < 0) != (b < 0))) ? q - 1 : q;
+}
+static inline int32_t floormod(int32_t a, int32_t b) {
+  int32_t r = a % b;
+  return (r != 0 && ((r < 0) != (b < 0))) ? r + b : r;
+}
+/* JAX dynamic-index gather: negative index wraps once, then clamp into range. */
+static inline int64_t jidx(int64_t i, int64_t n) {
+  if (i < 0) i += n;
+  if (i < 0) i = 0;
+  if (i > n - 1) i = n - 1;
+  return i;
+}
+static inline int32_t f32_to_i32(float x) { /* .astype(int32): truncation toward zero */
+  if (!(x == x)) return 0;
+  if (x >= 2147483647.0f) return 2147483647;
+  if (x <= -2147483648.0f) return (int32_t)0x80000000u;
+  return (int32_t)x;
+}
+
+/* fixed_point.py:32-44 round_shift */
+int32_t so_round_shift(int32_t x, int32_t shift_bits, int32_t round_mode) {
+  if (shift_bits == 0) return x;
+  if (round_mode == SO_ROUND) x = wadd(x, (int32_t)(1u << (shift_bits - 1)));
+  return x >> shift_bits;
+}
+
+/* fixed_point.py:47-65 wide_mul_shift */
+int32_t so_wide_mul_shift(int32_t a, int32_t v, int32_t shift_bits, int32_t round_mode) {
+  int32_t hi = v >> shift_bits;
+  int32_t lo = v & (int32_t)((1u << shift_bits) - 1u);
+  return wadd(wmul(a, hi), so_round_shift(wmul(a, lo), shift_bits, round_mode));
+}
+
+/* fixed_point.py:68-90 fit_to_bits */
+int32_t so_fit_to_bits(int32_t x, int32_t total_bits, int32_t overflow_mode, int32_t *overflowed) {
+  int32_t half = (int32_t)(1u << (total_bits - 1));
+  *overflowed = (x < -half) || (x >= half);
+  if (overflow_mode == SO_SATURATE) {
+    if (x < -half) return -half;
+    if (x > half - 1) return half - 1;
+    return x;
+  }
+  int32_t masked = x & (int32_t)((1u << total_bits) - 1u);
+  return masked >= half ? masked - (int32_t)(1u << total_bits) : masked;
+}
+
+/* quant/scan.py:22-52 process_event */
+int32_t so_process_event(int32_t v0, int32_t a, int32_t is_identity, int32_t q, int32_t has_vth,
+                         int32_t vth, int32_t f_a, int32_t f_V, int32_t i_V, int32_t round_mode,
+                         int32_t overflow_mode, int32_t *is_spiked, int32_t *overflowed,
+                         int32_t *v_unfitted) {
+  int32_t decayed_active = so_wide_mul_shift(a, v0, f_a, round_mode);
+  int32_t decayed = is_identity ? v0 : decayed_active;
+  int32_t u = wadd(decayed, wmul(q, (int32_t)(1u << f_V)));
+  int32_t fitted = so_fit_to_bits(u, i_V + f_V, overflow_mode, overflowed);
+  *v_unfitted = u;
+  if (!has_vth) {
+    *is_spiked = 0;
+    return fitted;
+  }
+  *is_spiked = fitted >= vth;
+  return *is_spiked ? 0 : fitted;
+}
+
+/* quant/codes.py:87-105 apply_decay_table_int */
+void so_apply_decay_table(const float *delta_t, int64_t n, const int32_t *lut, int32_t lut_len,
+                          int32_t *a_int, uint8_t *is_identity) {
+  for (int64_t i = 0; i < n; ++i) {
+    int32_t dt = f32_to_i32(delta_t[i]);
+    int32_t gathered = 0;
+    if (lut_len > 0) {
+      int32_t idx = dt - 1;
+      if (idx < 0) idx = 0;
+      if (idx > lut_len - 1) idx = lut_len - 1;
+      gathered = lut[idx];
+    }
+    a_int[i] = dt > lut_len ? 0 : gathered;
+    is_identity[i] = dt == 0;
+  }
+}
+
+/* quant/scan.py:97-132 _run_layer_scan (trace=False): every one of the L columns is applied. */
+void so_run_layer(const int32_t *a_int, const uint8_t *is_identity, const int32_t *q_int,
+                  const int32_t *vth, int32_t n, int32_t L, int32_t f_a, int32_t f_V, int32_t i_V,
+                  int32_t round_mode, int32_t overflow_mode, uint8_t *spike_mask,
+                  uint8_t *overflowed, int32_t *v_final, int32_t *vmin, int32_t *vmax) {
+  for (int32_t i = 0; i < n; ++i) {
+    int32_t v = 0, lo = 0, hi = 0;
+    for (int32_t t = 0; t < L; ++t) {
+      int64_t e = (int64_t)i * L + t;
+      int32_t spk, ovf, u;
+      v = so_process_event(v, a_int[e], is_identity[e], q_int[e], vth != NULL,
+                           vth ? vth[i] : 0, f_a, f_V, i_V, round_mode, overflow_mode, &spk, &ovf,
+                           &u);
+      if (u < lo) lo = u;
+      if (u > hi) hi = u;
+      if (spike_mask) spike_mask[e] = (uint8_t)spk;
+      if (overflowed) overflowed[e] = (uint8_t)ovf;
+    }
+    v_final[i] = v;
+    vmin[i] = lo;
+    vmax[i] = hi;
+  }
+}
+
+/* connectivity/conv.py:15-29 _axis_candidates (one event, one axis). */
+static void axis_candidates(int32_t i, int32_t K, int32_t S, int32_t P, int32_t N, int32_t O_max,
+                            int32_t *o, uint8_t *valid) {
+  int32_t o_min = floordiv(i + P - K + 1 + S - 1, S);
+  int32_t upper = floordiv(i + P, S);
+  for (int32_t r = 0; r < N; ++r) {
+    o[r] = o_min + r;
+    valid[r] = (o[r] <= upper) && (o[r] >= 0) && (o[r] < O_max);
+  }
+}
+
+static int32_t conv_h_out(const so_conv_geom *g) { return (g->h_in + 2 * g->p - g->k) / g->s + 1; }
+static int32_t conv_w_out(const so_conv_geom *g) { return (g->w_in + 2 * g->p - g->k) / g->s + 1; }
+
+typedef struct {
+  int32_t n, j;
+} cand_t;
+
+/* Stable sort of candidates by n (candidates are generated in j order, so this is the
+ * reference's lexsort((j, n)) at conv.py:71).  Counting sort over n in [0, n_sp]. */
+static void stable_sort_by_n(cand_t *c, int64_t C, int32_t n_buckets, cand_t *tmp) {
+  int64_t *cnt = (int64_t *)calloc((size_t)n_buckets + 1, sizeof(int64_t));
+  for (int64_t i = 0; i < C; ++i) cnt[c[i].n + 1]++;
+  for (int32_t b = 0; b < n_buckets; ++b) cnt[b + 1] += cnt[b];
+  for (int64_t i = 0; i < C; ++i) tmp[cnt[c[i].n]++] = c[i];
+  memcpy(c, tmp, (size_t)C * sizeof(cand_t));
+  free(cnt);
+}
+
+/* connectivity/conv.py:128-172 build_conv_structure, with _compress_candidates (:57-99) and
+ * _delta_t_three_regimes (:102-125). */
+int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *src, int32_t E_len,
+                      int32_t n_in, int32_t *l2g, int32_t *n_real, float *delta_t, int32_t *tap_c,
+                      int32_t *tap_ky, int32_t *tap_kx) {
+  const int32_t K = g->k, S = g->s, P = g->p, L = g->max_queue_len;
+  const int32_t h_out = conv_h_out(g), w_out = conv_w_out(g), n_sp = h_out * w_out;
+  const int32_t N = (K - 1) / S + 1, hw = g->h_in * g->w_in;
+  if (E_len <= 0 || L <= 0 || n_sp <= 0) return -1;
+
+  int32_t *ex = (int32_t *)malloc(sizeof(int32_t) * (size_t)E_len * 3);
+  int32_t *ey = ex + E_len, *ec = ey + E_len;
+  for (int32_t j = 0; j < E_len; ++j) { /* conv.py:32-43 unravel_conv_source */
+    int32_t s = src[j];
+    ec[j] = floordiv(s, hw);
+    int32_t rem = floormod(s, hw);
+    ey[j] = floordiv(rem, g->w_in);
+    ex[j] = floormod(rem, g->w_in);
+  }
+
+  int64_t C = (int64_t)E_len * N * N;
+  cand_t *cand = (cand_t *)malloc(sizeof(cand_t) * (size_t)C);
+  cand_t *tmp = (cand_t *)malloc(sizeof(cand_t) * (size_t)C);
+  int32_t oy[64], ox[64];
+  uint8_t vy[64], vx[64];
+  if (N > 64) return -2;
+  for (int32_t j = 0; j < E_len; ++j) {
+    axis_candidates(ey[j], K, S, P, N, h_out, oy, vy);
+    axis_candidates(ex[j], K, S, P, N, w_out, ox, vx);
+    int real = j < n_in;
+    for (int32_t a = 0; a < N; ++a)
+      for (int32_t b = 0; b < N; ++b) {
+        int64_t k = ((int64_t)j * N + a) * N + b;
+        int valid = vy[a] && vx[b] && real;
+        cand[k].n = valid ? oy[a] * w_out + ox[b] : n_sp;
+        cand[k].j = j;
+      }
+  }
+  stable_sort_by_n(cand, C, n_sp + 1, tmp);
+
+  for (int64_t i = 0; i < (int64_t)n_sp * L; ++i) l2g[i] = E_len;
+  memset(n_real, 0, sizeof(int32_t) * (size_t)n_sp);
+  int64_t last_start = 0;
+  for (int64_t i = 0; i < C; ++i) {
+    if (i == 0 || cand[i].n != cand[i - 1].n) last_start = i;
+    int64_t rank = i - last_start;
+    if (cand[i].n >= n_sp) continue; /* trash row */
+    if (rank < L) l2g[(int64_t)cand[i].n * L + rank] = cand[i].j;
+    if (rank + 1 > n_real[cand[i].n]) n_real[cand[i].n] = (int32_t)(rank + 1);
+  }
+
+  /* conv.py:159-162: empty columns clamp to the last real event; gather semantics as JAX. */
+  float global_last = times[jidx((int64_t)n_in - 1, E_len)];
+  for (int32_t pos = 0; pos < n_sp; ++pos) {
+    int32_t oyy = pos / w_out, oxx = pos % w_out;
+    const int32_t *row = l2g + (int64_t)pos * L;
+    float *dt = delta_t + (int64_t)pos * L;
+    /* gathered times per column */
+    int32_t nr = n_real[pos];
+    int32_t last_real_col = nr - 1;
+    if (last_real_col < 0) last_real_col = 0;
+    if (last_real_col > L - 1) last_real_col = L - 1;
+    int32_t ej_last = row[last_real_col] < n_in - 1 ? row[last_real_col] : n_in - 1;
+    float t_last_real = times[jidx(ej_last, E_len)];
+    float prev = 0.0f;
+    for (int32_t col = 0; col < L; ++col) {
+      int32_t ej = row[col] < n_in - 1 ? row[col] : n_in - 1;
+      int64_t gi = jidx(ej, E_len);
+      float tg = times[gi];
+      float d_real = tg - prev;
+      prev = tg;
+      if (col < nr)
+        dt[col] = d_real;
+      else if (col == nr)
+        dt[col] = global_last - t_last_real;
+      else
+        dt[col] = 0.0f;
+      /* conv.py:164-171 taps, clipped into the kernel */
+      int32_t ky = ey[gi] - oyy * S + P, kx = ex[gi] - oxx * S + P;
+      tap_ky[(int64_t)pos * L + col] = ky < 0 ? 0 : (ky > K - 1 ? K - 1 : ky);
+      tap_kx[(int64_t)pos * L + col] = kx < 0 ? 0 : (kx > K - 1 ? K - 1 : kx);
+      tap_c[(int64_t)pos * L + col] = ec[gi];
+    }
+  }
+  free(ex);
+  free(cand);
+  free(tmp);
+  return 0;
+}
+
+/* stream.py:49-64 _select_spikes + :24-46 _pack_stream.  global_j_of(neuron, col) is given
+ * as a callback-free table: for conv it is l2g[(neuron % n_sp) * L + col], for fc it is col. */
+static void select_and_pack(const uint8_t *mask, int32_t n, int32_t L, const int32_t *l2g,
+                            int32_t n_sp, const float *times, int32_t E_len, int32_t M,
+                            float *out_times, int32_t *out_src, int32_t *n_real_out) {
+  int32_t *nidx = (int32_t *)calloc((size_t)(M > 0 ? M : 1), sizeof(int32_t));
+  int32_t *cidx = (int32_t *)calloc((size_t)(M > 0 ? M : 1), sizeof(int32_t));
+  int64_t total = 0;
+  for (int32_t i = 0; i < n; ++i)
+    for (int32_t t = 0; t < L; ++t)
+      if (mask[(int64_t)i * L + t]) {
+        if (total < M) {
+          nidx[total] = i;
+          cidx[total] = t;
+        }
+        total++;
+      }
+  int32_t nr = (int32_t)total;
+  int32_t *key = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  int32_t *gj = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  for (int32_t k = 0; k < M; ++k) {
+    int32_t col = cidx[k] < L - 1 ? cidx[k] : L - 1;
+    int32_t g = l2g ? l2g[(int64_t)(nidx[k] % n_sp) * L + col] : cidx[k];
+    gj[k] = g;
+    key[k] = k < nr ? g : E_len;
+  }
+  /* stable sort of indices 0..M-1 by key (jnp.lexsort on a single key is stable) */
+  int32_t *order = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  int32_t *tmpo = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  for (int32_t k = 0; k < M; ++k) order[k] = k;
+  for (int32_t width = 1; width < M; width *= 2) { /* bottom-up stable merge sort */
+    for (int32_t lo = 0; lo < M; lo += 2 * width) {
+      int32_t mid = lo + width < M ? lo + width : M, hi = lo + 2 * width < M ? lo + 2 * width : M;
+      int32_t a = lo, b = mid, o = lo;
+      while (a < mid && b < hi) tmpo[o++] = key[order[b]] < key[order[a]] ? order[b++] : order[a++];
+      while (a < mid) tmpo[o++] = order[a++];
+      while (b < hi) tmpo[o++] = order[b++];
+    }
+    memcpy(order, tmpo, sizeof(int32_t) * (size_t)M);
+  }
+  for (int32_t k = 0; k < M; ++k) {
+    int32_t src_k = order[k];
+    int real = src_k < nr;
+    int32_t safe = gj[src_k] < E_len - 1 ? gj[src_k] : E_len - 1;
+    out_times[k] = real ? times[jidx(safe, E_len)] : SO_PAD_TIME;
+    out_src[k] = nidx[src_k];
+  }
+  *n_real_out = nr;
+  free(nidx);
+  free(cidx);
+  free(key);
+  free(gj);
+  free(order);
+  free(tmpo);
+}
+
+static void reduce_layer(so_layer_out *out, int32_t n, int32_t L, const uint8_t *ovf) {
+  out->any_overflow = 0;
+  for (int64_t e = 0; e < (int64_t)n * L; ++e)
+    if (ovf[e]) {
+      out->any_overflow = 1;
+      break;
+    }
+  int32_t lo = out->vmin[0], hi = out->vmax[0];
+  for (int32_t i = 1; i < n; ++i) {
+    if (out->vmin[i] < lo) lo = out->vmin[i];
+    if (out->vmax[i] > hi) hi = out->vmax[i];
+  }
+  out->vmin_all = lo;
+  out->vmax_all = hi;
+}
+
+/* layers/conv.py:209-234 ConvLayer.forward with QuantBackend.scan (quant/backend.py:31-53). */
+int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const float *times,
+                    const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out) {
+  const int32_t L = g->max_queue_len, h_out = conv_h_out(g), w_out = conv_w_out(g);
+  const int32_t n_sp = h_out * w_out, OC = g->oc, n = OC * n_sp, K = g->k;
+  if (h_out < 1 || w_out < 1 || L < 1) return -1;
+  size_t nl = (size_t)n_sp * L;
+  int32_t *l2g = (int32_t *)malloc(sizeof(int32_t) * nl);
+  int32_t *nreal = (int32_t *)malloc(sizeof(int32_t) * (size_t)n_sp);
+  float *dt = (float *)malloc(sizeof(float) * nl);
+  int32_t *tc = (int32_t *)malloc(sizeof(int32_t) * nl * 3);
+  int32_t *tky = tc + nl, *tkx = tky + nl;
+  int rc = so_conv_structure(g, times, src, E_len, n_in, l2g, nreal, dt, tc, tky, tkx);
+  if (rc) return rc;
+
+  /* neuron_delta_t = tile_channels(delta_t) (layers/conv.py:252-254); codes per conv.py:209-218 */
+  size_t NL = (size_t)n * L;
+  int32_t *a = (int32_t *)malloc(sizeof(int32_t) * NL);
+  uint8_t *isid = (uint8_t *)malloc(NL);
+  int32_t *qi = (int32_t *)malloc(sizeof(int32_t) * NL);
+  int32_t *a_sp = (int32_t *)malloc(sizeof(int32_t) * nl);
+  uint8_t *id_sp = (uint8_t *)malloc(nl);
+  so_apply_decay_table(dt, (int64_t)nl, qp->lut, qp->lut_len, a_sp, id_sp);
+  for (int32_t o = 0; o < OC; ++o)
+    for (int32_t pos = 0; pos < n_sp; ++pos)
+      for (int32_t col = 0; col < L; ++col) {
+        size_t e = ((size_t)o * n_sp + pos) * L + col, es = (size_t)pos * L + col;
+        a[e] = a_sp[es];
+        isid[e] = id_sp[es];
+        int real = col < nreal[pos];
+        int64_t c = jidx(tc[es], g->ic);
+        int32_t qv = qp->q[(((int64_t)o * g->ic + c) * K + tky[es]) * K + tkx[es]];
+        qi[e] = real ? qv : 0;
+      }
+  uint8_t *mask = out->spike_mask ? out->spike_mask : (uint8_t *)malloc(NL);
+  uint8_t *ovf = out->overflowed ? out->overflowed : (uint8_t *)malloc(NL);
+  so_run_layer(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
+               qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax);
+  select_and_pack(mask, n, L, l2g, n_sp, times, E_len, g->max_out_spikes, out->out_times,
+                  out->out_src, &out->n_real_out);
+  out->spike_count = out->n_real_out;
+  int32_t mx = 0;
+  for (int32_t pos = 0; pos < n_sp; ++pos)
+    if (nreal[pos] > mx) mx = nreal[pos];
+  out->needed_queue = mx + 1; /* layers/conv.py:222-224 */
+  reduce_layer(out, n, L, ovf);
+  out->fits = out->needed_queue <= L && out->n_real_out <= g->max_out_spikes &&
+              0 <= g->max_extra_steps; /* capacity.py:60-63 */
+  if (!out->spike_mask) free(mask);
+  if (!out->overflowed) free(ovf);
+  free(l2g);
+  free(nreal);
+  free(dt);
+  free(tc);
+  free(a);
+  free(isid);
+  free(qi);
+  free(a_sp);
+  free(id_sp);
+  return 0;
+}
+
+/* layers/fc.py:385-402 FCLayer.forward with QuantBackend; structure per connectivity/fc.py:20-33,
+ * codes per fc.py:54-61. */
+int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *times,
+                  const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out) {
+  const int32_t n = g->n_out, L = E_len;
+  if (E_len <= 0) return -1;
+  float *dt = (float *)malloc(sizeof(float) * (size_t)L);
+  float prev = 0.0f;
+  for (int32_t j = 0; j < L; ++j) {
+    float gap = times[j] - prev;
+    prev = times[j];
+    dt[j] = j < n_in ? gap : 0.0f;
+  }
+  int32_t *a1 = (int32_t *)malloc(sizeof(int32_t) * (size_t)L);
+  uint8_t *id1 = (uint8_t *)malloc((size_t)L);
+  so_apply_decay_table(dt, L, qp->lut, qp->lut_len, a1, id1);
+  size_t NL = (size_t)n * L;
+  int32_t *a = (int32_t *)malloc(sizeof(int32_t) * NL);
+  uint8_t *isid = (uint8_t *)malloc(NL);
+  int32_t *qi = (int32_t *)malloc(sizeof(int32_t) * NL);
+  for (int32_t o = 0; o < n; ++o)
+    for (int32_t j = 0; j < L; ++j) {
+      size_t e = (size_t)o * L + j;
+      a[e] = a1[j];
+      isid[e] = id1[j];
+      qi[e] = j < n_in ? qp->q[(int64_t)o * g->n_in + jidx(src[j], g->n_in)] : 0;
+    }
+  uint8_t *mask = out->spike_mask ? out->spike_mask : (uint8_t *)malloc(NL);
+  uint8_t *ovf = out->overflowed ? out->overflowed : (uint8_t *)malloc(NL);
+  so_run_layer(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
+               qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax);
+  select_and_pack(mask, n, L, NULL, 1, times, E_len, g->max_out_spikes, out->out_times,
+                  out->out_src, &out->n_real_out);
+  out->spike_count = out->n_real_out;
+  out->needed_queue = 0;
+  reduce_layer(out, n, L, ovf);
+  out->fits = out->n_real_out <= g->max_out_spikes && 0 <= g->max_extra_steps;
+  if (!out->spike_mask) free(mask);
+  if (!out->overflowed) free(ovf);
+  free(dt);
+  free(a1);
+  free(id1);
+  free(a);
+  free(isid);
+  free(qi);
+  return 0;
+}
+
+/* ---- multi-threaded batch driver (CPU baseline only) ---- */
+typedef struct {
+  const so_layer_spec *layers;
+  int32_t n_layers;
+  const float *times;
+  const int32_t *src, *n_real;
+  int32_t B, E_len;
+  int32_t *v_final_last, *spike_counts, *fits;
+  atomic_int next;
+  atomic_int err;
+} batch_ctx;
+
+static int32_t layer_neurons(const so_layer_spec *l) {
+  if (l->kind == 1) return l->fc.n_out;
+  const so_conv_geom *g = &l->conv;
+  return g->oc * conv_h_out(g) * conv_w_out(g);
+}
+
+static void *batch_worker(void *arg) {
+  batch_ctx *c = (batch_ctx *)arg;
+  for (;;) {
+    int b = atomic_fetch_add(&c->next, 1);
+    if (b >= c->B) break;
+    const float *t = c->times + (int64_t)b * c->E_len;
+    const int32_t *s = c->src + (int64_t)b * c->E_len;
+    int32_t E = c->E_len, nin = c->n_real[b];
+    float *t_own = NULL;
+    int32_t *s_own = NULL;
+    int fits = 1;
+    for (int32_t l = 0; l < c->n_layers; ++l) {
+      const so_layer_spec *ls = &c->layers[l];
+      int32_t n = layer_neurons(ls);
+      int32_t M = ls->kind == 1 ? ls->fc.max_out_spikes : ls->conv.max_out_spikes;
+      so_layer_out o;
+      memset(&o, 0, sizeof(o));
+      o.v_final = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
+      o.vmin = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
+      o.vmax = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
+      o.out_times = (float *)malloc(sizeof(float) * (size_t)(M > 0 ? M : 1));
+      o.out_src = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+      int rc = ls->kind == 1 ? so_fc_forward(&ls->fc, &ls->qp, t, s, E, nin, &o)
+                             : so_conv_forward(&ls->conv, &ls->qp, t, s, E, nin, &o);
+      if (rc) atomic_store(&c->err, rc);
+      fits = fits && o.fits;
+      c->spike_counts[(int64_t)b * c->n_layers + l] = o.spike_count;
+      if (l == c->n_layers - 1)
+        memcpy(c->v_final_last + (int64_t)b * n, o.v_final, sizeof(int32_t) * (size_t)n);
+      free(t_own);
+      free(s_own);
+      t_own = o.out_times;
+      s_own = o.out_src;
+      t = t_own;
+      s = s_own;
+      E = M;
+      nin = o.n_real_out;
+      free(o.v_final);
+      free(o.vmin);
+      free(o.vmax);
+    }
+    c->fits[b] = fits;
+    free(t_own);
+    free(s_own);
+  }
+  return NULL;
+}
+
+int so_network_batch(const so_layer_spec *layers, int32_t n_layers, const float *times,
+                     const int32_t *src, const int32_t *n_real, int32_t B, int32_t E_len,
+                     int32_t threads, int32_t *v_final_last, int32_t *spike_counts,
+                     int32_t *fits) {
+  batch_ctx c;
+  c.layers = layers;
+  c.n_layers = n_layers;
+  c.times = times;
+  c.src = src;
+  c.n_real = n_real;
+  c.B = B;
+  c.E_len = E_len;
+  c.v_final_last = v_final_last;
+  c.spike_counts = spike_counts;
+  c.fits = fits;
+  atomic_init(&c.next, 0);
+  atomic_init(&c.err, 0);
+  if (threads < 1) threads = 1;
+  pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)threads);
+  for (int i = 0; i < threads; ++i) pthread_create(&th[i], NULL, batch_worker, &c);
+  for (int i = 0; i < threads; ++i) pthread_join(th[i], NULL);
+  free(th);
+  return atomic_load(&c.err);
+}

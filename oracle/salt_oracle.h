@@ -1,0 +1,116 @@
+/*
+ * CPU oracle for the SALT integer event-driven forward — TEST INFRASTRUCTURE ONLY.
+ *
+ * A literal, single-sample restatement of the reference's JAX code path
+ *   salt_core/quant/fixed_point.py, salt_core/quant/codes.py (apply_decay_table_int),
+ *   salt_core/quant/scan.py, salt_core/connectivity/{conv,fc}.py, salt_core/stream.py,
+ *   salt_core/layers/{conv,fc}.py forward, salt_core/capacity.py fits.
+ * It builds the reference's dense (n, L) queue arrays, scans every one of the L columns for
+ * every neuron, selects spikes in jnp.nonzero row-major order and stable-sorts them by the
+ * global event index, exactly as the reference does.  It is deliberately NOT shaped like the
+ * GPU kernels so that it checks them independently.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may use this library.
+ * The product path never links or calls it.
+ */
+#ifndef SALT_ORACLE_H
+#define SALT_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { SO_ROUND = 0, SO_TRUNCATE = 1 };
+enum { SO_WRAP = 0, SO_SATURATE = 1 };
+
+/* Quantised per-layer parameters (salt_core/quant/params.py:9-21). */
+typedef struct {
+  const int32_t *q;        /* conv: (oc, ic, k, k); fc: (n_out, n_in) */
+  const int32_t *lut;      /* decay_table_int, lut_len entries */
+  int32_t lut_len;
+  const int32_t *vth;      /* per-neuron integer threshold, or NULL = never fires */
+  int32_t f_a, f_V, i_V;
+  int32_t round_mode;      /* SO_ROUND / SO_TRUNCATE */
+  int32_t overflow_mode;   /* SO_WRAP / SO_SATURATE */
+} so_quant_params;
+
+typedef struct {
+  int32_t ic, h_in, w_in, oc, k, s, p;
+  int32_t max_queue_len, max_out_spikes, max_extra_steps;
+} so_conv_geom;
+
+typedef struct {
+  int32_t n_in, n_out;
+  int32_t max_out_spikes, max_extra_steps;
+} so_fc_geom;
+
+/* Output of one layer for one sample.  Arrays are caller-allocated:
+ *   v_final, vmin, vmax: n_neurons
+ *   spike_mask, overflowed: n_neurons * L (may be NULL)
+ *   out_times, out_src: max_out_spikes
+ */
+typedef struct {
+  int32_t *v_final, *vmin, *vmax;
+  uint8_t *spike_mask, *overflowed;
+  float *out_times;
+  int32_t *out_src;
+  int32_t n_real_out;      /* total spikes (not clipped to max_out_spikes) */
+  int32_t spike_count;     /* same as n_real_out (sum of spike_mask) */
+  int32_t needed_queue;    /* conv: max(n_real per position) + 1; fc: 0 */
+  int32_t any_overflow;
+  int32_t vmin_all, vmax_all;
+  int32_t fits;
+} so_layer_out;
+
+/* fixed_point.py:32-44, :47-65, :68-90 */
+int32_t so_round_shift(int32_t x, int32_t shift_bits, int32_t round_mode);
+int32_t so_wide_mul_shift(int32_t a, int32_t v, int32_t shift_bits, int32_t round_mode);
+int32_t so_fit_to_bits(int32_t x, int32_t total_bits, int32_t overflow_mode, int32_t *overflowed);
+
+/* quant/scan.py:22-52 — one event update; returns v_final and writes the other results. */
+int32_t so_process_event(int32_t v0, int32_t a, int32_t is_identity, int32_t q, int32_t has_vth,
+                         int32_t vth, int32_t f_a, int32_t f_V, int32_t i_V, int32_t round_mode,
+                         int32_t overflow_mode, int32_t *is_spiked, int32_t *overflowed,
+                         int32_t *v_unfitted);
+
+/* quant/codes.py:87-105 */
+void so_apply_decay_table(const float *delta_t, int64_t n, const int32_t *lut, int32_t lut_len,
+                          int32_t *a_int, uint8_t *is_identity);
+
+/* quant/scan.py:97-132 over (n, L) inputs. spike_mask/overflowed may be NULL. */
+void so_run_layer(const int32_t *a_int, const uint8_t *is_identity, const int32_t *q_int,
+                  const int32_t *vth, int32_t n, int32_t L, int32_t f_a, int32_t f_V, int32_t i_V,
+                  int32_t round_mode, int32_t overflow_mode, uint8_t *spike_mask,
+                  uint8_t *overflowed, int32_t *v_final, int32_t *vmin, int32_t *vmax);
+
+/* connectivity/conv.py:128-172 (+ :57-125). Outputs (n_sp, L) arrays and n_real (n_sp). */
+int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *src, int32_t E_len,
+                      int32_t n_in, int32_t *l2g, int32_t *n_real, float *delta_t, int32_t *tap_c,
+                      int32_t *tap_ky, int32_t *tap_kx);
+
+/* Whole layers (layers/conv.py:209-234, layers/fc.py:385-402 with QuantBackend). */
+int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const float *times,
+                    const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out);
+int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *times,
+                  const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out);
+
+/* Multi-threaded batch driver used only as the timed CPU baseline: runs a chain of layers over
+ * B samples with `threads` workers (one sample per task).  kinds[l]: 0 conv, 1 fc.
+ * Writes the last layer's v_final (B, n_last) and per-(sample, layer) spike counts. */
+typedef struct {
+  int32_t kind;
+  so_conv_geom conv;
+  so_fc_geom fc;
+  so_quant_params qp;
+} so_layer_spec;
+
+int so_network_batch(const so_layer_spec *layers, int32_t n_layers, const float *times,
+                     const int32_t *src, const int32_t *n_real, int32_t B, int32_t E_len,
+                     int32_t threads, int32_t *v_final_last, int32_t *spike_counts,
+                     int32_t *fits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

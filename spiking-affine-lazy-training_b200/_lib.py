@@ -1,0 +1,119 @@
+"""ctypes binding of libsalt_b200.so (include/salt_b200.h).
+
+The library must have been built (``build.py``); importing the product path without it raises:
+there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsalt_b200.so")
+
+SALT_OK, SALT_BAD_ARG, SALT_CUDA_ERROR, SALT_NO_DEVICE, SALT_WORKSPACE_TOO_SMALL = 0, 1, 2, 3, 4
+_i32 = ctypes.c_int32
+_vp = ctypes.c_void_p
+
+
+class QuantDesc(ctypes.Structure):
+    _fields_ = [(n, _i32) for n in ("f_a", "f_V", "i_V", "round_mode", "overflow_mode", "lut_len",
+                                    "has_vth", "q_bits", "needs_tail")]
+
+
+class ConvDesc(ctypes.Structure):
+    _fields_ = [(n, _i32) for n in ("ic", "h_in", "w_in", "oc", "k", "s", "p", "max_queue_len",
+                                    "max_out_spikes", "max_extra_steps")]
+
+
+class FCDesc(ctypes.Structure):
+    _fields_ = [(n, _i32) for n in ("n_in", "n_out", "max_out_spikes", "max_extra_steps")]
+
+
+class StreamIn(ctypes.Structure):
+    _fields_ = [("times", _vp), ("src", _vp), ("n_real", _vp), ("capacity", _i32),
+                ("virtual_pads", _i32)]
+
+
+class StreamOut(ctypes.Structure):
+    _fields_ = [("times", _vp), ("src", _vp), ("n_real", _vp)]
+
+
+class LayerStats(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("spike_count", "needed_queue", "overflowed", "vmin", "vmax",
+                                   "fits")]
+
+
+class LayerSpec(ctypes.Structure):
+    _fields_ = [("kind", _i32), ("conv", ConvDesc), ("fc", FCDesc), ("quant", QuantDesc),
+                ("q_host", _vp), ("lut_host", _vp), ("vth_host", _vp)]
+
+
+# every function of include/salt_b200.h: name -> (restype, argtypes)
+_SIGS = {
+    "salt_conv_layer_workspace_size": (_i32, [_vp, _vp, _i32, _i32, _vp]),
+    "salt_conv_layer_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
+                                       ctypes.c_size_t, _vp]),
+    "salt_fc_layer_workspace_size": (_i32, [_vp, _vp, _i32, _i32, _vp]),
+    "salt_fc_layer_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
+                                     ctypes.c_size_t, _vp]),
+    "salt_quant_scan_dense": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     _vp, _vp]),
+    "salt_network_create": (_i32, [_vp, _i32, _vp]),
+    "salt_network_destroy": (_i32, [_vp]),
+    "salt_network_workspace_size": (_i32, [_vp, _i32, _i32, _vp]),
+    "salt_network_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    ctypes.c_size_t, _vp]),
+    "salt_network_last_launch_count": (_i32, [_vp]),
+    "salt_float_fc_scan": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, ctypes.c_float,
+                                  _vp, _vp, _i32, _vp, _vp, ctypes.c_size_t, _vp]),
+    "salt_float_fc_scan_workspace_size": (_i32, [_i32, _i32, _vp]),
+    "salt_last_error": (ctypes.c_char_p, []),
+    "salt_version": (ctypes.c_char_p, []),
+    "salt_launch_counter": (ctypes.c_int64, [_i32]),
+}
+
+_lib = None
+
+
+class SaltError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"salt_b200 status {status}: {message}")
+        self.status = status
+
+
+class ArgumentError(SaltError, ValueError):
+    """SALT_BAD_ARG: the reference raises ValueError for the same inputs."""
+
+
+def lib():
+    """The loaded library; raises when it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with build.py (there is no "
+                               "CPU fallback for the salt_b200 kernels)")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = h
+    return _lib
+
+
+def check(status: int) -> None:
+    if status == SALT_OK:
+        return
+    msg = lib().salt_last_error().decode(errors="replace")
+    if status == SALT_BAD_ARG:
+        raise ArgumentError(status, msg)
+    raise SaltError(status, msg)
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def byref(x):
+    return ctypes.cast(ctypes.pointer(x), _vp)

@@ -1,0 +1,213 @@
+// Integer FC layer for B200 (sm_100a).
+//
+// Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:385-402): every output
+// neuron scans the whole input stream (connectivity/fc.py:20-33 — Δt against the previous
+// entry, the first against t=0, pads masked to Δt=0 and weight 0), applying
+// quant/scan.py:22-52 per entry; spikes leave as per-event neuron bitmasks and are compacted
+// into the next EventStream in (event, neuron) order (stream.py:24-81).
+//
+// fc_scan: one warp per (sample, group of 32 output neurons); lane = neuron.  Events are read
+// 32 at a time (one coalesced load per lane) and broadcast with shuffles; the weight codes of
+// the 32 events are fetched before the dependent recurrence so their latency overlaps.
+// Pad entries are identity steps that can only fire when v_th_int <= 0, so they are walked
+// only in that case (tail mode).
+#include "salt_layers.cuh"
+
+namespace salt {
+
+template <bool FIRES>
+__global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
+  __shared__ int32_t lut_s[kLutSmemMax];
+  const bool lut_smem = P.qc.lut_len <= kLutSmemMax;
+  if (lut_smem)
+    for (int i = threadIdx.x; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
+  __syncthreads();
+  const int32_t* lut = lut_smem ? lut_s : P.lut;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= (int64_t)P.batch * P.G) return;
+  const int b = (int)(gw / P.G), g = (int)(gw % P.G);
+  const int o = g * 32 + lane;
+  const bool active = o < P.n_out;
+  const int32_t n_in = P.in_nreal[b];
+  const int32_t n_eff = P.n_eff(b);
+  const int32_t nproc = P.tail_mode ? P.in.capacity : n_eff;
+  const int32_t vth = (P.has_vth && active) ? P.vth[o] : 0;
+  uint32_t* sw_b = FIRES ? P.sw + (int64_t)b * P.sw_stride : nullptr;
+  int32_t* chunk_b = FIRES ? P.chunk_spikes + (int64_t)b * P.n_spk_chunks : nullptr;
+
+  int32_t V = 0, vmin = 0, vmax = 0, ovf_any = 0, nspk = 0;
+  float tprev = 0.0f;
+  for (int32_t base = 0; base < nproc; base += 32) {
+    const int32_t jl = base + lane;
+    float t_l = 0.0f;
+    int32_t s_l = 0;
+    if (jl < nproc) {
+      t_l = P.in.time(b, jl, n_eff);
+      s_l = P.in.source(b, jl, n_eff);
+    }
+    const int cnt = min(32, nproc - base);
+    int32_t qv[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int32_t s = __shfl_sync(0xffffffffu, s_l, e);
+      const bool real = (base + e) < n_in && e < cnt;  // fc.py:29 is_real = j < n_real
+      qv[e] = (real && active) ? __ldg(&P.qT[jax_index(s, P.n_in) * P.n_out + o]) : 0;
+    }
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      if (e < cnt) {
+        const int32_t j = base + e;
+        const float t = __shfl_sync(0xffffffffu, t_l, e);
+        const bool real = j < n_in;
+        const int32_t dt = real ? dt_from_times(t, tprev) : 0;
+        tprev = t;
+        const int32_t a = decay_code(dt, lut, P.qc.lut_len);
+        int32_t u;
+        bool ovf;
+        const int32_t w = quant_step(V, a, dt == 0, qv[e], P.qc, u, ovf);
+        const bool spike = FIRES && active && w >= vth;
+        V = spike ? 0 : w;
+        if (active) {
+          vmin = min(vmin, u);
+          vmax = max(vmax, u);
+          ovf_any |= (int32_t)ovf;
+        }
+        nspk += spike;
+        if (FIRES) {
+          const uint32_t bal = __ballot_sync(0xffffffffu, spike);
+          if (lane == 0) {
+            sw_b[(int64_t)j * P.G + g] = bal;
+            if (bal) atomicAdd(&chunk_b[j >> kSpkChunkShift], __popc(bal));
+          }
+        }
+      }
+    }
+  }
+  if (active) P.v_final[(int64_t)b * P.n_out + o] = V;
+  if (FIRES && active) P.n_spk[(int64_t)b * P.n_out + o] = nspk;
+  vmin = warp_min(vmin);
+  vmax = warp_max(vmax);
+  ovf_any = warp_or(ovf_any);
+  const int32_t tot = warp_sum(nspk);
+  if (lane == 0) {
+    atomicMin(&P.vmin[b], vmin);
+    atomicMax(&P.vmax[b], vmax);
+    if (ovf_any) atomicOr(&P.ovf[b], 1);
+    if (tot) atomicAdd(&P.s_total[b], tot);
+  }
+}
+
+
+__global__ void __launch_bounds__(kCompactThreads)
+fc_compact(FCLaunch P, salt_stream_out out) {
+  __shared__ int32_t s_scan[kScanSmem];
+  const int b = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
+  if (P.s_total[b] > P.M) return;
+  const int32_t n_eff = P.n_eff(b);
+  const int32_t nproc = P.tail_mode ? P.in.capacity : n_eff;
+  const int32_t j = c * kSpkChunk + tid;
+  const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.G;
+  int32_t cnt = 0;
+  if (j < nproc)
+    for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[g]);
+  int32_t total;
+  const int32_t off = block_exclusive_scan(cnt, s_scan, total);
+  if (cnt == 0) return;
+  int32_t k = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
+  const float t = P.in.time(b, j, n_eff);
+  for (int g = 0; g < P.G; ++g) {
+    uint32_t wd = sw_j[g];
+    while (wd) {
+      const int bit = __ffs(wd) - 1;
+      wd &= wd - 1u;
+      out.times[(int64_t)b * P.M + k] = t;
+      out.src[(int64_t)b * P.M + k] = g * 32 + bit;
+      ++k;
+    }
+  }
+}
+
+// Samples with more than max_out spikes keep the first M in neuron-major order (stream.py:60):
+// every spike of neurons < n*, and the first r of neuron n* (by event index).
+__global__ void __launch_bounds__(kCompactThreads)
+fc_truncated(FCLaunch P, salt_stream_out out) {
+  __shared__ int32_t s_scan[kScanSmem];
+  __shared__ int32_t s_cut[4];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int32_t S = P.s_total[b], M = P.M;
+  if (S <= M || M <= 0) return;
+  const int32_t n_eff = P.n_eff(b);
+  const int32_t nproc = P.tail_mode ? P.in.capacity : n_eff;
+  if (tid == 0) {
+    int32_t cum = 0, nst = P.n_out - 1;
+    for (int o = 0; o < P.n_out; ++o) {
+      const int32_t c = P.n_spk[(int64_t)b * P.n_out + o];
+      if (cum + c >= M) {
+        nst = o;
+        break;
+      }
+      cum += c;
+    }
+    s_cut[0] = nst;
+    s_cut[1] = M - cum;
+    s_cut[2] = 0x7fffffff;
+  }
+  __syncthreads();
+  const int nst = s_cut[0], gq = nst >> 5, bq = nst & 31;
+  int32_t seen = 0;
+  for (int32_t j0 = 0; j0 < nproc; j0 += blockDim.x) {
+    const int32_t j = j0 + tid;
+    const int32_t hit =
+        j < nproc ? (int32_t)((P.sw[(int64_t)b * P.sw_stride + (int64_t)j * P.G + gq] >> bq) & 1u)
+                  : 0;
+    int32_t total;
+    const int32_t off = block_exclusive_scan(hit, s_scan, total);
+    if (hit && seen + off + 1 == s_cut[1]) s_cut[2] = j;
+    seen += total;
+    __syncthreads();
+    if (s_cut[2] != 0x7fffffff) break;
+  }
+  __syncthreads();
+  const int32_t j_cut = s_cut[2];
+  int32_t written = 0;
+  for (int32_t j0 = 0; j0 < nproc; j0 += blockDim.x) {
+    const int32_t j = j0 + tid;
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.G;
+    int32_t cnt = 0;
+    if (j < nproc)
+      for (int g = 0; g < P.G; ++g) {
+        uint32_t wd = sw_j[g];
+        while (wd) {
+          const int o = g * 32 + __ffs(wd) - 1;
+          wd &= wd - 1u;
+          cnt += (o < nst) || (o == nst && j <= j_cut);
+        }
+      }
+    int32_t total;
+    const int32_t off = block_exclusive_scan(cnt, s_scan, total);
+    if (cnt) {
+      const float t = P.in.time(b, j, n_eff);
+      int32_t k = written + off;
+      for (int g = 0; g < P.G; ++g) {
+        uint32_t wd = sw_j[g];
+        while (wd) {
+          const int o = g * 32 + __ffs(wd) - 1;
+          wd &= wd - 1u;
+          if ((o < nst) || (o == nst && j <= j_cut)) {
+            out.times[(int64_t)b * M + k] = t;
+            out.src[(int64_t)b * M + k] = o;
+            ++k;
+          }
+        }
+      }
+    }
+    written += total;
+  }
+}
+
+void* fc_scan_kernel(bool fires) {
+  return fires ? (void*)fc_scan<true> : (void*)fc_scan<false>;
+}
+
+}  // namespace salt

@@ -1,0 +1,766 @@
+// Host side of libsalt_b200: argument checks, launch planning, workspace layout, the C ABI of
+// include/salt_b200.h and the native network plan.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "salt_layers.cuh"
+
+namespace salt {
+
+
+static thread_local std::string g_err;
+static thread_local int64_t g_launches = 0;
+
+static salt_status fail(salt_status s, const std::string& msg) {
+  g_err = msg;
+  return s;
+}
+
+#define SALT_CUDA(call)                                                                \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(SALT_CUDA_ERROR, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define SALT_LAUNCHED(name)                                                             \
+  do {                                                                                  \
+    ++g_launches;                                                                       \
+    cudaError_t e_ = cudaGetLastError();                                                \
+    if (e_ != cudaSuccess)                                                              \
+      return fail(SALT_CUDA_ERROR, std::string("launch ") + name + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Sequential carving of a workspace; with base == nullptr it only measures.
+struct Carver {
+  char* base;
+  size_t off = 0;
+  explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+  template <typename T>
+  T* take(size_t n) {
+    off = align256(off);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+  size_t size() const { return align256(off); }
+};
+
+// ---------------------------------------------------------------- small kernels
+
+// One warp per sample: exclusive scan in place of the spike counts per event chunk.
+__global__ void spike_chunk_scan(int32_t* __restrict__ chunk, int32_t n_chunks, int32_t batch) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= batch) return;
+  int32_t* c = chunk + (int64_t)warp * n_chunks;
+  int32_t carry = 0;
+  for (int base = 0; base < n_chunks; base += 32) {
+    const int i = base + lane;
+    const int32_t v = i < n_chunks ? c[i] : 0;
+    int32_t incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (i < n_chunks) c[i] = carry + incl - v;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
+
+struct FinishArgs {
+  const int32_t *s_total, *needed, *vmin, *vmax, *ovf;
+  int32_t L, M, max_extra, is_conv, batch;
+};
+
+// Per-sample diagnostics and Capacity.fits (salt_core/capacity.py:60-63; layers/conv.py:222-226,
+// layers/fc.py:393-395).
+__global__ void layer_finish(FinishArgs A, int32_t* out_nreal, salt_layer_stats st) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= A.batch) return;
+  const int32_t S = A.s_total[b];
+  const int32_t nq = A.is_conv ? A.needed[b] : 0;
+  if (out_nreal) out_nreal[b] = S;
+  if (st.spike_count) st.spike_count[b] = S;
+  if (st.needed_queue) st.needed_queue[b] = nq;
+  if (st.overflowed) st.overflowed[b] = A.ovf[b] != 0;
+  if (st.vmin) st.vmin[b] = A.vmin[b];
+  if (st.vmax) st.vmax[b] = A.vmax[b];
+  if (st.fits)
+    st.fits[b] = (A.is_conv ? nq <= A.L : 1) && S <= A.M && 0 <= A.max_extra;
+}
+
+__global__ void transpose_i32(const int32_t* __restrict__ q, int32_t* __restrict__ qT, int rows,
+                              int cols) {  // qT[c][r] = q[r][c]
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * cols) return;
+  const int r = (int)(i / cols), c = (int)(i % cols);
+  qT[(int64_t)c * rows + r] = q[i];
+}
+
+// fits of layer l for sample b lives at per_layer[l * layer_stride + b].
+__global__ void fits_and(const int32_t* __restrict__ per_layer, int n_layers, int64_t layer_stride,
+                         int batch, int32_t* __restrict__ fits) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  int32_t f = 1;
+  for (int l = 0; l < n_layers; ++l) f &= per_layer[(int64_t)l * layer_stride + b] != 0;
+  fits[b] = f;
+}
+
+// quant/scan.py:97-132 on materialised (n, L) inputs: one thread per neuron, every column.
+__global__ void dense_scan(QuantCfg qc, int32_t n, int32_t L, const int32_t* __restrict__ a_int,
+                           const uint8_t* __restrict__ is_id, const int32_t* __restrict__ q_int,
+                           const int32_t* __restrict__ vth, uint8_t* __restrict__ mask,
+                           uint8_t* __restrict__ ovf_out, int32_t* __restrict__ v_final,
+                           int32_t* __restrict__ vmin, int32_t* __restrict__ vmax) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int32_t v = 0, lo = 0, hi = 0;
+  const int32_t th = vth ? vth[i] : 0;
+  for (int32_t t = 0; t < L; ++t) {
+    const int64_t e = i * L + t;
+    int32_t u;
+    bool ovf;
+    const int32_t w = quant_step(v, a_int[e], is_id[e] != 0, q_int[e], qc, u, ovf);
+    const bool spike = vth != nullptr && w >= th;
+    v = spike ? 0 : w;
+    lo = min(lo, u);
+    hi = max(hi, u);
+    if (mask) mask[e] = spike;
+    if (ovf_out) ovf_out[e] = ovf;
+  }
+  v_final[i] = v;
+  vmin[i] = lo;
+  vmax[i] = hi;
+}
+
+// ---------------------------------------------------------------- checks
+
+static salt_status check_quant(const salt_quant_desc* q) {
+  if (!q) return fail(SALT_BAD_ARG, "quant descriptor is NULL");
+  if (q->f_a < 0 || q->f_a > 15)
+    return fail(SALT_BAD_ARG, "f_a must be in [0, 15] (fixed_point.MAX_SHIFT_BITS)");
+  if (q->f_V < 0 || q->i_V < 1 || q->i_V + q->f_V > 30)
+    return fail(SALT_BAD_ARG, "need f_V >= 0, i_V >= 1, i_V + f_V <= 30 (MAX_REGISTER_BITS)");
+  if (q->round_mode != SALT_ROUND && q->round_mode != SALT_TRUNCATE)
+    return fail(SALT_BAD_ARG, "round_mode must be SALT_ROUND or SALT_TRUNCATE");
+  if (q->overflow_mode != SALT_WRAP && q->overflow_mode != SALT_SATURATE)
+    return fail(SALT_BAD_ARG, "overflow_mode must be SALT_WRAP or SALT_SATURATE");
+  if (q->lut_len < 0) return fail(SALT_BAD_ARG, "lut_len must be >= 0");
+  return SALT_OK;
+}
+
+static QuantCfg make_qc(const salt_quant_desc* q) {
+  QuantCfg c;
+  c.f_a = q->f_a;
+  c.f_V = q->f_V;
+  c.total_bits = q->i_V + q->f_V;
+  c.round_half = (q->round_mode == SALT_ROUND && q->f_a > 0) ? (1 << (q->f_a - 1)) : 0;
+  c.saturate = q->overflow_mode == SALT_SATURATE;
+  c.lut_len = q->lut_len;
+  return c;
+}
+
+static salt_status check_stream_in(const salt_stream_in* in, int32_t batch) {
+  if (!in || !in->times || !in->src || !in->n_real)
+    return fail(SALT_BAD_ARG, "input stream pointers must be non-NULL");
+  if (in->capacity < 1) return fail(SALT_BAD_ARG, "input stream capacity must be >= 1");
+  if (batch < 1 || batch > 65535) return fail(SALT_BAD_ARG, "batch must be in [1, 65535]");
+  return SALT_OK;
+}
+
+// ---------------------------------------------------------------- conv planning
+
+struct ConvPlan {
+  int32_t h_out, w_out, n_sp, ncand, nslots, lpu, G, ocp, wt_bytes;
+  int64_t n_neurons;
+  int32_t tile_h, tile_w, tiles_x, tiles_y, T, n_part_chunks, n_spk_chunks, tail_mode;
+  int64_t list_stride;
+  size_t smem;
+};
+
+static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, const ConvPlan& p,
+                         int npm) {
+  size_t s = 0;
+  s += align16((size_t)d->ic * d->k * d->k * p.ocp * p.wt_bytes);
+  s += align16((size_t)(q->lut_len <= kLutSmemMax ? q->lut_len : 0) * 4);
+  s += align16((size_t)npm * p.ocp * 4);
+  s += align16((size_t)npm * 4) * 2;
+  s += align16((size_t)npm * (kFusedChunk / 32) * 4);
+  s += align16((size_t)kFusedChunk * 20);
+  s += align16((size_t)p.ocp * 4);
+  s += 64;
+  return s;
+}
+
+static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, int32_t batch,
+                             int32_t E, ConvPlan& p) {
+  if (!d) return fail(SALT_BAD_ARG, "conv descriptor is NULL");
+  if (d->ic < 1 || d->h_in < 1 || d->w_in < 1 || d->oc < 1 || d->k < 1 || d->s < 1 || d->p < 0)
+    return fail(SALT_BAD_ARG, "conv geometry: ic,h_in,w_in,oc,k,s must be >= 1 and p >= 0");
+  if (d->h_in + d->p > 32000 || d->w_in + d->p > 32000)
+    return fail(SALT_BAD_ARG, "conv input plane too large (h_in + p and w_in + p <= 32000)");
+  p.h_out = (d->h_in + 2 * d->p - d->k) / d->s + 1;
+  p.w_out = (d->w_in + 2 * d->p - d->k) / d->s + 1;
+  if (d->h_in + 2 * d->p - d->k < 0 || p.h_out < 1 || p.w_out < 1)
+    return fail(SALT_BAD_ARG, "conv geometry degenerates to an empty output plane");
+  if (d->max_queue_len < 1) return fail(SALT_BAD_ARG, "max_queue_len must be >= 1");
+  if (d->max_out_spikes < 1) return fail(SALT_BAD_ARG, "max_out_spikes must be >= 1");
+  p.n_sp = p.h_out * p.w_out;
+  p.n_neurons = (int64_t)d->oc * p.n_sp;
+  if (p.n_neurons > 0x7fffffffLL) return fail(SALT_BAD_ARG, "too many neurons");
+  p.ncand = (d->k - 1) / d->s + 1;
+  p.nslots = p.ncand * p.ncand;
+  if (p.ncand > 16) return fail(SALT_BAD_ARG, "k / s too large (at most 16 candidates per axis)");
+  int lpu = 1;
+  while (lpu < d->oc && lpu < 32) lpu <<= 1;
+  p.lpu = lpu;
+  p.G = (d->oc + lpu - 1) / lpu;
+  p.ocp = p.G * lpu;
+  p.wt_bytes = q->q_bits <= 8 ? 1 : (q->q_bits <= 16 ? 2 : 4);
+  p.tail_mode = q->needs_tail ? 1 : 0;
+  // Positions per block: as many as fit a ~100 KB shared-memory budget (two blocks per SM),
+  // at most 256 (balanced chunk work), never fewer than one candidate window.
+  const size_t budget = 100 * 1024;
+  int npm_cap = 256;
+  while (npm_cap > 1 && fused_smem(d, q, p, npm_cap) > budget) npm_cap >>= 1;
+  if (p.n_sp <= npm_cap) {
+    p.tile_h = p.h_out;
+    p.tile_w = p.w_out;
+  } else {
+    p.tile_w = std::min(p.w_out, std::max(16, p.ncand));
+    p.tile_h = std::max(1, npm_cap / p.tile_w);
+    p.tile_h = std::min(p.h_out, std::max(p.tile_h, std::min(p.ncand, p.h_out)));
+    if (p.tile_w < p.w_out && p.tile_w < p.ncand) p.tile_w = std::min(p.w_out, p.ncand);
+  }
+  p.tiles_x = (p.w_out + p.tile_w - 1) / p.tile_w;
+  p.tiles_y = (p.h_out + p.tile_h - 1) / p.tile_h;
+  p.T = p.tiles_x * p.tiles_y;
+  const int per_y = p.tiles_y > 1 ? (p.ncand - 1 + p.tile_h - 1) / p.tile_h + 1 : 1;
+  const int per_x = p.tiles_x > 1 ? (p.ncand - 1 + p.tile_w - 1) / p.tile_w + 1 : 1;
+  p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
+  p.n_part_chunks = (E + kPartChunk - 1) / kPartChunk;
+  p.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
+  p.smem = fused_smem(d, q, p, p.tile_h * p.tile_w);
+  if (p.smem > 227 * 1024)
+    return fail(SALT_BAD_ARG, "conv layer weights do not fit in shared memory (ic*k*k*oc too "
+                              "large for the chosen weight width)");
+  (void)batch;
+  return SALT_OK;
+}
+
+struct ConvScratch {
+  int32_t *stats, *s_total, *needed, *vmin, *vmax, *ovf, *tail_total, *oc_total, *chunk;
+  size_t stats_bytes;
+  uint32_t* sw;
+  int32_t *tail_cnt, *counts, *tile_len, *tile_off, *lists, *hist;
+};
+
+static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, int32_t E,
+                         void* ws, ConvScratch& s) {
+  Carver c(ws);
+  const size_t nstat = (size_t)B * 6 + (size_t)B * d->oc + (size_t)B * p.n_spk_chunks;
+  s.stats = c.take<int32_t>(nstat);
+  s.stats_bytes = nstat * 4;
+  if (s.stats) {
+    s.s_total = s.stats;
+    s.needed = s.stats + B;
+    s.vmin = s.stats + 2 * B;
+    s.vmax = s.stats + 3 * B;
+    s.ovf = s.stats + 4 * B;
+    s.tail_total = s.stats + 5 * B;
+    s.oc_total = s.stats + 6 * B;
+    s.chunk = s.oc_total + (size_t)B * d->oc;
+  }
+  s.sw = c.take<uint32_t>((size_t)B * E * p.nslots * p.G);
+  s.tail_cnt = p.tail_mode ? c.take<int32_t>((size_t)B * p.n_neurons) : nullptr;
+  if (p.T > 1) {
+    s.counts = c.take<int32_t>((size_t)B * p.n_part_chunks * p.T);
+    s.tile_len = c.take<int32_t>((size_t)B * p.T);
+    s.tile_off = c.take<int32_t>((size_t)B * p.T);
+    s.lists = c.take<int32_t>((size_t)B * p.list_stride);
+  } else {
+    s.counts = s.tile_len = s.tile_off = s.lists = nullptr;
+  }
+  s.hist = c.take<int32_t>((size_t)B * 2 * p.n_sp);
+  return c.size();
+}
+
+static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_desc* q,
+                                     const int32_t* qw, const int32_t* lut, const int32_t* vth,
+                                     int32_t B, const salt_stream_in* in, salt_stream_out* out,
+                                     int32_t* v_final, const salt_layer_stats* stats, void* ws,
+                                     size_t ws_bytes, cudaStream_t st) {
+  salt_status rc = check_quant(q);
+  if (rc) return rc;
+  if ((rc = check_stream_in(in, B))) return rc;
+  if (!qw || (q->lut_len > 0 && !lut) || (q->has_vth && !vth) || !out || !out->times ||
+      !out->src || !out->n_real || !v_final)
+    return fail(SALT_BAD_ARG, "conv layer: NULL parameter or output pointer");
+  const int32_t E = in->capacity;
+  ConvPlan p;
+  if ((rc = plan_conv(d, q, B, E, p))) return rc;
+  ConvScratch s;
+  const size_t need = conv_carve(d, p, B, E, nullptr, s);
+  if (!ws || ws_bytes < need) return fail(SALT_WORKSPACE_TOO_SMALL, "conv workspace too small");
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return fail(SALT_BAD_ARG, "workspace not 256-byte aligned");
+  conv_carve(d, p, B, E, ws, s);
+
+  ConvLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.ic = d->ic; L.h_in = d->h_in; L.w_in = d->w_in; L.hw_in = d->h_in * d->w_in;
+  L.oc = d->oc; L.k = d->k; L.s = d->s; L.p = d->p;
+  L.h_out = p.h_out; L.w_out = p.w_out; L.n_sp = p.n_sp; L.n_neurons = p.n_neurons;
+  L.ncand = p.ncand; L.nslots = p.nslots;
+  L.L = d->max_queue_len; L.M = d->max_out_spikes; L.max_extra = d->max_extra_steps;
+  L.lpu = p.lpu; L.G = p.G; L.ocp = p.ocp;
+  L.tile_h = p.tile_h; L.tile_w = p.tile_w; L.tiles_x = p.tiles_x; L.T = p.T;
+  L.n_part_chunks = p.n_part_chunks; L.list_stride = p.list_stride;
+  L.in.times = in->times; L.in.src = in->src; L.in.capacity = E; L.in.virtual_pads = in->virtual_pads;
+  L.in_nreal = in->n_real; L.batch = B;
+  L.q = qw; L.lut = lut; L.lut_in_smem = q->lut_len <= kLutSmemMax; L.vth = vth;
+  L.has_vth = q->has_vth != 0; L.qc = make_qc(q);
+  L.v_final = v_final;
+  L.sw = s.sw; L.sw_stride = (int64_t)E * p.nslots * p.G;
+  L.chunk_spikes = s.chunk; L.chunk_off = s.chunk; L.n_spk_chunks = p.n_spk_chunks;
+  L.s_total = s.s_total; L.oc_total = s.oc_total; L.needed = s.needed; L.vmin = s.vmin;
+  L.vmax = s.vmax; L.ovf = s.ovf; L.tail_total = s.tail_total;
+  L.tail_mode = p.tail_mode; L.tail_cnt = s.tail_cnt;
+  L.tile_len = s.tile_len; L.tile_off = s.tile_off; L.tile_lists = s.lists;
+
+  SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
+  if (p.T > 1) {
+    dim3 gp(p.n_part_chunks, B);
+    conv_tile_count<<<gp, 256, p.T * sizeof(int32_t), st>>>(L, s.counts);
+    SALT_LAUNCHED("conv_tile_count");
+    conv_tile_scan_offsets<<<(B * 32 + 255) / 256, 256, 0, st>>>(L, s.counts, s.tile_len,
+                                                                 s.tile_off);
+    SALT_LAUNCHED("conv_tile_scan_offsets");
+    conv_tile_scatter<<<gp, 256, 2 * p.T * (kPartChunk / 32) * sizeof(uint32_t), st>>>(
+        L, s.counts, s.lists);
+    SALT_LAUNCHED("conv_tile_scatter");
+  }
+  void* fn = conv_fused_kernel(p.wt_bytes, p.lpu);
+  SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+  void* args[] = {&L};
+  SALT_CUDA(cudaLaunchKernel(fn, dim3(p.T, B), dim3(kFusedThreads), args, p.smem, st));
+  SALT_LAUNCHED("conv_fused");
+  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
+  SALT_LAUNCHED("spike_chunk_scan");
+  conv_compact<<<dim3(p.n_spk_chunks, B), kCompactThreads, 0, st>>>(L, *out);
+  SALT_LAUNCHED("conv_compact");
+  if (p.tail_mode) {
+    conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
+    SALT_LAUNCHED("conv_tail_append");
+  }
+  conv_truncated<<<B, kCompactThreads, 0, st>>>(L, *out, s.hist);
+  SALT_LAUNCHED("conv_truncated");
+  FinishArgs fa{s.s_total, s.needed, s.vmin, s.vmax, s.ovf, d->max_queue_len, d->max_out_spikes,
+                d->max_extra_steps, 1, B};
+  salt_layer_stats none{};
+  layer_finish<<<(B + 255) / 256, 256, 0, st>>>(fa, out->n_real, stats ? *stats : none);
+  SALT_LAUNCHED("layer_finish");
+  return SALT_OK;
+}
+
+// ---------------------------------------------------------------- fc
+
+struct FCScratch {
+  int32_t *stats, *s_total, *vmin, *vmax, *ovf, *chunk, *n_spk, *qT;
+  size_t stats_bytes;
+  uint32_t* sw;
+};
+
+static size_t fc_carve(const salt_fc_desc* d, const salt_quant_desc* q, int32_t B, int32_t E,
+                       bool need_qT, void* ws, FCScratch& s) {
+  Carver c(ws);
+  const int G = (d->n_out + 31) / 32;
+  const int nsc = (E + kSpkChunk - 1) / kSpkChunk;
+  const size_t nstat = (size_t)B * 4 + (q->has_vth ? (size_t)B * nsc : 0);
+  s.stats = c.take<int32_t>(nstat);
+  s.stats_bytes = nstat * 4;
+  if (s.stats) {
+    s.s_total = s.stats;
+    s.vmin = s.stats + B;
+    s.vmax = s.stats + 2 * B;
+    s.ovf = s.stats + 3 * B;
+    s.chunk = q->has_vth ? s.stats + 4 * B : nullptr;
+  }
+  s.sw = q->has_vth ? c.take<uint32_t>((size_t)B * E * G) : nullptr;
+  s.n_spk = q->has_vth ? c.take<int32_t>((size_t)B * d->n_out) : nullptr;
+  s.qT = need_qT ? c.take<int32_t>((size_t)d->n_in * d->n_out) : nullptr;
+  return c.size();
+}
+
+static salt_status check_fc(const salt_fc_desc* d) {
+  if (!d) return fail(SALT_BAD_ARG, "fc descriptor is NULL");
+  if (d->n_in < 1 || d->n_out < 1) return fail(SALT_BAD_ARG, "fc: n_in and n_out must be >= 1");
+  if (d->max_out_spikes < 1) return fail(SALT_BAD_ARG, "max_out_spikes must be >= 1");
+  return SALT_OK;
+}
+
+static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc* q,
+                                   const int32_t* qw, bool q_is_transposed, const int32_t* lut,
+                                   const int32_t* vth, int32_t B, const salt_stream_in* in,
+                                   salt_stream_out* out, int32_t* v_final,
+                                   const salt_layer_stats* stats, void* ws, size_t ws_bytes,
+                                   cudaStream_t st) {
+  salt_status rc = check_quant(q);
+  if (rc) return rc;
+  if ((rc = check_stream_in(in, B))) return rc;
+  if ((rc = check_fc(d))) return rc;
+  if (!qw || (q->lut_len > 0 && !lut) || (q->has_vth && !vth) || !out || !out->n_real ||
+      !v_final || (q->has_vth && (!out->times || !out->src)))
+    return fail(SALT_BAD_ARG, "fc layer: NULL parameter or output pointer");
+  const int32_t E = in->capacity;
+  FCScratch s;
+  const size_t need = fc_carve(d, q, B, E, !q_is_transposed, nullptr, s);
+  if (!ws || ws_bytes < need) return fail(SALT_WORKSPACE_TOO_SMALL, "fc workspace too small");
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return fail(SALT_BAD_ARG, "workspace not 256-byte aligned");
+  fc_carve(d, q, B, E, !q_is_transposed, ws, s);
+  const int32_t* qT = qw;
+  if (!q_is_transposed) {
+    const int64_t n = (int64_t)d->n_in * d->n_out;
+    transpose_i32<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(qw, s.qT, d->n_out, d->n_in);
+    SALT_LAUNCHED("transpose_i32");
+    qT = s.qT;
+  }
+  FCLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.n_in = d->n_in; L.n_out = d->n_out; L.G = (d->n_out + 31) / 32;
+  L.M = d->max_out_spikes; L.max_extra = d->max_extra_steps;
+  L.in.times = in->times; L.in.src = in->src; L.in.capacity = E; L.in.virtual_pads = in->virtual_pads;
+  L.in_nreal = in->n_real; L.batch = B;
+  L.qT = qT; L.lut = lut; L.vth = vth; L.has_vth = q->has_vth != 0; L.qc = make_qc(q);
+  L.v_final = v_final;
+  L.sw = s.sw; L.sw_stride = (int64_t)E * L.G;
+  L.chunk_spikes = s.chunk; L.chunk_off = s.chunk; L.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
+  L.s_total = s.s_total; L.vmin = s.vmin; L.vmax = s.vmax; L.ovf = s.ovf; L.n_spk = s.n_spk;
+  L.tail_mode = q->has_vth && q->needs_tail;
+  SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
+  const int64_t warps = (int64_t)B * L.G;
+  const int wpb = kFcThreads / 32;
+  const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
+  void* scan_args[] = {&L};
+  SALT_CUDA(cudaLaunchKernel(fc_scan_kernel(q->has_vth != 0), dim3(grid), dim3(kFcThreads),
+                             scan_args, 0, st));
+  SALT_LAUNCHED("fc_scan");
+  if (q->has_vth) {
+    spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
+    SALT_LAUNCHED("spike_chunk_scan");
+    fc_compact<<<dim3(L.n_spk_chunks, B), kCompactThreads, 0, st>>>(L, *out);
+    SALT_LAUNCHED("fc_compact");
+    fc_truncated<<<B, kCompactThreads, 0, st>>>(L, *out);
+    SALT_LAUNCHED("fc_truncated");
+  }
+  FinishArgs fa{s.s_total, nullptr, s.vmin, s.vmax, s.ovf, 0, d->max_out_spikes,
+                d->max_extra_steps, 0, B};
+  salt_layer_stats none{};
+  layer_finish<<<(B + 255) / 256, 256, 0, st>>>(fa, out->n_real, stats ? *stats : none);
+  SALT_LAUNCHED("layer_finish");
+  return SALT_OK;
+}
+
+}  // namespace salt
+
+// ==================================================================== C ABI
+using namespace salt;
+
+struct LayerRec {
+  salt_layer_spec spec;
+  int32_t *d_q = nullptr, *d_lut = nullptr, *d_vth = nullptr;
+  int64_t n_neurons = 0;
+  int32_t M = 0;
+};
+
+struct salt_network {
+  std::vector<LayerRec> layers;
+  int32_t last_launches = 0;
+};
+
+extern "C" {
+
+const char* salt_last_error(void) { return g_err.c_str(); }
+const char* salt_version(void) { return "salt_b200 0.1 (sm_100a)"; }
+int64_t salt_launch_counter(int32_t reset) {
+  const int64_t v = g_launches;
+  if (reset) g_launches = 0;
+  return v;
+}
+
+salt_status salt_conv_layer_workspace_size(const salt_conv_desc* layer, const salt_quant_desc* quant,
+                                           int32_t batch, int32_t in_capacity, size_t* bytes) {
+  salt_status rc = check_quant(quant);
+  if (rc) return rc;
+  if (!bytes || batch < 1 || in_capacity < 1) return fail(SALT_BAD_ARG, "bad batch/capacity");
+  ConvPlan p;
+  if ((rc = plan_conv(layer, quant, batch, in_capacity, p))) return rc;
+  ConvScratch s;
+  *bytes = conv_carve(layer, p, batch, in_capacity, nullptr, s);
+  return SALT_OK;
+}
+
+salt_status salt_conv_layer_forward(const salt_conv_desc* layer, const salt_quant_desc* quant,
+                                    const int32_t* q, const int32_t* lut, const int32_t* vth,
+                                    int32_t batch, const salt_stream_in* in, salt_stream_out* out,
+                                    int32_t* v_final, const salt_layer_stats* stats,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  return conv_forward_impl(layer, quant, q, lut, vth, batch, in, out, v_final, stats, workspace,
+                           workspace_bytes, (cudaStream_t)stream);
+}
+
+salt_status salt_fc_layer_workspace_size(const salt_fc_desc* layer, const salt_quant_desc* quant,
+                                         int32_t batch, int32_t in_capacity, size_t* bytes) {
+  salt_status rc = check_quant(quant);
+  if (rc) return rc;
+  if ((rc = check_fc(layer))) return rc;
+  if (!bytes || batch < 1 || in_capacity < 1) return fail(SALT_BAD_ARG, "bad batch/capacity");
+  FCScratch s;
+  *bytes = fc_carve(layer, quant, batch, in_capacity, true, nullptr, s);
+  return SALT_OK;
+}
+
+salt_status salt_fc_layer_forward(const salt_fc_desc* layer, const salt_quant_desc* quant,
+                                  const int32_t* q, const int32_t* lut, const int32_t* vth,
+                                  int32_t batch, const salt_stream_in* in, salt_stream_out* out,
+                                  int32_t* v_final, const salt_layer_stats* stats, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  return fc_forward_impl(layer, quant, q, false, lut, vth, batch, in, out, v_final, stats,
+                         workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+salt_status salt_quant_scan_dense(const salt_quant_desc* quant, int32_t n, int32_t L,
+                                  const int32_t* a_int, const uint8_t* is_identity,
+                                  const int32_t* q_int, const int32_t* vth, uint8_t* spike_mask,
+                                  uint8_t* overflowed, int32_t* v_final, int32_t* vmin,
+                                  int32_t* vmax, void* stream) {
+  salt_status rc = check_quant(quant);
+  if (rc) return rc;
+  if (n < 1 || L < 1 || !a_int || !is_identity || !q_int || !v_final || !vmin || !vmax ||
+      (quant->has_vth && !vth))
+    return fail(SALT_BAD_ARG, "dense scan: bad sizes or NULL pointers");
+  dense_scan<<<(unsigned)((n + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
+      make_qc(quant), n, L, a_int, is_identity, q_int, quant->has_vth ? vth : nullptr, spike_mask,
+      overflowed, v_final, vmin, vmax);
+  SALT_LAUNCHED("dense_scan");
+  return SALT_OK;
+}
+
+// ---------------------------------------------------------------- network plan
+
+static int q_bits_of(const int32_t* q, int64_t n) {
+  int bits = 8;
+  for (int64_t i = 0; i < n; ++i) {
+    if (q[i] < -32768 || q[i] > 32767) return 32;
+    if (q[i] < -128 || q[i] > 127) bits = 16;
+  }
+  return bits;
+}
+
+salt_status salt_network_create(const salt_layer_spec* layers, int32_t n_layers,
+                                salt_network** out) {
+  if (!layers || n_layers < 1 || !out) return fail(SALT_BAD_ARG, "network: no layers");
+  auto* net = new salt_network();
+  for (int l = 0; l < n_layers; ++l) {
+    LayerRec r;
+    r.spec = layers[l];
+    salt_quant_desc& qd = r.spec.quant;
+    salt_status rc = check_quant(&qd);
+    int64_t nq = 0, nvth = 0;
+    if (!rc && r.spec.kind == 0) {
+      ConvPlan p;
+      rc = plan_conv(&r.spec.conv, &qd, 1, 1, p);
+      nq = (int64_t)r.spec.conv.oc * r.spec.conv.ic * r.spec.conv.k * r.spec.conv.k;
+      nvth = p.n_neurons;
+      r.n_neurons = p.n_neurons;
+      r.M = r.spec.conv.max_out_spikes;
+    } else if (!rc && r.spec.kind == 1) {
+      rc = check_fc(&r.spec.fc);
+      nq = (int64_t)r.spec.fc.n_in * r.spec.fc.n_out;
+      nvth = r.spec.fc.n_out;
+      r.n_neurons = r.spec.fc.n_out;
+      r.M = r.spec.fc.max_out_spikes;
+    } else if (!rc) {
+      rc = fail(SALT_BAD_ARG, "layer kind must be 0 (conv) or 1 (fc)");
+    }
+    if (!rc && (!r.spec.q_host || (qd.lut_len > 0 && !r.spec.lut_host) ||
+                (qd.has_vth && !r.spec.vth_host)))
+      rc = fail(SALT_BAD_ARG, "network: NULL host parameter pointer");
+    if (rc) {
+      salt_network_destroy(net);
+      return rc;
+    }
+    qd.q_bits = q_bits_of(r.spec.q_host, nq);
+    bool tail = false;
+    if (qd.has_vth)
+      for (int64_t i = 0; i < nvth; ++i) tail |= r.spec.vth_host[i] <= 0;
+    for (int i = 0; i < qd.lut_len; ++i)
+      tail |= r.spec.lut_host[i] < 0 || r.spec.lut_host[i] >= (1 << qd.f_a);
+    qd.needs_tail = qd.needs_tail || tail;
+    std::vector<int32_t> qbuf(r.spec.q_host, r.spec.q_host + nq);
+    if (r.spec.kind == 1) {  // store FC weights transposed: (n_in, n_out)
+      const int n_in = r.spec.fc.n_in, n_out = r.spec.fc.n_out;
+      for (int o = 0; o < n_out; ++o)
+        for (int i = 0; i < n_in; ++i) qbuf[(int64_t)i * n_out + o] = r.spec.q_host[(int64_t)o * n_in + i];
+    }
+    cudaError_t e = cudaMalloc(&r.d_q, sizeof(int32_t) * std::max<int64_t>(nq, 1));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(r.d_q, qbuf.data(), sizeof(int32_t) * nq, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && qd.lut_len > 0) {
+      e = cudaMalloc(&r.d_lut, sizeof(int32_t) * qd.lut_len);
+      if (e == cudaSuccess)
+        e = cudaMemcpy(r.d_lut, r.spec.lut_host, sizeof(int32_t) * qd.lut_len,
+                       cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess && qd.has_vth) {
+      e = cudaMalloc(&r.d_vth, sizeof(int32_t) * nvth);
+      if (e == cudaSuccess)
+        e = cudaMemcpy(r.d_vth, r.spec.vth_host, sizeof(int32_t) * nvth, cudaMemcpyHostToDevice);
+    }
+    r.spec.q_host = r.spec.lut_host = r.spec.vth_host = nullptr;
+    net->layers.push_back(r);
+    if (e != cudaSuccess) {
+      salt_network_destroy(net);
+      return fail(SALT_CUDA_ERROR, std::string("network parameter upload: ") + cudaGetErrorString(e));
+    }
+  }
+  *out = net;
+  return SALT_OK;
+}
+
+salt_status salt_network_destroy(salt_network* net) {
+  if (!net) return SALT_OK;
+  for (auto& r : net->layers) {
+    cudaFree(r.d_q);
+    cudaFree(r.d_lut);
+    cudaFree(r.d_vth);
+  }
+  delete net;
+  return SALT_OK;
+}
+
+struct NetLayout {
+  float* st_t[2];
+  int32_t* st_s[2];
+  int32_t* st_n[2];
+  int32_t* vtmp;
+  int32_t* stats;  // 6 * n_layers * B
+  void* scratch;
+  size_t scratch_bytes, total;
+};
+
+static salt_status net_layout(const salt_network* net, int32_t B, int32_t E0, void* ws,
+                              NetLayout& o) {
+  const int nl = (int)net->layers.size();
+  int32_t maxM = 1;
+  int64_t maxN = 1;
+  for (int l = 0; l + 1 < nl; ++l) {
+    maxM = std::max(maxM, net->layers[l].M);
+    maxN = std::max(maxN, net->layers[l].n_neurons);
+  }
+  size_t scratch = 0;
+  int32_t E = E0;
+  for (int l = 0; l < nl; ++l) {
+    const LayerRec& r = net->layers[l];
+    size_t b = 0;
+    if (r.spec.kind == 0) {
+      ConvPlan p;
+      salt_status rc = plan_conv(&r.spec.conv, &r.spec.quant, B, E, p);
+      if (rc) return rc;
+      ConvScratch s;
+      b = conv_carve(&r.spec.conv, p, B, E, nullptr, s);
+    } else {
+      FCScratch s;
+      b = fc_carve(&r.spec.fc, &r.spec.quant, B, E, false, nullptr, s);
+    }
+    scratch = std::max(scratch, b);
+    E = r.M;
+  }
+  Carver c(ws);
+  for (int i = 0; i < 2; ++i) {
+    o.st_t[i] = c.take<float>((size_t)B * maxM);
+    o.st_s[i] = c.take<int32_t>((size_t)B * maxM);
+    o.st_n[i] = c.take<int32_t>((size_t)B);
+  }
+  o.vtmp = c.take<int32_t>((size_t)B * maxN);
+  o.stats = c.take<int32_t>((size_t)6 * nl * B);
+  o.scratch = c.take<char>(scratch);
+  o.scratch_bytes = scratch;
+  o.total = c.size();
+  return SALT_OK;
+}
+
+salt_status salt_network_workspace_size(const salt_network* net, int32_t batch,
+                                        int32_t in_capacity, size_t* bytes) {
+  if (!net || !bytes || batch < 1 || in_capacity < 1)
+    return fail(SALT_BAD_ARG, "network workspace: bad arguments");
+  NetLayout o;
+  salt_status rc = net_layout(net, batch, in_capacity, nullptr, o);
+  if (rc) return rc;
+  *bytes = o.total;
+  return SALT_OK;
+}
+
+salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_stream_in* in,
+                                 int32_t* logits, int32_t* spike_count, int32_t* overflowed,
+                                 int32_t* vmin, int32_t* vmax, int32_t* needed_queue,
+                                 int32_t* fits, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  if (!net || !logits) return fail(SALT_BAD_ARG, "network forward: NULL network or logits");
+  salt_status rc = check_stream_in(in, batch);
+  if (rc) return rc;
+  NetLayout o;
+  if ((rc = net_layout(net, batch, in->capacity, nullptr, o))) return rc;
+  if (!workspace || workspace_bytes < o.total)
+    return fail(SALT_WORKSPACE_TOO_SMALL, "network workspace too small");
+  net_layout(net, batch, in->capacity, workspace, o);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t launches0 = g_launches;
+  const int nl = (int)net->layers.size();
+  const int B = batch;
+  salt_stream_in cur = *in;
+  for (int l = 0; l < nl; ++l) {
+    LayerRec& r = net->layers[l];
+    const bool last = l == nl - 1;
+    salt_stream_out so{o.st_t[l & 1], o.st_s[l & 1], o.st_n[l & 1]};
+    int32_t* vf = last ? logits : o.vtmp;
+    int32_t* sb = o.stats + (size_t)6 * l * B;
+    salt_layer_stats ls{spike_count ? spike_count + (size_t)l * B : sb,
+                        needed_queue ? needed_queue + (size_t)l * B : sb + B,
+                        overflowed ? overflowed + (size_t)l * B : sb + 2 * B,
+                        vmin ? vmin + (size_t)l * B : sb + 3 * B,
+                        vmax ? vmax + (size_t)l * B : sb + 4 * B,
+                        sb + 5 * B};
+    if (r.spec.kind == 0)
+      rc = conv_forward_impl(&r.spec.conv, &r.spec.quant, r.d_q, r.d_lut, r.d_vth, B, &cur, &so,
+                             vf, &ls, o.scratch, o.scratch_bytes, st);
+    else
+      rc = fc_forward_impl(&r.spec.fc, &r.spec.quant, r.d_q, true, r.d_lut, r.d_vth, B, &cur, &so,
+                           vf, &ls, o.scratch, o.scratch_bytes, st);
+    if (rc) return rc;
+    cur.times = so.times;
+    cur.src = so.src;
+    cur.n_real = so.n_real;
+    cur.capacity = r.M;
+    cur.virtual_pads = 1;
+  }
+  if (fits) {  // per-layer fits sit at offset 5*B of each layer's (6, B) stats block
+    fits_and<<<(B + 255) / 256, 256, 0, st>>>(o.stats + 5 * B, nl, (int64_t)6 * B, B, fits);
+    SALT_LAUNCHED("fits_and");
+  }
+  net->last_launches = (int32_t)(g_launches - launches0);
+  return SALT_OK;
+}
+
+int32_t salt_network_last_launch_count(const salt_network* net) {
+  return net ? net->last_launches : 0;
+}
+
+
+}  // extern "C"

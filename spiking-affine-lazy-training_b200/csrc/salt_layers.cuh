@@ -1,0 +1,157 @@
+// Launch parameter blocks and block-level helpers shared by the layer kernels.
+#pragma once
+#include "../../include/salt_b200.h"
+#include "salt_common.cuh"
+
+namespace salt {
+
+constexpr int kFusedThreads = 256;   // conv_fused block size (8 warps)
+constexpr int kFusedChunk = 512;     // events bucketed per shared-memory chunk
+constexpr int kPartChunk = 1024;     // events per tile-partition block
+constexpr int kCompactThreads = 256; // compaction block size == events per spike chunk
+constexpr int kSpkChunkShift = 8;
+constexpr int kSpkChunk = 1 << kSpkChunkShift;
+static_assert(kSpkChunk == kCompactThreads, "one compaction block per spike chunk");
+constexpr int kLutSmemMax = 4096;    // decay tables longer than this are read from global
+constexpr int kScanSmem = 33;        // ints of shared memory block_exclusive_scan needs
+
+__host__ __device__ __forceinline__ size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+struct ConvLaunch {
+  // geometry (salt_core/layers/conv.py:107-167)
+  int32_t ic, h_in, w_in, hw_in, oc, k, s, p, h_out, w_out, n_sp;
+  int64_t n_neurons;
+  int32_t ncand, nslots;      // candidates per axis (k-1)//s+1 and per event (ncand^2)
+  int32_t L, M, max_extra;    // max_queue_len, max_out_spikes, max_extra_steps
+  int32_t lpu, G, ocp;        // lanes per channel group, channel groups, padded channel stride
+  // tiling of the output plane
+  int32_t tile_h, tile_w, tiles_x, T;
+  int32_t n_part_chunks;
+  int64_t list_stride;        // per-sample stride of the tile event lists
+  // input stream
+  StreamView in;
+  const int32_t* in_nreal;
+  int32_t batch;
+  // parameters
+  const int32_t* q;
+  const int32_t* lut;
+  int32_t lut_in_smem;
+  const int32_t* vth;
+  int32_t has_vth;
+  QuantCfg qc;
+  // outputs
+  int32_t* v_final;
+  // scratch (workspace)
+  uint32_t* sw;               // spike words [B][E][nslots][G]
+  int64_t sw_stride;
+  int32_t* chunk_spikes;      // [B][n_spk_chunks]; scanned in place into offsets
+  const int32_t* chunk_off;
+  int32_t n_spk_chunks;
+  int32_t *s_total, *oc_total, *needed, *vmin, *vmax, *ovf, *tail_total;
+  int32_t tail_mode;
+  int32_t* tail_cnt;          // [B][n_neurons] (tail mode only)
+  const int32_t* tile_len;    // [B][T] events per tile
+  const int32_t* tile_off;    // [B][T] start of each tile's list in the sample's region
+  const int32_t* tile_lists;  // [B][list_stride] event indices, tile-major, arrival order
+
+  __device__ __forceinline__ int32_t n_eff(int b) const {
+    int32_t n = in_nreal[b];
+    return n < 0 ? 0 : (n < in.capacity ? n : in.capacity);
+  }
+};
+
+struct FCLaunch {
+  int32_t n_in, n_out, G;
+  int32_t M, max_extra;
+  StreamView in;
+  const int32_t* in_nreal;
+  int32_t batch;
+  const int32_t* qT;          // (n_in, n_out) int32, transposed weight codes
+  const int32_t* lut;
+  const int32_t* vth;
+  int32_t has_vth;
+  QuantCfg qc;
+  int32_t* v_final;
+  uint32_t* sw;               // spike words [B][E][G] (firing layers only)
+  int64_t sw_stride;
+  int32_t* chunk_spikes;
+  const int32_t* chunk_off;
+  int32_t n_spk_chunks;
+  int32_t *s_total, *vmin, *vmax, *ovf;
+  int32_t* n_spk;             // [B][n_out] spikes per neuron
+  int32_t tail_mode;          // process pad columns too (some v_th_int <= 0)
+
+  __device__ __forceinline__ int32_t n_eff(int b) const {
+    int32_t n = in_nreal[b];
+    return n < 0 ? 0 : (n < in.capacity ? n : in.capacity);
+  }
+};
+
+// ---------------------------------------------------------------- warp / block helpers
+__device__ __forceinline__ int32_t warp_sum(int32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ int32_t warp_min(int32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int32_t warp_max(int32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int32_t warp_or(int32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide exclusive scan; every thread of the block must call it.  `s` must hold 33 ints
+// (kScanSmem).  Returns the exclusive prefix and writes the block total to `total`.
+__device__ __forceinline__ int32_t block_exclusive_scan(int32_t v, int32_t* s, int32_t& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  __syncthreads();
+  if (lane == 31) s[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int32_t x = lane < nw ? s[lane] : 0, xi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int32_t n = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += n;
+    }
+    if (lane < nw) s[lane] = xi - x;
+    if (lane == nw - 1) s[32] = xi;
+  }
+  __syncthreads();
+  total = s[32];
+  const int32_t r = s[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// Kernel declarations (definitions in conv_layer.cu / fc_layer.cu).
+__global__ void conv_tile_count(ConvLaunch P, int32_t* counts);
+__global__ void conv_tile_scan_offsets(ConvLaunch P, int32_t* counts, int32_t* tile_len,
+                                       int32_t* tile_off);
+__global__ void conv_tile_scatter(ConvLaunch P, const int32_t* counts, int32_t* lists);
+__global__ void conv_compact(ConvLaunch P, salt_stream_out out);
+__global__ void conv_tail_append(ConvLaunch P, salt_stream_out out);
+__global__ void conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* scratch_hist);
+__global__ void fc_compact(FCLaunch P, salt_stream_out out);
+__global__ void fc_truncated(FCLaunch P, salt_stream_out out);
+// Kernel entry points of the templated kernels, for cudaLaunchKernel.
+void* conv_fused_kernel(int wt_bytes, int lpu);
+void* fc_scan_kernel(bool fires);
+constexpr int kFcThreads = 128;
+
+}  // namespace salt
