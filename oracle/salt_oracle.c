@@ -182,6 +182,12 @@ int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *
   int64_t C = (int64_t)E_len * N * N;
   cand_t *cand = (cand_t *)malloc(sizeof(cand_t) * (size_t)C);
   cand_t *tmp = (cand_t *)malloc(sizeof(cand_t) * (size_t)C);
+  if (!ex || !cand || !tmp) {
+    free(ex);
+    free(cand);
+    free(tmp);
+    return -3;
+  }
   int32_t oy[64], ox[64];
   uint8_t vy[64], vx[64];
   if (N > 64) return -2;
@@ -327,6 +333,8 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
   const int32_t L = g->max_queue_len, h_out = conv_h_out(g), w_out = conv_w_out(g);
   const int32_t n_sp = h_out * w_out, OC = g->oc, n = OC * n_sp, K = g->k;
   if (h_out < 1 || w_out < 1 || L < 1) return -1;
+  /* the dense (n, L) restatement needs n*L cells per array: refuse absurd capacities */
+  if ((double)OC * n_sp * L > 4.0e9) return -4;
   size_t nl = (size_t)n_sp * L;
   int32_t *l2g = (int32_t *)malloc(sizeof(int32_t) * nl);
   int32_t *nreal = (int32_t *)malloc(sizeof(int32_t) * (size_t)n_sp);

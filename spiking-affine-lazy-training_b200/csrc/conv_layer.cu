@@ -10,38 +10,35 @@
 //        only when the output plane is split into several tiles: a stable partition of each
 //        sample's events by the tiles their receptive-field candidates fall in.
 //   conv_fused   one block per (tile, sample).  Streams the tile's events in arrival order in
-//        chunks; per chunk it buckets the candidates by output position with order-independent
-//        shared-memory atomicOr bitmasks (so the per-position queues come out in global
-//        event order, exactly the stable (position, j) order of conv.py:71), then lane groups
-//        (one lane per output channel) run the integer recurrence of their position over the
-//        chunk.  Spikes leave as per-(event, candidate-slot) channel bitmasks ("spike words").
-//   spike_chunk_scan   per-sample exclusive scan of spike counts per event chunk.
+//        chunks.  Per chunk it buckets the candidates by output position into per-position
+//        bitmasks (one word per warp of events, built with match_any, so every position's
+//        queue comes out in global event order: the stable (position, j) order of conv.py:71);
+//        then lane groups (one lane per output channel) run their position's integer
+//        recurrence over the chunk.  Spikes are recorded as per-(event, candidate slot) channel
+//        bitmasks ("spike words"), staged in shared memory and written out once per chunk.
 //   conv_compact       per (event chunk, sample): emits spikes in (event, neuron) order — the
 //        stable sort of stream.py:40 — into the output stream.
 //   conv_tail_append / conv_truncated   rare paths: spikes on catch-up/identity columns
-//        (only possible when some v_th_int <= 0) and samples whose spike count exceeds
-//        max_out_spikes (the first max_out spikes in neuron-major order are kept,
-//        stream.py:60, then sorted by event).
-//   layer_finish       per-sample diagnostics and Capacity.fits.
+//        (only possible when some v_th_int <= 0 or a decay code is out of range) and samples
+//        whose spike count exceeds max_out_spikes (the first max_out spikes in neuron-major
+//        order are kept, stream.py:60, then sorted by event).
 #include "salt_layers.cuh"
 
 namespace salt {
 
-// ------------------------------------------------------------------ geometry helpers
-
-struct Cand {  // receptive-field candidates of one event along one axis (conv.py:15-29)
-  int32_t o_min;  // first candidate output coordinate (may be invalid)
-  int32_t lo, hi; // valid output coordinates are [lo, hi] (empty when lo > hi)
+// Valid candidate ranges of one event (both axes).
+struct EvCand {
+  int32_t oy_min, oy_lo, oy_hi, ox_min, ox_lo, ox_hi;
+  __device__ __forceinline__ bool empty() const { return oy_lo > oy_hi || ox_lo > ox_hi; }
 };
 
-__host__ __device__ __forceinline__ Cand axis_cand(int32_t i, int32_t K, int32_t S, int32_t P,
-                                                   int32_t N, int32_t O) {
-  Cand c;
-  c.o_min = floordiv(i + P - K + S, S);   // ceil((i+P-K+1)/S)
-  int32_t upper = floordiv(i + P, S);
-  c.lo = max(c.o_min, 0);
-  c.hi = min(min(upper, c.o_min + N - 1), O - 1);
-  return c;
+__device__ __forceinline__ EvCand event_cand(const ConvLaunch& P, int32_t src, int32_t& c,
+                                             int32_t& y, int32_t& x) {
+  EvCand r;
+  P.decode(src, c, y, x);
+  P.axis(y, P.h_out, r.oy_min, r.oy_lo, r.oy_hi);
+  P.axis(x, P.w_out, r.ox_min, r.ox_lo, r.ox_hi);
+  return r;
 }
 
 // ------------------------------------------------------------------ tile partition
@@ -53,16 +50,13 @@ __global__ void conv_tile_count(ConvLaunch P, int32_t* __restrict__ counts) {
   __syncthreads();
   const int32_t n_eff = P.n_eff(b);
   for (int32_t e = threadIdx.x; e < kPartChunk; e += blockDim.x) {
-    int32_t jj = ch * kPartChunk + e;
+    const int32_t jj = ch * kPartChunk + e;
     if (jj >= n_eff) break;
-    int32_t s = P.in.src[(int64_t)b * P.in.capacity + jj];
-    int32_t rem = floormod(s, P.hw_in);
-    int32_t y = rem / P.w_in, x = rem % P.w_in;
-    Cand cy = axis_cand(y, P.k, P.s, P.p, P.ncand, P.h_out);
-    Cand cx = axis_cand(x, P.k, P.s, P.p, P.ncand, P.w_out);
-    if (cy.lo > cy.hi || cx.lo > cx.hi) continue;
-    for (int ty = cy.lo / P.tile_h; ty <= cy.hi / P.tile_h; ++ty)
-      for (int tx = cx.lo / P.tile_w; tx <= cx.hi / P.tile_w; ++tx)
+    int32_t c, y, x;
+    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + jj], c, y, x);
+    if (k.empty()) continue;
+    for (int ty = k.oy_lo / P.tile_h; ty <= k.oy_hi / P.tile_h; ++ty)
+      for (int tx = k.ox_lo / P.tile_w; tx <= k.ox_hi / P.tile_w; ++tx)
         atomicAdd(&s_cnt[ty * P.tiles_x + tx], 1);
   }
   __syncthreads();
@@ -112,16 +106,13 @@ __global__ void conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ coun
   __syncthreads();
   const int32_t n_eff = P.n_eff(b);
   for (int32_t e = threadIdx.x; e < kPartChunk; e += blockDim.x) {
-    int32_t jj = ch * kPartChunk + e;
+    const int32_t jj = ch * kPartChunk + e;
     if (jj >= n_eff) break;
-    int32_t s = P.in.src[(int64_t)b * P.in.capacity + jj];
-    int32_t rem = floormod(s, P.hw_in);
-    int32_t y = rem / P.w_in, x = rem % P.w_in;
-    Cand cy = axis_cand(y, P.k, P.s, P.p, P.ncand, P.h_out);
-    Cand cx = axis_cand(x, P.k, P.s, P.p, P.ncand, P.w_out);
-    if (cy.lo > cy.hi || cx.lo > cx.hi) continue;
-    for (int ty = cy.lo / P.tile_h; ty <= cy.hi / P.tile_h; ++ty)
-      for (int tx = cx.lo / P.tile_w; tx <= cx.hi / P.tile_w; ++tx)
+    int32_t c, y, x;
+    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + jj], c, y, x);
+    if (k.empty()) continue;
+    for (int ty = k.oy_lo / P.tile_h; ty <= k.oy_hi / P.tile_h; ++ty)
+      for (int tx = k.ox_lo / P.tile_w; tx <= k.ox_hi / P.tile_w; ++tx)
         atomicOr(&s_mask[(ty * P.tiles_x + tx) * W + (e >> 5)], 1u << (e & 31));
   }
   __syncthreads();
@@ -135,82 +126,103 @@ __global__ void conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ coun
   __syncthreads();
   int32_t* list_b = lists + (int64_t)b * P.list_stride;
   for (int32_t e = threadIdx.x; e < kPartChunk; e += blockDim.x) {
-    int32_t jj = ch * kPartChunk + e;
+    const int32_t jj = ch * kPartChunk + e;
     if (jj >= n_eff) break;
-    int32_t s = P.in.src[(int64_t)b * P.in.capacity + jj];
-    int32_t rem = floormod(s, P.hw_in);
-    int32_t y = rem / P.w_in, x = rem % P.w_in;
-    Cand cy = axis_cand(y, P.k, P.s, P.p, P.ncand, P.h_out);
-    Cand cx = axis_cand(x, P.k, P.s, P.p, P.ncand, P.w_out);
-    if (cy.lo > cy.hi || cx.lo > cx.hi) continue;
-    for (int ty = cy.lo / P.tile_h; ty <= cy.hi / P.tile_h; ++ty)
-      for (int tx = cx.lo / P.tile_w; tx <= cx.hi / P.tile_w; ++tx) {
-        int t = ty * P.tiles_x + tx;
-        uint32_t m = s_mask[t * W + (e >> 5)] & ((1u << (e & 31)) - 1u);
-        int32_t rank = (int32_t)(s_pre[t * W + (e >> 5)] + __popc(m));
-        int32_t base = counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t];
-        list_b[base + rank] = jj;
+    int32_t c, y, x;
+    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + jj], c, y, x);
+    if (k.empty()) continue;
+    for (int ty = k.oy_lo / P.tile_h; ty <= k.oy_hi / P.tile_h; ++ty)
+      for (int tx = k.ox_lo / P.tile_w; tx <= k.ox_hi / P.tile_w; ++tx) {
+        const int t = ty * P.tiles_x + tx;
+        const uint32_t m = s_mask[t * W + (e >> 5)] & ((1u << (e & 31)) - 1u);
+        const int32_t rank = (int32_t)(s_pre[t * W + (e >> 5)] + __popc(m));
+        list_b[counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t] + rank] = jj;
       }
   }
 }
 
 // ------------------------------------------------------------------ fused bucket + scan
 
-// Shared-memory event record of one chunk entry.
-struct EvRec {
+// Shared-memory record of one chunk event (16 bytes: one vector load).
+struct __align__(16) EvRec {
   float t;
-  int32_t j;
-  int32_t ckk;      // clamped channel * k * k (weight tap base)
-  uint32_t yx;      // (y + p) << 16 | (x + p)
-  uint32_t omin;    // (o_min_y + 32768) << 16 | (o_min_x + 32768)
+  int32_t ckk;     // clamped channel * k * k (weight tap base)
+  uint32_t yx;     // (y + p) << 16 | (x + p)
+  uint32_t omin;   // (o_min_y + 32768) << 16 | (o_min_x + 32768)
 };
+
+// Shared-memory layout of conv_fused; the host sizes it with the same function.
+struct FusedSmem {
+  size_t w, lut, v, tprev, cnt, mask, ev, ej, sw, list, posoff, poscnt, act, ocspk, misc, total;
+  __host__ __device__ FusedSmem(const ConvLaunch& P, int wt_bytes) {
+    const size_t npm = (size_t)P.tile_h * P.tile_w;
+    size_t o = 0;
+    w = o;     o += align16((size_t)P.ic * P.k * P.k * P.ocp * wt_bytes);
+    lut = o;   o += align16((size_t)(P.lut_in_smem ? P.qc.lut_len : 0) * 4);
+    v = o;     o += align16(npm * P.ocp * 4);
+    tprev = o; o += align16(npm * P.G * 4);   // one copy per (position, channel group)
+    cnt = o;   o += align16(npm * P.G * 4);
+    mask = o;  o += align16(npm * (kFusedChunk / 32) * 4);
+    ev = o;    o += align16((size_t)kFusedChunk * sizeof(EvRec));
+    ej = o;    o += align16((size_t)(P.T > 1 ? kFusedChunk : 0) * 4);
+    sw = o;    o += align16((size_t)kFusedChunk * P.nslots * P.G * 4);
+    list = o;  o += align16((size_t)kFusedChunk * P.nslots * 2);
+    posoff = o; o += align16(npm * 4);
+    poscnt = o; o += align16(npm * 4);
+    act = o;   o += align16(npm * 4);
+    ocspk = o; o += align16((size_t)P.ocp * 4);
+    misc = o;  o += 64;
+    total = o;
+  }
+};
+
+size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes) {
+  return FusedSmem(P, wt_bytes).total;
+}
 
 template <typename WT, int LPU>
 __global__ void __launch_bounds__(kFusedThreads)
 conv_fused(ConvLaunch P) {
-  constexpr int UPW = 32 / LPU;  // units (positions x channel groups) per warp
+  constexpr int UPW = 32 / LPU;  // units (position x channel group) per warp
   constexpr int CHW = kFusedChunk / 32;
   extern __shared__ __align__(16) uint8_t smem[];
+  const FusedSmem L(P, sizeof(WT));
+  WT* w_s = reinterpret_cast<WT*>(smem + L.w);
+  int32_t* lut_s = reinterpret_cast<int32_t*>(smem + L.lut);
+  int32_t* v_s = reinterpret_cast<int32_t*>(smem + L.v);
+  float* tprev_s = reinterpret_cast<float*>(smem + L.tprev);
+  int32_t* cnt_s = reinterpret_cast<int32_t*>(smem + L.cnt);
+  uint32_t* mask_s = reinterpret_cast<uint32_t*>(smem + L.mask);
+  EvRec* ev_s = reinterpret_cast<EvRec*>(smem + L.ev);
+  int32_t* ej_s = reinterpret_cast<int32_t*>(smem + L.ej);
+  uint32_t* sw_s = reinterpret_cast<uint32_t*>(smem + L.sw);
+  uint16_t* list_s = reinterpret_cast<uint16_t*>(smem + L.list);
+  int32_t* posoff_s = reinterpret_cast<int32_t*>(smem + L.posoff);
+  int32_t* poscnt_s = reinterpret_cast<int32_t*>(smem + L.poscnt);
+  int32_t* act_s = reinterpret_cast<int32_t*>(smem + L.act);
+  __shared__ int32_t s_scan[kScanSmem];
+  int32_t* ocspk_s = reinterpret_cast<int32_t*>(smem + L.ocspk);
+  int32_t* misc_s = reinterpret_cast<int32_t*>(smem + L.misc);
+
   const int b = blockIdx.y, tile = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gi = lane / LPU, glane = lane % LPU;
   const uint32_t gmask_bits = LPU == 32 ? 0xffffffffu : ((1u << LPU) - 1u);
-
-  // ---- shared memory carve-up (sizes computed identically on the host)
   const int OCP = P.ocp, NPM = P.tile_h * P.tile_w, KK = P.k * P.k;
-  uint8_t* sp = smem;
-  WT* w_s = reinterpret_cast<WT*>(sp);
-  sp += align16((size_t)P.ic * KK * OCP * sizeof(WT));
-  int32_t* lut_s = reinterpret_cast<int32_t*>(sp);
-  sp += align16((size_t)(P.lut_in_smem ? P.qc.lut_len : 0) * 4);
-  int32_t* v_s = reinterpret_cast<int32_t*>(sp);
-  sp += align16((size_t)NPM * OCP * 4);
-  float* tprev_s = reinterpret_cast<float*>(sp);
-  sp += align16((size_t)NPM * 4);
-  int32_t* cnt_s = reinterpret_cast<int32_t*>(sp);
-  sp += align16((size_t)NPM * 4);
-  uint32_t* mask_s = reinterpret_cast<uint32_t*>(sp);
-  sp += align16((size_t)NPM * CHW * 4);
-  EvRec* ev_s = reinterpret_cast<EvRec*>(sp);
-  sp += align16((size_t)kFusedChunk * sizeof(EvRec));
-  int32_t* ocspk_s = reinterpret_cast<int32_t*>(sp);
-  sp += align16((size_t)OCP * 4);
-  int32_t* misc_s = reinterpret_cast<int32_t*>(sp);  // [0] task counter, [1..] reductions
+  const int SWW = P.nslots * P.G;  // spike words per event
 
-  // ---- tile geometry
-  const int ty = tile / P.tiles_x, tx = tile % P.tiles_x;
+  const int ty = tile / P.tiles_x, tx = tile - ty * P.tiles_x;
   const int oy0 = ty * P.tile_h, ox0 = tx * P.tile_w;
   const int th = min(P.tile_h, P.h_out - oy0), tw = min(P.tile_w, P.w_out - ox0);
 
-  // ---- init
   for (int i = tid; i < P.ic * KK * OCP; i += blockDim.x) {
-    int tap = i / OCP, oc = i % OCP;
+    const int tap = i / OCP, oc = i - tap * OCP;
     w_s[i] = oc < P.oc ? (WT)P.q[(int64_t)oc * P.ic * KK + tap] : (WT)0;
   }
   if (P.lut_in_smem)
     for (int i = tid; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
   for (int i = tid; i < NPM * OCP; i += blockDim.x) v_s[i] = 0;
-  for (int i = tid; i < NPM; i += blockDim.x) {
+  for (int i = tid; i < NPM * P.G; i += blockDim.x) {
     tprev_s[i] = 0.0f;
     cnt_s[i] = 0;
   }
@@ -227,118 +239,206 @@ conv_fused(ConvLaunch P) {
   uint32_t* sw_b = P.sw + (int64_t)b * P.sw_stride;
   int32_t* chunk_spk_b = P.chunk_spikes + (int64_t)b * P.n_spk_chunks;
 
-  // lane-level accumulators for the block reductions
   int32_t acc_min = 0, acc_max = 0, acc_ovf = 0, acc_spk = 0;
-  const int ntasks = (NPM * P.G + UPW - 1) / UPW;
+  const int ntasks_all = (NPM * P.G + UPW - 1) / UPW;
   __syncthreads();
 
   for (int32_t base = 0; base < nev; base += kFusedChunk) {
-    // -------- phase 1: load chunk, bucket by position (bitmask per position)
+    const int32_t nchunk = min(kFusedChunk, nev - base);
+    // -------- phase 1: decode the chunk and bucket its candidates by position
     for (int i = tid; i < NPM * CHW; i += blockDim.x) mask_s[i] = 0;
+    for (int i = tid; i < kFusedChunk * SWW; i += blockDim.x) sw_s[i] = 0;
     if (tid == 0) misc_s[0] = 0;
     __syncthreads();
-    const int32_t nchunk = min(kFusedChunk, nev - base);
-    for (int e = tid; e < nchunk; e += blockDim.x) {
-      int32_t j = list ? list[base + e] : base + e;
-      float t = P.in.times[row * P.in.capacity + j];
-      int32_t s = P.in.src[row * P.in.capacity + j];
-      int32_t c = floordiv(s, P.hw_in);
-      int32_t rem = floormod(s, P.hw_in);
-      int32_t y = rem / P.w_in, x = rem % P.w_in;
-      Cand cy = axis_cand(y, P.k, P.s, P.p, P.ncand, P.h_out);
-      Cand cx = axis_cand(x, P.k, P.s, P.p, P.ncand, P.w_out);
-      EvRec r;
-      r.t = t;
-      r.j = j;
-      r.ckk = (int32_t)jax_index(c, P.ic) * KK;
-      r.yx = ((uint32_t)(y + P.p) << 16) | (uint32_t)(x + P.p);
-      r.omin = ((uint32_t)(cy.o_min + 32768) << 16) | (uint32_t)(cx.o_min + 32768);
-      ev_s[e] = r;
-      int lo_y = max(cy.lo, oy0), hi_y = min(cy.hi, oy0 + th - 1);
-      int lo_x = max(cx.lo, ox0), hi_x = min(cx.hi, ox0 + tw - 1);
-      for (int oy = lo_y; oy <= hi_y; ++oy)
-        for (int ox = lo_x; ox <= hi_x; ++ox)
-          atomicOr(&mask_s[((oy - oy0) * P.tile_w + (ox - ox0)) * CHW + (e >> 5)],
-                   1u << (e & 31));
+    for (int e0 = warp * 32; e0 < kFusedChunk; e0 += blockDim.x) {  // warp-uniform trip count
+      const int e = e0 + lane;
+      const bool in = e < nchunk;
+      EvCand k{0, 1, 0, 0, 1, 0};
+      if (in) {
+        const int32_t j = list ? list[base + e] : base + e;
+        const float t = P.in.times[row * P.in.capacity + j];
+        int32_t c, y, x;
+        k = event_cand(P, P.in.src[row * P.in.capacity + j], c, y, x);
+        EvRec r;
+        r.t = t;
+        r.ckk = c * KK;
+        r.yx = ((uint32_t)(y + P.p) << 16) | (uint32_t)(x + P.p);
+        r.omin = ((uint32_t)(k.oy_min + 32768) << 16) | (uint32_t)(k.ox_min + 32768);
+        ev_s[e] = r;
+        if (list) ej_s[e] = j;
+        // clip to this tile
+        k.oy_lo = max(k.oy_lo, oy0);
+        k.oy_hi = min(k.oy_hi, oy0 + th - 1);
+        k.ox_lo = max(k.ox_lo, ox0);
+        k.ox_hi = min(k.ox_hi, ox0 + tw - 1);
+      }
+      // one candidate slot per round; lanes hitting the same position share one mask word,
+      // written by the group's first lane (no other warp writes this word)
+      const int wrd = e0 >> 5;
+      for (int a = 0; a < P.ncand; ++a)
+        for (int bb = 0; bb < P.ncand; ++bb) {
+          const int oy = k.oy_min + a, ox = k.ox_min + bb;
+          const bool ok = in && oy >= k.oy_lo && oy <= k.oy_hi && ox >= k.ox_lo && ox <= k.ox_hi;
+          const int pl = ok ? (oy - oy0) * P.tile_w + (ox - ox0) : -1;
+          const uint32_t same = __match_any_sync(0xffffffffu, pl);
+          if (ok && (__ffs(same) - 1) == lane) mask_s[pl * CHW + wrd] |= same;
+        }
     }
     __syncthreads();
 
-    // -------- phase 2: lane groups run their position's queue over this chunk
+    // -------- phase 1.5: per-position event lists (arrival order) and the active positions
+    int32_t n_active = 0;
+    {
+      int32_t run = 0;
+      for (int p0 = 0; p0 < NPM; p0 += blockDim.x) {  // block-uniform trip count
+        const int p = p0 + tid;
+        int32_t c = 0;
+        if (p < NPM)
+          for (int w = 0; w < CHW; ++w) c += __popc(mask_s[p * CHW + w]);
+        int32_t tot, atot;
+        const int32_t off = run + block_exclusive_scan(c, s_scan, tot);
+        const int32_t aoff = n_active + block_exclusive_scan(c > 0, s_scan, atot);
+        if (p < NPM) {
+          posoff_s[p] = off;
+          poscnt_s[p] = c;
+          if (c > 0) act_s[aoff] = p;
+          int32_t k = off;
+          for (int w = 0; w < CHW && c > 0; ++w) {
+            uint32_t m = mask_s[p * CHW + w];
+            while (m) {
+              list_s[k++] = (uint16_t)(w * 32 + __ffs(m) - 1);
+              m &= m - 1u;
+            }
+          }
+        }
+        run += tot;
+        n_active += atot;
+      }
+    }
+    __syncthreads();
+
+    // -------- phase 2: lane groups run the active positions' queues over this chunk.  A batch
+    // of up to LPU events is prepared lane-parallel (one event per lane: Δt, decay code, weight
+    // tap, spike-word slot); only the register update itself walks the batch sequentially.
+    const int ntasks = (n_active * P.G + UPW - 1) / UPW;
     for (;;) {
       int task = 0;
       if (lane == 0) task = atomicAdd(&misc_s[0], 1);
       task = __shfl_sync(0xffffffffu, task, 0);
       if (task >= ntasks) break;
       const int unit = task * UPW + gi;
-      const int pl = unit / P.G, g = unit % P.G;
-      const int ly = pl / P.tile_w, lx = pl % P.tile_w;
-      const bool unit_ok = pl < NPM && ly < th && lx < tw;
+      const bool unit_ok = unit < n_active * P.G;
+      const int ai = P.G == 1 ? unit : (int)P.fd_G.div((uint32_t)unit);
+      const int g = unit - ai * P.G;
+      const int pl = unit_ok ? act_s[ai] : 0;
+      const int ly = (int)P.fd_tw.div((uint32_t)pl), lx = pl - ly * P.tile_w;
       const int oc = g * LPU + glane;
       const bool lane_ok = unit_ok && oc < P.oc;
-      const int oy = oy0 + ly, ox = ox0 + lx, pos = oy * P.w_out + ox;
+      const int oy = oy0 + ly, ox = ox0 + lx;
+      const int oys = oy * P.s, oxs = ox * P.s;
+      const int32_t n = unit_ok ? poscnt_s[pl] : 0;
+      const int32_t lbase = unit_ok ? posoff_s[pl] : 0;
       int32_t V = 0, cn = 0, vth = 0;
       float tp = 0.0f;
       if (unit_ok) {
         V = v_s[pl * OCP + oc];
-        tp = tprev_s[pl];
-        cn = cnt_s[pl];
+        tp = tprev_s[pl * P.G + g];
+        cn = cnt_s[pl * P.G + g];
       }
-      if (lane_ok && P.has_vth) vth = P.vth[(int64_t)oc * P.n_sp + pos];
-      // Groups without a unit in this tile start exhausted: they must not walk any mask row.
-      const uint32_t* mrow = mask_s + (unit_ok ? pl : 0) * CHW;
-      int wi = unit_ok ? 0 : CHW;
-      uint32_t cur = unit_ok ? mrow[0] : 0u;
+      if (lane_ok && P.has_vth) vth = __ldg(&P.vth[(int64_t)oc * P.n_sp + oy * P.w_out + ox]);
+      const int32_t nmax = __reduce_max_sync(0xffffffffu, n);
       int32_t spk_visit = 0;
-      for (;;) {
-        while (cur == 0u && wi < CHW - 1) cur = mrow[++wi];
-        const bool has = cur != 0u;
-        if (!__any_sync(0xffffffffu, has)) break;
-        bool spike = false;
-        int e = 0;
-        if (has) {
-          e = wi * 32 + __ffs(cur) - 1;
-          cur &= cur - 1u;
-          const EvRec r = ev_s[e];
-          if (cn < P.L) {
-            int32_t dt = dt_from_times(r.t, tp);
-            tp = r.t;
-            int32_t a = decay_code(dt, lut, P.qc.lut_len);
-            int32_t ky = (int32_t)(r.yx >> 16) - oy * P.s;
-            int32_t kx = (int32_t)(r.yx & 0xffffu) - ox * P.s;
-            int32_t qv = (int32_t)w_s[(r.ckk + ky * P.k + kx) * OCP + oc];
+      for (int32_t b0 = 0; b0 < nmax; b0 += LPU) {
+        const int32_t idx = b0 + glane;
+        const bool has = idx < n;
+        const int e = has ? list_s[lbase + idx] : 0;
+        const EvRec r = ev_s[e];
+        float tpv = __shfl_up_sync(0xffffffffu, r.t, 1, LPU);
+        if (glane == 0) tpv = tp;
+        const bool kept = has && (cn + glane) < P.L;  // cn already counts earlier batches
+        const int32_t dt = dt_from_times(r.t, tpv);
+        const int32_t a = decay_code(dt, lut, P.qc.lut_len);
+        const int32_t ky = (int32_t)(r.yx >> 16) - oys;
+        const int32_t kx = (int32_t)(r.yx & 0xffffu) - oxs;
+        const int32_t tap = r.ckk + ky * P.k + kx;
+        // lanes without a kept event pack 0: their placeholder record may give a negative tap
+        const uint32_t T = kept ? (((uint32_t)tap & 0x3fffffffu) | ((uint32_t)(dt == 0) << 30) |
+                                   0x80000000u)
+                                : 0u;
+        const int sy = oy - ((int32_t)(r.omin >> 16) - 32768);
+        const int sx = ox - ((int32_t)(r.omin & 0xffffu) - 32768);
+        const int widx = e * SWW + (sy * P.ncand + sx) * P.G + g;
+        const int32_t nb = min(n - b0, LPU);  // this group's events in the batch (may be <= 0)
+        const float last_t = __shfl_sync(0xffffffffu, r.t, nb > 0 ? nb - 1 : 0, LPU);
+        if (nb > 0) tp = last_t;
+        const int32_t nbw = min(nmax - b0, LPU);  // warp-uniform batch length
+        uint32_t mybits = 0;
+        for (int32_t st = 0; st < nbw; ++st) {
+          const int32_t as = __shfl_sync(0xffffffffu, a, st, LPU);
+          const uint32_t Ts = __shfl_sync(0xffffffffu, T, st, LPU);
+          bool spike = false;
+          if ((Ts >> 31) && lane_ok) {
+            const int32_t qv = (int32_t)w_s[(int32_t)(Ts & 0x3fffffffu) * OCP + oc];
             int32_t u;
             bool ovf;
-            int32_t w = quant_step(V, a, dt == 0, qv, P.qc, u, ovf);
-            spike = lane_ok && P.has_vth && w >= vth;
+            const int32_t w = quant_step(V, as, (Ts >> 30) & 1u, qv, P.qc, u, ovf);
+            spike = P.has_vth && w >= vth;
             V = spike ? 0 : w;
-            if (lane_ok) {
-              acc_min = min(acc_min, u);
-              acc_max = max(acc_max, u);
-              acc_ovf |= (int32_t)ovf;
-            }
+            acc_min = min(acc_min, u);
+            acc_max = max(acc_max, u);
+            acc_ovf |= (int32_t)ovf;
           }
-          ++cn;
+          const uint32_t bits = (__ballot_sync(0xffffffffu, spike) >> (gi * LPU)) & gmask_bits;
+          if (glane == st) mybits = bits;
+          spk_visit += spike;
         }
-        const uint32_t bal = __ballot_sync(0xffffffffu, spike);
-        if (has && glane == 0) {
-          const EvRec r = ev_s[e];
-          const int sy = oy - ((int32_t)(r.omin >> 16) - 32768);
-          const int sx = ox - ((int32_t)(r.omin & 0xffffu) - 32768);
-          const uint32_t bits = (bal >> (gi * LPU)) & gmask_bits;
-          sw_b[((int64_t)r.j * P.nslots + sy * P.ncand + sx) * P.G + g] = bits;
-          if (bits) atomicAdd(&chunk_spk_b[r.j >> kSpkChunkShift], __popc(bits));
-        }
-        spk_visit += spike;
+        if (has) sw_s[widx] = mybits;
+        cn += max(nb, 0);
       }
       if (unit_ok) {
         v_s[pl * OCP + oc] = V;
-        if (glane == 0 && g == 0) {
-          tprev_s[pl] = tp;
-          cnt_s[pl] = cn;
+        if (glane == 0) {
+          tprev_s[pl * P.G + g] = tp;
+          cnt_s[pl * P.G + g] = cn;
         }
         if (spk_visit && oc < P.oc) atomicAdd(&ocspk_s[oc], spk_visit);
       }
       acc_spk += spk_visit;
+    }
+    __syncthreads();
+
+    // -------- flush the chunk's spike words and its spike counts per 256-event group
+    if (!list) {
+      uint32_t* dst = sw_b + (int64_t)base * SWW;
+      for (int i = tid; i < nchunk * SWW; i += blockDim.x) dst[i] = sw_s[i];
+      for (int e0 = warp * 32; e0 < kFusedChunk; e0 += blockDim.x) {
+        const int e = e0 + lane;
+        int32_t cnt = 0;
+        if (e < nchunk)
+          for (int i = 0; i < SWW; ++i) cnt += __popc(sw_s[e * SWW + i]);
+        cnt = warp_sum(cnt);
+        if (lane == 0 && cnt) atomicAdd(&chunk_spk_b[(base + e0) >> kSpkChunkShift], cnt);
+      }
+    } else {
+      // several tiles share an event: write only the slots whose position is in this tile
+      for (int e = tid; e < nchunk; e += blockDim.x) {
+        const int32_t j = ej_s[e];
+        const EvRec r = ev_s[e];
+        const int oym = (int32_t)(r.omin >> 16) - 32768, oxm = (int32_t)(r.omin & 0xffffu) - 32768;
+        int32_t cnt = 0;
+        for (int sy = 0; sy < P.ncand; ++sy)
+          for (int sx = 0; sx < P.ncand; ++sx) {
+            const int oy = oym + sy, ox = oxm + sx;
+            if (oy < oy0 || oy >= oy0 + th || ox < ox0 || ox >= ox0 + tw) continue;
+            for (int g = 0; g < P.G; ++g) {
+              const int slot = (sy * P.ncand + sx) * P.G + g;
+              const uint32_t wd = sw_s[e * SWW + slot];
+              sw_b[(int64_t)j * SWW + slot] = wd;
+              cnt += __popc(wd);
+            }
+          }
+        if (cnt) atomicAdd(&chunk_spk_b[j >> kSpkChunkShift], cnt);
+      }
     }
     __syncthreads();
   }
@@ -354,17 +454,18 @@ conv_fused(ConvLaunch P) {
     int task = 0;
     if (lane == 0) task = atomicAdd(&misc_s[0], 1);
     task = __shfl_sync(0xffffffffu, task, 0);
-    if (task >= ntasks) break;
+    if (task >= ntasks_all) break;
     const int unit = task * UPW + gi;
-    const int pl = unit / P.G, g = unit % P.G;
-    const int ly = pl / P.tile_w, lx = pl % P.tile_w;
+    const int pl = P.G == 1 ? unit : (int)P.fd_G.div((uint32_t)unit);
+    const int g = unit - pl * P.G;
+    const int ly = (int)P.fd_tw.div((uint32_t)pl), lx = pl - ly * P.tile_w;
     const bool unit_ok = pl < NPM && ly < th && lx < tw;
     const int oc = g * LPU + glane;
     if (unit_ok && oc < P.oc) {
       const int oy = oy0 + ly, ox = ox0 + lx, pos = oy * P.w_out + ox;
       int32_t V = v_s[pl * OCP + oc];
-      const int32_t cn = cnt_s[pl];
-      const float tp = tprev_s[pl];
+      const int32_t cn = cnt_s[pl * P.G + g];
+      const float tp = tprev_s[pl * P.G + g];
       const int32_t vth = P.has_vth ? P.vth[(int64_t)oc * P.n_sp + pos] : 0;
       int32_t tail = 0;
       if (cn < P.L) {
@@ -437,46 +538,43 @@ conv_compact(ConvLaunch P, salt_stream_out out) {
   const int32_t n_eff = P.n_eff(b);
   const int32_t j = c * kSpkChunk + tid;
   const bool ok = j < n_eff;
-  const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.nslots * P.G;
+  const int SWW = P.nslots * P.G;
+  const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
   int32_t cnt = 0;
-  Cand cy{}, cx{};
+  EvCand k{0, 1, 0, 0, 1, 0};
   if (ok) {
-    int32_t s = P.in.src[(int64_t)b * P.in.capacity + j];
-    int32_t rem = floormod(s, P.hw_in);
-    int32_t y = rem / P.w_in, x = rem % P.w_in;
-    cy = axis_cand(y, P.k, P.s, P.p, P.ncand, P.h_out);
-    cx = axis_cand(x, P.k, P.s, P.p, P.ncand, P.w_out);
-    for (int oy = cy.lo; oy <= cy.hi; ++oy)
-      for (int ox = cx.lo; ox <= cx.hi; ++ox) {
-        const int slot = (oy - cy.o_min) * P.ncand + (ox - cx.o_min);
+    int32_t cc, y, x;
+    k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
+    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
+        const int slot = (oy - k.oy_min) * P.ncand + (ox - k.ox_min);
         for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[slot * P.G + g]);
       }
   }
   int32_t total;
-  int32_t off = block_exclusive_scan(cnt, s_scan, total);
+  const int32_t off = block_exclusive_scan(cnt, s_scan, total);
   if (cnt == 0) return;
   const int32_t base = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
   const float t = P.in.time(b, j, n_eff);
   float* ot = out.times + (int64_t)b * P.M;
   int32_t* os = out.src + (int64_t)b * P.M;
-  int32_t k = 0;
-  const int lpu = P.lpu;
+  int32_t kk = 0;
   for (int g = 0; g < P.G; ++g) {
     uint32_t uni = 0;
-    for (int oy = cy.lo; oy <= cy.hi; ++oy)
-      for (int ox = cx.lo; ox <= cx.hi; ++ox)
-        uni |= sw_j[((oy - cy.o_min) * P.ncand + (ox - cx.o_min)) * P.G + g];
+    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
+        uni |= sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
     while (uni) {
       const int bit = __ffs(uni) - 1;
       uni &= uni - 1u;
-      const int oc = g * lpu + bit;
-      for (int oy = cy.lo; oy <= cy.hi; ++oy)
-        for (int ox = cx.lo; ox <= cx.hi; ++ox) {
-          const uint32_t wd = sw_j[((oy - cy.o_min) * P.ncand + (ox - cx.o_min)) * P.G + g];
+      const int oc = g * P.lpu + bit;
+      for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+        for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
+          const uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
           if (wd & (1u << bit)) {
-            ot[base + k] = t;
-            os[base + k] = oc * P.n_sp + oy * P.w_out + ox;
-            ++k;
+            ot[base + kk] = t;
+            os[base + kk] = oc * P.n_sp + oy * P.w_out + ox;
+            ++kk;
           }
         }
     }
@@ -488,27 +586,22 @@ conv_compact(ConvLaunch P, salt_stream_out out) {
 // neuron order; their time is the input stream's last entry.
 __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out) {
   __shared__ int32_t s_scan[kScanSmem];
-  __shared__ int32_t s_carry;
   const int b = blockIdx.x, tid = threadIdx.x;
   const int32_t S = P.s_total[b], Tb = P.tail_total[b];
   if (S > P.M || Tb == 0) return;
   const int32_t E = P.in.capacity;
   const float t = P.in.time(b, E - 1, P.n_eff(b));
-  int32_t base = S - Tb;
-  if (tid == 0) s_carry = 0;
-  __syncthreads();
+  int32_t written = S - Tb;
   for (int64_t n0 = 0; n0 < P.n_neurons; n0 += blockDim.x) {
     const int64_t n = n0 + tid;
     const int32_t c = n < P.n_neurons ? P.tail_cnt[(int64_t)b * P.n_neurons + n] : 0;
     int32_t total;
     const int32_t off = block_exclusive_scan(c, s_scan, total);
     for (int32_t k = 0; k < c; ++k) {
-      out.times[(int64_t)b * P.M + base + s_carry + off + k] = t;
-      out.src[(int64_t)b * P.M + base + s_carry + off + k] = (int32_t)n;
+      out.times[(int64_t)b * P.M + written + off + k] = t;
+      out.src[(int64_t)b * P.M + written + off + k] = (int32_t)n;
     }
-    __syncthreads();
-    if (tid == 0) s_carry += total;
-    __syncthreads();
+    written += total;
   }
 }
 
@@ -518,17 +611,18 @@ __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out) {
 __global__ void __launch_bounds__(kCompactThreads)
 conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_hist) {
   __shared__ int32_t s_scan[kScanSmem];
-  __shared__ int32_t s_cut[8];  // oc*, pos*, j_cut, tail_keep, running base
+  __shared__ int32_t s_cut[8];
   const int b = blockIdx.x, tid = threadIdx.x;
   const int32_t S = P.s_total[b], M = P.M;
   if (S <= M || M <= 0) return;
   const int32_t n_eff = P.n_eff(b);
+  const int SWW = P.nslots * P.G;
   int32_t* hist = scratch_hist + (int64_t)b * P.n_sp * 2;  // [n_sp] real, [n_sp] tail
-  // 1. channel cut
+  // 1. channel cut: the channel holding the M-th spike in neuron-major order
   if (tid == 0) {
     int32_t cum = 0, occ = P.oc - 1;
     for (int oc = 0; oc < P.oc; ++oc) {
-      int32_t t = P.oc_total[(int64_t)b * P.oc + oc];
+      const int32_t t = P.oc_total[(int64_t)b * P.oc + oc];
       if (cum + t >= M) {
         occ = oc;
         break;
@@ -544,14 +638,12 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   const int gq = occ / P.lpu, bq = occ % P.lpu;
   // 2. per-position spike counts of channel occ
   for (int32_t j = tid; j < n_eff; j += blockDim.x) {
-    int32_t s = P.in.src[(int64_t)b * P.in.capacity + j];
-    int32_t rem = floormod(s, P.hw_in);
-    Cand cy = axis_cand(rem / P.w_in, P.k, P.s, P.p, P.ncand, P.h_out);
-    Cand cx = axis_cand(rem % P.w_in, P.k, P.s, P.p, P.ncand, P.w_out);
-    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.nslots * P.G;
-    for (int oy = cy.lo; oy <= cy.hi; ++oy)
-      for (int ox = cx.lo; ox <= cx.hi; ++ox)
-        if (sw_j[((oy - cy.o_min) * P.ncand + (ox - cx.o_min)) * P.G + gq] & (1u << bq))
+    int32_t cc, y, x;
+    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
+    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
+        if (sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + gq] & (1u << bq))
           atomicAdd(&hist[oy * P.w_out + ox], 1);
   }
   if (P.tail_mode)
@@ -559,43 +651,42 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
       hist[P.n_sp + pos] = P.tail_cnt[(int64_t)b * P.n_neurons + (int64_t)occ * P.n_sp + pos];
   __syncthreads();
   if (tid == 0) {
-    int32_t need = s_cut[1], cum = 0, pstar = P.n_sp - 1;
+    const int32_t need = s_cut[1];
+    int32_t cum = 0, pstar = P.n_sp - 1;
     for (int pos = 0; pos < P.n_sp; ++pos) {
-      int32_t t = hist[pos] + hist[P.n_sp + pos];
+      const int32_t t = hist[pos] + hist[P.n_sp + pos];
       if (cum + t >= need) {
         pstar = pos;
         break;
       }
       cum += t;
     }
-    int32_t r2 = need - cum;  // spikes to keep of neuron (occ, pstar), counted in column order
+    const int32_t r2 = need - cum;  // spikes kept of neuron (occ, pstar), in column order
     s_cut[1] = pstar;
     if (r2 <= hist[pstar]) {
       s_cut[2] = r2;  // the r2-th real spike is the last kept one: located below
       s_cut[3] = 0;
     } else {
-      s_cut[2] = hist[pstar] > 0 ? hist[pstar] : 0;
+      s_cut[2] = hist[pstar];
       s_cut[3] = r2 - hist[pstar];
     }
     s_cut[4] = 0x7fffffff;  // j_cut
   }
   __syncthreads();
   const int pstar = s_cut[1];
-  // 3. locate the j of the s_cut[2]-th real spike of neuron (occ, pstar)
+  // 3. the event index of the s_cut[2]-th real spike of neuron (occ, pstar)
   if (s_cut[2] > 0) {
-    int32_t seen = 0;  // block-uniform running count
+    int32_t seen = 0;
+    const int py = pstar / P.w_out, px = pstar % P.w_out;
     for (int32_t j0 = 0; j0 < n_eff; j0 += blockDim.x) {
       const int32_t j = j0 + tid;
       int32_t hit = 0;
       if (j < n_eff) {
-        int32_t s = P.in.src[(int64_t)b * P.in.capacity + j];
-        int32_t rem = floormod(s, P.hw_in);
-        Cand cy = axis_cand(rem / P.w_in, P.k, P.s, P.p, P.ncand, P.h_out);
-        Cand cx = axis_cand(rem % P.w_in, P.k, P.s, P.p, P.ncand, P.w_out);
-        const int py = pstar / P.w_out, px = pstar % P.w_out;
-        if (py >= cy.lo && py <= cy.hi && px >= cx.lo && px <= cx.hi) {
-          const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.nslots * P.G;
-          hit = (sw_j[((py - cy.o_min) * P.ncand + (px - cx.o_min)) * P.G + gq] >> bq) & 1u;
+        int32_t cc, y, x;
+        const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
+        if (py >= k.oy_lo && py <= k.oy_hi && px >= k.ox_lo && px <= k.ox_hi) {
+          const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
+          hit = (sw_j[((py - k.oy_min) * P.ncand + (px - k.ox_min)) * P.G + gq] >> bq) & 1u;
         }
       }
       int32_t total;
@@ -616,17 +707,15 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   for (int32_t j0 = 0; j0 < n_eff; j0 += blockDim.x) {
     const int32_t j = j0 + tid;
     int32_t cnt = 0;
-    Cand cy{}, cx{};
-    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.nslots * P.G;
+    EvCand k{0, 1, 0, 0, 1, 0};
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
     if (j < n_eff) {
-      int32_t s = P.in.src[(int64_t)b * P.in.capacity + j];
-      int32_t rem = floormod(s, P.hw_in);
-      cy = axis_cand(rem / P.w_in, P.k, P.s, P.p, P.ncand, P.h_out);
-      cx = axis_cand(rem % P.w_in, P.k, P.s, P.p, P.ncand, P.w_out);
+      int32_t cc, y, x;
+      k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
       for (int g = 0; g < P.G; ++g)
-        for (int oy = cy.lo; oy <= cy.hi; ++oy)
-          for (int ox = cx.lo; ox <= cx.hi; ++ox) {
-            uint32_t wd = sw_j[((oy - cy.o_min) * P.ncand + (ox - cx.o_min)) * P.G + g];
+        for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+          for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
+            uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
             while (wd) {
               const int bit = __ffs(wd) - 1;
               wd &= wd - 1u;
@@ -634,32 +723,29 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
               cnt += (n < nstar) || (n == nstar && j <= j_cut);
             }
           }
-    } else {
-      cy.lo = 1;
-      cy.hi = 0;
     }
     int32_t total;
     const int32_t off = block_exclusive_scan(cnt, s_scan, total);
     if (cnt) {
       const float t = P.in.time(b, j, n_eff);
-      int32_t k = written + off;
+      int32_t kk = written + off;
       for (int g = 0; g < P.G; ++g) {
         uint32_t uni = 0;
-        for (int oy = cy.lo; oy <= cy.hi; ++oy)
-          for (int ox = cx.lo; ox <= cx.hi; ++ox)
-            uni |= sw_j[((oy - cy.o_min) * P.ncand + (ox - cx.o_min)) * P.G + g];
+        for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+          for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
+            uni |= sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
         while (uni) {
           const int bit = __ffs(uni) - 1;
           uni &= uni - 1u;
           const int oc = g * P.lpu + bit;
-          for (int oy = cy.lo; oy <= cy.hi; ++oy)
-            for (int ox = cx.lo; ox <= cx.hi; ++ox) {
-              const uint32_t wd = sw_j[((oy - cy.o_min) * P.ncand + (ox - cx.o_min)) * P.G + g];
+          for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+            for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
+              const uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
               const int64_t n = (int64_t)oc * P.n_sp + oy * P.w_out + ox;
               if ((wd & (1u << bit)) && ((n < nstar) || (n == nstar && j <= j_cut))) {
-                ot[k] = t;
-                os[k] = (int32_t)n;
-                ++k;
+                ot[kk] = t;
+                os[kk] = (int32_t)n;
+                ++kk;
               }
             }
         }
@@ -678,9 +764,9 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
       else if (n == nstar) c = tail_keep;
       int32_t total;
       const int32_t off = block_exclusive_scan(c, s_scan, total);
-      for (int32_t k = 0; k < c; ++k) {
-        ot[written + off + k] = t;
-        os[written + off + k] = (int32_t)n;
+      for (int32_t kq = 0; kq < c; ++kq) {
+        ot[written + off + kq] = t;
+        os[written + off + kq] = (int32_t)n;
       }
       written += total;
     }

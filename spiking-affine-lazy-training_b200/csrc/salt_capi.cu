@@ -185,18 +185,22 @@ struct ConvPlan {
   size_t smem;
 };
 
+// A launch block carrying only what the shared-memory layout depends on.
 static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, const ConvPlan& p,
-                         int npm) {
-  size_t s = 0;
-  s += align16((size_t)d->ic * d->k * d->k * p.ocp * p.wt_bytes);
-  s += align16((size_t)(q->lut_len <= kLutSmemMax ? q->lut_len : 0) * 4);
-  s += align16((size_t)npm * p.ocp * 4);
-  s += align16((size_t)npm * 4) * 2;
-  s += align16((size_t)npm * (kFusedChunk / 32) * 4);
-  s += align16((size_t)kFusedChunk * 20);
-  s += align16((size_t)p.ocp * 4);
-  s += 64;
-  return s;
+                         int tile_h, int tile_w, int T) {
+  ConvLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.ic = d->ic;
+  L.k = d->k;
+  L.ocp = p.ocp;
+  L.G = p.G;
+  L.nslots = p.nslots;
+  L.tile_h = tile_h;
+  L.tile_w = tile_w;
+  L.T = T;
+  L.lut_in_smem = q->lut_len <= kLutSmemMax;
+  L.qc.lut_len = q->lut_len;
+  return conv_fused_smem_bytes(L, p.wt_bytes);
 }
 
 static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, int32_t batch,
@@ -225,11 +229,11 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.ocp = p.G * lpu;
   p.wt_bytes = q->q_bits <= 8 ? 1 : (q->q_bits <= 16 ? 2 : 4);
   p.tail_mode = q->needs_tail ? 1 : 0;
-  // Positions per block: as many as fit a ~100 KB shared-memory budget (two blocks per SM),
-  // at most 256 (balanced chunk work), never fewer than one candidate window.
+  // Positions per block: as many as fit a ~100 KB shared-memory budget (two or more blocks
+  // per SM), at most 256 (balanced chunk work), never fewer than one candidate window.
   const size_t budget = 100 * 1024;
   int npm_cap = 256;
-  while (npm_cap > 1 && fused_smem(d, q, p, npm_cap) > budget) npm_cap >>= 1;
+  while (npm_cap > 1 && fused_smem(d, q, p, 1, npm_cap, 2) > budget) npm_cap >>= 1;
   if (p.n_sp <= npm_cap) {
     p.tile_h = p.h_out;
     p.tile_w = p.w_out;
@@ -247,7 +251,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
   p.n_part_chunks = (E + kPartChunk - 1) / kPartChunk;
   p.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
-  p.smem = fused_smem(d, q, p, p.tile_h * p.tile_w);
+  p.smem = fused_smem(d, q, p, p.tile_h, p.tile_w, p.T);
   if (p.smem > 227 * 1024)
     return fail(SALT_BAD_ARG, "conv layer weights do not fit in shared memory (ic*k*k*oc too "
                               "large for the chosen weight width)");
@@ -292,11 +296,17 @@ static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, 
   return c.size();
 }
 
+// Optional CUDA-event pair recorded around the fused kernel (network profiling).
+struct KernelTimer {
+  cudaEvent_t start = nullptr, stop = nullptr;
+};
+
 static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_desc* q,
                                      const int32_t* qw, const int32_t* lut, const int32_t* vth,
                                      int32_t B, const salt_stream_in* in, salt_stream_out* out,
                                      int32_t* v_final, const salt_layer_stats* stats, void* ws,
-                                     size_t ws_bytes, cudaStream_t st) {
+                                     size_t ws_bytes, cudaStream_t st,
+                                     const KernelTimer* timer = nullptr) {
   salt_status rc = check_quant(q);
   if (rc) return rc;
   if ((rc = check_stream_in(in, B))) return rc;
@@ -321,6 +331,11 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.L = d->max_queue_len; L.M = d->max_out_spikes; L.max_extra = d->max_extra_steps;
   L.lpu = p.lpu; L.G = p.G; L.ocp = p.ocp;
   L.tile_h = p.tile_h; L.tile_w = p.tile_w; L.tiles_x = p.tiles_x; L.T = p.T;
+  L.fd_hw = FastDiv((uint32_t)(d->h_in * d->w_in));
+  L.fd_w = FastDiv((uint32_t)d->w_in);
+  L.fd_s = FastDiv((uint32_t)d->s);
+  L.fd_G = FastDiv((uint32_t)p.G);
+  L.fd_tw = FastDiv((uint32_t)p.tile_w);
   L.n_part_chunks = p.n_part_chunks; L.list_stride = p.list_stride;
   L.in.times = in->times; L.in.src = in->src; L.in.capacity = E; L.in.virtual_pads = in->virtual_pads;
   L.in_nreal = in->n_real; L.batch = B;
@@ -349,8 +364,10 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   void* fn = conv_fused_kernel(p.wt_bytes, p.lpu);
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
   void* args[] = {&L};
+  if (timer) SALT_CUDA(cudaEventRecord(timer->start, st));
   SALT_CUDA(cudaLaunchKernel(fn, dim3(p.T, B), dim3(kFusedThreads), args, p.smem, st));
   SALT_LAUNCHED("conv_fused");
+  if (timer) SALT_CUDA(cudaEventRecord(timer->stop, st));
   spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
   SALT_LAUNCHED("spike_chunk_scan");
   conv_compact<<<dim3(p.n_spk_chunks, B), kCompactThreads, 0, st>>>(L, *out);
@@ -479,9 +496,17 @@ struct LayerRec {
   int32_t M = 0;
 };
 
+struct TimedLaunch {
+  int32_t layer;
+  KernelTimer ev;
+};
+
 struct salt_network {
   std::vector<LayerRec> layers;
   int32_t last_launches = 0;
+  bool profiling = false;
+  std::vector<TimedLaunch> timed;   // recorded, not yet read
+  std::vector<KernelTimer> pool;    // events free for reuse
 };
 
 extern "C" {
@@ -636,6 +661,11 @@ salt_status salt_network_create(const salt_layer_spec* layers, int32_t n_layers,
 
 salt_status salt_network_destroy(salt_network* net) {
   if (!net) return SALT_OK;
+  for (auto& t : net->timed) net->pool.push_back(t.ev);
+  for (auto& e : net->pool) {
+    cudaEventDestroy(e.start);
+    cudaEventDestroy(e.stop);
+  }
   for (auto& r : net->layers) {
     cudaFree(r.d_q);
     cudaFree(r.d_lut);
@@ -737,9 +767,21 @@ salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_st
                         vmin ? vmin + (size_t)l * B : sb + 3 * B,
                         vmax ? vmax + (size_t)l * B : sb + 4 * B,
                         sb + 5 * B};
+    KernelTimer timer;
+    if (net->profiling && r.spec.kind == 0) {
+      if (net->pool.empty()) {
+        SALT_CUDA(cudaEventCreate(&timer.start));
+        SALT_CUDA(cudaEventCreate(&timer.stop));
+      } else {
+        timer = net->pool.back();
+        net->pool.pop_back();
+      }
+      net->timed.push_back({l, timer});
+    }
     if (r.spec.kind == 0)
       rc = conv_forward_impl(&r.spec.conv, &r.spec.quant, r.d_q, r.d_lut, r.d_vth, B, &cur, &so,
-                             vf, &ls, o.scratch, o.scratch_bytes, st);
+                             vf, &ls, o.scratch, o.scratch_bytes, st,
+                             timer.start ? &timer : nullptr);
     else
       rc = fc_forward_impl(&r.spec.fc, &r.spec.quant, r.d_q, true, r.d_lut, r.d_vth, B, &cur, &so,
                            vf, &ls, o.scratch, o.scratch_bytes, st);
@@ -760,6 +802,34 @@ salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_st
 
 int32_t salt_network_last_launch_count(const salt_network* net) {
   return net ? net->last_launches : 0;
+}
+
+salt_status salt_network_set_profiling(salt_network* net, int32_t enable) {
+  if (!net) return fail(SALT_BAD_ARG, "NULL network");
+  net->profiling = enable != 0;
+  return SALT_OK;
+}
+
+salt_status salt_network_profile_read(salt_network* net, float* fused_ms, int32_t* launches,
+                                      int32_t reset) {
+  if (!net || !fused_ms || !launches) return fail(SALT_BAD_ARG, "profile_read: NULL argument");
+  const size_t nl = net->layers.size();
+  for (size_t l = 0; l < nl; ++l) {
+    fused_ms[l] = 0.0f;
+    launches[l] = 0;
+  }
+  for (auto& t : net->timed) {
+    SALT_CUDA(cudaEventSynchronize(t.ev.stop));
+    float ms = 0.0f;
+    SALT_CUDA(cudaEventElapsedTime(&ms, t.ev.start, t.ev.stop));
+    fused_ms[t.layer] += ms;
+    launches[t.layer] += 1;
+  }
+  if (reset) {
+    for (auto& t : net->timed) net->pool.push_back(t.ev);
+    net->timed.clear();
+  }
+  return SALT_OK;
 }
 
 

@@ -97,3 +97,24 @@ struct StreamView {
 };
 
 }  // namespace salt
+
+namespace salt {
+
+// Division of a non-negative int32 by a runtime constant d >= 1 with a precomputed multiplier
+// (round-up method: q = (umulhi(x, m) + x) >> l, l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1; exact for 0 <= x < 2^31).  Built on the host.
+struct FastDiv {
+  uint32_t d, m, l;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    l = 0;
+    while ((1ull << l) < divisor) ++l;
+    m = (uint32_t)((((1ull << 32) * ((1ull << l) - divisor)) / divisor) + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t x) const {
+    return (__umulhi(x, m) + x) >> l;
+  }
+  __device__ __forceinline__ uint32_t mod(uint32_t x) const { return x - div(x) * d; }
+};
+
+}  // namespace salt

@@ -24,6 +24,8 @@ struct ConvLaunch {
   int32_t ncand, nslots;      // candidates per axis (k-1)//s+1 and per event (ncand^2)
   int32_t L, M, max_extra;    // max_queue_len, max_out_spikes, max_extra_steps
   int32_t lpu, G, ocp;        // lanes per channel group, channel groups, padded channel stride
+  // host-built divisors: h_in*w_in, w_in, stride, channel groups, tile width
+  FastDiv fd_hw, fd_w, fd_s, fd_G, fd_tw;
   // tiling of the output plane
   int32_t tile_h, tile_w, tiles_x, T;
   int32_t n_part_chunks;
@@ -57,6 +59,32 @@ struct ConvLaunch {
   __device__ __forceinline__ int32_t n_eff(int b) const {
     int32_t n = in_nreal[b];
     return n < 0 ? 0 : (n < in.capacity ? n : in.capacity);
+  }
+
+  // Flat source index -> (clamped channel, y, x) with JAX's floor division / modulo
+  // (connectivity/conv.py:32-43) and the channel gather clamp of q[oc][c] (conv.py:175-178).
+  __device__ __forceinline__ void decode(int32_t src, int32_t& c, int32_t& y, int32_t& x) const {
+    int32_t rem;
+    if (src >= 0) {
+      c = (int32_t)fd_hw.div((uint32_t)src);
+      rem = src - c * hw_in;
+    } else {
+      c = floordiv(src, hw_in);
+      rem = floormod(src, hw_in);
+    }
+    y = (int32_t)fd_w.div((uint32_t)rem);
+    x = rem - y * w_in;
+    c = (int32_t)jax_index(c, ic);
+  }
+  // Receptive-field candidates of coordinate i along one axis (conv.py:15-29): the first
+  // candidate o_min = ceil((i+p-k+1)/s) and the valid range [lo, hi].
+  __device__ __forceinline__ void axis(int32_t i, int32_t O, int32_t& o_min, int32_t& lo,
+                                       int32_t& hi) const {
+    // i + p - k + s >= 1 - k, so adding k*s keeps the dividend non-negative
+    o_min = (int32_t)fd_s.div((uint32_t)(i + p - k + s + k * s)) - k;
+    const int32_t upper = (int32_t)fd_s.div((uint32_t)(i + p));
+    lo = max(o_min, 0);
+    hi = min(min(upper, o_min + ncand - 1), O - 1);
   }
 };
 
@@ -151,6 +179,8 @@ __global__ void fc_compact(FCLaunch P, salt_stream_out out);
 __global__ void fc_truncated(FCLaunch P, salt_stream_out out);
 // Kernel entry points of the templated kernels, for cudaLaunchKernel.
 void* conv_fused_kernel(int wt_bytes, int lpu);
+// Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
+size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 void* fc_scan_kernel(bool fires);
 constexpr int kFcThreads = 128;
 

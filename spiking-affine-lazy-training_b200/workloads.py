@@ -1,0 +1,238 @@
+"""Seeded synthetic workloads with the shapes and value distributions of the five benchmark
+configurations (no public dataset is involved; N-MNIST conventions — a 2x34x34 polarity grid,
+src = c*H*W + y*W + x, integer-ms timestamps — shape configs 1-3).
+
+Every generator is deterministic given its seed (numpy PCG64).  Capacities that the
+configurations leave open are sized like the reference's run_until_fits
+(example/quant_run.py:122-132): run once with room to spare, then grow each knob to
+ceil(1.5 x the largest need) (capacity.py GrowthPolicy factor 1.5), or to 4x the expected need
+where a configuration says so.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from .layers import ConvLayer, FCLayer, conv, fc
+from .network import InputEvents, Network
+from .quant import QuantizedLayerParams, build_decay_table_int
+
+F_A, F_V, I_V, TAU = 10, 0, 24, 20.0   # reference defaults: configs/quant/baseline.yaml:16-25
+
+
+@dataclass
+class Workload:
+    name: str
+    network: Network
+    params: list
+    times: np.ndarray       # (B, E) float32 integer ms
+    src: np.ndarray         # (B, E) int32
+    n_real: np.ndarray      # (B,) int32
+
+    @property
+    def batch(self) -> int:
+        return int(self.times.shape[0])
+
+    @property
+    def events(self) -> int:
+        return int(np.minimum(self.n_real, self.times.shape[1]).sum())
+
+    def raw(self) -> InputEvents:
+        return InputEvents(self.times, self.src, self.n_real)
+
+    def subset(self, idx) -> "Workload":
+        idx = np.asarray(idx)
+        return replace(self, times=self.times[idx], src=self.src[idx], n_real=self.n_real[idx])
+
+
+def _pack(per_sample_t, per_sample_s, E_cap=None):
+    B = len(per_sample_t)
+    E = E_cap or max(1, max(len(t) for t in per_sample_t))
+    times = np.zeros((B, E), np.float32)
+    src = np.zeros((B, E), np.int32)
+    nr = np.zeros(B, np.int32)
+    for b, (t, s) in enumerate(zip(per_sample_t, per_sample_s)):
+        n = len(t)
+        nr[b] = n
+        times[b, :n] = t
+        src[b, :n] = s
+        if n < E:                     # pads repeat the last real time (any value works)
+            times[b, n:] = t[-1] if n else 0.0
+    return times, src, nr
+
+
+def _qparams(layer, rng, sigma, fires, v_th_int=None):
+    if sigma is None:
+        q = rng.integers(-127, 128, size=layer.weight_shape)
+    else:
+        q = np.clip(np.round(rng.normal(0.0, sigma, size=layer.weight_shape)), -127, 127)
+    q = q.astype(np.int32)
+    if fires:
+        v = int(rng.integers(128, 513)) if v_th_int is None else int(v_th_int)
+        vth = np.full(layer.n_neurons, v, np.int32)
+    else:
+        vth = None
+    return QuantizedLayerParams(q=q, decay_table_int=build_decay_table_int(F_A, layer.tau),
+                                v_th_int=vth, scale=np.float32(1.0), f_a=F_A, f_V=F_V, i_V=I_V,
+                                overflow_mode="wrap")
+
+
+def config1(seed: int = 0) -> Workload:
+    """FC 2312->128, one sample of 5000 uniform events in [0, 300) ms, v_th_int = 256."""
+    rng = np.random.default_rng(seed)
+    t = np.sort(rng.integers(0, 300, size=5000)).astype(np.float32)
+    s = rng.integers(0, 2312, size=5000).astype(np.int32)
+    net = Network.build((2, 34, 34), [fc(128, init_k=5.0, tau=TAU, max_out_spikes=8192)])
+    params = [_qparams(net.layers[0], rng, None, True, v_th_int=256)]
+    times, src, nr = _pack([t], [s])
+    return Workload("config1_fc2312x128_b1", net, params, times, src, nr)
+
+
+def _conv_net_small(p1: int):
+    return [conv(16, k=3, s=2, p=p1, init_k=5.0, tau=TAU, max_queue_len=1 << 30,
+                 max_out_spikes=1 << 16),
+            conv(32, k=3, s=2, p=1, init_k=5.0, tau=TAU, max_queue_len=1 << 30,
+                 max_out_spikes=1 << 16),
+            fc(10, init_k=5.0, tau=TAU, v_th=1e9, max_out_spikes=1)]
+
+
+def _uniform_events(rng, n, n_addr, t_max=300):
+    return (np.sort(rng.integers(0, t_max, size=n)).astype(np.float32),
+            rng.integers(0, n_addr, size=n).astype(np.int32))
+
+
+def config2(seed: int = 0, p1: int = 0) -> Workload:
+    """conv 2->16 (k3 s2 p0) -> conv 16->32 (k3 s2 p1) -> FC 2048->10, batch 64, Poisson(5000)
+    uniform events.  p1=1 gives the reference's production padding (FC input 32*9*9)."""
+    rng = np.random.default_rng(seed)
+    ts, ss = [], []
+    for _ in range(64):
+        t, s = _uniform_events(rng, int(rng.poisson(5000)), 2 * 34 * 34)
+        ts.append(t)
+        ss.append(s)
+    net = Network.build((2, 34, 34), _conv_net_small(p1))
+    params = [_qparams(l, rng, 40.0, i < 2) for i, l in enumerate(net.layers)]
+    times, src, nr = _pack(ts, ss)
+    return Workload(f"config2_convnet_b64_p{p1}", net, params, times, src, nr)
+
+
+def blob_events(rng, n):
+    """90 % of events from a sigma=6 px Gaussian blob around a centre moving linearly across the
+    34x34 frame over 300 ms, 10 % uniform; uniform polarity; sorted integer ms in [0, 300)."""
+    t = np.sort(rng.integers(0, 300, size=n)).astype(np.float32)
+    c0, c1 = rng.uniform(0, 33, size=2), rng.uniform(0, 33, size=2)
+    frac = (t / 300.0)[:, None]
+    centre = c0[None, :] + (c1 - c0)[None, :] * frac
+    xy = np.clip(np.round(rng.normal(centre, 6.0)), 0, 33).astype(np.int32)
+    noise = rng.random(n) < 0.1
+    xy[noise] = rng.integers(0, 34, size=(int(noise.sum()), 2))
+    pol = rng.integers(0, 2, size=n)
+    return t, (pol * 34 * 34 + xy[:, 1] * 34 + xy[:, 0]).astype(np.int32)
+
+
+def config3(seed: int = 0, batch: int = 4096, p1: int = 0) -> Workload:
+    """The config-2 network at batch 4096, log-uniform [2000, 20000] events per sample from a
+    moving Gaussian blob plus 10 % noise."""
+    rng = np.random.default_rng(seed)
+    net = Network.build((2, 34, 34), _conv_net_small(p1))
+    params = [_qparams(l, rng, 40.0, i < 2) for i, l in enumerate(net.layers)]
+    ts, ss = [], []
+    for _ in range(batch):
+        n = int(math.floor(math.exp(rng.uniform(math.log(2000), math.log(20000)))))
+        t, s = blob_events(rng, n)
+        ts.append(t)
+        ss.append(s)
+    times, src, nr = _pack(ts, ss, E_cap=20000)
+    return Workload(f"config3_convnet_blob_b{batch}_p{p1}", net, params, times, src, nr)
+
+
+def burst_events(rng, n, n_addr):
+    """Bursts arriving as a Poisson process (mean gap 5 ms), 200-2000 events per burst sharing
+    one integer-ms timestamp, uniform addresses."""
+    t = np.empty(n, np.float32)
+    k, clock = 0, 0.0
+    while k < n:
+        clock += rng.exponential(5.0)
+        m = min(int(rng.integers(200, 2001)), n - k)
+        t[k:k + m] = math.floor(clock)
+        k += m
+    return t, rng.integers(0, n_addr, size=n).astype(np.int32)
+
+
+def config4(seed: int = 0, batch: int = 256) -> Workload:
+    """Four conv k3 s2 p1 layers 2->32->64->64->64 on 2x128x128 input, FC 4096->10, batch 256,
+    50k-200k bursty events per sample."""
+    rng = np.random.default_rng(seed)
+    specs = [conv(c, k=3, s=2, p=1, init_k=5.0, tau=TAU, max_queue_len=1 << 30,
+                  max_out_spikes=1 << 20) for c in (32, 64, 64, 64)]
+    specs.append(fc(10, init_k=5.0, tau=TAU, v_th=1e9, max_out_spikes=1))
+    net = Network.build((2, 128, 128), specs)
+    params = [_qparams(l, rng, 30.0, i < 4) for i, l in enumerate(net.layers)]
+    ts, ss = [], []
+    for _ in range(batch):
+        t, s = burst_events(rng, int(rng.integers(50_000, 200_001)), 2 * 128 * 128)
+        ts.append(t)
+        ss.append(s)
+    times, src, nr = _pack(ts, ss, E_cap=200_000)
+    return Workload(f"config4_deepconv_b{batch}", net, params, times, src, nr)
+
+
+CONFIGS = {1: config1, 2: config2, 3: config3, 4: config4}
+
+
+def candidates_per_event(layer: ConvLayer, src: np.ndarray) -> np.ndarray:
+    """Valid receptive-field candidates of each event (connectivity/conv.py:15-29,147-155)."""
+    hw = layer.h_in * layer.w_in
+    rem = np.mod(src, hw)
+    y, x = rem // layer.w_in, rem % layer.w_in
+
+    def axis(i, O):
+        o_min = (i + layer.p - layer.k + layer.s) // layer.s
+        upper = (i + layer.p) // layer.s
+        n = (layer.k - 1) // layer.s + 1
+        lo = np.maximum(o_min, 0)
+        hi = np.minimum(np.minimum(upper, o_min + n - 1), O - 1)
+        return np.maximum(hi - lo + 1, 0)
+
+    return axis(y, layer.h_out) * axis(x, layer.w_out)
+
+
+def size_capacities(wl: Workload, backend, *, factor: float = 1.5, rounds: int = 4,
+                    expected_factor: float | None = None) -> Workload:
+    """Grow every capacity knob to fit the workload: run with room to spare, then set each knob
+    to ceil(factor x the largest need) and repeat until every sample fits (run_until_fits with
+    GrowthPolicy's factor).  With expected_factor, each knob is instead expected_factor x its
+    expected need (the config-4 rule): the queue knob from the mean number of receptive-field
+    candidates per output position, the output knob from the mean spike count."""
+    layers = list(wl.network.layers)
+    for _ in range(rounds):
+        out = backend.run_network(layers, wl.params, wl.network.input_stream(wl.raw()),
+                                  keep_streams=expected_factor is not None)
+        new, stream_src, stream_n = [], wl.src, wl.n_real
+        for li, (layer, diag) in enumerate(zip(layers, out.diags)):
+            need = diag.needed
+            knobs = {}
+            if expected_factor is None:
+                knobs["max_out_spikes"] = max(1, math.ceil(int(np.max(need["max_out_spikes"]))
+                                                           * factor))
+                if isinstance(layer, ConvLayer):
+                    knobs["max_queue_len"] = max(1, math.ceil(int(np.max(need["max_queue_len"]))
+                                                              * factor))
+            else:
+                knobs["max_out_spikes"] = max(1, math.ceil(float(np.mean(need["max_out_spikes"]))
+                                                           * expected_factor))
+                if isinstance(layer, ConvLayer):
+                    E = stream_src.shape[1]
+                    real = np.arange(E)[None, :] < np.minimum(stream_n, E)[:, None]
+                    cand = np.where(real, candidates_per_event(layer, stream_src), 0).sum(axis=1)
+                    per_pos = float(np.mean(cand)) / (layer.h_out * layer.w_out)
+                    knobs["max_queue_len"] = max(2, math.ceil(per_pos * expected_factor))
+                s_out = out.streams[li]
+                stream_src, stream_n = s_out.event_source_idx, s_out.n_real_events
+            new.append(replace(layer, **knobs))
+        layers = new
+        if expected_factor is not None or bool(np.all(out.fits)):
+            break
+    return replace(wl, network=wl.network.replace_layers(layers))
