@@ -311,6 +311,52 @@ def network_forward(layers, params, times, src, n_real, round_mode="round") -> l
     return out
 
 
+def compress_candidates(n_flat, j_flat, n_out_spatial, max_queue_len, n_events):
+    """salt_core/connectivity/conv.py:57-99 -> (local_to_global_j, n_real_per_neuron)."""
+    nf = np.ascontiguousarray(n_flat, dtype=np.int32)
+    jf = np.ascontiguousarray(j_flat, dtype=np.int32)
+    l2g = np.empty((n_out_spatial, max_queue_len), np.int32)
+    nr = np.empty(n_out_spatial, np.int32)
+    rc = lib().so_compress_candidates(_p(nf, _i32p), _p(jf, _i32p), ctypes.c_int64(nf.size),
+                                      n_out_spatial, max_queue_len, n_events, _p(l2g, _i32p),
+                                      _p(nr, _i32p))
+    if rc:
+        raise ValueError(f"compress failed rc={rc}")
+    return l2g, nr
+
+
+def delta_t_three_regimes(t_gathered, n_real_per_neuron, global_last_time):
+    """salt_core/connectivity/conv.py:102-125"""
+    tg = np.ascontiguousarray(t_gathered, dtype=np.float32)
+    nr = np.ascontiguousarray(n_real_per_neuron, dtype=np.int32)
+    n, L = tg.shape
+    dt = np.empty((n, L), np.float32)
+    lib().so_delta_t_regimes(_p(tg, _f32p), _p(nr, _i32p), ctypes.c_float(global_last_time), n, L,
+                             _p(dt, _f32p))
+    return dt
+
+
+def extract_output_events(spike_mask, spike_event_idx, event_times, max_total_spikes,
+                          local_to_global_j=None):
+    """salt_core/stream.py:67-100 (fc when local_to_global_j is None, else conv with the
+    tiled (rows, L) table) -> (times, source_idx, n_real_events)."""
+    m = np.ascontiguousarray(spike_mask, dtype=np.uint8)
+    n, steps = m.shape
+    ei = None if spike_event_idx is None else np.ascontiguousarray(spike_event_idx, np.int32)
+    t = np.ascontiguousarray(event_times, dtype=np.float32)
+    l2g = None if local_to_global_j is None else np.ascontiguousarray(local_to_global_j, np.int32)
+    M = int(max_total_spikes)
+    ot = np.empty(max(M, 1), np.float32)
+    osrc = np.empty(max(M, 1), np.int32)
+    nr = ctypes.c_int32(0)
+    lib().so_extract_output_events(
+        _p(m, _u8p), None if ei is None else _p(ei, _i32p), n, steps,
+        None if l2g is None else _p(l2g, _i32p), 1 if l2g is None else l2g.shape[0],
+        1 if l2g is None else l2g.shape[1], _p(t, _f32p), t.shape[0], M, _p(ot, _f32p),
+        _p(osrc, _i32p), ctypes.byref(nr))
+    return ot[:M], osrc[:M], int(nr.value)
+
+
 def conv_structure(layer, times, src, n_in):
     """salt_core/connectivity/conv.py:128-172 -> dict of the ConvQueueStructure arrays."""
     t = np.ascontiguousarray(np.asarray(times, dtype=np.float32))

@@ -159,6 +159,68 @@ static void stable_sort_by_n(cand_t *c, int64_t C, int32_t n_buckets, cand_t *tm
   free(cnt);
 }
 
+/* connectivity/conv.py:57-99 _compress_candidates.  lexsort((j, n)) is a stable sort by n of
+ * candidates listed in j order; ties on (n, j) occur only among invalid candidates. */
+int so_compress_candidates(const int32_t *n_flat, const int32_t *j_flat, int64_t C, int32_t n_sp,
+                           int32_t L, int32_t n_events, int32_t *l2g, int32_t *n_real) {
+  if (C < 0 || n_sp < 0 || L < 0) return -1;
+  cand_t *c = (cand_t *)malloc(sizeof(cand_t) * (size_t)(C > 0 ? C : 1));
+  cand_t *tmp = (cand_t *)malloc(sizeof(cand_t) * (size_t)(C > 0 ? C : 1));
+  if (!c || !tmp) {
+    free(c);
+    free(tmp);
+    return -3;
+  }
+  /* lexsort orders by n then by j: sort by j first (stable), then by n (stable) */
+  for (int64_t i = 0; i < C; ++i) {
+    c[i].n = n_flat[i] < n_sp ? n_flat[i] : n_sp; /* any n >= n_sp is the invalid bucket */
+    c[i].j = j_flat[i];
+  }
+  /* stable order by j: candidates may be given in any order */
+  for (int64_t w = 1; w < C; w *= 2) {
+    for (int64_t lo = 0; lo < C; lo += 2 * w) {
+      int64_t mid = lo + w < C ? lo + w : C, hi = lo + 2 * w < C ? lo + 2 * w : C;
+      int64_t a = lo, b = mid, o = lo;
+      while (a < mid && b < hi) tmp[o++] = c[b].j < c[a].j ? c[b++] : c[a++];
+      while (a < mid) tmp[o++] = c[a++];
+      while (b < hi) tmp[o++] = c[b++];
+    }
+    memcpy(c, tmp, sizeof(cand_t) * (size_t)C);
+  }
+  stable_sort_by_n(c, C, n_sp + 1, tmp);
+  for (int64_t i = 0; i < (int64_t)n_sp * L; ++i) l2g[i] = n_events;
+  memset(n_real, 0, sizeof(int32_t) * (size_t)n_sp);
+  int64_t last_start = 0;
+  for (int64_t i = 0; i < C; ++i) {
+    if (i == 0 || c[i].n != c[i - 1].n) last_start = i;
+    int64_t rank = i - last_start;
+    if (c[i].n >= n_sp) continue; /* trash row */
+    if (rank < L) l2g[(int64_t)c[i].n * L + rank] = c[i].j;
+    if (rank + 1 > n_real[c[i].n]) n_real[c[i].n] = (int32_t)(rank + 1);
+  }
+  free(c);
+  free(tmp);
+  return 0;
+}
+
+/* connectivity/conv.py:102-125 _delta_t_three_regimes */
+void so_delta_t_regimes(const float *t_gathered, const int32_t *n_real, float global_last,
+                        int32_t n, int32_t L, float *delta_t) {
+  for (int32_t i = 0; i < n; ++i) {
+    const float *tg = t_gathered + (int64_t)i * L;
+    int32_t lr = n_real[i] - 1;
+    if (lr < 0) lr = 0;
+    if (lr > L - 1) lr = L - 1;
+    float catchup = global_last - tg[lr];
+    float prev = 0.0f;
+    for (int32_t col = 0; col < L; ++col) {
+      float d = tg[col] - prev;
+      prev = tg[col];
+      delta_t[(int64_t)i * L + col] = col < n_real[i] ? d : (col == n_real[i] ? catchup : 0.0f);
+    }
+  }
+}
+
 /* connectivity/conv.py:128-172 build_conv_structure, with _compress_candidates (:57-99) and
  * _delta_t_three_regimes (:102-125). */
 int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *src, int32_t E_len,
@@ -203,17 +265,26 @@ int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *
         cand[k].j = j;
       }
   }
-  stable_sort_by_n(cand, C, n_sp + 1, tmp);
-
-  for (int64_t i = 0; i < (int64_t)n_sp * L; ++i) l2g[i] = E_len;
-  memset(n_real, 0, sizeof(int32_t) * (size_t)n_sp);
-  int64_t last_start = 0;
-  for (int64_t i = 0; i < C; ++i) {
-    if (i == 0 || cand[i].n != cand[i - 1].n) last_start = i;
-    int64_t rank = i - last_start;
-    if (cand[i].n >= n_sp) continue; /* trash row */
-    if (rank < L) l2g[(int64_t)cand[i].n * L + rank] = cand[i].j;
-    if (rank + 1 > n_real[cand[i].n]) n_real[cand[i].n] = (int32_t)(rank + 1);
+  free(tmp);
+  {
+    int32_t *nf = (int32_t *)malloc(sizeof(int32_t) * (size_t)C * 2);
+    if (!nf) {
+      free(ex);
+      free(cand);
+      return -3;
+    }
+    int32_t *jf = nf + C;
+    for (int64_t i = 0; i < C; ++i) {
+      nf[i] = cand[i].n;
+      jf[i] = cand[i].j;
+    }
+    free(cand);
+    int rc = so_compress_candidates(nf, jf, C, n_sp, L, E_len, l2g, n_real);
+    free(nf);
+    if (rc) {
+      free(ex);
+      return rc;
+    }
   }
 
   /* conv.py:159-162: empty columns clamp to the last real event; gather semantics as JAX. */
@@ -250,42 +321,46 @@ int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *
     }
   }
   free(ex);
-  free(cand);
-  free(tmp);
   return 0;
 }
 
-/* stream.py:49-64 _select_spikes + :24-46 _pack_stream.  global_j_of(neuron, col) is given
- * as a callback-free table: for conv it is l2g[(neuron % n_sp) * L + col], for fc it is col. */
-static void select_and_pack(const uint8_t *mask, int32_t n, int32_t L, const int32_t *l2g,
-                            int32_t n_sp, const float *times, int32_t E_len, int32_t M,
-                            float *out_times, int32_t *out_src, int32_t *n_real_out) {
-  int32_t *nidx = (int32_t *)calloc((size_t)(M > 0 ? M : 1), sizeof(int32_t));
-  int32_t *cidx = (int32_t *)calloc((size_t)(M > 0 ? M : 1), sizeof(int32_t));
+/* stream.py:49-64 _select_spikes + :84-100 / :67-81 + :24-46 _pack_stream. */
+void so_extract_output_events(const uint8_t *mask, const int32_t *event_idx, int32_t n,
+                              int32_t steps, const int32_t *l2g, int32_t l2g_rows, int32_t L,
+                              const float *times, int32_t E_len, int32_t M, float *out_times,
+                              int32_t *out_src, int32_t *n_real_out) {
+  size_t cap = (size_t)(M > 0 ? M : 1);
+  int32_t *nidx = (int32_t *)calloc(cap, sizeof(int32_t)); /* nonzero(..., fill_value=0) */
+  int32_t *sidx = (int32_t *)calloc(cap, sizeof(int32_t));
   int64_t total = 0;
   for (int32_t i = 0; i < n; ++i)
-    for (int32_t t = 0; t < L; ++t)
-      if (mask[(int64_t)i * L + t]) {
+    for (int32_t t = 0; t < steps; ++t)
+      if (mask[(int64_t)i * steps + t]) {
         if (total < M) {
           nidx[total] = i;
-          cidx[total] = t;
+          sidx[total] = t;
         }
         total++;
       }
-  int32_t nr = (int32_t)total;
-  int32_t *key = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
-  int32_t *gj = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  const int32_t nr = (int32_t)total;
+  int32_t *key = (int32_t *)malloc(sizeof(int32_t) * cap);
+  int32_t *gj = (int32_t *)malloc(sizeof(int32_t) * cap);
   for (int32_t k = 0; k < M; ++k) {
-    int32_t col = cidx[k] < L - 1 ? cidx[k] : L - 1;
-    int32_t g = l2g ? l2g[(int64_t)(nidx[k] % n_sp) * L + col] : cidx[k];
+    /* queue column of the selected step (spike_event_idx[neuron, step]) */
+    int32_t col = event_idx ? event_idx[(int64_t)nidx[k] * steps + sidx[k]] : sidx[k];
+    int32_t g = col;
+    if (l2g) { /* conv: local column -> global index via tile_channels(local_to_global_j) */
+      int32_t c = col < L - 1 ? col : L - 1;
+      g = l2g[(int64_t)(nidx[k] % l2g_rows) * L + c];
+    }
     gj[k] = g;
     key[k] = k < nr ? g : E_len;
   }
-  /* stable sort of indices 0..M-1 by key (jnp.lexsort on a single key is stable) */
-  int32_t *order = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
-  int32_t *tmpo = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  /* stable sort of 0..M-1 by key: jnp.lexsort on one key is stable */
+  int32_t *order = (int32_t *)malloc(sizeof(int32_t) * cap);
+  int32_t *tmpo = (int32_t *)malloc(sizeof(int32_t) * cap);
   for (int32_t k = 0; k < M; ++k) order[k] = k;
-  for (int32_t width = 1; width < M; width *= 2) { /* bottom-up stable merge sort */
+  for (int32_t width = 1; width < M; width *= 2) {
     for (int32_t lo = 0; lo < M; lo += 2 * width) {
       int32_t mid = lo + width < M ? lo + width : M, hi = lo + 2 * width < M ? lo + 2 * width : M;
       int32_t a = lo, b = mid, o = lo;
@@ -304,7 +379,7 @@ static void select_and_pack(const uint8_t *mask, int32_t n, int32_t L, const int
   }
   *n_real_out = nr;
   free(nidx);
-  free(cidx);
+  free(sidx);
   free(key);
   free(gj);
   free(order);
@@ -367,8 +442,8 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
   uint8_t *ovf = out->overflowed ? out->overflowed : (uint8_t *)malloc(NL);
   so_run_layer(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
                qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax);
-  select_and_pack(mask, n, L, l2g, n_sp, times, E_len, g->max_out_spikes, out->out_times,
-                  out->out_src, &out->n_real_out);
+  so_extract_output_events(mask, NULL, n, L, l2g, n_sp, L, times, E_len, g->max_out_spikes,
+                           out->out_times, out->out_src, &out->n_real_out);
   out->spike_count = out->n_real_out;
   int32_t mx = 0;
   for (int32_t pos = 0; pos < n_sp; ++pos)
@@ -422,8 +497,8 @@ int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *t
   uint8_t *ovf = out->overflowed ? out->overflowed : (uint8_t *)malloc(NL);
   so_run_layer(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
                qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax);
-  select_and_pack(mask, n, L, NULL, 1, times, E_len, g->max_out_spikes, out->out_times,
-                  out->out_src, &out->n_real_out);
+  so_extract_output_events(mask, NULL, n, L, NULL, 1, L, times, E_len, g->max_out_spikes,
+                           out->out_times, out->out_src, &out->n_real_out);
   out->spike_count = out->n_real_out;
   out->needed_queue = 0;
   reduce_layer(out, n, L, ovf);

@@ -89,6 +89,21 @@ int so_conv_structure(const so_conv_geom *g, const float *times, const int32_t *
                       int32_t n_in, int32_t *l2g, int32_t *n_real, float *delta_t, int32_t *tap_c,
                       int32_t *tap_ky, int32_t *tap_kx);
 
+/* connectivity/conv.py:57-99 _compress_candidates: (n_flat, j_flat) candidates -> per-position
+ * queues l2g (n_sp, L) (empty = n_events) and n_real (n_sp). */
+int so_compress_candidates(const int32_t *n_flat, const int32_t *j_flat, int64_t C, int32_t n_sp,
+                           int32_t L, int32_t n_events, int32_t *l2g, int32_t *n_real);
+/* connectivity/conv.py:102-125 _delta_t_three_regimes on (n, L) gathered times. */
+void so_delta_t_regimes(const float *t_gathered, const int32_t *n_real, float global_last,
+                        int32_t n, int32_t L, float *delta_t);
+/* stream.py:49-100 extract_output_events_{fc,conv}: spike grid (n, steps) with the queue column
+ * of every step (event_idx, NULL = the step itself), optional local_to_global_j (rows, L) tiled
+ * over neurons (NULL = the column is the global index, FC), into a max_out stream. */
+void so_extract_output_events(const uint8_t *mask, const int32_t *event_idx, int32_t n,
+                              int32_t steps, const int32_t *l2g, int32_t l2g_rows, int32_t L,
+                              const float *times, int32_t E_len, int32_t max_out, float *out_times,
+                              int32_t *out_src, int32_t *n_real_out);
+
 /* Whole layers (layers/conv.py:209-234, layers/fc.py:385-402 with QuantBackend). */
 int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const float *times,
                     const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out);

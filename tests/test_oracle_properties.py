@@ -1,0 +1,100 @@
+"""Properties of the CPU oracle that need no GPU: the split wide multiply equals exact big-integer
+arithmetic (as salt_core/tests/test_fixed_point.py:101-118 checks), the C queue construction
+equals an independent dense restatement (every neuron sees every event, as the reference's
+salt_core/tests/_reference.py does), and the threaded batch driver agrees with the per-sample
+path."""
+import numpy as np
+import pytest
+
+import oracle as O
+import salt_b200 as S
+from _cases import make_events, make_params
+
+
+def test_wide_mul_shift_equals_exact_integer_arithmetic():
+    rng = np.random.default_rng(3)
+    shift = 15
+    for a, v in zip(rng.integers(0, 2 ** shift, 500), rng.integers(-(2 ** 29), 2 ** 29, 500)):
+        exact = int(a) * int(v)
+        assert O.wide_mul_shift(int(a), int(v), shift, "round") == (exact + (1 << 14)) >> shift
+        assert O.wide_mul_shift(int(a), int(v), shift, "truncate") == exact >> shift
+
+
+def test_decay_step_never_grows_magnitude():
+    """salt_core/tests/test_fixed_point.py:49-58"""
+    rng = np.random.default_rng(0)
+    for a, v in zip(rng.integers(0, 64, 2000), rng.integers(-100000, 100000, 2000)):
+        for mode in ("round", "truncate"):
+            assert abs(O.wide_mul_shift(int(a), int(v), 6, mode)) <= abs(int(v))
+
+
+def _dense_conv_reference(layer, params, times, src, n_in):
+    """Every output neuron scans every real input event; events outside its receptive field are
+    skipped, the catch-up decay to the last input time is applied at the end (the reference's
+    dense oracle, salt_core/tests/_reference.py:19-61, in integer form).  Returns v_final."""
+    K, Sd, P = layer.k, layer.s, layer.p
+    hw = layer.h_in * layer.w_in
+    lut = params.decay_table_int
+    v_final = np.zeros(layer.n_neurons, np.int64)
+    n_eff = min(n_in, len(times))
+    for oc in range(layer.oc):
+        for oy in range(layer.h_out):
+            for ox in range(layer.w_out):
+                nid = (oc * layer.h_out + oy) * layer.w_out + ox
+                v, prev, count = 0, 0.0, 0
+                for j in range(n_eff):
+                    c, rem = divmod(int(src[j]), hw)
+                    y, x = divmod(rem, layer.w_in)
+                    ky, kx = y + P - oy * Sd, x + P - ox * Sd
+                    if not (0 <= ky < K and 0 <= kx < K):
+                        continue
+                    if count >= layer.max_queue_len:
+                        count += 1
+                        continue
+                    dt = int(np.float32(times[j]) - np.float32(prev))
+                    prev = np.float32(times[j])
+                    a = 0 if dt > len(lut) else int(lut[min(max(dt - 1, 0), len(lut) - 1)])
+                    r = O.process_event(v, a, dt == 0, int(params.q[oc, c, ky, kx]),
+                                        int(params.v_th_int[nid]), f_a=params.f_a, f_V=params.f_V,
+                                        i_V=params.i_V)
+                    v = r.v_final
+                    count += 1
+                if count < layer.max_queue_len:
+                    last = np.float32(times[n_eff - 1]) if n_eff else np.float32(0)
+                    dt = int(last - np.float32(prev)) if count else 0
+                    a = 0 if dt > len(lut) else int(lut[min(max(dt - 1, 0), len(lut) - 1)])
+                    v = O.process_event(v, a, dt == 0, 0, int(params.v_th_int[nid]),
+                                        f_a=params.f_a, f_V=params.f_V, i_V=params.i_V).v_final
+                v_final[nid] = v
+    return v_final
+
+
+@pytest.mark.parametrize("geom", [(1, 6, 6, 2, 3, 2, 1), (2, 5, 7, 3, 3, 1, 1), (1, 7, 5, 2, 2, 2, 0)])
+def test_oracle_conv_matches_dense_per_neuron_scan(geom):
+    ic, h, w, oc, k, s, p = geom
+    rng = np.random.default_rng(sum(geom))
+    layer = S.ConvLayer(name="c", ic=ic, h_in=h, w_in=w, oc=oc, k=k, s=s, p=p, init_k=1.0,
+                        tau=8.0, max_queue_len=12, max_out_spikes=500)
+    params = make_params(layer, rng, vth=(30, 80), f_a=6)
+    times, src, nr = make_events(rng, 3, 40, ic * h * w, t_max=60)
+    for b in range(3):
+        ref = _dense_conv_reference(layer, params, times[b], src[b], int(nr[b]))
+        got = O.conv_forward(layer, params, times[b], src[b], int(nr[b]))
+        np.testing.assert_array_equal(got.v_final, ref)
+
+
+def test_threaded_batch_driver_matches_per_sample_forward():
+    rng = np.random.default_rng(5)
+    net = S.Network.build((2, 8, 8), [
+        S.conv(4, k=3, s=1, p=1, init_k=5.0, max_queue_len=40, max_out_spikes=512),
+        S.conv(4, k=3, s=2, p=1, init_k=5.0, max_queue_len=128, max_out_spikes=256),
+        S.fc(10, init_k=5.0, v_th=1e9, max_out_spikes=1)])
+    params = [make_params(l, rng, vth=(40, 90), f_a=8, fires=i < 2)
+              for i, l in enumerate(net.layers)]
+    times, src, nr = make_events(rng, 5, 40, 128, t_max=30)
+    vf, sc, fits = O.network_batch(net.layers, params, times, src, nr, threads=3)
+    for b in range(5):
+        refs = O.network_forward(net.layers, params, times[b], src[b], nr[b])
+        np.testing.assert_array_equal(vf[b], refs[-1].v_final)
+        assert list(sc[b]) == [r.spike_count for r in refs]
+        assert fits[b] == all(r.fits for r in refs)
