@@ -270,7 +270,7 @@ def run_b200(args):
         torch.cuda.synchronize()
         barrier()
     plan.set_profiling(False)
-    fused_ms, fused_n = plan.profile_read(reset=True)
+    fused_ms, layer_ms, fused_n = plan.profile_read(reset=True)
     launches_per_step = plan.last_launch_count()
     ms = start.elapsed_time(stop) / args.steps
     t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -341,6 +341,10 @@ def run_b200(args):
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": f"conv_fused (layer {layers[dom].name})",
                          "kernel_ms": avg_ms, "algorithmic_bytes": alg_bytes,
+                         "per_layer_ms": {l.name: {"layer": float(layer_ms[i] / max(fused_n[i], 1)),
+                                                   "fused_kernel": float(fused_ms[i] /
+                                                                         max(fused_n[i], 1))}
+                                          for i, l in enumerate(layers)},
                          "peak_source": peak_kind,
                          "note": "integer-ALU bound recurrence; see profiles/ for the "
                                  "integer-pipe utilisation"},

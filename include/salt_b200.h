@@ -171,12 +171,13 @@ salt_status salt_network_forward(salt_network *net, int32_t batch, const salt_st
 /* Number of kernel launches the last salt_network_forward enqueued (for launch accounting). */
 int32_t salt_network_last_launch_count(const salt_network *net);
 /* Kernel timing of the forwards enqueued while profiling is on: CUDA events are recorded on the
- * launching stream around every conv layer's fused bucket+scan kernel (the dominant kernel).
- * salt_network_profile_read synchronises on those events and writes, per layer, the summed
- * milliseconds (fused_ms) and the number of timed launches (launches); reset clears them. */
+ * launching stream around every conv layer's fused bucket+scan kernel (the dominant kernel) and
+ * around every whole layer.  salt_network_profile_read synchronises on those events and writes,
+ * per layer, the summed milliseconds of the fused kernel (fused_ms, 0 for FC layers) and of the
+ * whole layer (layer_ms), and the number of timed forwards (launches); reset clears them. */
 salt_status salt_network_set_profiling(salt_network *net, int32_t enable);
-salt_status salt_network_profile_read(salt_network *net, float *fused_ms, int32_t *launches,
-                                      int32_t reset);
+salt_status salt_network_profile_read(salt_network *net, float *fused_ms, float *layer_ms,
+                                      int32_t *launches, int32_t reset);
 
 /* ---------------------------------------------------------------- float chunked scan
  * Replaces FloatBackend.scan on an FC layer (salt_core/float/backend.py:16-31 ->

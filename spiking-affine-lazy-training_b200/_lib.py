@@ -66,7 +66,7 @@ _SIGS = {
                                     ctypes.c_size_t, _vp]),
     "salt_network_last_launch_count": (_i32, [_vp]),
     "salt_network_set_profiling": (_i32, [_vp, _i32]),
-    "salt_network_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
+    "salt_network_profile_read": (_i32, [_vp, _vp, _vp, _vp, _i32]),
     "salt_float_fc_scan": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, ctypes.c_float,
                                   _vp, _vp, _i32, _vp, _vp, ctypes.c_size_t, _vp]),
     "salt_float_fc_scan_workspace_size": (_i32, [_i32, _i32, _vp]),

@@ -180,7 +180,7 @@ size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes) {
   return FusedSmem(P, wt_bytes).total;
 }
 
-template <typename WT, int LPU>
+template <typename WT, int LPU, bool SAT>
 __global__ void __launch_bounds__(kFusedThreads)
 conv_fused(ConvLaunch P) {
   constexpr int UPW = 32 / LPU;  // units (position x channel group) per warp
@@ -240,6 +240,7 @@ conv_fused(ConvLaunch P) {
   int32_t* chunk_spk_b = P.chunk_spikes + (int64_t)b * P.n_spk_chunks;
 
   int32_t acc_min = 0, acc_max = 0, acc_ovf = 0, acc_spk = 0;
+  const StepConsts sc(P.qc);
   const int ntasks_all = (NPM * P.G + UPW - 1) / UPW;
   __syncthreads();
 
@@ -345,6 +346,9 @@ conv_fused(ConvLaunch P) {
         tp = tprev_s[pl * P.G + g];
         cn = cnt_s[pl * P.G + g];
       }
+      // a layer without a threshold, and lanes past the channel count, never fire: their register
+      // stays inside total_bits < 31 bits, below INT32_MAX
+      vth = INT32_MAX;
       if (lane_ok && P.has_vth) vth = __ldg(&P.vth[(int64_t)oc * P.n_sp + oy * P.w_out + ox]);
       const int32_t nmax = __reduce_max_sync(0xffffffffu, n);
       int32_t spk_visit = 0;
@@ -357,14 +361,12 @@ conv_fused(ConvLaunch P) {
         if (glane == 0) tpv = tp;
         const bool kept = has && (cn + glane) < P.L;  // cn already counts earlier batches
         const int32_t dt = dt_from_times(r.t, tpv);
-        const int32_t a = decay_code(dt, lut, P.qc.lut_len);
+        const int32_t a = dt == 0 ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
         const int32_t ky = (int32_t)(r.yx >> 16) - oys;
         const int32_t kx = (int32_t)(r.yx & 0xffffu) - oxs;
-        const int32_t tap = r.ckk + ky * P.k + kx;
-        // lanes without a kept event pack 0: their placeholder record may give a negative tap
-        const uint32_t T = kept ? (((uint32_t)tap & 0x3fffffffu) | ((uint32_t)(dt == 0) << 30) |
-                                   0x80000000u)
-                                : 0u;
+        // weight row offset of the event's tap; -1 marks lanes without a kept event (their
+        // placeholder record may give a negative tap)
+        const int32_t T = kept ? (r.ckk + ky * P.k + kx) * OCP : -1;
         const int sy = oy - ((int32_t)(r.omin >> 16) - 32768);
         const int sx = ox - ((int32_t)(r.omin & 0xffffu) - 32768);
         const int widx = e * SWW + (sy * P.ncand + sx) * P.G + g;
@@ -375,18 +377,17 @@ conv_fused(ConvLaunch P) {
         uint32_t mybits = 0;
         for (int32_t st = 0; st < nbw; ++st) {
           const int32_t as = __shfl_sync(0xffffffffu, a, st, LPU);
-          const uint32_t Ts = __shfl_sync(0xffffffffu, T, st, LPU);
+          const int32_t Ts = __shfl_sync(0xffffffffu, T, st, LPU);
           bool spike = false;
-          if ((Ts >> 31) && lane_ok) {
-            const int32_t qv = (int32_t)w_s[(int32_t)(Ts & 0x3fffffffu) * OCP + oc];
+          if (Ts >= 0 && lane_ok) {
+            const int32_t qv = (int32_t)w_s[Ts + oc];
             int32_t u;
-            bool ovf;
-            const int32_t w = quant_step(V, as, (Ts >> 30) & 1u, qv, P.qc, u, ovf);
-            spike = P.has_vth && w >= vth;
+            const int32_t w = sc.step<SAT>(V, as, qv, u);
+            spike = w >= vth;
             V = spike ? 0 : w;
+            // overflow is read off the unfitted range at the end of the layer (layer_finish)
             acc_min = min(acc_min, u);
             acc_max = max(acc_max, u);
-            acc_ovf |= (int32_t)ovf;
           }
           const uint32_t bits = (__ballot_sync(0xffffffffu, spike) >> (gi * LPU)) & gmask_bits;
           if (glane == st) mybits = bits;
@@ -528,55 +529,57 @@ conv_fused(ConvLaunch P) {
 
 // ------------------------------------------------------------------ compaction
 
-// Emits the spikes of events [c*CHC, (c+1)*CHC) of sample b, in (event, neuron) order.
+// Emits sample b's spikes in (event, neuron) order; block x walks the sample's 256-event chunks
+// x, x + gridDim.x, ... (each chunk's output offset comes from the scanned per-chunk counts).
 __global__ void __launch_bounds__(kCompactThreads)
 conv_compact(ConvLaunch P, salt_stream_out out) {
   __shared__ int32_t s_scan[kScanSmem];
-  const int b = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
+  const int b = blockIdx.y, tid = threadIdx.x;
   const int32_t S = P.s_total[b];
   if (S > P.M) return;  // truncated samples go through conv_truncated
   const int32_t n_eff = P.n_eff(b);
-  const int32_t j = c * kSpkChunk + tid;
-  const bool ok = j < n_eff;
   const int SWW = P.nslots * P.G;
-  const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
-  int32_t cnt = 0;
-  EvCand k{0, 1, 0, 0, 1, 0};
-  if (ok) {
-    int32_t cc, y, x;
-    k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
-    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
-      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
-        const int slot = (oy - k.oy_min) * P.ncand + (ox - k.ox_min);
-        for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[slot * P.G + g]);
-      }
-  }
-  int32_t total;
-  const int32_t off = block_exclusive_scan(cnt, s_scan, total);
-  if (cnt == 0) return;
-  const int32_t base = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
-  const float t = P.in.time(b, j, n_eff);
   float* ot = out.times + (int64_t)b * P.M;
   int32_t* os = out.src + (int64_t)b * P.M;
-  int32_t kk = 0;
-  for (int g = 0; g < P.G; ++g) {
-    uint32_t uni = 0;
-    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
-      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
-        uni |= sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
-    while (uni) {
-      const int bit = __ffs(uni) - 1;
-      uni &= uni - 1u;
-      const int oc = g * P.lpu + bit;
+  for (int32_t c = blockIdx.x; c * kSpkChunk < n_eff; c += gridDim.x) {
+    const int32_t j = c * kSpkChunk + tid;
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
+    int32_t cnt = 0;
+    EvCand k{0, 1, 0, 0, 1, 0};
+    if (j < n_eff) {
+      int32_t cc, y, x;
+      k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
       for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
         for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
-          const uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
-          if (wd & (1u << bit)) {
-            ot[base + kk] = t;
-            os[base + kk] = oc * P.n_sp + oy * P.w_out + ox;
-            ++kk;
-          }
+          const int slot = (oy - k.oy_min) * P.ncand + (ox - k.ox_min);
+          for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[slot * P.G + g]);
         }
+    }
+    int32_t total;
+    const int32_t off = block_exclusive_scan(cnt, s_scan, total);
+    if (cnt == 0) continue;
+    const int32_t base = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
+    const float t = P.in.time(b, j, n_eff);
+    int32_t kk = 0;
+    for (int g = 0; g < P.G; ++g) {
+      uint32_t uni = 0;
+      for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+        for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
+          uni |= sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
+      while (uni) {
+        const int bit = __ffs(uni) - 1;
+        uni &= uni - 1u;
+        const int oc = g * P.lpu + bit;
+        for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+          for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
+            const uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
+            if (wd & (1u << bit)) {
+              ot[base + kk] = t;
+              os[base + kk] = oc * P.n_sp + oy * P.w_out + ox;
+              ++kk;
+            }
+          }
+      }
     }
   }
 }
@@ -773,23 +776,29 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   }
 }
 
-// Host-side dispatch over the (weight width, lanes per channel group) instantiations.
-template <typename WT>
+// Host-side dispatch over the (weight width, lanes per channel group, overflow mode)
+// instantiations.
+template <typename WT, bool SAT>
 static void* fused_for_lpu(int lpu) {
   switch (lpu) {
-    case 1: return (void*)conv_fused<WT, 1>;
-    case 2: return (void*)conv_fused<WT, 2>;
-    case 4: return (void*)conv_fused<WT, 4>;
-    case 8: return (void*)conv_fused<WT, 8>;
-    case 16: return (void*)conv_fused<WT, 16>;
-    default: return (void*)conv_fused<WT, 32>;
+    case 1: return (void*)conv_fused<WT, 1, SAT>;
+    case 2: return (void*)conv_fused<WT, 2, SAT>;
+    case 4: return (void*)conv_fused<WT, 4, SAT>;
+    case 8: return (void*)conv_fused<WT, 8, SAT>;
+    case 16: return (void*)conv_fused<WT, 16, SAT>;
+    default: return (void*)conv_fused<WT, 32, SAT>;
   }
 }
 
-void* conv_fused_kernel(int wt_bytes, int lpu) {
-  if (wt_bytes == 1) return fused_for_lpu<int8_t>(lpu);
-  if (wt_bytes == 2) return fused_for_lpu<int16_t>(lpu);
-  return fused_for_lpu<int32_t>(lpu);
+void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate) {
+  if (saturate) {
+    if (wt_bytes == 1) return fused_for_lpu<int8_t, true>(lpu);
+    if (wt_bytes == 2) return fused_for_lpu<int16_t, true>(lpu);
+    return fused_for_lpu<int32_t, true>(lpu);
+  }
+  if (wt_bytes == 1) return fused_for_lpu<int8_t, false>(lpu);
+  if (wt_bytes == 2) return fused_for_lpu<int16_t, false>(lpu);
+  return fused_for_lpu<int32_t, false>(lpu);
 }
 
 }  // namespace salt

@@ -15,7 +15,7 @@
 
 namespace salt {
 
-template <bool FIRES>
+template <bool FIRES, bool SAT>
 __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   __shared__ int32_t lut_s[kLutSmemMax];
   const bool lut_smem = P.qc.lut_len <= kLutSmemMax;
@@ -32,13 +32,17 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   const int32_t n_in = P.in_nreal[b];
   const int32_t n_eff = P.n_eff(b);
   const int32_t nproc = P.tail_mode ? P.in.capacity : n_eff;
-  const int32_t vth = (P.has_vth && active) ? P.vth[o] : 0;
+  // lanes past n_out never fire (their register stays 0); registers stay below INT32_MAX
+  const int32_t vth = (FIRES && active) ? P.vth[o] : INT32_MAX;
+  const StepConsts sc(P.qc);
   uint32_t* sw_b = FIRES ? P.sw + (int64_t)b * P.sw_stride : nullptr;
   int32_t* chunk_b = FIRES ? P.chunk_spikes + (int64_t)b * P.n_spk_chunks : nullptr;
 
-  int32_t V = 0, vmin = 0, vmax = 0, ovf_any = 0, nspk = 0;
+  int32_t V = 0, vmin = 0, vmax = 0, nspk = 0;
   float tprev = 0.0f;
   for (int32_t base = 0; base < nproc; base += 32) {
+    // Lane-parallel preparation of 32 events: time, source, Δt against the previous entry
+    // (connectivity/fc.py:26-29: the first against t=0, pads masked to 0) and decay code.
     const int32_t jl = base + lane;
     float t_l = 0.0f;
     int32_t s_l = 0;
@@ -46,7 +50,13 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
       t_l = P.in.time(b, jl, n_eff);
       s_l = P.in.source(b, jl, n_eff);
     }
+    float t_prev_l = __shfl_up_sync(0xffffffffu, t_l, 1);
+    if (lane == 0) t_prev_l = tprev;
+    const bool real_l = jl < n_in;
+    const int32_t dt_l = real_l ? dt_from_times(t_l, t_prev_l) : 0;
+    const int32_t a_l = dt_l == 0 ? sc.ident_a : decay_code(dt_l, lut, P.qc.lut_len);
     const int cnt = min(32, nproc - base);
+    tprev = __shfl_sync(0xffffffffu, t_l, cnt - 1);
     int32_t qv[32];
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
@@ -57,26 +67,20 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
 #pragma unroll
     for (int e = 0; e < 32; ++e) {
       if (e < cnt) {
-        const int32_t j = base + e;
-        const float t = __shfl_sync(0xffffffffu, t_l, e);
-        const bool real = j < n_in;
-        const int32_t dt = real ? dt_from_times(t, tprev) : 0;
-        tprev = t;
-        const int32_t a = decay_code(dt, lut, P.qc.lut_len);
+        const int32_t a = __shfl_sync(0xffffffffu, a_l, e);
         int32_t u;
-        bool ovf;
-        const int32_t w = quant_step(V, a, dt == 0, qv[e], P.qc, u, ovf);
-        const bool spike = FIRES && active && w >= vth;
+        const int32_t w = sc.step<SAT>(V, a, qv[e], u);
+        const bool spike = FIRES && w >= vth;
         V = spike ? 0 : w;
-        if (active) {
-          vmin = min(vmin, u);
-          vmax = max(vmax, u);
-          ovf_any |= (int32_t)ovf;
-        }
+        // inactive lanes see q = 0 from V = 0, so u = 0 leaves the range untouched; overflow
+        // is read off the unfitted range at the end of the layer (layer_finish)
+        vmin = min(vmin, u);
+        vmax = max(vmax, u);
         nspk += spike;
         if (FIRES) {
           const uint32_t bal = __ballot_sync(0xffffffffu, spike);
           if (lane == 0) {
+            const int32_t j = base + e;
             sw_b[(int64_t)j * P.G + g] = bal;
             if (bal) atomicAdd(&chunk_b[j >> kSpkChunkShift], __popc(bal));
           }
@@ -88,42 +92,44 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   if (FIRES && active) P.n_spk[(int64_t)b * P.n_out + o] = nspk;
   vmin = warp_min(vmin);
   vmax = warp_max(vmax);
-  ovf_any = warp_or(ovf_any);
   const int32_t tot = warp_sum(nspk);
   if (lane == 0) {
     atomicMin(&P.vmin[b], vmin);
     atomicMax(&P.vmax[b], vmax);
-    if (ovf_any) atomicOr(&P.ovf[b], 1);
     if (tot) atomicAdd(&P.s_total[b], tot);
   }
 }
 
 
+// Emits sample b's spikes in (event, neuron) order; block x walks the sample's 256-event
+// chunks x, x + gridDim.x, ... (chunk offsets come from the scanned per-chunk counts).
 __global__ void __launch_bounds__(kCompactThreads)
 fc_compact(FCLaunch P, salt_stream_out out) {
   __shared__ int32_t s_scan[kScanSmem];
-  const int b = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
+  const int b = blockIdx.y, tid = threadIdx.x;
   if (P.s_total[b] > P.M) return;
   const int32_t n_eff = P.n_eff(b);
   const int32_t nproc = P.tail_mode ? P.in.capacity : n_eff;
-  const int32_t j = c * kSpkChunk + tid;
-  const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.G;
-  int32_t cnt = 0;
-  if (j < nproc)
-    for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[g]);
-  int32_t total;
-  const int32_t off = block_exclusive_scan(cnt, s_scan, total);
-  if (cnt == 0) return;
-  int32_t k = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
-  const float t = P.in.time(b, j, n_eff);
-  for (int g = 0; g < P.G; ++g) {
-    uint32_t wd = sw_j[g];
-    while (wd) {
-      const int bit = __ffs(wd) - 1;
-      wd &= wd - 1u;
-      out.times[(int64_t)b * P.M + k] = t;
-      out.src[(int64_t)b * P.M + k] = g * 32 + bit;
-      ++k;
+  for (int32_t c = blockIdx.x; c * kSpkChunk < nproc; c += gridDim.x) {
+    const int32_t j = c * kSpkChunk + tid;
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * P.G;
+    int32_t cnt = 0;
+    if (j < nproc)
+      for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[g]);
+    int32_t total;
+    const int32_t off = block_exclusive_scan(cnt, s_scan, total);
+    if (cnt == 0) continue;
+    int32_t k = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
+    const float t = P.in.time(b, j, n_eff);
+    for (int g = 0; g < P.G; ++g) {
+      uint32_t wd = sw_j[g];
+      while (wd) {
+        const int bit = __ffs(wd) - 1;
+        wd &= wd - 1u;
+        out.times[(int64_t)b * P.M + k] = t;
+        out.src[(int64_t)b * P.M + k] = g * 32 + bit;
+        ++k;
+      }
     }
   }
 }
@@ -206,8 +212,9 @@ fc_truncated(FCLaunch P, salt_stream_out out) {
   }
 }
 
-void* fc_scan_kernel(bool fires) {
-  return fires ? (void*)fc_scan<true> : (void*)fc_scan<false>;
+void* fc_scan_kernel(bool fires, bool saturate) {
+  if (saturate) return fires ? (void*)fc_scan<true, true> : (void*)fc_scan<false, true>;
+  return fires ? (void*)fc_scan<true, false> : (void*)fc_scan<false, false>;
 }
 
 }  // namespace salt

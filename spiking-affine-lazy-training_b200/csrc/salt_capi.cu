@@ -76,6 +76,7 @@ __global__ void spike_chunk_scan(int32_t* __restrict__ chunk, int32_t n_chunks, 
 struct FinishArgs {
   const int32_t *s_total, *needed, *vmin, *vmax, *ovf;
   int32_t L, M, max_extra, is_conv, batch;
+  int32_t half;  // 2^(i_V + f_V - 1): the register range is [-half, half)
 };
 
 // Per-sample diagnostics and Capacity.fits (salt_core/capacity.py:60-63; layers/conv.py:222-226,
@@ -88,7 +89,10 @@ __global__ void layer_finish(FinishArgs A, int32_t* out_nreal, salt_layer_stats 
   if (out_nreal) out_nreal[b] = S;
   if (st.spike_count) st.spike_count[b] = S;
   if (st.needed_queue) st.needed_queue[b] = nq;
-  if (st.overflowed) st.overflowed[b] = A.ovf[b] != 0;
+  // the hot scans track only the unfitted range; an update overflowed iff it left the register
+  // range, so the sample overflowed iff its unfitted range did
+  if (st.overflowed)
+    st.overflowed[b] = A.ovf[b] != 0 || A.vmin[b] < -A.half || A.vmax[b] >= A.half;
   if (st.vmin) st.vmin[b] = A.vmin[b];
   if (st.vmax) st.vmax[b] = A.vmax[b];
   if (st.fits)
@@ -361,7 +365,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
         L, s.counts, s.lists);
     SALT_LAUNCHED("conv_tile_scatter");
   }
-  void* fn = conv_fused_kernel(p.wt_bytes, p.lpu);
+  void* fn = conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE);
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
   void* args[] = {&L};
   if (timer) SALT_CUDA(cudaEventRecord(timer->start, st));
@@ -370,7 +374,8 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   if (timer) SALT_CUDA(cudaEventRecord(timer->stop, st));
   spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
   SALT_LAUNCHED("spike_chunk_scan");
-  conv_compact<<<dim3(p.n_spk_chunks, B), kCompactThreads, 0, st>>>(L, *out);
+  conv_compact<<<dim3(std::min(p.n_spk_chunks, kCompactBlocksPerSample), B), kCompactThreads, 0,
+                 st>>>(L, *out);
   SALT_LAUNCHED("conv_compact");
   if (p.tail_mode) {
     conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
@@ -379,7 +384,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   conv_truncated<<<B, kCompactThreads, 0, st>>>(L, *out, s.hist);
   SALT_LAUNCHED("conv_truncated");
   FinishArgs fa{s.s_total, s.needed, s.vmin, s.vmax, s.ovf, d->max_queue_len, d->max_out_spikes,
-                d->max_extra_steps, 1, B};
+                d->max_extra_steps, 1, B, 1 << (q->i_V + q->f_V - 1)};
   salt_layer_stats none{};
   layer_finish<<<(B + 255) / 256, 256, 0, st>>>(fa, out->n_real, stats ? *stats : none);
   SALT_LAUNCHED("layer_finish");
@@ -465,19 +470,20 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   const int wpb = kFcThreads / 32;
   const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
   void* scan_args[] = {&L};
-  SALT_CUDA(cudaLaunchKernel(fc_scan_kernel(q->has_vth != 0), dim3(grid), dim3(kFcThreads),
+  SALT_CUDA(cudaLaunchKernel(fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE), dim3(grid), dim3(kFcThreads),
                              scan_args, 0, st));
   SALT_LAUNCHED("fc_scan");
   if (q->has_vth) {
     spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
     SALT_LAUNCHED("spike_chunk_scan");
-    fc_compact<<<dim3(L.n_spk_chunks, B), kCompactThreads, 0, st>>>(L, *out);
+    fc_compact<<<dim3(std::min(L.n_spk_chunks, kCompactBlocksPerSample), B), kCompactThreads, 0,
+                 st>>>(L, *out);
     SALT_LAUNCHED("fc_compact");
     fc_truncated<<<B, kCompactThreads, 0, st>>>(L, *out);
     SALT_LAUNCHED("fc_truncated");
   }
   FinishArgs fa{s.s_total, nullptr, s.vmin, s.vmax, s.ovf, 0, d->max_out_spikes,
-                d->max_extra_steps, 0, B};
+                d->max_extra_steps, 0, B, 1 << (q->i_V + q->f_V - 1)};
   salt_layer_stats none{};
   layer_finish<<<(B + 255) / 256, 256, 0, st>>>(fa, out->n_real, stats ? *stats : none);
   SALT_LAUNCHED("layer_finish");
@@ -498,6 +504,7 @@ struct LayerRec {
 
 struct TimedLaunch {
   int32_t layer;
+  int32_t whole_layer;  // 1: events bracket the whole layer, 0: the fused kernel
   KernelTimer ev;
 };
 
@@ -767,16 +774,25 @@ salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_st
                         vmin ? vmin + (size_t)l * B : sb + 3 * B,
                         vmax ? vmax + (size_t)l * B : sb + 4 * B,
                         sb + 5 * B};
-    KernelTimer timer;
-    if (net->profiling && r.spec.kind == 0) {
+    KernelTimer timer, whole;
+    auto take = [&](KernelTimer& t) -> salt_status {
       if (net->pool.empty()) {
-        SALT_CUDA(cudaEventCreate(&timer.start));
-        SALT_CUDA(cudaEventCreate(&timer.stop));
+        SALT_CUDA(cudaEventCreate(&t.start));
+        SALT_CUDA(cudaEventCreate(&t.stop));
       } else {
-        timer = net->pool.back();
+        t = net->pool.back();
         net->pool.pop_back();
       }
-      net->timed.push_back({l, timer});
+      return SALT_OK;
+    };
+    if (net->profiling) {
+      if ((rc = take(whole))) return rc;
+      net->timed.push_back({l, 1, whole});
+      SALT_CUDA(cudaEventRecord(whole.start, st));
+      if (r.spec.kind == 0) {
+        if ((rc = take(timer))) return rc;
+        net->timed.push_back({l, 0, timer});
+      }
     }
     if (r.spec.kind == 0)
       rc = conv_forward_impl(&r.spec.conv, &r.spec.quant, r.d_q, r.d_lut, r.d_vth, B, &cur, &so,
@@ -786,6 +802,7 @@ salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_st
       rc = fc_forward_impl(&r.spec.fc, &r.spec.quant, r.d_q, true, r.d_lut, r.d_vth, B, &cur, &so,
                            vf, &ls, o.scratch, o.scratch_bytes, st);
     if (rc) return rc;
+    if (whole.stop) SALT_CUDA(cudaEventRecord(whole.stop, st));
     cur.times = so.times;
     cur.src = so.src;
     cur.n_real = so.n_real;
@@ -810,20 +827,26 @@ salt_status salt_network_set_profiling(salt_network* net, int32_t enable) {
   return SALT_OK;
 }
 
-salt_status salt_network_profile_read(salt_network* net, float* fused_ms, int32_t* launches,
-                                      int32_t reset) {
-  if (!net || !fused_ms || !launches) return fail(SALT_BAD_ARG, "profile_read: NULL argument");
+salt_status salt_network_profile_read(salt_network* net, float* fused_ms, float* layer_ms,
+                                      int32_t* launches, int32_t reset) {
+  if (!net || !fused_ms || !layer_ms || !launches)
+    return fail(SALT_BAD_ARG, "profile_read: NULL argument");
   const size_t nl = net->layers.size();
   for (size_t l = 0; l < nl; ++l) {
     fused_ms[l] = 0.0f;
+    layer_ms[l] = 0.0f;
     launches[l] = 0;
   }
   for (auto& t : net->timed) {
     SALT_CUDA(cudaEventSynchronize(t.ev.stop));
     float ms = 0.0f;
     SALT_CUDA(cudaEventElapsedTime(&ms, t.ev.start, t.ev.stop));
-    fused_ms[t.layer] += ms;
-    launches[t.layer] += 1;
+    if (t.whole_layer) {
+      layer_ms[t.layer] += ms;
+      launches[t.layer] += 1;
+    } else {
+      fused_ms[t.layer] += ms;
+    }
   }
   if (reset) {
     for (auto& t : net->timed) net->pool.push_back(t.ev);

@@ -66,6 +66,35 @@ __device__ __forceinline__ int32_t quant_step(int32_t v, int32_t a, bool is_iden
   return w;
 }
 
+// The same update for the hot loops, with the identity step folded into the decay code: a
+// step with Δt = 0 uses a = 2^f_a, for which the split multiply returns v exactly (hi * 2^f_a
+// + lo, the rounding term is (2^f_a * lo + half) >> f_a = lo) for every register value of at
+// most 30 bits; a decay code equal to 2^f_a likewise leaves v unchanged.  The overflow mode is a
+// compile-time choice; ovf is "the fitted value differs from the unfitted one".
+template <bool SAT>
+__device__ __forceinline__ int32_t quant_step_a(int32_t v, int32_t a, int32_t q_shifted,
+                                                int32_t f_a, int32_t lo_mask, int32_t round_half,
+                                                int32_t half, int32_t wrap_shift, int32_t& u) {
+  const int32_t dec = wadd(wmul(a, v >> f_a), wadd(wmul(a, v & lo_mask), round_half) >> f_a);
+  u = wadd(dec, q_shifted);
+  if (SAT) return min(max(u, -half), half - 1);
+  return (int32_t)((uint32_t)u << wrap_shift) >> wrap_shift;
+}
+
+// Loop-invariant constants of quant_step_a.
+struct StepConsts {
+  int32_t f_a, f_V, lo_mask, round_half, half, wrap_shift, ident_a;
+  __device__ __forceinline__ explicit StepConsts(const QuantCfg& c)
+      : f_a(c.f_a), f_V(c.f_V), lo_mask((int32_t)((1u << c.f_a) - 1u)), round_half(c.round_half),
+        half((int32_t)(1u << (c.total_bits - 1))), wrap_shift(32 - c.total_bits),
+        ident_a((int32_t)(1u << c.f_a)) {}
+  template <bool SAT>
+  __device__ __forceinline__ int32_t step(int32_t v, int32_t a, int32_t q, int32_t& u) const {
+    return quant_step_a<SAT>(v, a, wmul(q, (int32_t)(1u << f_V)), f_a, lo_mask, round_half, half,
+                             wrap_shift, u);
+  }
+};
+
 // apply_decay_table_int (salt_core/quant/codes.py:87-105) on an integer Δt.
 __device__ __forceinline__ int32_t decay_code(int32_t dt, const int32_t* lut, int32_t lut_len) {
   if (lut_len <= 0) return 0;

@@ -13,6 +13,7 @@ constexpr int kSpkChunkShift = 8;
 constexpr int kSpkChunk = 1 << kSpkChunkShift;
 static_assert(kSpkChunk == kCompactThreads, "one compaction block per spike chunk");
 constexpr int kLutSmemMax = 4096;    // decay tables longer than this are read from global
+constexpr int kCompactBlocksPerSample = 8;  // compaction blocks per sample (grid-stride)
 constexpr int kScanSmem = 33;        // ints of shared memory block_exclusive_scan needs
 
 __host__ __device__ __forceinline__ size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -178,10 +179,10 @@ __global__ void conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* scrat
 __global__ void fc_compact(FCLaunch P, salt_stream_out out);
 __global__ void fc_truncated(FCLaunch P, salt_stream_out out);
 // Kernel entry points of the templated kernels, for cudaLaunchKernel.
-void* conv_fused_kernel(int wt_bytes, int lpu);
+void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate);
 // Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
-void* fc_scan_kernel(bool fires);
+void* fc_scan_kernel(bool fires, bool saturate);
 constexpr int kFcThreads = 128;
 
 }  // namespace salt

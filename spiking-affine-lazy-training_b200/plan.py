@@ -72,14 +72,15 @@ class NetworkPlan:
         _lib.check(_lib.lib().salt_network_set_profiling(self._net, int(bool(enable))))
 
     def profile_read(self, reset: bool = True):
-        """(fused-kernel milliseconds summed per layer, timed launches per layer)."""
+        """(fused-kernel ms summed per layer, whole-layer ms summed per layer, timed forwards)."""
         nl = len(self.layers)
-        ms = np.zeros(nl, np.float32)
+        fused = np.zeros(nl, np.float32)
+        whole = np.zeros(nl, np.float32)
         n = np.zeros(nl, np.int32)
         _lib.check(_lib.lib().salt_network_profile_read(
-            self._net, ms.ctypes.data_as(ctypes.c_void_p), n.ctypes.data_as(ctypes.c_void_p),
-            int(bool(reset))))
-        return ms, n
+            self._net, fused.ctypes.data_as(ctypes.c_void_p), whole.ctypes.data_as(ctypes.c_void_p),
+            n.ctypes.data_as(ctypes.c_void_p), int(bool(reset))))
+        return fused, whole, n
 
     def last_launch_count(self) -> int:
         return int(_lib.lib().salt_network_last_launch_count(self._net))

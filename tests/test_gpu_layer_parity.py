@@ -106,6 +106,19 @@ def test_conv_narrow_register_modes(overflow, round_mode):
     assert np.any(out.result.overflowed)
 
 
+@pytest.mark.parametrize("overflow,round_mode,fires", [
+    ("saturate", "round", True), ("wrap", "truncate", True), ("saturate", "truncate", False),
+    ("wrap", "round", False)])
+def test_fc_narrow_register_modes(overflow, round_mode, fires):
+    rng = np.random.default_rng(41)
+    layer = S.FCLayer(name="f", n_in=96, n_out=40, init_k=1.0, tau=20.0, max_out_spikes=500)
+    params = make_params(layer, rng, vth=(100, 250), f_a=8, f_V=2, i_V=8, overflow=overflow,
+                         fires=fires)
+    times, src, nr = make_events(rng, 4, 200, 96)
+    out = _check_layer(layer, params, times, src, nr, round_mode=round_mode)
+    assert np.any(out.result.overflowed)
+
+
 def test_conv_empty_and_overfull_inputs():
     rng = np.random.default_rng(50)
     layer = S.ConvLayer(name="c", ic=2, h_in=6, w_in=6, oc=4, k=3, s=2, p=0, init_k=1.0,
