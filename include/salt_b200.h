@@ -112,6 +112,32 @@ salt_status salt_conv_layer_forward(const salt_conv_desc *layer, const salt_quan
                                     int32_t *v_final, const salt_layer_stats *stats,
                                     void *workspace, size_t workspace_bytes, void *stream);
 
+/* Size of the library's fixed device scratch (64 MiB), the largest conv workspace that
+ * salt_conv_layer_forward_noalloc accepts. */
+#define SALT_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/* salt_conv_layer_forward without a caller workspace, for callers that cannot allocate device
+ * memory at call time (a plugin host that hands out no scratch buffers, a loop that must not
+ * call cudaMalloc).  No counterpart in the reference: there JAX owns every buffer.
+ *   - Same arguments, results and errors as salt_conv_layer_forward minus the workspace; the
+ *     layer's scratch lives in a fixed SALT_NOALLOC_SCRATCH_BYTES device array inside the
+ *     library, and the call allocates no device memory.
+ *   - A layer whose salt_conv_layer_workspace_size exceeds SALT_NOALLOC_SCRATCH_BYTES is
+ *     rejected with SALT_WORKSPACE_TOO_SMALL before anything is enqueued.
+ *   - Nothing has to start at zero: every call clears the counters it uses, on `stream`.
+ *   - The first call on a device does a one-time setup (it looks up the scratch's device
+ *     address, which loads the module holding it); make that first call before any stream
+ *     capture.
+ *   - All calls on one device share the one scratch: calls that may overlap in time (other
+ *     streams, other host threads) race and corrupt each other's results.  Order them on one
+ *     stream, or with events. */
+salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc *layer,
+                                            const salt_quant_desc *quant, const int32_t *q,
+                                            const int32_t *lut, const int32_t *vth, int32_t batch,
+                                            const salt_stream_in *in, salt_stream_out *out,
+                                            int32_t *v_final, const salt_layer_stats *stats,
+                                            void *stream);
+
 /* ---------------------------------------------------------------- fc layer
  * Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:385-402 calling
  * build_fc_structure connectivity/fc.py:20-33, fc_weight_codes :54-61, QuantBackend.scan,

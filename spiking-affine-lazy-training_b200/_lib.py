@@ -54,6 +54,8 @@ _SIGS = {
     "salt_conv_layer_workspace_size": (_i32, [_vp, _vp, _i32, _i32, _vp]),
     "salt_conv_layer_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
                                        ctypes.c_size_t, _vp]),
+    "salt_conv_layer_forward_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp,
+                                               _vp, _vp]),
     "salt_fc_layer_workspace_size": (_i32, [_vp, _vp, _i32, _i32, _vp]),
     "salt_fc_layer_forward": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
                                      ctypes.c_size_t, _vp]),

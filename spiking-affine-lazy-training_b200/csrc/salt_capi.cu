@@ -547,6 +547,27 @@ salt_status salt_conv_layer_forward(const salt_conv_desc* layer, const salt_quan
                            workspace_bytes, (cudaStream_t)stream);
 }
 
+salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc* layer,
+                                            const salt_quant_desc* quant, const int32_t* q,
+                                            const int32_t* lut, const int32_t* vth, int32_t batch,
+                                            const salt_stream_in* in, salt_stream_out* out,
+                                            int32_t* v_final, const salt_layer_stats* stats,
+                                            void* stream) {
+  size_t need = 0;
+  salt_status rc = salt_conv_layer_workspace_size(layer, quant, batch, in ? in->capacity : 0, &need);
+  if (rc) return rc;
+  if (need > SALT_NOALLOC_SCRATCH_BYTES)
+    return fail(SALT_WORKSPACE_TOO_SMALL,
+                "conv layer needs " + std::to_string(need) + " bytes of scratch; the fixed scratch "
+                "of salt_conv_layer_forward_noalloc holds " +
+                std::to_string(SALT_NOALLOC_SCRATCH_BYTES) +
+                " (use salt_conv_layer_forward with a workspace, or a smaller batch)");
+  void* ws = nullptr;
+  SALT_CUDA(fixed_scratch_address(&ws));
+  return conv_forward_impl(layer, quant, q, lut, vth, batch, in, out, v_final, stats, ws, need,
+                           (cudaStream_t)stream);
+}
+
 salt_status salt_fc_layer_workspace_size(const salt_fc_desc* layer, const salt_quant_desc* quant,
                                          int32_t batch, int32_t in_capacity, size_t* bytes) {
   salt_status rc = check_quant(quant);

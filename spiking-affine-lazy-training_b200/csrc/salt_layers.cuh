@@ -183,6 +183,9 @@ void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate);
 // Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 void* fc_scan_kernel(bool fires, bool saturate);
+
+// Device address of the fixed scratch behind salt_conv_layer_forward_noalloc (fixed_scratch.cu).
+cudaError_t fixed_scratch_address(void** ptr);
 constexpr int kFcThreads = 128;
 
 }  // namespace salt
