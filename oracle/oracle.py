@@ -411,3 +411,89 @@ def network_batch(layers, params, times, src, n_real, round_mode="round", thread
     if rc:
         raise ValueError(f"oracle batch failed rc={rc}")
     return vf, sc, fits.astype(bool)
+
+
+# ---------------------------------------------------------------- float chunked scan
+
+class _FloatGeom(ctypes.Structure):
+    _fields_ = [("n_in", ctypes.c_int32), ("n_out", ctypes.c_int32),
+                ("chunk_size", ctypes.c_int32), ("max_out_spikes", ctypes.c_int32),
+                ("max_extra_steps", ctypes.c_int32), ("v_th", ctypes.c_float)]
+
+
+class _FloatOut(ctypes.Structure):
+    _fields_ = [("v_final", _f32p), ("spike_mask", _u8p), ("spike_event_idx", _i32p),
+                ("out_times", _f32p), ("out_src", _i32p), ("out_gain", _f32p),
+                ("n_real_out", ctypes.c_int32), ("extra_steps_needed", ctypes.c_int32),
+                ("fits", ctypes.c_int32)]
+
+
+class FloatResult(NamedTuple):
+    """FCLayer.forward with FloatBackend (layers/fc.py:84-106): FloatLayerResult's forward
+    values (float/scan.py:10-16; s_spike and s_value equal spike_mask there), the output
+    EventStream (stream.py:16-21) and the layer's needs (LayerDiag.needed)."""
+    v_final: np.ndarray           # (n_out,) float32
+    spike_mask: np.ndarray | None  # (n_out, max_steps) bool
+    spike_event_idx: np.ndarray | None
+    event_times: np.ndarray       # (max_out_spikes,) float32
+    event_source_idx: np.ndarray  # (max_out_spikes,) int32
+    event_gain: np.ndarray        # (max_out_spikes,) float32
+    n_real_events: int            # spikes in the layer, not clipped to max_out_spikes
+    spike_count: int
+    extra_steps_needed: int
+    fits: bool
+
+
+def decay_base(tau) -> np.ndarray:
+    """float32(1 - 1/tau) per neuron: the base XLA raises to the Δt power (affine.py:27-31,
+    where a Python-float base meets a float32 exponent array)."""
+    return np.asarray(1.0 - 1.0 / np.asarray(tau, dtype=np.float64), dtype=np.float32)
+
+
+def float_fc_forward(layer, w, times, src, n_real, gain=None, tau=None, *, dense=True,
+                     threads=1) -> FloatResult:
+    """One float FC layer over one stream.  layer has the FCLayer fields n_in, n_out, tau,
+    v_th, chunk_size, max_out_spikes, max_extra_steps; w is (n_out, n_in) float32; tau, when
+    given, overrides layer.tau per neuron (n_out,).  dense=True also returns the
+    (n_out, max_steps) spike_mask / spike_event_idx arrays."""
+    n_out, n_in = int(layer.n_out), int(layer.n_in)
+    t = np.ascontiguousarray(np.asarray(times, dtype=np.float32))
+    s = np.ascontiguousarray(np.asarray(src), dtype=np.int32)
+    L = int(t.shape[0])
+    wf = np.ascontiguousarray(np.asarray(w, dtype=np.float32).reshape(n_out, n_in))
+    base = decay_base(np.broadcast_to(layer.tau if tau is None else tau, (n_out,)))
+    g = None if gain is None else np.ascontiguousarray(np.asarray(gain, dtype=np.float32))
+    C = int(layer.chunk_size)
+    steps = -(-L // C) + int(layer.max_extra_steps)
+    M = int(layer.max_out_spikes)
+    geom = _FloatGeom(n_in, n_out, C, M, int(layer.max_extra_steps), float(layer.v_th))
+    vf = np.empty(n_out, np.float32)
+    mask = np.empty((n_out, steps), np.uint8) if dense else None
+    eidx = np.empty((n_out, steps), np.int32) if dense else None
+    ot = np.empty(max(M, 1), np.float32)
+    os_ = np.empty(max(M, 1), np.int32)
+    og = np.empty(max(M, 1), np.float32)
+    out = _FloatOut(_p(vf, _f32p), _p(mask, _u8p) if dense else None,
+                    _p(eidx, _i32p) if dense else None, _p(ot, _f32p), _p(os_, _i32p),
+                    _p(og, _f32p), 0, 0, 0)
+    rc = lib().so_float_fc_forward(ctypes.byref(geom), _p(wf, _f32p), _p(base, _f32p),
+                                   _p(t, _f32p), _p(s, _i32p),
+                                   _p(g, _f32p) if g is not None else None, L, int(n_real),
+                                   int(threads), ctypes.byref(out))
+    if rc:
+        raise ValueError(f"oracle float layer failed rc={rc}")
+    return FloatResult(vf, mask.astype(bool) if dense else None, eidx, ot[:M], os_[:M], og[:M],
+                       int(out.n_real_out), int(out.n_real_out), int(out.extra_steps_needed),
+                       bool(out.fits))
+
+
+def affine_scan(a, b):
+    """lax.associative_scan(combine, AffineMap(a, b)) of float/affine.py:20-24, in float32."""
+    a = np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+    b = np.ascontiguousarray(np.asarray(b, dtype=np.float32))
+    oa, ob = np.empty_like(a), np.empty_like(b)
+    rc = lib().so_affine_scan(_p(a, _f32p), _p(b, _f32p), ctypes.c_int64(a.shape[0]),
+                              _p(oa, _f32p), _p(ob, _f32p))
+    if rc:
+        raise ValueError(f"oracle affine scan failed rc={rc}")
+    return oa, ob

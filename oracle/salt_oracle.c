@@ -604,3 +604,275 @@ int so_network_batch(const so_layer_spec *layers, int32_t n_layers, const float 
   free(th);
   return atomic_load(&c.err);
 }
+
+/* ================================================================ float chunked scan */
+
+/* float/affine.py:20-24 combine(left, right): the map `right` applied after `left`. */
+static inline void affine_combine(float la, float lb, float ra, float rb, float *oa, float *ob) {
+  *oa = ra * la;
+  *ob = ra * lb + rb;
+}
+
+/* lax.associative_scan's recursion (JAX, associative_scan._scan): combine neighbouring pairs,
+ * scan the n/2 pair maps recursively (these are the prefixes ending at odd indices), then
+ * combine each odd prefix with the following even-index map; element 0 is its own prefix.
+ * work holds at least 4n floats. */
+static void affine_scan_rec(const float *a, const float *b, int64_t n, float *oa, float *ob,
+                            float *work) {
+  if (n < 2) {
+    if (n == 1) {
+      oa[0] = a[0];
+      ob[0] = b[0];
+    }
+    return;
+  }
+  const int64_t m = n / 2;
+  float *ra = work, *rb = work + m, *sa = work + 2 * m, *sb = work + 3 * m, *next = work + 4 * m;
+  for (int64_t i = 0; i < m; ++i)
+    affine_combine(a[2 * i], b[2 * i], a[2 * i + 1], b[2 * i + 1], &ra[i], &rb[i]);
+  affine_scan_rec(ra, rb, m, sa, sb, next);
+  oa[0] = a[0];
+  ob[0] = b[0];
+  const int64_t n_even = (n % 2 == 0) ? m - 1 : m;
+  for (int64_t i = 0; i < n_even; ++i)
+    affine_combine(sa[i], sb[i], a[2 * i + 2], b[2 * i + 2], &oa[2 * i + 2], &ob[2 * i + 2]);
+  for (int64_t i = 0; i < m; ++i) {
+    oa[2 * i + 1] = sa[i];
+    ob[2 * i + 1] = sb[i];
+  }
+}
+
+int so_affine_scan(const float *a, const float *b, int64_t n, float *out_a, float *out_b) {
+  if (n < 0) return -1;
+  float *work = (float *)malloc(sizeof(float) * (size_t)(4 * n + 8));
+  if (!work) return -2;
+  affine_scan_rec(a, b, n, out_a, out_b, work);
+  free(work);
+  return 0;
+}
+
+typedef struct {
+  int32_t *step, *j; /* the neuron's spikes: scan step and global event index */
+  int32_t n, cap;
+  int32_t step0_idx; /* spike_event_idx[neuron, 0] */
+  uint8_t step0_spk; /* spike_mask[neuron, 0] */
+  int32_t extra;     /* extra_steps_upper_bound - base_scan_steps for this neuron */
+} fneuron_t;
+
+typedef struct {
+  const so_float_fc_geom *g;
+  const float *w, *decay_base, *times, *gain;
+  const int32_t *src;
+  int32_t L, n_real, max_steps;
+  so_float_out *out;
+  fneuron_t *nr;
+  atomic_int next, err;
+} float_ctx;
+
+static int push_spike(fneuron_t *r, int32_t step, int32_t j) {
+  if (r->n == r->cap) {
+    int32_t cap = r->cap ? 2 * r->cap : 64;
+    int32_t *s = (int32_t *)realloc(r->step, sizeof(int32_t) * (size_t)cap);
+    if (!s) return -2;
+    r->step = s;
+    int32_t *jj = (int32_t *)realloc(r->j, sizeof(int32_t) * (size_t)cap);
+    if (!jj) return -2;
+    r->j = jj;
+    r->cap = cap;
+  }
+  r->step[r->n] = step;
+  r->j[r->n] = j;
+  ++r->n;
+  return 0;
+}
+
+/* One neuron: fc_float_values (connectivity/fc.py:36-51) + float/scan.py:100-131 step loop +
+ * affine.py:57-88 bound. */
+static int float_neuron(float_ctx *c, int32_t i, float *a_pad, float *b_pad, float *ca, float *cb,
+                        float *A, float *B, float *work) {
+  const so_float_fc_geom *g = c->g;
+  const int32_t L = c->L, C = g->chunk_size, Lp = L + C;
+  const float base = c->decay_base[i], v_th = g->v_th;
+  fneuron_t *r = &c->nr[i];
+  /* build_fc_structure (fc.py:20-33): gap to the previous entry (the first against t=0), 0 on
+   * pads; create_affine_maps (affine.py:27-31); mask_pad_events (affine.py:42-54);
+   * _pad_queue (scan.py:19-25) appends chunk_size identity maps. */
+  int32_t m_pos = 0;
+  float sum_pos = 0.0f;
+  for (int32_t j = 0; j < Lp; ++j) {
+    float a = 1.0f, b = 0.0f;
+    if (j < L && j < c->n_real) {
+      const float prev = j == 0 ? 0.0f : c->times[j - 1];
+      const float dt = c->times[j] - prev;
+      a = powf(base, dt);
+      b = c->w[(int64_t)i * g->n_in + jidx(c->src[j], g->n_in)];
+      if (c->gain) b = b * c->gain[j];
+    }
+    a_pad[j] = a;
+    b_pad[j] = b;
+    if (j < L) { /* spike_step_upper_bound sums over the (n, L) maps, pads included as b = 0 */
+      m_pos += b > 0.0f;
+      sum_pos += b > 0.0f ? b : 0.0f;
+    }
+  }
+  const float m_star = fminf((float)m_pos, floorf(sum_pos / v_th));
+  const float steps_f = m_star + ceilf(((float)L - m_star) / (float)C);
+  r->extra = f32_to_i32(steps_f) - (L + C - 1) / C;
+
+  float v = 0.0f;
+  int64_t ptr = 0;
+  uint8_t *mask = c->out->spike_mask ? c->out->spike_mask + (int64_t)i * c->max_steps : NULL;
+  int32_t *eidx = c->out->spike_event_idx ? c->out->spike_event_idx + (int64_t)i * c->max_steps
+                                          : NULL;
+  for (int32_t step = 0; step < c->max_steps; ++step) {
+    for (int32_t k = 0; k < C; ++k) { /* take_chunk: jnp.take(..., mode='clip') */
+      int64_t idx = ptr + k;
+      if (idx > Lp - 1) idx = Lp - 1;
+      ca[k] = a_pad[idx];
+      cb[k] = b_pad[idx];
+    }
+    affine_scan_rec(ca, cb, C, A, B, work);
+    int32_t sidx = C; /* process_chunk (affine.py:99-126) */
+    float v_spk = 0.0f;
+    for (int32_t k = 0; k < C; ++k) {
+      const float vs = A[k] * v + B[k];
+      if (vs - v_th >= 0.0f) {
+        sidx = k;
+        v_spk = vs;
+        break;
+      }
+    }
+    const int spiked = sidx < C;
+    v = spiked ? (1.0f - 1.0f) * v_spk : A[C - 1] * v + B[C - 1];
+    const int32_t ev = (int32_t)(ptr + sidx);
+    if (mask) mask[step] = (uint8_t)spiked;
+    if (eidx) eidx[step] = ev;
+    if (step == 0) {
+      r->step0_idx = ev;
+      r->step0_spk = (uint8_t)spiked;
+    }
+    if (spiked && push_spike(r, step, ev)) return -2;
+    ptr += spiked ? sidx + 1 : C;
+  }
+  c->out->v_final[i] = v;
+  return 0;
+}
+
+static void *float_worker(void *arg) {
+  float_ctx *c = (float_ctx *)arg;
+  const int32_t C = c->g->chunk_size, Lp = c->L + C;
+  float *a_pad = (float *)malloc(sizeof(float) * (size_t)Lp);
+  float *b_pad = (float *)malloc(sizeof(float) * (size_t)Lp);
+  float *buf = (float *)malloc(sizeof(float) * (size_t)(8 * C + 8));
+  if (!a_pad || !b_pad || !buf) {
+    atomic_store(&c->err, -2);
+  } else {
+    for (;;) {
+      const int i = atomic_fetch_add(&c->next, 1);
+      if (i >= c->g->n_out) break;
+      if (float_neuron(c, i, a_pad, b_pad, buf, buf + C, buf + 2 * C, buf + 3 * C, buf + 4 * C))
+        atomic_store(&c->err, -2);
+    }
+  }
+  free(a_pad);
+  free(b_pad);
+  free(buf);
+  return NULL;
+}
+
+typedef struct {
+  int64_t key, pos;
+} fkey_t;
+
+static int fkey_cmp(const void *x, const void *y) {
+  const fkey_t *a = (const fkey_t *)x, *b = (const fkey_t *)y;
+  if (a->key != b->key) return a->key < b->key ? -1 : 1;
+  return a->pos < b->pos ? -1 : (a->pos > b->pos);
+}
+
+int so_float_fc_forward(const so_float_fc_geom *g, const float *w, const float *decay_base,
+                        const float *times, const int32_t *src, const float *gain, int32_t L,
+                        int32_t n_real, int32_t threads, so_float_out *out) {
+  if (!g || g->n_out < 1 || g->n_in < 1 || g->chunk_size < 1 || L < 1 || g->max_out_spikes < 0 ||
+      g->max_extra_steps < 0)
+    return -1;
+  if ((int64_t)L + g->chunk_size > (1 << 30)) return -1;
+  float_ctx c;
+  memset(&c, 0, sizeof(c));
+  c.g = g;
+  c.w = w;
+  c.decay_base = decay_base;
+  c.times = times;
+  c.gain = gain;
+  c.src = src;
+  c.L = L;
+  c.n_real = n_real;
+  c.max_steps = (L + g->chunk_size - 1) / g->chunk_size + g->max_extra_steps;
+  c.out = out;
+  c.nr = (fneuron_t *)calloc((size_t)g->n_out, sizeof(fneuron_t));
+  if (!c.nr) return -2;
+  atomic_init(&c.next, 0);
+  atomic_init(&c.err, 0);
+  if (threads < 1) threads = 1;
+  if (threads > 256) threads = 256;
+  pthread_t tid[256];
+  int started = 0;
+  for (int t = 1; t < threads; ++t)
+    if (pthread_create(&tid[started], NULL, float_worker, &c) == 0) ++started;
+  float_worker(&c);
+  for (int t = 0; t < started; ++t) pthread_join(tid[t], NULL);
+  int rc = atomic_load(&c.err);
+
+  /* layers/fc.py:96-100, stream.py:49-64 _select_spikes + :24-46 _pack_stream */
+  int64_t total = 0;
+  int32_t extra = (int32_t)0x80000000u;
+  for (int32_t i = 0; i < g->n_out; ++i) {
+    total += c.nr[i].n;
+    if (c.nr[i].extra > extra) extra = c.nr[i].extra;
+  }
+  const int32_t M = g->max_out_spikes;
+  fkey_t *keys = (fkey_t *)malloc(sizeof(fkey_t) * (size_t)(M > 0 ? M : 1));
+  int32_t *nidx = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  int32_t *jdx = (int32_t *)malloc(sizeof(int32_t) * (size_t)(M > 0 ? M : 1));
+  float *sraw = (float *)malloc(sizeof(float) * (size_t)(M > 0 ? M : 1));
+  if (!keys || !nidx || !jdx || !sraw) rc = -2;
+  if (!rc) {
+    int32_t k = 0;
+    for (int32_t i = 0; i < g->n_out && k < M; ++i)
+      for (int32_t s = 0; s < c.nr[i].n && k < M; ++s, ++k) {
+        nidx[k] = i;
+        jdx[k] = c.nr[i].j[s];
+        sraw[k] = 1.0f;
+      }
+    for (; k < M; ++k) { /* jnp.nonzero fill_value=0: neuron 0, step 0 */
+      nidx[k] = 0;
+      jdx[k] = c.nr[0].step0_idx;
+      sraw[k] = c.nr[0].step0_spk ? 1.0f : 0.0f;
+    }
+    for (int32_t q = 0; q < M; ++q) {
+      keys[q].key = q < total ? jdx[q] : L;
+      keys[q].pos = q;
+    }
+    qsort(keys, (size_t)M, sizeof(fkey_t), fkey_cmp);
+    for (int32_t q = 0; q < M; ++q) {
+      const int64_t p = keys[q].pos;
+      const int32_t jj = jdx[p] < L - 1 ? jdx[p] : L - 1;
+      out->out_times[q] = p < total ? times[jj] : SO_PAD_TIME;
+      out->out_src[q] = nidx[p];
+      out->out_gain[q] = sraw[p];
+    }
+    out->n_real_out = (int32_t)total;
+    out->extra_steps_needed = extra;
+    out->fits = total <= M && extra <= g->max_extra_steps;
+  }
+  for (int32_t i = 0; i < g->n_out; ++i) {
+    free(c.nr[i].step);
+    free(c.nr[i].j);
+  }
+  free(c.nr);
+  free(keys);
+  free(nidx);
+  free(jdx);
+  free(sraw);
+  return rc;
+}

@@ -125,6 +125,40 @@ int so_network_batch(const so_layer_spec *layers, int32_t n_layers, const float 
                      int32_t threads, int32_t *v_final_last, int32_t *spike_counts,
                      int32_t *fits);
 
+/* ---------------------------------------------------------------- float chunked scan
+ * FCLayer.forward with FloatBackend (layers/fc.py:84-106 -> build_fc_structure
+ * connectivity/fc.py:20-33, fc_float_values :36-51, float/scan.py:34-50 run_layer,
+ * float/affine.py:99-126 process_chunk, extract_output_events_fc stream.py:67-81,
+ * extra_steps_upper_bound float/affine.py:57-88).  Float32 throughout, as XLA computes it:
+ * each chunk's maps are composed in lax.associative_scan's odd/even recursion order.
+ * decay_base[i] = float32(1 - 1/tau_i): one entry per neuron (the reference's scalar tau is the
+ * case where all entries are equal). */
+typedef struct {
+  int32_t n_in, n_out, chunk_size, max_out_spikes, max_extra_steps;
+  float v_th;
+} so_float_fc_geom;
+
+typedef struct {
+  float *v_final;            /* (n_out) */
+  uint8_t *spike_mask;       /* (n_out, max_steps) or NULL */
+  int32_t *spike_event_idx;  /* (n_out, max_steps) or NULL */
+  float *out_times;          /* (max_out_spikes) */
+  int32_t *out_src;          /* (max_out_spikes) */
+  float *out_gain;           /* (max_out_spikes) */
+  int32_t n_real_out;        /* spikes in the layer (not clipped to max_out_spikes) */
+  int32_t extra_steps_needed;
+  int32_t fits;
+} so_float_out;
+
+/* max_steps = ceil(L / chunk_size) + max_extra_steps (layers/fc.py:128-130).  gain may be NULL
+ * (all ones).  threads > 1 splits the neurons over worker threads. */
+int so_float_fc_forward(const so_float_fc_geom *g, const float *w, const float *decay_base,
+                        const float *times, const int32_t *src, const float *gain, int32_t L,
+                        int32_t n_real, int32_t threads, so_float_out *out);
+
+/* lax.associative_scan(combine, maps) of float/affine.py:20-24 over n maps (exposed for tests). */
+int so_affine_scan(const float *a, const float *b, int64_t n, float *out_a, float *out_b);
+
 #ifdef __cplusplus
 }
 #endif

@@ -176,6 +176,48 @@ case("fc_layer", "salt_core/tests/test_stream_tiebreak.py:31-70 (integer restate
      times=[1.0, 1.0], src=[0, 1], n_real=2, max_out_spikes=4, v_final=[0, 0],
      spike_count=2, src_prefix=[1, 0], times_prefix=[1.0, 1.0])
 
+# ---------------------------------------------------------------- float chunked scan (FC)
+F = "salt_core/tests/test_fc_forward.py"
+# test_fc_forward.py:1-13 hand example (docs/math/全連接forward訓練範例.md): b1 fires once at
+# global event 2 and resets; b2 never fires and ends at 0.539.  The result must not depend on
+# chunk_size (1 or the whole stream); max_steps = n_real_events.
+for chunk, extra in ((1, 0), (3, 2)):
+    case("float_fc_layer", f"{F}:30-64 (chunk_size={chunk})", n_in=2, n_out=2, tau=4.0,
+         v_th=1.0, w=[[0.6, 0.5], [0.3, 0.2]], times=[1.0, 2.0, 4.0], src=[0, 1, 0], n_real=3,
+         chunk_size=chunk, max_extra_steps=extra, max_out_spikes=6, v_final=[0.0, 0.539],
+         v_tol=1e-4, spikes_per_neuron=[[2], []])
+# test_fc_layer.py:17-55: one neuron, inputs 0 (w=1.0, fires alone) and 1 (w=0.1), events at
+# 0..9 ms with input 0 at events 0 and 5.  chunk 5 needs 3 steps (1, 5, 4 events) but gets 2:
+# extra-steps need 2 (b>0: 10 events, energy floor(2.8/1)=2, m*=2, bound 2+ceil(8/5)=4, base 2).
+# With enough steps every event is used and V matches chunk_size=1: after the reset at event 5,
+# four events of 0.1 with Δt=1 (a=15/16): 0.1, 0.19375, 0.281640625, 0.36403808...
+T = "salt_core/tests/test_fc_layer.py"
+TWO = dict(n_in=2, n_out=1, tau=16.0, v_th=1.0, w=[[1.0, 0.1]],
+           times=[float(i) for i in range(10)], src=[0, 1, 1, 1, 1, 0, 1, 1, 1, 1], n_real=10)
+case("float_fc_layer", f"{T}:33-43", chunk_size=5, max_extra_steps=0, max_out_spikes=8192,
+     fits=False, extra_steps_needed=2, v_final_differs=[0.36403808], **TWO)
+case("float_fc_layer", f"{T}:46-55", chunk_size=5, max_extra_steps=2, max_out_spikes=8192,
+     fits=True, spike_count=2, v_final=[0.36403808], v_tol=1e-6, **TWO)
+case("float_fc_layer", f"{T}:46-55 (chunk_size=1)", chunk_size=1, max_extra_steps=0,
+     max_out_spikes=8192, fits=True, spike_count=2, v_final=[0.36403808], v_tol=1e-6, **TWO)
+case("float_fc_layer", f"{T}:58-65", chunk_size=1, max_extra_steps=0, max_out_spikes=1,
+     fits=False, n_real_out=2, **TWO)
+case("float_fc_layer", f"{T}:58-65 (roomy)", chunk_size=1, max_extra_steps=0, max_out_spikes=2,
+     fits=True, n_real_out=2, **TWO)
+# test_stream_tiebreak.py: same-timestamp spikes leave in global event order, not neuron order;
+# chunk_size = stream length and max_steps = 1, so a neuron stops after its first spike.
+S = "salt_core/tests/test_stream_tiebreak.py"
+case("float_fc_layer", f"{S}:31-70", n_in=1, n_out=2, tau=4.0, v_th=1.0, w=[[0.6], [1.2]],
+     times=[1.0, 1.0], src=[0, 0], n_real=2, chunk_size=2, max_extra_steps=0, max_out_spikes=4,
+     spikes_per_neuron=[[1], [0]], src_prefix=[1, 0], times_prefix=[1.0, 1.0], n_real_out=2)
+case("float_fc_layer", f"{S}:73-111", n_in=1, n_out=3, tau=4.0, v_th=1.0,
+     w=[[0.4], [1.2], [0.6]], times=[1.0, 1.0, 1.0], src=[0, 0, 0], n_real=3, chunk_size=3,
+     max_extra_steps=0, max_out_spikes=6, spikes_per_neuron=[[2], [0], [1]],
+     src_prefix=[1, 2, 0], times_prefix=[1.0, 1.0, 1.0], n_real_out=3)
+# test_affine.py:21-49: the composed prefix maps equal the sequential h = V*a + w (1e-6).
+case("affine_scan", "salt_core/tests/test_affine.py:21-49", tau=16.0, v0=0.37,
+     n_ms=[0, 2, 1, 5, 0, 3], w=[0.3, -0.1, 0.5, 0.2, 0.05, -0.2], tol=1e-6)
+
 if __name__ == "__main__":
     out = os.path.join(os.path.dirname(os.path.abspath(__file__)), "known_answers.json")
     with open(out, "w") as f:
