@@ -205,22 +205,45 @@ salt_status salt_network_set_profiling(salt_network *net, int32_t enable);
 salt_status salt_network_profile_read(salt_network *net, float *fused_ms, float *layer_ms,
                                       int32_t *launches, int32_t reset);
 
-/* ---------------------------------------------------------------- float chunked scan
- * Replaces FloatBackend.scan on an FC layer (salt_core/float/backend.py:16-31 ->
- * fc_float_values connectivity/fc.py:36-51 -> float.scan.run_layer float/scan.py:34-50,
- * process_chunk float/affine.py:99-126) for the forward value only, with a per-neuron tau.
- *   times/src (n_events) one stream; w (n_in, n_out) float32 — transposed so one event reads
- *   one contiguous row; decay_base (n_out) = 1 - 1/tau; v_th scalar.
- *   v_final (n_out) float32; spikes are written as (event index, neuron) int32 pairs in
- *   spike_pairs (capacity max_spikes pairs) in (event, neuron) order — the order of
- *   extract_output_events_fc (stream.py:67-81); *n_spikes (device) gets the total count, which
- *   may exceed max_spikes (then only the first max_spikes pairs in that order are kept). */
-salt_status salt_float_fc_scan(int32_t n_in, int32_t n_out, int32_t n_events, int32_t n_real,
-                               const float *times, const int32_t *src, const float *w,
-                               const float *decay_base, float v_th, float *v_final,
-                               int32_t *spike_pairs, int32_t max_spikes, int32_t *n_spikes,
-                               void *workspace, size_t workspace_bytes, void *stream);
-salt_status salt_float_fc_scan_workspace_size(int32_t n_out, int32_t n_events, size_t *bytes);
+/* ---------------------------------------------------------------- float FC layer
+ * Replaces FCLayer.forward with FloatBackend (salt_core/layers/fc.py:84-106 calling
+ * build_fc_structure connectivity/fc.py:20-33, fc_float_values :36-51, FloatBackend.scan
+ * float/backend.py:16-31 -> float.scan.run_layer float/scan.py:34-50 over process_chunk
+ * float/affine.py:99-126, extract_output_events_fc stream.py:67-81, extra_steps_upper_bound
+ * float/affine.py:57-88) — the forward values.
+ *   w (n_out, n_in) float32 as FCLayer holds it; decay_base (n_out) = float32(1 - 1/tau) per
+ *   neuron (all equal for the reference's scalar tau; per-neuron values extend it).
+ *   in_gain (batch, capacity) event gains or NULL for all ones (the forward s_spike of an upstream
+ *   float layer is 1).  v_final (batch, n_out).  The output stream's gains are 1 for every real
+ *   entry and are not written.
+ *   stats (optional, each pointer optional): spike_count (batch) = Σ spike_mask;
+ *   needed_extra_steps (batch) = LayerDiag.needed["max_extra_steps"]; fits (batch).
+ * v_th must be > 0 (a threshold <= 0 fires on padding, which only the reference's fixed step
+ * count bounds).  Float results follow the reference within float32 rounding: the scan runs the
+ * recurrence v = a*v + b in event order, where the reference composes each chunk's maps first. */
+typedef struct {
+  int32_t n_in, n_out;
+  int32_t chunk_size;       /* FCLayer.chunk_size */
+  int32_t max_out_spikes;   /* FCLayer.max_out_spikes */
+  int32_t max_extra_steps;  /* FCLayer.max_extra_steps */
+  float v_th;               /* FCLayer.v_th */
+} salt_float_fc_desc;
+
+typedef struct {
+  int32_t *spike_count;
+  int32_t *needed_extra_steps;
+  int32_t *fits;
+} salt_float_layer_stats;
+
+salt_status salt_float_fc_layer_workspace_size(const salt_float_fc_desc *layer, int32_t batch,
+                                               int32_t in_capacity, int32_t has_gain,
+                                               size_t *bytes);
+salt_status salt_float_fc_layer_forward(const salt_float_fc_desc *layer, const float *w,
+                                        const float *decay_base, int32_t batch,
+                                        const salt_stream_in *in, const float *in_gain,
+                                        salt_stream_out *out, float *v_final,
+                                        const salt_float_layer_stats *stats, void *workspace,
+                                        size_t workspace_bytes, void *stream);
 
 /* Library facts and errors (host). */
 const char *salt_last_error(void);

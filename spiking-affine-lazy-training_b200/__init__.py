@@ -1,4 +1,5 @@
-"""salt_b200 — B200-native (sm_100a) implementation of SALT's integer event-driven forward pass.
+"""salt_b200 — B200-native (sm_100a) implementation of SALT's integer event-driven forward pass
+and of the float chunked affine scan of its FC layers.
 
 Host API mirrors the reference (salt_core): EventStream, InputEvents, ConvLayer/FCLayer and their
 specs, Network/run_network, QuantizedLayerParams and the offline integer codes.  The compute runs
@@ -17,6 +18,9 @@ def __getattr__(name):  # the CUDA-backed objects load the library lazily
     if name in ("QuantB200Backend", "QuantLayerResult", "NetworkOutput", "default_backend"):
         from . import backend
         return getattr(backend, name)
+    if name in ("FloatB200Backend", "FloatLayerResult"):
+        from . import float_backend
+        return getattr(float_backend, name)
     if name == "NetworkPlan":
         from .plan import NetworkPlan
         return NetworkPlan
@@ -24,7 +28,7 @@ def __getattr__(name):  # the CUDA-backed objects load the library lazily
 
 
 __all__ = ["Capacity", "ConvLayer", "ConvSpec", "EventStream", "FCLayer", "FCSpec", "GrowthPolicy",
-           "InputEvents", "LayerDiag", "LayerOutput", "MAX_REGISTER_BITS", "MAX_SHIFT_BITS",
+           "FloatB200Backend", "FloatLayerResult", "InputEvents", "LayerDiag", "LayerOutput", "MAX_REGISTER_BITS", "MAX_SHIFT_BITS",
            "Network", "NetworkPlan", "OverflowMode", "PAD_TIME", "QuantB200Backend",
            "QuantizedLayerParams", "RoundMode", "build_decay_table_int", "check_layer_connections",
            "conv", "delta_t_max", "fc", "grown_to_fit", "input_stream", "quantize_to_int",

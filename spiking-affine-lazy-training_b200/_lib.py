@@ -44,6 +44,15 @@ class LayerStats(ctypes.Structure):
                                    "fits")]
 
 
+class FloatFCDesc(ctypes.Structure):
+    _fields_ = [("n_in", _i32), ("n_out", _i32), ("chunk_size", _i32), ("max_out_spikes", _i32),
+                ("max_extra_steps", _i32), ("v_th", ctypes.c_float)]
+
+
+class FloatLayerStats(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("spike_count", "needed_extra_steps", "fits")]
+
+
 class LayerSpec(ctypes.Structure):
     _fields_ = [("kind", _i32), ("conv", ConvDesc), ("fc", FCDesc), ("quant", QuantDesc),
                 ("q_host", _vp), ("lut_host", _vp), ("vth_host", _vp)]
@@ -69,9 +78,9 @@ _SIGS = {
     "salt_network_last_launch_count": (_i32, [_vp]),
     "salt_network_set_profiling": (_i32, [_vp, _i32]),
     "salt_network_profile_read": (_i32, [_vp, _vp, _vp, _vp, _i32]),
-    "salt_float_fc_scan": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, ctypes.c_float,
-                                  _vp, _vp, _i32, _vp, _vp, ctypes.c_size_t, _vp]),
-    "salt_float_fc_scan_workspace_size": (_i32, [_i32, _i32, _vp]),
+    "salt_float_fc_layer_workspace_size": (_i32, [_vp, _i32, _i32, _i32, _vp]),
+    "salt_float_fc_layer_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
+                                           ctypes.c_size_t, _vp]),
     "salt_last_error": (ctypes.c_char_p, []),
     "salt_version": (ctypes.c_char_p, []),
     "salt_launch_counter": (ctypes.c_int64, [_i32]),

@@ -490,6 +490,146 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   return SALT_OK;
 }
 
+// ---------------------------------------------------------------- float fc
+
+struct FloatScratch {
+  int32_t *stats, *s_total, *needed, *exact, *chunk, *hist, *n_spk;
+  size_t stats_bytes;
+  float *wT, *lut;
+  uint32_t* sw;
+  float *r_vend, *r_u1, *r_A1, *r_M, *r_Aseg, *r_sum;
+  int32_t *r_k1, *r_nspk, *r_cnt, *r_mono;
+};
+
+// Time segments per sample: enough (segment, group) warps to fill the GPU, at least 256
+// events per segment so that the in-order fix-up stays short.
+static int32_t float_segments(int32_t G, int32_t B, int32_t E) {
+  const int64_t target = 148LL * 48;
+  const int64_t per = (int64_t)G * B;
+  const int64_t s = (target + per - 1) / per;
+  return (int32_t)std::max<int64_t>(1, std::min<int64_t>(s, std::max(1, E / 256)));
+}
+
+static size_t float_carve(const salt_float_fc_desc* d, int32_t B, int32_t E, bool gain, void* ws,
+                          FloatScratch& s) {
+  Carver c(ws);
+  const int G = (d->n_out + 31) / 32, S = float_segments(G, B, E);
+  const int nsc = (E + kSpkChunk - 1) / kSpkChunk;
+  const size_t nstat = (size_t)B * 2 + (size_t)B * G + (size_t)B * nsc +
+                       (gain ? 0 : (size_t)B * d->n_in);
+  s.stats = c.take<int32_t>(nstat);
+  s.stats_bytes = nstat * 4;
+  if (s.stats) {
+    s.s_total = s.stats;
+    s.needed = s.stats + B;
+    s.exact = s.stats + 2 * B;
+    s.chunk = s.exact + (size_t)B * G;
+    s.hist = gain ? nullptr : s.chunk + (size_t)B * nsc;
+  }
+  s.wT = c.take<float>((size_t)d->n_in * d->n_out);
+  s.lut = c.take<float>((size_t)kFloatLut * d->n_out);
+  s.sw = c.take<uint32_t>((size_t)B * E * G);
+  s.n_spk = c.take<int32_t>((size_t)B * d->n_out);
+  const size_t nr = (size_t)B * S * d->n_out;
+  s.r_vend = c.take<float>(nr);
+  s.r_u1 = c.take<float>(nr);
+  s.r_A1 = c.take<float>(nr);
+  s.r_M = c.take<float>(nr);
+  s.r_Aseg = c.take<float>(nr);
+  s.r_k1 = c.take<int32_t>(nr);
+  s.r_nspk = c.take<int32_t>(nr);
+  s.r_sum = gain ? c.take<float>(nr) : nullptr;
+  s.r_cnt = gain ? c.take<int32_t>(nr) : nullptr;
+  s.r_mono = c.take<int32_t>((size_t)B * S);
+  return c.size();
+}
+
+static salt_status check_float(const salt_float_fc_desc* d) {
+  if (!d) return fail(SALT_BAD_ARG, "float fc descriptor is NULL");
+  if (d->n_in < 1 || d->n_out < 1) return fail(SALT_BAD_ARG, "float fc: n_in and n_out must be >= 1");
+  if (d->chunk_size < 1) return fail(SALT_BAD_ARG, "float fc: chunk_size must be >= 1");
+  if (d->max_out_spikes < 1) return fail(SALT_BAD_ARG, "max_out_spikes must be >= 1");
+  if (d->max_extra_steps < 0) return fail(SALT_BAD_ARG, "max_extra_steps must be >= 0");
+  if (!(d->v_th > 0.0f) || d->v_th == INFINITY)
+    return fail(SALT_BAD_ARG, "float fc: v_th must be a finite value > 0 (a threshold <= 0 "
+                              "fires on pad entries)");
+  return SALT_OK;
+}
+
+__global__ void float_finish(const int32_t* __restrict__ s_total,
+                             const int32_t* __restrict__ needed, int32_t M, int32_t max_extra,
+                             int32_t batch, int32_t* out_nreal, salt_float_layer_stats st) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const int32_t S = s_total[b], need = needed[b];
+  if (out_nreal) out_nreal[b] = S;
+  if (st.spike_count) st.spike_count[b] = S;
+  if (st.needed_extra_steps) st.needed_extra_steps[b] = need;
+  if (st.fits) st.fits[b] = S <= M && need <= max_extra;  // capacity.py:60-63
+}
+
+static salt_status float_forward_impl(const salt_float_fc_desc* d, const float* w,
+                                      const float* decay_base, int32_t B,
+                                      const salt_stream_in* in, const float* gain,
+                                      salt_stream_out* out, float* v_final,
+                                      const salt_float_layer_stats* stats, void* ws,
+                                      size_t ws_bytes, cudaStream_t st) {
+  salt_status rc = check_float(d);
+  if (rc) return rc;
+  if ((rc = check_stream_in(in, B))) return rc;
+  if (!w || !decay_base || !out || !out->times || !out->src || !out->n_real || !v_final)
+    return fail(SALT_BAD_ARG, "float fc layer: NULL parameter or output pointer");
+  const int32_t E = in->capacity;
+  const int64_t base_steps = ((int64_t)E + d->chunk_size - 1) / d->chunk_size;
+  if (base_steps + d->max_extra_steps > INT32_MAX)
+    return fail(SALT_BAD_ARG, "float fc: ceil(capacity / chunk_size) + max_extra_steps overflows");
+  FloatScratch s;
+  const size_t need = float_carve(d, B, E, gain != nullptr, nullptr, s);
+  if (!ws || ws_bytes < need) return fail(SALT_WORKSPACE_TOO_SMALL, "float fc workspace too small");
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return fail(SALT_BAD_ARG, "workspace not 256-byte aligned");
+  float_carve(d, B, E, gain != nullptr, ws, s);
+
+  FloatLaunch P;
+  memset(&P, 0, sizeof(P));
+  P.n_in = d->n_in; P.n_out = d->n_out; P.G = (d->n_out + 31) / 32;
+  P.S = float_segments(P.G, B, E);
+  P.C = d->chunk_size; P.base_steps = (int32_t)base_steps;
+  P.max_steps = (int32_t)(base_steps + d->max_extra_steps);
+  P.vth = d->v_th; P.margin = d->v_th * 1.5e-5f;
+  P.in.times = in->times; P.in.src = in->src; P.in.capacity = E; P.in.virtual_pads = in->virtual_pads;
+  P.in_nreal = in->n_real; P.batch = B; P.gain = gain;
+  P.w = w; P.wT = s.wT; P.decay_base = decay_base; P.lut = s.lut; P.v_final = v_final;
+  P.sw = s.sw; P.sw_stride = (int64_t)E * P.G;
+  P.chunk_spikes = s.chunk; P.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
+  P.s_total = s.s_total; P.needed = s.needed; P.n_spk = s.n_spk; P.exact = s.exact; P.hist = s.hist;
+  P.r_vend = s.r_vend; P.r_u1 = s.r_u1; P.r_A1 = s.r_A1; P.r_M = s.r_M; P.r_Aseg = s.r_Aseg;
+  P.r_sum = s.r_sum; P.r_k1 = s.r_k1; P.r_nspk = s.r_nspk; P.r_cnt = s.r_cnt; P.r_mono = s.r_mono;
+  SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
+  SALT_CUDA(float_fc_launch(P, st, &g_launches));
+
+  // the FC compaction reads the spike words and per-neuron counts in the integer layer's form
+  FCLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.n_in = d->n_in; L.n_out = d->n_out; L.G = P.G; L.M = d->max_out_spikes;
+  L.in = P.in; L.in_nreal = in->n_real; L.batch = B;
+  L.sw = s.sw; L.sw_stride = P.sw_stride;
+  L.chunk_spikes = s.chunk; L.chunk_off = s.chunk; L.n_spk_chunks = P.n_spk_chunks;
+  L.s_total = s.s_total; L.n_spk = s.n_spk; L.tail_mode = 0;
+  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
+  SALT_LAUNCHED("spike_chunk_scan");
+  fc_compact<<<dim3(std::min(L.n_spk_chunks, kCompactBlocksPerSample), B), kCompactThreads, 0,
+               st>>>(L, *out);
+  SALT_LAUNCHED("fc_compact");
+  fc_truncated<<<B, kCompactThreads, 0, st>>>(L, *out);
+  SALT_LAUNCHED("fc_truncated");
+  salt_float_layer_stats none{};
+  float_finish<<<(B + 255) / 256, 256, 0, st>>>(s.s_total, s.needed, d->max_out_spikes,
+                                                d->max_extra_steps, B, out->n_real,
+                                                stats ? *stats : none);
+  SALT_LAUNCHED("float_finish");
+  return SALT_OK;
+}
+
 }  // namespace salt
 
 // ==================================================================== C ABI
@@ -566,6 +706,27 @@ salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc* layer,
   SALT_CUDA(fixed_scratch_address(&ws));
   return conv_forward_impl(layer, quant, q, lut, vth, batch, in, out, v_final, stats, ws, need,
                            (cudaStream_t)stream);
+}
+
+salt_status salt_float_fc_layer_workspace_size(const salt_float_fc_desc* layer, int32_t batch,
+                                               int32_t in_capacity, int32_t has_gain,
+                                               size_t* bytes) {
+  salt_status rc = check_float(layer);
+  if (rc) return rc;
+  if (!bytes || batch < 1 || in_capacity < 1) return fail(SALT_BAD_ARG, "bad batch/capacity");
+  FloatScratch s;
+  *bytes = float_carve(layer, batch, in_capacity, has_gain != 0, nullptr, s);
+  return SALT_OK;
+}
+
+salt_status salt_float_fc_layer_forward(const salt_float_fc_desc* layer, const float* w,
+                                        const float* decay_base, int32_t batch,
+                                        const salt_stream_in* in, const float* in_gain,
+                                        salt_stream_out* out, float* v_final,
+                                        const salt_float_layer_stats* stats, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  return float_forward_impl(layer, w, decay_base, batch, in, in_gain, out, v_final, stats,
+                            workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 salt_status salt_fc_layer_workspace_size(const salt_fc_desc* layer, const salt_quant_desc* quant,

@@ -116,6 +116,49 @@ struct FCLaunch {
   }
 };
 
+// Float FC layer (float chunked affine scan).  Per-(sample, segment, neuron) records of the
+// speculative pass are laid out [b][s][neuron] so that a warp's 32 lanes touch 128 B.
+constexpr int kFloatLut = 64;  // decay table rows: powf(base, d) for whole d in [0, 64)
+constexpr int kFloatSegWarps = 4;
+
+struct FloatLaunch {
+  int32_t n_in, n_out, G, S;  // S time segments per sample
+  int32_t C;                  // chunk_size
+  int32_t max_steps;          // ceil(L / C) + max_extra_steps
+  int32_t base_steps;         // ceil(L / C)
+  float vth, margin;
+  StreamView in;
+  const int32_t* in_nreal;
+  int32_t batch;
+  const float* gain;          // (B, L) event gains or nullptr (all ones)
+  const float* w;             // (n_out, n_in) as the caller holds it
+  float* wT;                  // (n_in, n_out) transposed copy
+  const float* decay_base;    // (n_out) float32(1 - 1/tau_i)
+  float* lut;                 // [kFloatLut][n_out]
+  float* v_final;             // (B, n_out)
+  uint32_t* sw;               // spike words [B][L][G]
+  int64_t sw_stride;
+  int32_t* chunk_spikes;      // [B][n_spk_chunks]
+  int32_t n_spk_chunks;
+  int32_t *s_total, *needed;  // (B)
+  int32_t* n_spk;             // (B, n_out)
+  int32_t* exact;             // (B, G) groups that the step limit may cut
+  int32_t* hist;              // (B, n_in) real events per source (gain == nullptr only)
+  float *r_vend, *r_u1, *r_A1, *r_M, *r_Aseg, *r_sum;
+  int32_t *r_k1, *r_nspk, *r_cnt, *r_mono;
+
+  __device__ __forceinline__ int32_t n_eff(int b) const {
+    int32_t n = in_nreal[b];
+    return n < 0 ? 0 : (n < in.capacity ? n : in.capacity);
+  }
+  // events per segment: a multiple of 32 so that 32-event batches never straddle segments or
+  // 256-event spike chunks
+  __device__ __forceinline__ int32_t seg_len(int32_t n_eff) const {
+    const int32_t l = (n_eff + S - 1) / S;
+    return max(32, (l + 31) & ~31);
+  }
+};
+
 // ---------------------------------------------------------------- warp / block helpers
 __device__ __forceinline__ int32_t warp_sum(int32_t v) {
 #pragma unroll
@@ -186,6 +229,10 @@ void* fc_scan_kernel(bool fires, bool saturate);
 
 // Device address of the fixed scratch behind salt_conv_layer_forward_noalloc (fixed_scratch.cu).
 cudaError_t fixed_scratch_address(void** ptr);
+
+// Enqueues the float FC layer's kernels up to the final spike words (float_scan.cu); adds the
+// number of launches to *launches.
+cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches);
 constexpr int kFcThreads = 128;
 
 }  // namespace salt
