@@ -8,6 +8,9 @@ diagnostics and fits) over one batch of synthetic input resident in HBM, plus th
 all-gather of the int32 logits when N > 1.  Metric: input events/s over all ranks.  Prints one
 JSON line on rank 0.  The default workload is configuration 3 of the benchmark (the conv network
 on 4096 blob samples, the configuration quoted at 1/2/4/8 GPUs); --config selects another.
+--config 5 measures the float FC layer (4096->4096, one stream of 10^6 events, chunk 4096): one
+step = one layer forward; N > 1 runs one independent stream per rank (weak scaling, no
+collective on the data path).
 """
 from __future__ import annotations
 
@@ -26,6 +29,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "input events/sec (bit-exact integer forward)"
+FLOAT_METRIC = "input events/sec (float FC chunked affine scan)"
 UNIT = "events/s"
 
 
@@ -35,7 +39,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4])
+    ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=None,
@@ -399,9 +403,222 @@ def traffic_from_profile(wl, layer_index):
     return None
 
 
+# ---------------------------------------------------------------- configuration 5 (float)
+
+def _float_sub_layer(wl, k):
+    """The first k neurons of the float layer (neurons are independent), with the output
+    capacity scaled by k / n_out so that the per-layer output extraction scales with them."""
+    from dataclasses import replace
+    M = max(1, -(-wl.layer.max_out_spikes * k // wl.layer.n_out))
+    layer = replace(wl.layer, n_out=k, max_out_spikes=M)
+    return layer, wl.w[:k], wl.tau[:k]
+
+
+def _float_oracle_run(wl, k, threads):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    layer, w, tau = _float_sub_layer(wl, k)
+    t0 = time.perf_counter()
+    for b in range(wl.batch):
+        O.float_fc_forward(layer, w, wl.times[b], wl.src[b], int(wl.n_real[b]), tau=tau,
+                           dense=False, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_float(wl, seconds, threads=None):
+    """The float oracle (chunk-by-chunk restatement, all host threads) over the full stream for
+    a bounded subset of the neurons, scaled to the full layer width."""
+    threads = threads or os.cpu_count() or 1
+    n = wl.layer.n_out
+    k0 = min(n, threads)
+    dt0 = _float_oracle_run(wl, k0, threads)
+    k = int(min(n, max(k0, k0 * seconds / max(dt0, 1e-6))))
+    dt = _float_oracle_run(wl, k, threads)
+    value = wl.events * k / dt / n
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{k} of {n} neurons over the full {wl.events}-event stream of {wl.name} "
+                      f"through the C float oracle, {threads} threads, {dt:.1f} s; scaled to "
+                      f"the full layer width"}
+
+
+def run_reference_float(args):
+    rank, world, _ = rank_info()
+    if rank != 0:
+        return
+    from salt_b200 import workloads as W
+    wl = W.config5(seed=args.seed)
+    threads = os.cpu_count() or 1
+    n = wl.layer.n_out
+    k = min(n, threads)
+    per = []
+    for step in range(args.warmup + args.steps):
+        dt = _float_oracle_run(wl, k, threads)
+        if step >= args.warmup:
+            per.append(dt)
+    tt = sum(per)
+    value = wl.events * k * len(per) / tt / n
+    line = {"impl": "reference", "metric": FLOAT_METRIC, "value": value, "unit": UNIT,
+            "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * tt / len(per), "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.name, "neurons_per_step": k},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{k} of {n} neurons per step over the full stream of "
+                                       f"{wl.name} through the C float oracle, {threads} "
+                                       f"threads; scaled to the full layer width"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200_float(args):
+    import torch
+    import torch.distributed as dist
+    rank, world, local = rank_info()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import salt_b200 as S
+    from salt_b200 import _lib
+    from salt_b200 import float_backend as F
+    from salt_b200 import workloads as W
+    from salt_b200.device import DeviceStream
+    be = S.FloatB200Backend()
+    wl = W.size_float_capacity(W.config5(seed=args.seed + rank), be)
+    layer = wl.layer
+    B, E = wl.batch, wl.times.shape[1]
+    plan = be.compile(layer, wl.w, B, E, tau=wl.tau)
+    t_d = torch.from_numpy(wl.times).cuda()
+    s_d = torch.from_numpy(wl.src).cuda()
+    n_d = torch.from_numpy(wl.n_real).cuda()
+    ds = DeviceStream(t_d, s_d, n_d, False)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB of L2
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        plan.forward_device(ds)
+    barrier()
+    lib = _lib.lib()
+    lib.salt_launch_counter(1)
+    plan.forward_device(ds)
+    launches_per_step = int(lib.salt_launch_counter(1))
+    barrier()
+    F.profile_read(reset=True)
+    F.set_profiling(True)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for _ in range(args.steps):
+            flush.zero_()  # outside the layer's timed events
+            plan.forward_device(ds)
+        torch.cuda.synchronize()
+    F.set_profiling(False)
+    seg_ms, layer_ms, n_timed = F.profile_read(reset=True)
+    barrier()
+    ms = layer_ms / max(n_timed, 1)
+    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    ev_all = torch.tensor([wl.events], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        dist.all_reduce(ev_all, op=dist.ReduceOp.SUM)
+    ms_max, events_step = float(t_max.item()), float(ev_all.item())
+    value = events_step / (ms_max / 1000.0)
+    spikes = int(plan.stats[0].sum().item())
+
+    # end to end through the public plan: H2D of the stream, the layer, D2H of v_final + stats
+    t_h = torch.from_numpy(wl.times).pin_memory()
+    s_h = torch.from_numpy(wl.src).pin_memory()
+    n_h = torch.from_numpy(wl.n_real).pin_memory()
+    v_h = torch.empty(plan.v_final.shape, dtype=torch.float32).pin_memory()
+    st_h = torch.empty(plan.stats.shape, dtype=torch.int32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 20))
+
+    def e2e_step():
+        t_d.copy_(t_h, non_blocking=True)
+        s_d.copy_(s_h, non_blocking=True)
+        n_d.copy_(n_h, non_blocking=True)
+        run = plan.forward_device(ds)
+        v_h.copy_(run.v_final, non_blocking=True)
+        st_h.copy_(run.stats, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = torch.tensor([start.elapsed_time(stop) / e2e_steps], dtype=torch.float64,
+                          device="cuda")
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = events_step / (float(e2e_ms.item()) / 1000.0)
+    h2d = int(t_h.numel() * 4 + s_h.numel() * 4 + n_h.numel() * 4)
+    d2h = int(v_h.numel() * 4 + st_h.numel() * 4)
+
+    seg_avg = seg_ms / max(n_timed, 1)
+    G = (layer.n_out + 31) // 32
+    # per segment-kernel launch: the stream (8 B/event), one weight row slice per event and
+    # neuron (4 B), one spike word per event and 32-neuron group (4 B)
+    alg = float(8 * wl.events + 4 * layer.n_out * wl.events + 4 * G * wl.events)
+    peak, peak_kind = peak_hbm()
+    achieved = alg / (seg_avg / 1000.0) / 1e9
+    if rank == 0:
+        line = {
+            "metric": FLOAT_METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": wl.name, "n_in": layer.n_in, "n_out": layer.n_out,
+                       "events_per_step": int(events_step), "chunk_size": layer.chunk_size,
+                       "max_out_spikes": layer.max_out_spikes,
+                       "max_extra_steps": layer.max_extra_steps, "spikes_per_step": spikes,
+                       "parallelism": f"{world} independent streams (replicas)",
+                       "l2": "256 MiB written between timed steps (L2 flush, outside the "
+                             "layer's timed events)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": float_traffic_from_profile(wl),
+                         "kernel": "ffc_segment (speculative segment scan)",
+                         "kernel_ms": seg_avg, "algorithmic_bytes": alg,
+                         "layer_ms": ms, "peak_source": peak_kind,
+                         "note": "the 64 MB weight matrix is re-read per event from L2; "
+                                 "achieved counts those bytes against the HBM peak"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_float(wl, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def float_traffic_from_profile(wl):
+    """DRAM bytes per segment-kernel launch from the committed ncu summary, scaled by events."""
+    path = os.path.join(ROOT, "profiles", "ffc_segment_config5.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_input_event:"):
+                    return float(line.split(":", 1)[1]) * wl.events
+    except OSError:
+        pass
+    return None
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.config == 5:
+        (run_reference_float if args.impl == "reference" else run_b200_float)(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

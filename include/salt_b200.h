@@ -245,6 +245,15 @@ salt_status salt_float_fc_layer_forward(const salt_float_fc_desc *layer, const f
                                         const salt_float_layer_stats *stats, void *workspace,
                                         size_t workspace_bytes, void *stream);
 
+/* Optional timing of the float FC layers that the calling thread enqueues: with profiling on,
+ * CUDA events are recorded on the launching stream around each layer's speculative segment
+ * kernel (the dominant kernel) and around the whole layer.  salt_float_fc_profile_read
+ * synchronises on them and writes the summed milliseconds and the number of timed layers;
+ * reset clears the sums. */
+salt_status salt_float_fc_set_profiling(int32_t enable);
+salt_status salt_float_fc_profile_read(float *segment_ms, float *layer_ms, int32_t *layers,
+                                       int32_t reset);
+
 /* Library facts and errors (host). */
 const char *salt_last_error(void);
 const char *salt_version(void);

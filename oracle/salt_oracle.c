@@ -724,7 +724,23 @@ static int float_neuron(float_ctx *c, int32_t i, float *a_pad, float *b_pad, flo
   uint8_t *mask = c->out->spike_mask ? c->out->spike_mask + (int64_t)i * c->max_steps : NULL;
   int32_t *eidx = c->out->spike_event_idx ? c->out->spike_event_idx + (int64_t)i * c->max_steps
                                           : NULL;
+  const int64_t id_from = L < c->n_real ? L : (c->n_real > 0 ? c->n_real : 0);
   for (int32_t step = 0; step < c->max_steps; ++step) {
+    if (ptr >= id_from && !(v - v_th >= 0.0f)) {
+      /* Every map from here on is the identity (1, 0), which composes to exactly (1, 0): each
+       * remaining step leaves v unchanged, does not fire and consumes a whole chunk. */
+      for (; step < c->max_steps; ++step) {
+        const int32_t ev = (int32_t)(ptr + C < INT32_MAX ? ptr + C : INT32_MAX);
+        if (mask) mask[step] = 0;
+        if (eidx) eidx[step] = ev;
+        if (step == 0) {
+          r->step0_idx = ev;
+          r->step0_spk = 0;
+        }
+        ptr += C;
+      }
+      break;
+    }
     for (int32_t k = 0; k < C; ++k) { /* take_chunk: jnp.take(..., mode='clip') */
       int64_t idx = ptr + k;
       if (idx > Lp - 1) idx = Lp - 1;

@@ -79,6 +79,8 @@ _SIGS = {
     "salt_network_set_profiling": (_i32, [_vp, _i32]),
     "salt_network_profile_read": (_i32, [_vp, _vp, _vp, _vp, _i32]),
     "salt_float_fc_layer_workspace_size": (_i32, [_vp, _i32, _i32, _i32, _vp]),
+    "salt_float_fc_set_profiling": (_i32, [_i32]),
+    "salt_float_fc_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "salt_float_fc_layer_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                            ctypes.c_size_t, _vp]),
     "salt_last_error": (ctypes.c_char_p, []),

@@ -14,17 +14,21 @@
 // ceil(L / chunk) + S steps: a neuron with S <= max_extra_steps is never cut.
 //
 // Parallel form (neurons are independent; time is split into segments):
-//  1. ffc_segment: every (segment, 32-neuron group) warp runs its segment from v = 0 (a guess
-//     for the true incoming state), writing one spike word per event and a record per neuron:
-//     first spike (event, pre-reset value u1, decay product A1 up to it), the largest value
-//     before it (M), the product of all decays (Aseg), the end state and the spike count.
+//  1. ffc_segment: every (segment, 32-neuron group) warp guesses the state at its segment's
+//     start by a warm-up run from v = 0 over the events just before it (runs that fire at a
+//     common event agree exactly from then on, so the guess is usually the exact float32 state),
+//     then runs its segment from that guess v_start, writing one spike word per event and a
+//     record per neuron: first spike (event, pre-reset value u1, decay product A1 up to it), the
+//     largest value before it (M), the product of all decays (Aseg), the end state, the spike
+//     count.
 //  2. ffc_fixup: one warp per group walks the segments in order with the true incoming state
-//     v_in.  Before the guessed run's first spike the true value is guess + A_k * v_in with
-//     0 <= A_k <= 1, so the records decide most segments outright: with v_in > 0 and
-//     M + v_in < v_th, or v_in < 0 and u1 + A1 * v_in >= v_th, both runs fire first at the same
-//     event and agree from there on; without any spike the end state is Aseg * v_in + guess.
-//     Otherwise the lanes concerned re-run the segment from v_in, rewriting their spike bits,
-//     until they fire at an event where the guess also fired.
+//     v_in.  A guess equal to v_in leaves nothing to do.  Otherwise, with d = v_in - v_start,
+//     the true value before the guessed run's first spike is guess + A_k * d with 0 <= A_k <= 1,
+//     so the records decide most segments outright: with d > 0 and M + d < v_th, or d < 0 and
+//     u1 + A1 * d >= v_th, both runs fire first at the same event and agree from there on;
+//     without any spike the end state is Aseg * d + guess.  Otherwise the lanes concerned re-run
+//     the segment from v_in, rewriting their spike bits, until they fire at an event where the
+//     guess also fired.
 //  3. ffc_exact: groups holding a neuron that the step limit may cut are re-run sequentially
 //     with the reference's step accounting (chunk phase, step count, cut-off).
 // Spike words then go through the FC compaction (fc_layer.cu) in (event, neuron) order.
@@ -80,24 +84,37 @@ __device__ __forceinline__ int32_t extra_steps_bound(int32_t m_pos, double sum_p
 }
 
 // With unit gains b = w[o][src], so the sums over events are sums over sources weighted by the
-// number of events each source sent.
-__global__ void ffc_bound(FloatLaunch P) {
+// number of events each source sent.  Block (x, b, z) adds sources z, z + gridDim.z, ... into
+// the per-neuron totals.
+__global__ void ffc_bound_partial(FloatLaunch P) {
   const int b = blockIdx.y;
   const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= P.n_out) return;
   const int32_t* h = P.hist + (int64_t)b * P.n_in;
   int32_t m = 0;
   double sum = 0.0;
-  if (o < P.n_out)
-    for (int s = 0; s < P.n_in; ++s) {
-      const int32_t c = __ldg(&h[s]);
-      if (c == 0) continue;  // uniform across the block
-      const float w = __ldg(&P.wT[(int64_t)s * P.n_out + o]);
-      if (w > 0.0f) {
-        m += c;
-        sum += (double)c * (double)w;
-      }
+  for (int s = blockIdx.z; s < P.n_in; s += gridDim.z) {
+    const int32_t c = __ldg(&h[s]);
+    if (c == 0) continue;
+    const float w = __ldg(&P.wT[(int64_t)s * P.n_out + o]);
+    if (w > 0.0f) {
+      m += c;
+      sum += (double)c * (double)w;
     }
-  int32_t extra = o < P.n_out ? extra_steps_bound(m, sum, P) : 0;
+  }
+  if (m) {
+    atomicAdd(&P.bcnt[(int64_t)b * P.n_out + o], m);
+    atomicAdd(&P.bsum[(int64_t)b * P.n_out + o], sum);
+  }
+}
+
+__global__ void ffc_bound(FloatLaunch P) {
+  const int b = blockIdx.y;
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  int32_t extra = 0;
+  if (o < P.n_out)
+    extra = extra_steps_bound(P.bcnt[(int64_t)b * P.n_out + o], P.bsum[(int64_t)b * P.n_out + o],
+                              P);
   extra = max(extra, __shfl_xor_sync(kFull, extra, 16));
   extra = max(extra, __shfl_xor_sync(kFull, extra, 8));
   extra = max(extra, __shfl_xor_sync(kFull, extra, 4));
@@ -125,27 +142,45 @@ struct Batch {
   int cnt;
 };
 
+// Lane-parallel raw loads of one batch (lane e: event base + e, when before jend).
+struct Raw {
+  float t;
+  int32_t src;
+  float gain;
+};
+
+template <bool GAIN>
+__device__ __forceinline__ Raw load_raw(const FloatLaunch& P, int b, int32_t base, int32_t jend,
+                                        int lane) {
+  Raw r{0.0f, 0, 1.0f};
+  const int32_t j = base + lane;
+  if (j < jend) {
+    const int64_t row = (int64_t)b * P.in.capacity;
+    r.t = P.in.times[row + j];
+    r.src = (int32_t)jax_index(P.in.src[row + j], P.n_in);
+    if (GAIN) r.gain = P.gain[row + j];
+  }
+  return r;
+}
+
+__device__ __forceinline__ Batch make_batch(const Raw& r, int32_t base, int32_t jend,
+                                            float& tprev, int lane) {
+  Batch x;
+  x.src = r.src;
+  x.gain = r.gain;
+  float tp = __shfl_up_sync(kFull, r.t, 1);
+  if (lane == 0) tp = tprev;
+  x.cnt = min(32, jend - base);
+  tprev = __shfl_sync(kFull, r.t, x.cnt - 1);
+  x.dt = r.t - tp;
+  x.row = decay_row(x.dt);
+  return x;
+}
+
 template <bool GAIN>
 __device__ __forceinline__ Batch load_batch(const FloatLaunch& P, int b, int32_t base,
                                             int32_t jend, float& tprev, int lane) {
-  Batch x;
-  const int32_t j = base + lane;
-  const int64_t row = (int64_t)b * P.in.capacity;
-  float t = 0.0f;
-  x.src = 0;
-  x.gain = 1.0f;
-  if (j < jend) {
-    t = P.in.times[row + j];
-    x.src = (int32_t)jax_index(P.in.src[row + j], P.n_in);
-    if (GAIN) x.gain = P.gain[row + j];
-  }
-  float tp = __shfl_up_sync(kFull, t, 1);
-  if (lane == 0) tp = tprev;
-  x.cnt = min(32, jend - base);
-  tprev = __shfl_sync(kFull, t, x.cnt - 1);
-  x.dt = t - tp;
-  x.row = decay_row(x.dt);
-  return x;
+  return make_batch(load_raw<GAIN>(P, b, base, jend, lane), base, jend, tprev, lane);
 }
 
 // b of the 32 events for this lane's neuron: w[o][src] * gain (0 for lanes that sit out).
@@ -161,11 +196,110 @@ __device__ __forceinline__ void load_b(const FloatLaunch& P, const Batch& x, int
   }
 }
 
+// powf for the rare gaps that the table does not hold; kept out of line so that the common
+// path never evaluates it.
+__device__ __noinline__ float decay_pow(float base, float dt) { return powf(base, dt); }
+
+// a of event e for this lane's neuron.  The row is the same for all lanes, so the branch is
+// warp-uniform.
 __device__ __forceinline__ float decay_of(const Batch& x, int e, float base, const float* lut_s,
                                           int lane) {
   const int32_t row = __shfl_sync(kFull, x.row, e);
-  const float dt = __shfl_sync(kFull, x.dt, e);
-  return row >= 0 ? lut_s[row * 32 + lane] : powf(base, dt);
+  if (row >= 0) return lut_s[(row << 5) + lane];
+  return decay_pow(base, __shfl_sync(kFull, x.dt, e));
+}
+
+// The decay factors of the batch's 32 events for this lane's neuron, gathered before the
+// recurrence so that its dependent chain holds no loads.
+__device__ __forceinline__ void load_a(const Batch& x, float base, const float* lut_s, int lane,
+                                       float (&av)[32]) {
+  if (__any_sync(kFull, lane < x.cnt && x.row < 0)) {  // a gap beyond the table: rare
+#pragma unroll
+    for (int e = 0; e < 32; ++e) av[e] = decay_of(x, e, base, lut_s, lane);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int32_t row = __shfl_sync(kFull, x.row, e);
+      av[e] = lut_s[(max(row, 0) << 5) + lane];
+    }
+  }
+}
+
+// The speculative run over one batch: FULL (32 events) needs no per-event bound check; TRACK
+// also follows the first fire and the values before it (only until every lane has fired once).
+// wb[e * 32 + lane] holds event e's weight for this lane's neuron; each event's spike ballot
+// goes to bal_s[e].
+template <bool TRACK, bool FULL, bool GAIN>
+__device__ __forceinline__ void seg_batch(const Batch& x, const float (&av)[32], const float* wb,
+                                          int lane, float vth, int32_t bs, uint32_t* bal_s,
+                                          float& v, int32_t& nspk, float& Ap, float& M, float& u1,
+                                          float& A1, int32_t& k1) {
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    if (FULL || e < x.cnt) {
+      float w = wb[(e << 5) + lane];
+      if (GAIN) w *= __shfl_sync(kFull, x.gain, e);
+      v = fmaf(av[e], v, w);
+      const bool spike = v >= vth;
+      if (TRACK) {
+        Ap *= av[e];
+        const bool before = k1 < 0;
+        M = (before && !spike) ? fmaxf(M, v) : M;
+        const bool first = before && spike;
+        A1 = first ? Ap : A1;
+        u1 = first ? v : u1;
+        k1 = first ? bs + e : k1;
+      }
+      v = spike ? 0.0f : v;
+      nspk += spike;
+      bal_s[e] = __ballot_sync(kFull, spike);
+    }
+  }
+}
+
+// ---- asynchronous weight staging (cp.async)
+__device__ __forceinline__ void cp_async16(float* smem, const float* gmem, int bytes) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem, int bytes) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all_but_one() {
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+}
+
+// Stages the batch's weight slices w[src_e][g*32 .. g*32+31] into wb[e*32 + k], zero for events
+// past cnt and neurons past n_out, as one cp.async group.  VEC moves 16-byte pieces (needs
+// n_out % 4 == 0 so that every piece is 16-byte aligned), otherwise 4-byte ones.
+template <bool VEC>
+__device__ __forceinline__ void stage_w(const FloatLaunch& P, const Raw& r, int cnt, int g,
+                                        float* wb, int lane) {
+  const int o0 = g * 32;
+  if (VEC) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = lane + 32 * i, e = c >> 3, q = (c & 7) << 2;
+      const int32_t s = __shfl_sync(kFull, r.src, e);
+      const int bytes = e < cnt ? max(0, min(16, (P.n_out - o0 - q) * 4)) : 0;
+      cp_async16(wb + e * 32 + q, bytes ? P.wT + (int64_t)s * P.n_out + o0 + q : P.wT, bytes);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int32_t s = __shfl_sync(kFull, r.src, e);
+      const int bytes = (e < cnt && o0 + lane < P.n_out) ? 4 : 0;
+      cp_async4(wb + e * 32 + lane, bytes ? P.wT + (int64_t)s * P.n_out + o0 + lane : P.wT,
+                bytes);
+    }
+  }
+  cp_async_commit();
 }
 
 // The group's decay table rows into shared memory: lut_s[d * 32 + lane].
@@ -186,15 +320,19 @@ __device__ __forceinline__ void segment_bounds(const FloatLaunch& P, int32_t n_e
 
 // ------------------------------------------------------------------ 1. speculative segments
 
-template <bool GAIN>
-__global__ void __launch_bounds__(32 * kFloatSegWarps, 4) ffc_segment(FloatLaunch P) {
+// One warp per block (segment x, group y, sample z): blocks of one warp let the scheduler fill
+// every SM evenly with the single wave of segments the host sized.  One pipelined pass covers
+// the warm-up [jw, j0) and the segment [j0, j1): the weights of batch k + 1 are staged into
+// shared memory (cp.async) and the events of batch k + 2 loaded while batch k runs.
+template <bool GAIN, bool VEC>
+__global__ void __launch_bounds__(32, kFloatSegBlocksPerSM) ffc_segment(FloatLaunch P) {
   __shared__ float lut_s[kFloatLut * 32];
-  const int g = blockIdx.y, b = blockIdx.z;
-  const int lane = threadIdx.x & 31;
-  load_lut(P, g, lut_s, threadIdx.x, blockDim.x);
-  __syncthreads();
-  const int s = blockIdx.x * kFloatSegWarps + (threadIdx.x >> 5);
-  if (s >= P.S) return;
+  __shared__ __align__(16) float wbuf[2][32 * 32];
+  __shared__ uint32_t bal_s[32];
+  const int g = blockIdx.y, b = blockIdx.z, s = blockIdx.x;
+  const int lane = threadIdx.x;
+  load_lut(P, g, lut_s, lane, 32);
+  __syncwarp();
   const int o = g * 32 + lane;
   const bool active = o < P.n_out;
   const float base = active ? P.decay_base[o] : 1.0f;
@@ -202,67 +340,86 @@ __global__ void __launch_bounds__(32 * kFloatSegWarps, 4) ffc_segment(FloatLaunc
   const int32_t n_eff = P.n_eff(b);
   int32_t j0, j1;
   segment_bounds(P, n_eff, s, j0, j1);
-  float tprev = j0 > 0 ? P.in.times[(int64_t)b * P.in.capacity + j0 - 1] : 0.0f;
   uint32_t* swb = P.sw + (int64_t)b * P.sw_stride;
   int32_t* chunk = P.chunk_spikes + (int64_t)b * P.n_spk_chunks;
 
-  float v = 0.0f, Ap = 1.0f, M = -INFINITY, u1 = 0.0f, A1 = 1.0f, psum = 0.0f;
+  // warm-up: from v = 0 over the (at most warm_max, at most half a segment) events before j0
+  const int32_t warm = min(P.warm_max, ((P.seg_len(n_eff) >> 1) + 31) & ~31);
+  const int32_t jw = j1 > j0 ? max(0, j0 - warm) : j0;
+  float tprev = jw > 0 ? P.in.times[(int64_t)b * P.in.capacity + jw - 1] : 0.0f;
+  float v = 0.0f, v_start = 0.0f;
+  float Ap = 1.0f, M = -INFINITY, u1 = 0.0f, A1 = 1.0f, psum = 0.0f;
   int32_t k1 = -1, nspk = 0, pcnt = 0;
   bool mono = true;
-  for (int32_t bs = j0; bs < j1; bs += 32) {
-    const Batch x = load_batch<GAIN>(P, b, bs, j1, tprev, lane);
-    mono &= __all_sync(kFull, lane >= x.cnt || x.dt >= 0.0f);
-    float bv[32];
-    load_b<GAIN>(P, x, o, active, bv);
-    if (GAIN) {
+  if (jw < j1) {
+    Raw r_cur = load_raw<GAIN>(P, b, jw, j1, lane);
+    stage_w<VEC>(P, r_cur, min(32, j1 - jw), g, wbuf[0], lane);
+    Raw r_nxt = load_raw<GAIN>(P, b, jw + 32, j1, lane);
+    int k = 0;
+    for (int32_t bs = jw; bs < j1; bs += 32, ++k) {
+      const Batch x = make_batch(r_cur, bs, j1, tprev, lane);
+      if (bs + 32 < j1)
+        stage_w<VEC>(P, r_nxt, min(32, j1 - bs - 32), g, wbuf[(k + 1) & 1], lane);
+      else
+        cp_async_commit();  // an empty group keeps the wait count uniform
+      const Raw r_after = load_raw<GAIN>(P, b, bs + 64, j1, lane);
+      float av[32];
+      load_a(x, base, lut_s, lane, av);
+      cp_async_wait_all_but_one();
+      __syncwarp();
+      const float* wb = wbuf[k & 1];
+      if (bs == j0) v_start = v;
+      if (bs < j0) {  // warm-up: state only
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        pcnt += bv[e] > 0.0f;
-        psum += fmaxf(bv[e], 0.0f);
-      }
-    }
-    uint32_t mybits = 0;
-    // Until every lane has fired once, also track the first fire and the values before it.
-    if (__any_sync(kFull, active && k1 < 0)) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        if (e < x.cnt) {
-          const float a = decay_of(x, e, base, lut_s, lane);
-          v = fmaf(a, v, bv[e]);
-          Ap *= a;
-          const bool spike = v >= vth;
-          const bool before = k1 < 0;
-          M = (before && !spike) ? fmaxf(M, v) : M;
-          const bool first = before && spike;
-          A1 = first ? Ap : A1;
-          u1 = first ? v : u1;
-          k1 = first ? bs + e : k1;
-          v = spike ? 0.0f : v;
-          nspk += spike;
-          const uint32_t bal = __ballot_sync(kFull, spike);
-          mybits = lane == e ? bal : mybits;
+        for (int e = 0; e < 32; ++e) {
+          if (e < x.cnt) {
+            float w = wb[(e << 5) + lane];
+            if (GAIN) w *= __shfl_sync(kFull, x.gain, e);
+            v = fmaf(av[e], v, w);
+            v = v >= vth ? 0.0f : v;
+          }
         }
-      }
-    } else {
+      } else {
+        mono &= __all_sync(kFull, lane >= x.cnt || x.dt >= 0.0f);
+        if (GAIN) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        if (e < x.cnt) {
-          const float a = decay_of(x, e, base, lut_s, lane);
-          v = fmaf(a, v, bv[e]);
-          const bool spike = v >= vth;
-          v = spike ? 0.0f : v;
-          nspk += spike;
-          const uint32_t bal = __ballot_sync(kFull, spike);
-          mybits = lane == e ? bal : mybits;
+          for (int e = 0; e < 32; ++e) {
+            const float w = wb[(e << 5) + lane] * __shfl_sync(kFull, x.gain, e);
+            pcnt += w > 0.0f;
+            psum += fmaxf(w, 0.0f);
+          }
         }
+        // Until every lane has fired once, also track the first fire and the values before it.
+        const bool track = __any_sync(kFull, active && k1 < 0);
+        if (x.cnt == 32) {
+          if (track)
+            seg_batch<true, true, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1, A1,
+                                        k1);
+          else
+            seg_batch<false, true, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1, A1,
+                                         k1);
+        } else {
+          if (track)
+            seg_batch<true, false, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1, A1,
+                                         k1);
+          else
+            seg_batch<false, false, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1,
+                                          A1, k1);
+        }
+        __syncwarp();
+        const uint32_t mybits = bal_s[lane];
+        if (lane < x.cnt) swb[(int64_t)(bs + lane) * P.G + g] = mybits;
+        const int32_t tot = warp_sum(lane < x.cnt ? __popc(mybits) : 0);
+        if (lane == 0 && tot) atomicAdd(&chunk[bs >> kSpkChunkShift], tot);
       }
+      __syncwarp();  // this buffer is restaged for batch k + 2
+      r_cur = r_nxt;
+      r_nxt = r_after;
     }
-    if (lane < x.cnt) swb[(int64_t)(bs + lane) * P.G + g] = mybits;
-    const int32_t tot = warp_sum(lane < x.cnt ? __popc(mybits) : 0);
-    if (lane == 0 && tot) atomicAdd(&chunk[bs >> kSpkChunkShift], tot);
   }
   if (active) {
     const int64_t r = ((int64_t)b * P.S + s) * P.n_out + o;
+    P.r_vstart[r] = v_start;
     P.r_vend[r] = v;
     P.r_k1[r] = k1;
     P.r_u1[r] = u1;
@@ -303,9 +460,10 @@ __global__ void __launch_bounds__(128) ffc_fixup(FloatLaunch P) {
   double psum = 0.0;
   for (int s = 0; s < P.S; ++s) {
     const int64_t r = ((int64_t)b * P.S + s) * P.n_out + o;
-    float vend = 0.0f, u1 = 0.0f, A1 = 1.0f, M = -INFINITY, Aseg = 1.0f;
+    float vstart = 0.0f, vend = 0.0f, u1 = 0.0f, A1 = 1.0f, M = -INFINITY, Aseg = 1.0f;
     int32_t k1 = -1, nspk = 0;
     if (active) {
+      vstart = P.r_vstart[r];
       vend = P.r_vend[r];
       k1 = P.r_k1[r];
       u1 = P.r_u1[r];
@@ -321,16 +479,17 @@ __global__ void __launch_bounds__(128) ffc_fixup(FloatLaunch P) {
     const bool mono = P.r_mono[(int64_t)b * P.S + s] != 0;
     bool need = false;
     float v_out = vend;
-    if (!active || s == 0 || v_in == 0.0f) {
-      spk += nspk;  // the guess v = 0 was the true incoming state
+    const float d = v_in - vstart;
+    if (!active || v_in == vstart) {
+      spk += nspk;  // the guess was the true incoming state
     } else if (!(base_ok && mono)) {
       need = true;
     } else if (k1 < 0) {
-      if (v_in <= 0.0f || M + v_in < vth - margin)
-        v_out = fmaf(Aseg, v_in, vend);  // no fire in the true run either
+      if (d <= 0.0f || M + d < vth - margin)
+        v_out = fmaf(Aseg, d, vend);  // no fire in the true run either
       else
         need = true;
-    } else if (v_in > 0.0f ? (M + v_in < vth - margin) : (u1 + A1 * v_in >= vth + margin)) {
+    } else if (d > 0.0f ? (M + d < vth - margin) : (u1 + A1 * d >= vth + margin)) {
       spk += nspk;  // the true run fires first at k1 too, and agrees from there on
     } else {
       need = true;
@@ -476,7 +635,8 @@ __global__ void __launch_bounds__(128) ffc_exact(FloatLaunch P) {
     if (e_ != cudaSuccess) return e_;                     \
   } while (0)
 
-cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches) {
+cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches,
+                            cudaEvent_t seg_start, cudaEvent_t seg_stop) {
   const int B = P.batch;
   ffc_transpose<<<dim3((P.n_in + 31) / 32, (P.n_out + 31) / 32), dim3(32, 8), 0, st>>>(
       P.w, P.wT, P.n_out, P.n_in);
@@ -489,21 +649,40 @@ cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* laun
     const int hb = std::min((P.in.capacity + 255) / 256, 64);
     ffc_hist<<<dim3(hb, B), 256, 0, st>>>(P);
     FFC_LAUNCHED();
+    const int split = std::max(1, std::min(P.n_in, 1184 / std::max(1, ((P.n_out + 127) / 128) * B)));
+    ffc_bound_partial<<<dim3((P.n_out + 127) / 128, B, split), 128, 0, st>>>(P);
+    FFC_LAUNCHED();
     ffc_bound<<<dim3((P.n_out + 127) / 128, B), 128, 0, st>>>(P);
     FFC_LAUNCHED();
   }
-  const dim3 sg((P.S + kFloatSegWarps - 1) / kFloatSegWarps, P.G, B);
+  const dim3 sg(P.S, P.G, B);
   const dim3 fg((P.G + 3) / 4, B);
+  if (seg_start) {
+    const cudaError_t e = cudaEventRecord(seg_start, st);
+    if (e != cudaSuccess) return e;
+  }
+  const bool vec = P.n_out % 4 == 0;
+  void* seg = gain ? (vec ? (void*)ffc_segment<true, true> : (void*)ffc_segment<true, false>)
+                   : (vec ? (void*)ffc_segment<false, true> : (void*)ffc_segment<false, false>);
+  // room for kFloatSegBlocksPerSM one-warp blocks of ~12 KB shared memory on every SM
+  cudaError_t ce = cudaFuncSetAttribute(seg, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared);
+  if (ce != cudaSuccess) return ce;
+  FloatLaunch Pc = P;
+  void* args[] = {&Pc};
+  ce = cudaLaunchKernel(seg, sg, dim3(32), args, 0, st);
+  if (ce != cudaSuccess) return ce;
+  FFC_LAUNCHED();
+  if (seg_stop) {
+    const cudaError_t e = cudaEventRecord(seg_stop, st);
+    if (e != cudaSuccess) return e;
+  }
   if (gain) {
-    ffc_segment<true><<<sg, 32 * kFloatSegWarps, 0, st>>>(P);
-    FFC_LAUNCHED();
     ffc_fixup<true><<<fg, 128, 0, st>>>(P);
     FFC_LAUNCHED();
     ffc_exact<true><<<fg, 128, 0, st>>>(P);
     FFC_LAUNCHED();
   } else {
-    ffc_segment<false><<<sg, 32 * kFloatSegWarps, 0, st>>>(P);
-    FFC_LAUNCHED();
     ffc_fixup<false><<<fg, 128, 0, st>>>(P);
     FFC_LAUNCHED();
     ffc_exact<false><<<fg, 128, 0, st>>>(P);

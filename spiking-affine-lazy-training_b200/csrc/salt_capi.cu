@@ -36,6 +36,12 @@ static salt_status fail(salt_status s, const std::string& msg) {
 
 static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Compaction blocks per sample: the per-sample minimum, or enough to fill the GPU when the
+// batch is small.
+static int compact_blocks(int32_t B) {
+  return std::max(kCompactBlocksPerSample, (1184 + B - 1) / std::max(B, 1));
+}
+
 // Sequential carving of a workspace; with base == nullptr it only measures.
 struct Carver {
   char* base;
@@ -374,7 +380,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   if (timer) SALT_CUDA(cudaEventRecord(timer->stop, st));
   spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
   SALT_LAUNCHED("spike_chunk_scan");
-  conv_compact<<<dim3(std::min(p.n_spk_chunks, kCompactBlocksPerSample), B), kCompactThreads, 0,
+  conv_compact<<<dim3(std::min(p.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0,
                  st>>>(L, *out);
   SALT_LAUNCHED("conv_compact");
   if (p.tail_mode) {
@@ -476,7 +482,7 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   if (q->has_vth) {
     spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
     SALT_LAUNCHED("spike_chunk_scan");
-    fc_compact<<<dim3(std::min(L.n_spk_chunks, kCompactBlocksPerSample), B), kCompactThreads, 0,
+    fc_compact<<<dim3(std::min(L.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0,
                  st>>>(L, *out);
     SALT_LAUNCHED("fc_compact");
     fc_truncated<<<B, kCompactThreads, 0, st>>>(L, *out);
@@ -493,21 +499,23 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
 // ---------------------------------------------------------------- float fc
 
 struct FloatScratch {
-  int32_t *stats, *s_total, *needed, *exact, *chunk, *hist, *n_spk;
+  int32_t *stats, *s_total, *needed, *exact, *chunk, *hist, *bcnt, *n_spk;
+  double* bsum;
   size_t stats_bytes;
   float *wT, *lut;
   uint32_t* sw;
-  float *r_vend, *r_u1, *r_A1, *r_M, *r_Aseg, *r_sum;
+  float *r_vstart, *r_vend, *r_u1, *r_A1, *r_M, *r_Aseg, *r_sum;
   int32_t *r_k1, *r_nspk, *r_cnt, *r_mono;
 };
 
-// Time segments per sample: enough (segment, group) warps to fill the GPU, at least 256
-// events per segment so that the in-order fix-up stays short.
+// Time segments per sample: as many (segment, group) warps as fit on the GPU in one wave (148
+// SMs x kFloatSegBlocksPerSM); one segment — a plain in-order scan, no guessing — when neurons x
+// samples already fill it.  Segments hold at least 4096 events so that the warm-up guess stays
+// affordable.
 static int32_t float_segments(int32_t G, int32_t B, int32_t E) {
-  const int64_t target = 148LL * 48;
+  const int64_t wave = 148LL * kFloatSegBlocksPerSM;
   const int64_t per = (int64_t)G * B;
-  const int64_t s = (target + per - 1) / per;
-  return (int32_t)std::max<int64_t>(1, std::min<int64_t>(s, std::max(1, E / 256)));
+  return (int32_t)std::max<int64_t>(1, std::min<int64_t>(wave / per, std::max(1, E / 4096)));
 }
 
 static size_t float_carve(const salt_float_fc_desc* d, int32_t B, int32_t E, bool gain, void* ws,
@@ -515,8 +523,11 @@ static size_t float_carve(const salt_float_fc_desc* d, int32_t B, int32_t E, boo
   Carver c(ws);
   const int G = (d->n_out + 31) / 32, S = float_segments(G, B, E);
   const int nsc = (E + kSpkChunk - 1) / kSpkChunk;
+  // one zeroed block: per-sample counters, flags, chunk counts and (unit gains) the bound's
+  // histogram and per-neuron sums
+  const size_t nb = gain ? 0 : (size_t)B * d->n_out;
   const size_t nstat = (size_t)B * 2 + (size_t)B * G + (size_t)B * nsc +
-                       (gain ? 0 : (size_t)B * d->n_in);
+                       (gain ? 0 : (size_t)B * d->n_in) + nb + 2 * nb + 1;
   s.stats = c.take<int32_t>(nstat);
   s.stats_bytes = nstat * 4;
   if (s.stats) {
@@ -525,12 +536,21 @@ static size_t float_carve(const salt_float_fc_desc* d, int32_t B, int32_t E, boo
     s.exact = s.stats + 2 * B;
     s.chunk = s.exact + (size_t)B * G;
     s.hist = gain ? nullptr : s.chunk + (size_t)B * nsc;
+    s.bcnt = gain ? nullptr : s.hist + (size_t)B * d->n_in;
+    // 8-byte aligned: the block starts 256-aligned and everything before it is 4-byte counts
+    int32_t* dbl = gain ? nullptr : s.bcnt + nb;
+    if (dbl && (reinterpret_cast<uintptr_t>(dbl) & 7)) ++dbl;
+    s.bsum = reinterpret_cast<double*>(dbl);
+  } else {
+    s.hist = s.bcnt = nullptr;
+    s.bsum = nullptr;
   }
   s.wT = c.take<float>((size_t)d->n_in * d->n_out);
   s.lut = c.take<float>((size_t)kFloatLut * d->n_out);
   s.sw = c.take<uint32_t>((size_t)B * E * G);
   s.n_spk = c.take<int32_t>((size_t)B * d->n_out);
   const size_t nr = (size_t)B * S * d->n_out;
+  s.r_vstart = c.take<float>(nr);
   s.r_vend = c.take<float>(nr);
   s.r_u1 = c.take<float>(nr);
   s.r_A1 = c.take<float>(nr);
@@ -568,6 +588,22 @@ __global__ void float_finish(const int32_t* __restrict__ s_total,
   if (st.fits) st.fits[b] = S <= M && need <= max_extra;  // capacity.py:60-63
 }
 
+// Optional per-thread timing of float FC layers: CUDA events around the speculative segment
+// kernel and around the whole layer, summed when read.
+struct FloatProfile {
+  bool on = false;
+  std::vector<cudaEvent_t> seg, layer;  // start/stop pairs, in order
+  double seg_ms = 0, layer_ms = 0;
+  int32_t n = 0;
+};
+static thread_local FloatProfile g_fprof;
+
+static cudaEvent_t timing_event() {
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
 static salt_status float_forward_impl(const salt_float_fc_desc* d, const float* w,
                                       const float* decay_base, int32_t B,
                                       const salt_stream_in* in, const float* gain,
@@ -602,10 +638,21 @@ static salt_status float_forward_impl(const salt_float_fc_desc* d, const float* 
   P.sw = s.sw; P.sw_stride = (int64_t)E * P.G;
   P.chunk_spikes = s.chunk; P.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
   P.s_total = s.s_total; P.needed = s.needed; P.n_spk = s.n_spk; P.exact = s.exact; P.hist = s.hist;
-  P.r_vend = s.r_vend; P.r_u1 = s.r_u1; P.r_A1 = s.r_A1; P.r_M = s.r_M; P.r_Aseg = s.r_Aseg;
+  P.bcnt = s.bcnt; P.bsum = s.bsum; P.warm_max = kFloatWarmMax;
+  P.r_vstart = s.r_vstart; P.r_vend = s.r_vend; P.r_u1 = s.r_u1; P.r_A1 = s.r_A1; P.r_M = s.r_M; P.r_Aseg = s.r_Aseg;
   P.r_sum = s.r_sum; P.r_k1 = s.r_k1; P.r_nspk = s.r_nspk; P.r_cnt = s.r_cnt; P.r_mono = s.r_mono;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};  // layer start/stop, segment start/stop
+  if (g_fprof.on) {
+    for (auto& e : ev)
+      if (!(e = timing_event())) return fail(SALT_CUDA_ERROR, "cudaEventCreate failed");
+    g_fprof.layer.push_back(ev[0]);
+    g_fprof.layer.push_back(ev[1]);
+    g_fprof.seg.push_back(ev[2]);
+    g_fprof.seg.push_back(ev[3]);
+    SALT_CUDA(cudaEventRecord(ev[0], st));
+  }
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
-  SALT_CUDA(float_fc_launch(P, st, &g_launches));
+  SALT_CUDA(float_fc_launch(P, st, &g_launches, ev[2], ev[3]));
 
   // the FC compaction reads the spike words and per-neuron counts in the integer layer's form
   FCLaunch L;
@@ -617,8 +664,8 @@ static salt_status float_forward_impl(const salt_float_fc_desc* d, const float* 
   L.s_total = s.s_total; L.n_spk = s.n_spk; L.tail_mode = 0;
   spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
   SALT_LAUNCHED("spike_chunk_scan");
-  fc_compact<<<dim3(std::min(L.n_spk_chunks, kCompactBlocksPerSample), B), kCompactThreads, 0,
-               st>>>(L, *out);
+  fc_compact<<<dim3(std::min(L.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0, st>>>(
+      L, *out);
   SALT_LAUNCHED("fc_compact");
   fc_truncated<<<B, kCompactThreads, 0, st>>>(L, *out);
   SALT_LAUNCHED("fc_truncated");
@@ -627,6 +674,7 @@ static salt_status float_forward_impl(const salt_float_fc_desc* d, const float* 
                                                 d->max_extra_steps, B, out->n_real,
                                                 stats ? *stats : none);
   SALT_LAUNCHED("float_finish");
+  if (ev[1]) SALT_CUDA(cudaEventRecord(ev[1], st));
   return SALT_OK;
 }
 
@@ -727,6 +775,40 @@ salt_status salt_float_fc_layer_forward(const salt_float_fc_desc* layer, const f
                                         size_t workspace_bytes, void* stream) {
   return float_forward_impl(layer, w, decay_base, batch, in, in_gain, out, v_final, stats,
                             workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+salt_status salt_float_fc_set_profiling(int32_t enable) {
+  g_fprof.on = enable != 0;
+  return SALT_OK;
+}
+
+salt_status salt_float_fc_profile_read(float* segment_ms, float* layer_ms, int32_t* layers,
+                                       int32_t reset) {
+  auto drain = [](std::vector<cudaEvent_t>& v, double& acc) -> cudaError_t {
+    for (size_t i = 0; i + 1 < v.size(); i += 2) {
+      cudaError_t e = cudaEventSynchronize(v[i + 1]);
+      if (e != cudaSuccess) return e;
+      float ms = 0;
+      e = cudaEventElapsedTime(&ms, v[i], v[i + 1]);
+      if (e != cudaSuccess) return e;
+      acc += ms;
+    }
+    for (cudaEvent_t e : v) cudaEventDestroy(e);
+    v.clear();
+    return cudaSuccess;
+  };
+  const int32_t added = (int32_t)(g_fprof.layer.size() / 2);
+  SALT_CUDA(drain(g_fprof.seg, g_fprof.seg_ms));
+  SALT_CUDA(drain(g_fprof.layer, g_fprof.layer_ms));
+  g_fprof.n += added;
+  if (segment_ms) *segment_ms = (float)g_fprof.seg_ms;
+  if (layer_ms) *layer_ms = (float)g_fprof.layer_ms;
+  if (layers) *layers = g_fprof.n;
+  if (reset) {
+    g_fprof.seg_ms = g_fprof.layer_ms = 0;
+    g_fprof.n = 0;
+  }
+  return SALT_OK;
 }
 
 salt_status salt_fc_layer_workspace_size(const salt_fc_desc* layer, const salt_quant_desc* quant,

@@ -118,8 +118,9 @@ struct FCLaunch {
 
 // Float FC layer (float chunked affine scan).  Per-(sample, segment, neuron) records of the
 // speculative pass are laid out [b][s][neuron] so that a warp's 32 lanes touch 128 B.
-constexpr int kFloatLut = 64;  // decay table rows: powf(base, d) for whole d in [0, 64)
-constexpr int kFloatSegWarps = 4;
+constexpr int kFloatLut = 32;  // decay table rows: powf(base, d) for whole d in [0, 32)
+constexpr int kFloatSegBlocksPerSM = 16;  // one-warp blocks resident per SM (128 registers)
+constexpr int kFloatWarmMax = 16384;  // longest warm-up run before a segment
 
 struct FloatLaunch {
   int32_t n_in, n_out, G, S;  // S time segments per sample
@@ -144,7 +145,10 @@ struct FloatLaunch {
   int32_t* n_spk;             // (B, n_out)
   int32_t* exact;             // (B, G) groups that the step limit may cut
   int32_t* hist;              // (B, n_in) real events per source (gain == nullptr only)
-  float *r_vend, *r_u1, *r_A1, *r_M, *r_Aseg, *r_sum;
+  double* bsum;               // (B, n_out) Σ of positive b (gain == nullptr only)
+  int32_t* bcnt;              // (B, n_out) count of positive b (gain == nullptr only)
+  int32_t warm_max;           // longest warm-up run before a segment
+  float *r_vstart, *r_vend, *r_u1, *r_A1, *r_M, *r_Aseg, *r_sum;
   int32_t *r_k1, *r_nspk, *r_cnt, *r_mono;
 
   __device__ __forceinline__ int32_t n_eff(int b) const {
@@ -231,8 +235,10 @@ void* fc_scan_kernel(bool fires, bool saturate);
 cudaError_t fixed_scratch_address(void** ptr);
 
 // Enqueues the float FC layer's kernels up to the final spike words (float_scan.cu); adds the
-// number of launches to *launches.
-cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches);
+// number of launches to *launches.  When given, seg_start/seg_stop are recorded around the
+// speculative segment kernel.
+cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches,
+                            cudaEvent_t seg_start = nullptr, cudaEvent_t seg_stop = nullptr);
 constexpr int kFcThreads = 128;
 
 }  // namespace salt

@@ -89,40 +89,76 @@ def _unit_gains(stream: EventStream) -> bool:
     return bool(np.all(np.where(real, g, 1.0) == 1.0))
 
 
+class FloatLayerPlan:
+    """One float FC layer prepared for repeated batched forwards: weights, decay bases, output
+    buffers and the workspace live on the device; each forward is one C-ABI call on the current
+    stream over a device-resident stream of the planned shape."""
+
+    def __init__(self, layer, w, batch: int, in_capacity: int, *, tau=None, gain: bool = False):
+        require_cuda()
+        self.layer, self.batch, self.capacity, self.gain = layer, int(batch), int(in_capacity), gain
+        self.desc = float_desc(layer)
+        n = int(layer.n_out)
+        self.w = to_device(np.asarray(w, dtype=np.float32).reshape(n, int(layer.n_in)), np.float32)
+        self.base = to_device(decay_base(layer.tau if tau is None else tau, n), np.float32)
+        B, M = self.batch, int(layer.max_out_spikes)
+        self.out_t = torch.empty((B, M), dtype=torch.float32, device="cuda")
+        self.out_s = torch.empty((B, M), dtype=torch.int32, device="cuda")
+        self.out_n = torch.empty((B,), dtype=torch.int32, device="cuda")
+        self.v_final = torch.empty((B, n), dtype=torch.float32, device="cuda")
+        self.stats = torch.zeros((3, B), dtype=torch.int32, device="cuda")
+        self._st = _lib.FloatLayerStats(*[ptr(self.stats[i]) for i in range(3)])
+        self._sout = _lib.StreamOut(ptr(self.out_t), ptr(self.out_s), ptr(self.out_n))
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().salt_float_fc_layer_workspace_size(
+            _lib.byref(self.desc), B, self.capacity, int(gain), _lib.byref(nbytes)))
+        self.ws_bytes = nbytes.value
+        self.ws = workspace(self.ws_bytes)
+
+    def forward_device(self, dstream: DeviceStream, gain: "torch.Tensor | None" = None
+                       ) -> _FloatRun:
+        if (dstream.batch, dstream.capacity) != (self.batch, self.capacity):
+            raise ValueError(f"stream shape {(dstream.batch, dstream.capacity)} does not match the "
+                             f"plan's {(self.batch, self.capacity)}")
+        if (gain is not None) != self.gain:
+            raise ValueError("gain given to a plan built without it, or missing")
+        sin = _lib.StreamIn(ptr(dstream.times), ptr(dstream.src), ptr(dstream.n_real),
+                            self.capacity, int(dstream.virtual_pads))
+        _lib.check(_lib.lib().salt_float_fc_layer_forward(
+            _lib.byref(self.desc), ptr(self.w), ptr(self.base), self.batch, _lib.byref(sin),
+            ptr(gain), _lib.byref(self._sout), ptr(self.v_final), _lib.byref(self._st),
+            ptr(self.ws), self.ws_bytes, current_stream()))
+        return _FloatRun(DeviceStream(self.out_t, self.out_s, self.out_n, True), self.v_final,
+                         self.stats)
+
+
+def set_profiling(enable: bool) -> None:
+    """Time each float layer this thread enqueues (segment kernel and whole layer)."""
+    _lib.check(_lib.lib().salt_float_fc_set_profiling(int(bool(enable))))
+
+
+def profile_read(reset: bool = True) -> tuple[float, float, int]:
+    """(segment kernel ms, whole layer ms, layers timed) summed since the last reset."""
+    seg, lay, n = ctypes.c_float(0), ctypes.c_float(0), ctypes.c_int32(0)
+    _lib.check(_lib.lib().salt_float_fc_profile_read(_lib.byref(seg), _lib.byref(lay),
+                                                     _lib.byref(n), int(bool(reset))))
+    return float(seg.value), float(lay.value), int(n.value)
+
+
 @dataclass(frozen=True)
 class FloatB200Backend:
     """FloatBackend's drop-in for FC layers (forward values) on B200."""
 
+    def compile(self, layer, w, batch: int, in_capacity: int, *, tau=None, gain: bool = False
+                ) -> FloatLayerPlan:
+        return FloatLayerPlan(layer, w, batch, in_capacity, tau=tau, gain=gain)
+
     def forward_layer_device(self, layer, w, dstream: DeviceStream, *, tau=None,
                              gain: "torch.Tensor | None" = None) -> _FloatRun:
         """One batched layer on device-resident streams; gain (B, capacity) or None (ones)."""
-        require_cuda()
-        lib = _lib.lib()
-        d = float_desc(layer)
-        B, E = dstream.batch, dstream.capacity
-        n = int(layer.n_out)
-        w_dev = to_device(np.asarray(w, dtype=np.float32).reshape(n, int(layer.n_in)), np.float32)
-        base_dev = to_device(decay_base(layer.tau if tau is None else tau, n), np.float32)
-        M = int(layer.max_out_spikes)
-        out_t = torch.empty((B, M), dtype=torch.float32, device="cuda")
-        out_s = torch.empty((B, M), dtype=torch.int32, device="cuda")
-        out_n = torch.empty((B,), dtype=torch.int32, device="cuda")
-        v_final = torch.empty((B, n), dtype=torch.float32, device="cuda")
-        stats = torch.zeros((3, B), dtype=torch.int32, device="cuda")
-        sin = _lib.StreamIn(ptr(dstream.times), ptr(dstream.src), ptr(dstream.n_real), E,
-                            int(dstream.virtual_pads))
-        sout = _lib.StreamOut(ptr(out_t), ptr(out_s), ptr(out_n))
-        st = _lib.FloatLayerStats(*[ptr(stats[i]) for i in range(3)])
-        nbytes = ctypes.c_size_t(0)
-        _lib.check(lib.salt_float_fc_layer_workspace_size(_lib.byref(d), B, E,
-                                                          int(gain is not None),
-                                                          _lib.byref(nbytes)))
-        ws = workspace(nbytes.value)
-        _lib.check(lib.salt_float_fc_layer_forward(
-            _lib.byref(d), ptr(w_dev), ptr(base_dev), B, _lib.byref(sin), ptr(gain),
-            _lib.byref(sout), ptr(v_final), _lib.byref(st), ptr(ws), nbytes.value,
-            current_stream()))
-        return _FloatRun(DeviceStream(out_t, out_s, out_n, True), v_final, stats)
+        plan = FloatLayerPlan(layer, w, dstream.batch, dstream.capacity, tau=tau,
+                              gain=gain is not None)
+        return plan.forward_device(dstream, gain)
 
     @staticmethod
     def _host_layer(layer, run: _FloatRun, n_in: np.ndarray):

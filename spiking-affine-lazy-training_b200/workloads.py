@@ -179,7 +179,57 @@ def config4(seed: int = 0, batch: int = 256) -> Workload:
     return Workload(f"config4_deepconv_b{batch}", net, params, times, src, nr)
 
 
-CONFIGS = {1: config1, 2: config2, 3: config3, 4: config4}
+@dataclass
+class FloatWorkload:
+    """A float FC layer over batched streams (configuration 5): weights (n_out, n_in) float32 and
+    a per-neuron tau (the configuration's extension of FCLayer.tau)."""
+    name: str
+    layer: FCLayer
+    w: np.ndarray
+    tau: np.ndarray
+    times: np.ndarray
+    src: np.ndarray
+    n_real: np.ndarray
+
+    @property
+    def batch(self) -> int:
+        return int(self.times.shape[0])
+
+    @property
+    def events(self) -> int:
+        return int(np.minimum(self.n_real, self.times.shape[1]).sum())
+
+
+def config5(seed: int = 0, events: int = 1_000_000, n: int = 4096, chunk: int = 4096,
+            batch: int = 1) -> FloatWorkload:
+    """Float FC n->n, w ~ N(0, 0.05), tau_i ~ U[5, 50], v_th = 1.0, chunk_size 4096, one stream
+    of 10^6 events with src ~ U{0..n-1} and t = sorted U{0..59999} ms; max_extra_steps is the
+    always-enough value (every event consumed).  max_out_spikes starts generous and is sized by
+    size_float_capacity."""
+    rng = np.random.default_rng(seed)
+    w = rng.normal(0.0, 0.05, (n, n)).astype(np.float32)
+    tau = rng.uniform(5.0, 50.0, n)
+    t = np.sort(rng.integers(0, 60000, (batch, events)), axis=1).astype(np.float32)
+    src = rng.integers(0, n, (batch, events)).astype(np.int32)
+    from .capacity import safe_extra_steps
+    layer = FCLayer(name="fc_float", n_in=n, n_out=n, init_k=1.0, tau=20.0, v_th=1.0,
+                    chunk_size=chunk, max_out_spikes=4 * events,
+                    max_extra_steps=safe_extra_steps(events, chunk))
+    return FloatWorkload(f"config5_float_fc{n}_e{events}_b{batch}", layer, w, tau, t, src,
+                         np.full(batch, events, np.int32))
+
+
+def size_float_capacity(wl: FloatWorkload, backend, factor: float = 1.5) -> FloatWorkload:
+    """max_out_spikes = ceil(factor x the largest spike count) after one generous run."""
+    from .device import DeviceStream, to_device
+    ds = DeviceStream(to_device(wl.times, np.float32), to_device(wl.src, np.int32),
+                      to_device(wl.n_real, np.int32), False)
+    run = backend.forward_layer_device(wl.layer, wl.w, ds, tau=wl.tau)
+    need = int(run.stats[0].max().item())
+    return replace(wl, layer=replace(wl.layer, max_out_spikes=max(1, math.ceil(need * factor))))
+
+
+CONFIGS = {1: config1, 2: config2, 3: config3, 4: config4, 5: config5}
 
 
 def candidates_per_event(layer: ConvLayer, src: np.ndarray) -> np.ndarray:
