@@ -226,35 +226,69 @@ __device__ __forceinline__ void load_a(const Batch& x, float base, const float* 
 }
 
 // The speculative run over one batch: FULL (32 events) needs no per-event bound check; TRACK
-// also follows the first fire and the values before it (only until every lane has fired once).
-// wb[e * 32 + lane] holds event e's weight for this lane's neuron; each event's spike ballot
-// goes to bal_s[e].
+// also keeps the decay product Ap and the batch's largest pre-reset value Mb (the exact first
+// fire is recovered afterwards by first_fire).  wb[e * 32 + lane] holds event e's weight for
+// this lane's neuron; bit e of the returned mask says whether this lane fired at event e.
 template <bool TRACK, bool FULL, bool GAIN>
-__device__ __forceinline__ void seg_batch(const Batch& x, const float (&av)[32], const float* wb,
-                                          int lane, float vth, int32_t bs, uint32_t* bal_s,
-                                          float& v, int32_t& nspk, float& Ap, float& M, float& u1,
-                                          float& A1, int32_t& k1) {
+__device__ __forceinline__ uint32_t seg_batch(const Batch& x, const float (&av)[32],
+                                              const float* wb, int lane, float vth, float& v,
+                                              float& Ap, float& Mb) {
+  uint32_t bits = 0;
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
     if (FULL || e < x.cnt) {
       float w = wb[(e << 5) + lane];
       if (GAIN) w *= __shfl_sync(kFull, x.gain, e);
       v = fmaf(av[e], v, w);
-      const bool spike = v >= vth;
       if (TRACK) {
         Ap *= av[e];
-        const bool before = k1 < 0;
-        M = (before && !spike) ? fmaxf(M, v) : M;
-        const bool first = before && spike;
-        A1 = first ? Ap : A1;
-        u1 = first ? v : u1;
-        k1 = first ? bs + e : k1;
+        Mb = fmaxf(Mb, v);
       }
+      const bool spike = v >= vth;
       v = spike ? 0.0f : v;
-      nspk += spike;
-      bal_s[e] = __ballot_sync(kFull, spike);
+      bits |= (uint32_t)spike << e;
     }
   }
+  return bits;
+}
+
+// For lanes whose first fire lies in this batch (first), replays the batch from its start
+// state (v0, A0) up to that fire: the largest value before it joins M, u1 is the value that
+// fired and A1 the decay product up to it.  The replay repeats the same float operations, so
+// it follows the batch's trajectory exactly.
+template <bool GAIN>
+__device__ __forceinline__ void first_fire(const Batch& x, const float (&av)[32], const float* wb,
+                                           int lane, bool first, int estar, float v0, float A0,
+                                           float& M, float& u1, float& A1) {
+  float vv = v0, AA = A0, MM = M;
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    if (e < x.cnt) {
+      float w = wb[(e << 5) + lane];
+      if (GAIN) w *= __shfl_sync(kFull, x.gain, e);
+      vv = fmaf(av[e], vv, w);
+      AA *= av[e];
+      if (first && e < estar) MM = fmaxf(MM, vv);
+      if (first && e == estar) {
+        u1 = vv;
+        A1 = AA;
+      }
+    }
+  }
+  if (first) M = MM;
+}
+
+// 32 x 32 bit transpose across the warp: lane l's bit e becomes lane e's bit l.
+__device__ __forceinline__ uint32_t transpose32(uint32_t x, int lane) {
+  const uint32_t masks[5] = {0x0000ffffu, 0x00ff00ffu, 0x0f0f0f0fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const int j = 16 >> i;
+    const uint32_t m = masks[i];
+    const uint32_t y = __shfl_xor_sync(kFull, x, j);
+    x = (lane & j) ? ((x & ~m) | ((y & ~m) >> j)) : ((x & m) | ((y & m) << j));
+  }
+  return x;
 }
 
 // ---- asynchronous weight staging (cp.async)
@@ -328,7 +362,6 @@ template <bool GAIN, bool VEC>
 __global__ void __launch_bounds__(32, kFloatSegBlocksPerSM) ffc_segment(FloatLaunch P) {
   __shared__ float lut_s[kFloatLut * 32];
   __shared__ __align__(16) float wbuf[2][32 * 32];
-  __shared__ uint32_t bal_s[32];
   const int g = blockIdx.y, b = blockIdx.z, s = blockIdx.x;
   const int lane = threadIdx.x;
   load_lut(P, g, lut_s, lane, 32);
@@ -389,27 +422,30 @@ __global__ void __launch_bounds__(32, kFloatSegBlocksPerSM) ffc_segment(FloatLau
             psum += fmaxf(w, 0.0f);
           }
         }
-        // Until every lane has fired once, also track the first fire and the values before it.
+        // Until every lane has fired once, track the first fire and the values before it.
         const bool track = __any_sync(kFull, active && k1 < 0);
-        if (x.cnt == 32) {
-          if (track)
-            seg_batch<true, true, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1, A1,
-                                        k1);
-          else
-            seg_batch<false, true, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1, A1,
-                                         k1);
-        } else {
-          if (track)
-            seg_batch<true, false, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1, A1,
-                                         k1);
-          else
-            seg_batch<false, false, GAIN>(x, av, wb, lane, vth, bs, bal_s, v, nspk, Ap, M, u1,
-                                          A1, k1);
+        const float v0 = v, A0 = Ap;
+        float Mb = -INFINITY;
+        uint32_t bits;
+        if (x.cnt == 32)
+          bits = track ? seg_batch<true, true, GAIN>(x, av, wb, lane, vth, v, Ap, Mb)
+                       : seg_batch<false, true, GAIN>(x, av, wb, lane, vth, v, Ap, Mb);
+        else
+          bits = track ? seg_batch<true, false, GAIN>(x, av, wb, lane, vth, v, Ap, Mb)
+                       : seg_batch<false, false, GAIN>(x, av, wb, lane, vth, v, Ap, Mb);
+        if (track) {
+          const bool first = k1 < 0 && bits != 0;
+          if (k1 < 0 && bits == 0) M = fmaxf(M, Mb);  // still silent: every value was before
+          if (__any_sync(kFull, first)) {
+            const int estar = __ffs(bits) - 1;
+            first_fire<GAIN>(x, av, wb, lane, first, estar, v0, A0, M, u1, A1);
+            if (first) k1 = bs + estar;
+          }
         }
-        __syncwarp();
-        const uint32_t mybits = bal_s[lane];
-        if (lane < x.cnt) swb[(int64_t)(bs + lane) * P.G + g] = mybits;
-        const int32_t tot = warp_sum(lane < x.cnt ? __popc(mybits) : 0);
+        nspk += __popc(bits);
+        const uint32_t word = transpose32(bits, lane);  // lane e: the group's fires at event e
+        if (lane < x.cnt) swb[(int64_t)(bs + lane) * P.G + g] = word;
+        const int32_t tot = warp_sum(__popc(bits));
         if (lane == 0 && tot) atomicAdd(&chunk[bs >> kSpkChunkShift], tot);
       }
       __syncwarp();  // this buffer is restaged for batch k + 2
@@ -483,7 +519,7 @@ __global__ void __launch_bounds__(128) ffc_fixup(FloatLaunch P) {
     if (!active || v_in == vstart) {
       spk += nspk;  // the guess was the true incoming state
     } else if (!(base_ok && mono)) {
-      need = true;
+      need = true;  // no usable bound: re-run
     } else if (k1 < 0) {
       if (d <= 0.0f || M + d < vth - margin)
         v_out = fmaf(Aseg, d, vend);  // no fire in the true run either

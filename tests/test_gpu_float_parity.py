@@ -39,11 +39,12 @@ def test_float_known_answers_on_gpu(c):
 
 
 def _batch(seed, B, n_in, n_out, E, chunk, extra, t_max, w_sd, M=None, tau=20.0, gain=False,
-           n_real=None, per_neuron_tau=False):
+           n_real=None, per_neuron_tau=False, silent=0):
     rng = np.random.default_rng(seed)
     layer = S.FCLayer(name="f", n_in=n_in, n_out=n_out, init_k=1.0, tau=tau, v_th=1.0,
                       chunk_size=chunk, max_out_spikes=M or 4 * E, max_extra_steps=extra)
     w = rng.normal(0.0, w_sd, (n_out, n_in)).astype(np.float32)
+    w[:silent] = -np.abs(w[:silent])  # inhibited neurons: never fire
     t = np.sort(rng.integers(0, t_max, (B, E)), axis=1).astype(np.float32)
     s = rng.integers(0, n_in, (B, E)).astype(np.int32)
     nr = (rng.integers(E // 2, E + 1, B) if n_real is None else np.asarray(n_real)).astype(np.int32)
@@ -111,6 +112,9 @@ PARITY = [
                            t_max=6000, w_sd=0.12)),
     ("big_gaps_powf", dict(seed=19, B=2, n_in=16, n_out=24, E=500, chunk=8, extra=500,
                            t_max=20000, w_sd=0.6)),
+    # segments longer than the first-fire tracking window, with neurons that never fire
+    ("silent_neurons", dict(seed=20, B=1, n_in=16, n_out=40, E=40000, chunk=128, extra=40000,
+                            t_max=8000, w_sd=0.15, silent=12)),
 ]
 
 
