@@ -1,13 +1,14 @@
-"""CPU oracle for the SALT integer forward — TEST INFRASTRUCTURE ONLY.
+"""CPU oracle for the SALT integer forward and float FC scan — TEST INFRASTRUCTURE ONLY.
 
 ctypes wrapper around ``oracle/libsalt_oracle.so`` (a literal C restatement of the reference's
 JAX integer path, see ``salt_oracle.c``).  Only ``tests/``, ``__graft_entry__.smoke()`` and the
 CPU-baseline leg of ``bench.py`` may import this module; the product path never does.
 
 Parity status: pinned against the reference's own known-answer tests
-(``tests/golden/known_answers.json``, transcribed from ``salt_core/tests/test_*.py``) and against
-fixtures produced by executing the reference's own Python source
-(``tests/golden/make_reference_fixtures.py``).
+(``tests/golden/known_answers.json``, transcribed from ``salt_core/tests/test_*.py``).  The
+reference itself cannot run in this image (it needs JAX), so no reference-generated outputs
+exist; independent restatements (a dense per-neuron conv scan, a float64 event-by-event float
+scan) cross-check the oracle in ``tests/``.
 
 The functions take duck-typed layer/params objects whose attribute names follow the reference
 (``ConvLayer`` fields ic, h_in, w_in, oc, k, s, p, max_queue_len, max_out_spikes,

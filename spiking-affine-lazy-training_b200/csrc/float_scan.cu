@@ -216,12 +216,11 @@ __device__ __forceinline__ void load_a(const Batch& x, float base, const float* 
   if (__any_sync(kFull, lane < x.cnt && x.row < 0)) {  // a gap beyond the table: rare
 #pragma unroll
     for (int e = 0; e < 32; ++e) av[e] = decay_of(x, e, base, lut_s, lane);
-  } else {
+  } else {  // every row is in the table
+    const float* col = lut_s + lane;
+    const int32_t off = x.row << 5;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const int32_t row = __shfl_sync(kFull, x.row, e);
-      av[e] = lut_s[(max(row, 0) << 5) + lane];
-    }
+    for (int e = 0; e < 32; ++e) av[e] = col[__shfl_sync(kFull, off, e)];
   }
 }
 
