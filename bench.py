@@ -56,18 +56,22 @@ def rank_info():
 
 
 def make_workload(config, seed, rank, world, scaling, backend=None, batch=None):
-    import salt_b200 as S
+    """Weak scaling: every rank generates its own batch (seed + rank).  Strong scaling: every
+    rank generates the same global batch and keeps its event-balanced shard of it."""
     from salt_b200 import workloads as W
+    from salt_b200.sharding import balanced_shards, take_shard
     kw = {}
     if config == 3:
-        total = batch or 4096
-        kw["batch"] = total if scaling == "weak" else total // world
+        kw["batch"] = batch or 4096
     if config == 4:
         kw["batch"] = batch or 256
     s = seed + (rank if (scaling == "weak" and world > 1) else 0)
     wl = W.CONFIGS[config](seed=s, **kw)
-    if scaling == "strong" and world > 1 and config in (3,):
-        pass  # each rank generated its own contiguous shard of the global batch
+    if scaling == "strong" and world > 1:
+        sh = balanced_shards(np.minimum(wl.n_real, wl.times.shape[1]), world)
+        t, src, n = take_shard([wl.times, wl.src, wl.n_real], sh, rank)
+        n = np.where(sh.of(rank) == sh.pad_index, 0, n).astype(np.int32)
+        wl = W.Workload(f"{wl.name}_shard{rank}of{world}", wl.network, wl.params, t, src, n)
     if backend is not None:
         if config == 4:
             wl = W.size_capacities(wl, backend, expected_factor=4.0)
@@ -335,9 +339,14 @@ def run_b200(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "int32", "data": "synthetic",
-            "config": {"workload": wl.name, "global_batch": B * world if args.scaling == "weak"
-                       else B * world, "per_rank_batch": B, "events_per_step": int(events_step),
-                       "stream_capacity": E, "parallelism": f"dp{world} (sample sharding)",
+            "config": {"workload": wl.name,
+                       "global_batch": B * world if args.scaling == "weak"
+                       else (args.batch or {3: 4096, 4: 256}.get(args.config, B)),
+                       "per_rank_batch": B, "events_per_step": int(events_step),
+                       "stream_capacity": E,
+                       "parallelism": f"dp{world} (" + ("one batch per rank" if args.scaling ==
+                                                        "weak" else "event-balanced shards of "
+                                                        "one batch") + ")",
                        "capacities": {l.name: dict(l.capacity) for l in layers},
                        "l2": "inputs larger than L2 (per-rank stream "
                              f"{wl.times.nbytes * 2 / 2**20:.0f} MiB > 126 MB), no flush"},
