@@ -12,6 +12,10 @@ from .quant import (MAX_REGISTER_BITS, MAX_SHIFT_BITS, OverflowMode, QuantizedLa
                     RoundMode, build_decay_table_int, delta_t_max, quantize_to_int,
                     round_half_away_from_zero, v_th_to_int)
 from .stream import PAD_TIME, EventStream
+from .io import (QuantizedModel, load_quantized, load_weights, network_from_dict,
+                 network_to_dict, save_quantized, save_weights)
+from .quant_run import (REFERENCE_FIELDS, QuantSplitOutput, check_quantized, quant_forward_split,
+                        reference_arrays, run_until_fits)
 
 
 def __getattr__(name):  # the CUDA-backed objects load the library lazily
@@ -27,7 +31,10 @@ def __getattr__(name):  # the CUDA-backed objects load the library lazily
     raise AttributeError(name)
 
 
-__all__ = ["Capacity", "ConvLayer", "ConvSpec", "EventStream", "FCLayer", "FCSpec", "GrowthPolicy",
+__all__ = ["REFERENCE_FIELDS", "QuantSplitOutput", "QuantizedModel", "check_quantized",
+           "load_quantized", "load_weights", "network_from_dict", "network_to_dict",
+           "quant_forward_split", "reference_arrays", "run_until_fits", "save_quantized",
+           "save_weights", "Capacity", "ConvLayer", "ConvSpec", "EventStream", "FCLayer", "FCSpec", "GrowthPolicy",
            "FloatB200Backend", "FloatLayerResult", "InputEvents", "LayerDiag", "LayerOutput", "MAX_REGISTER_BITS", "MAX_SHIFT_BITS",
            "Network", "NetworkPlan", "OverflowMode", "PAD_TIME", "QuantB200Backend",
            "QuantizedLayerParams", "RoundMode", "build_decay_table_int", "check_layer_connections",
