@@ -138,6 +138,37 @@ salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc *layer,
                                             int32_t *v_final, const salt_layer_stats *stats,
                                             void *stream);
 
+/* ---------------------------------------------------------------- traces
+ * Replace QuantBackend.scan with trace=True (salt_core/quant/backend.py:31-53 ->
+ * run_layer_traced quant/scan.py:83-94) and the event times of salt_core/trace.py:24-60: for
+ * every neuron of every sample, the register after each of its L queue columns (conv: L =
+ * max_queue_len; fc: L = the input stream capacity), whether it fired there and the time of the
+ * column's event (NaN for columns at or past the neuron's real events).  v_steps / spike_mask /
+ * event_ms are (batch, n_neurons, L) or NULL.  per_neuron (optional, each pointer optional,
+ * (batch, n_neurons) each) gives the first overflowing column (-1: none) with the register before
+ * and after it, whether that column fired and its event time — the fields example/quant_run.py
+ * (overflow_events, :191-223) reports — plus the unfitted extremes, v_final and the spike count.
+ * An analysis path: one thread per neuron rebuilds its queue from the stream. */
+typedef struct {
+  int32_t *first_overflow;
+  int32_t *v_before, *v_after;
+  int32_t *spiked;
+  float *time_ms;
+  int32_t *v_min, *v_max;
+  int32_t *v_final, *spike_count;
+} salt_neuron_trace;
+
+salt_status salt_conv_layer_trace(const salt_conv_desc *layer, const salt_quant_desc *quant,
+                                  const int32_t *q, const int32_t *lut, const int32_t *vth,
+                                  int32_t batch, const salt_stream_in *in, int32_t *v_steps,
+                                  uint8_t *spike_mask, float *event_ms,
+                                  const salt_neuron_trace *per_neuron, void *stream);
+salt_status salt_fc_layer_trace(const salt_fc_desc *layer, const salt_quant_desc *quant,
+                                const int32_t *q, const int32_t *lut, const int32_t *vth,
+                                int32_t batch, const salt_stream_in *in, int32_t *v_steps,
+                                uint8_t *spike_mask, float *event_ms,
+                                const salt_neuron_trace *per_neuron, void *stream);
+
 /* ---------------------------------------------------------------- fc layer
  * Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:385-402 calling
  * build_fc_structure connectivity/fc.py:20-33, fc_weight_codes :54-61, QuantBackend.scan,

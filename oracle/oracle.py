@@ -56,7 +56,7 @@ class _LayerOut(ctypes.Structure):
                 ("n_real_out", ctypes.c_int32), ("spike_count", ctypes.c_int32),
                 ("needed_queue", ctypes.c_int32), ("any_overflow", ctypes.c_int32),
                 ("vmin_all", ctypes.c_int32), ("vmax_all", ctypes.c_int32),
-                ("fits", ctypes.c_int32)]
+                ("fits", ctypes.c_int32), ("v_steps", _i32p), ("event_ms", _f32p)]
 
 
 class _LayerSpec(ctypes.Structure):
@@ -245,9 +245,11 @@ class LayerResult(NamedTuple):
     vmin_all: int
     vmax_all: int
     fits: bool
+    v_steps: np.ndarray | None = None   # (n, L) register after each column (trace=True)
+    event_ms: np.ndarray | None = None  # (n, L) time of each column's event, NaN when idle
 
 
-def _run(layer, params, times, src, n_in, round_mode, kind):
+def _run(layer, params, times, src, n_in, round_mode, kind, trace=False):
     keep = []
     t = np.ascontiguousarray(np.asarray(times, dtype=np.float32))
     s = np.ascontiguousarray(np.asarray(src), dtype=np.int32)
@@ -271,6 +273,10 @@ def _run(layer, params, times, src, n_in, round_mode, kind):
     o.v_final, o.vmin, o.vmax = _p(vf, _i32p), _p(lo, _i32p), _p(hi, _i32p)
     o.spike_mask, o.overflowed = _p(mask, _u8p), _p(ovf, _u8p)
     o.out_times, o.out_src = _p(ot, _f32p), _p(osrc, _i32p)
+    vs = np.empty((n, L), np.int32) if trace else None
+    ems = np.empty((n, L), np.float32) if trace else None
+    if trace:
+        o.v_steps, o.event_ms = _p(vs, _i32p), _p(ems, _f32p)
     if kind == "conv":
         g = _conv_geom(layer)
         rc = lib().so_conv_forward(ctypes.byref(g), ctypes.byref(qp), _p(t, _f32p), _p(s, _i32p),
@@ -284,17 +290,18 @@ def _run(layer, params, times, src, n_in, round_mode, kind):
     return LayerResult(vf, lo, hi, mask.astype(bool), ovf.astype(bool), ot[:M], osrc[:M],
                        int(o.n_real_out), int(o.spike_count), int(o.needed_queue),
                        bool(o.any_overflow),
-                       int(o.vmin_all), int(o.vmax_all), bool(o.fits))
+                       int(o.vmin_all), int(o.vmax_all), bool(o.fits), vs, ems)
 
 
-def conv_forward(layer, params, times, src, n_in, round_mode="round") -> LayerResult:
+def conv_forward(layer, params, times, src, n_in, round_mode="round", trace=False
+                 ) -> LayerResult:
     """salt_core/layers/conv.py:209-234 with salt_core/quant/backend.py:31-53."""
-    return _run(layer, params, times, src, n_in, round_mode, "conv")
+    return _run(layer, params, times, src, n_in, round_mode, "conv", trace)
 
 
-def fc_forward(layer, params, times, src, n_in, round_mode="round") -> LayerResult:
+def fc_forward(layer, params, times, src, n_in, round_mode="round", trace=False) -> LayerResult:
     """salt_core/layers/fc.py:385-402 with salt_core/quant/backend.py:31-53."""
-    return _run(layer, params, times, src, n_in, round_mode, "fc")
+    return _run(layer, params, times, src, n_in, round_mode, "fc", trace)
 
 
 def is_conv(layer) -> bool:

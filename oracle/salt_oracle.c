@@ -106,11 +106,27 @@ void so_apply_decay_table(const float *delta_t, int64_t n, const int32_t *lut, i
   }
 }
 
+static void run_layer_traced(const int32_t *a_int, const uint8_t *is_identity,
+                             const int32_t *q_int, const int32_t *vth, int32_t n, int32_t L,
+                             int32_t f_a, int32_t f_V, int32_t i_V, int32_t round_mode,
+                             int32_t overflow_mode, uint8_t *spike_mask, uint8_t *overflowed,
+                             int32_t *v_final, int32_t *vmin, int32_t *vmax, int32_t *v_steps);
+
 /* quant/scan.py:97-132 _run_layer_scan (trace=False): every one of the L columns is applied. */
 void so_run_layer(const int32_t *a_int, const uint8_t *is_identity, const int32_t *q_int,
                   const int32_t *vth, int32_t n, int32_t L, int32_t f_a, int32_t f_V, int32_t i_V,
                   int32_t round_mode, int32_t overflow_mode, uint8_t *spike_mask,
                   uint8_t *overflowed, int32_t *v_final, int32_t *vmin, int32_t *vmax) {
+  run_layer_traced(a_int, is_identity, q_int, vth, n, L, f_a, f_V, i_V, round_mode,
+                   overflow_mode, spike_mask, overflowed, v_final, vmin, vmax, NULL);
+}
+
+/* _run_layer_scan with trace=True (quant/scan.py:83-94): also the register after each column. */
+static void run_layer_traced(const int32_t *a_int, const uint8_t *is_identity,
+                             const int32_t *q_int, const int32_t *vth, int32_t n, int32_t L,
+                             int32_t f_a, int32_t f_V, int32_t i_V, int32_t round_mode,
+                             int32_t overflow_mode, uint8_t *spike_mask, uint8_t *overflowed,
+                             int32_t *v_final, int32_t *vmin, int32_t *vmax, int32_t *v_steps) {
   for (int32_t i = 0; i < n; ++i) {
     int32_t v = 0, lo = 0, hi = 0;
     for (int32_t t = 0; t < L; ++t) {
@@ -123,6 +139,7 @@ void so_run_layer(const int32_t *a_int, const uint8_t *is_identity, const int32_
       if (u > hi) hi = u;
       if (spike_mask) spike_mask[e] = (uint8_t)spk;
       if (overflowed) overflowed[e] = (uint8_t)ovf;
+      if (v_steps) v_steps[e] = v;
     }
     v_final[i] = v;
     vmin[i] = lo;
@@ -440,8 +457,18 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
       }
   uint8_t *mask = out->spike_mask ? out->spike_mask : (uint8_t *)malloc(NL);
   uint8_t *ovf = out->overflowed ? out->overflowed : (uint8_t *)malloc(NL);
-  so_run_layer(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
-               qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax);
+  run_layer_traced(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
+                   qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax,
+                   out->v_steps);
+  if (out->event_ms) /* trace.py:44-60 resolve_ms_conv with pointer = column */
+    for (int32_t o = 0; o < OC; ++o)
+      for (int32_t pos = 0; pos < n_sp; ++pos)
+        for (int32_t col = 0; col < L; ++col) {
+          int64_t j = l2g[(size_t)pos * L + col];
+          if (j > E_len - 1) j = E_len - 1;
+          out->event_ms[((size_t)o * n_sp + pos) * L + col] =
+              col >= nreal[pos] ? (float)NAN : times[j];
+        }
   so_extract_output_events(mask, NULL, n, L, l2g, n_sp, L, times, E_len, g->max_out_spikes,
                            out->out_times, out->out_src, &out->n_real_out);
   out->spike_count = out->n_real_out;
@@ -495,8 +522,13 @@ int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *t
     }
   uint8_t *mask = out->spike_mask ? out->spike_mask : (uint8_t *)malloc(NL);
   uint8_t *ovf = out->overflowed ? out->overflowed : (uint8_t *)malloc(NL);
-  so_run_layer(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
-               qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax);
+  run_layer_traced(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
+                   qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax,
+                   out->v_steps);
+  if (out->event_ms) /* trace.py:24-41 resolve_ms_fc: the column is the global event index */
+    for (int32_t o = 0; o < n; ++o)
+      for (int32_t j = 0; j < L; ++j)
+        out->event_ms[(size_t)o * L + j] = j >= n_in ? (float)NAN : times[j];
   so_extract_output_events(mask, NULL, n, L, NULL, 1, L, times, E_len, g->max_out_spikes,
                            out->out_times, out->out_src, &out->n_real_out);
   out->spike_count = out->n_real_out;

@@ -61,6 +61,11 @@ typedef struct {
   int32_t any_overflow;
   int32_t vmin_all, vmax_all;
   int32_t fits;
+  /* trace (quant/scan.py:83-94 run_layer_traced, trace.py:32-60 resolve_ms_*), may be NULL:
+   *   v_steps  (n_neurons, L) register value after each column (after the reset)
+   *   event_ms (n_neurons, L) time of the column's event, NaN for columns at or past n_real */
+  int32_t *v_steps;
+  float *event_ms;
 } so_layer_out;
 
 /* fixed_point.py:32-44, :47-65, :68-90 */

@@ -53,6 +53,11 @@ class FloatLayerStats(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("spike_count", "needed_extra_steps", "fits")]
 
 
+class NeuronTrace(ctypes.Structure):
+    _fields_ = [(n, _vp) for n in ("first_overflow", "v_before", "v_after", "spiked", "time_ms",
+                                   "v_min", "v_max", "v_final", "spike_count")]
+
+
 class LayerSpec(ctypes.Structure):
     _fields_ = [("kind", _i32), ("conv", ConvDesc), ("fc", FCDesc), ("quant", QuantDesc),
                 ("q_host", _vp), ("lut_host", _vp), ("vth_host", _vp)]
@@ -78,6 +83,9 @@ _SIGS = {
     "salt_network_last_launch_count": (_i32, [_vp]),
     "salt_network_set_profiling": (_i32, [_vp, _i32]),
     "salt_network_profile_read": (_i32, [_vp, _vp, _vp, _vp, _i32]),
+    "salt_conv_layer_trace": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
+                                     _vp]),
+    "salt_fc_layer_trace": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "salt_float_fc_layer_workspace_size": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "salt_float_fc_set_profiling": (_i32, [_i32]),
     "salt_float_fc_profile_read": (_i32, [_vp, _vp, _vp, _i32]),

@@ -188,6 +188,51 @@ class QuantB200Backend:
         # hands their memory to later work on this same stream, which runs after these kernels.
         return _LayerRun(DeviceStream(out_t, out_s, out_n, True), v_final, stats)
 
+    def trace_layer_device(self, layer, params, dstream: DeviceStream, *, dense: bool = True,
+                           per_neuron: bool = True) -> dict:
+        """Per-column trace of one layer over a device stream (salt_conv_layer_trace /
+        salt_fc_layer_trace): dense (B, n, L) v_steps / spike_mask / event_ms and per-neuron
+        first-overflow records, as torch tensors keyed by field name."""
+        require_cuda()
+        lib = _lib.lib()
+        B, E = dstream.batch, dstream.capacity
+        n = layer.n_neurons
+        conv = is_conv(layer)
+        L = int(layer.max_queue_len) if conv else E
+        qd, vth = quant_desc(params, self.round_mode, n)
+        q_dev = to_device(np.asarray(params.q).reshape(layer.weight_shape), np.int32)
+        lut_dev = to_device(np.asarray(params.decay_table_int, dtype=np.int32).reshape(-1),
+                            np.int32) if qd.lut_len else None
+        vth_dev = to_device(vth, np.int32) if vth is not None else None
+        out = {}
+        if dense:
+            out["v_steps"] = torch.empty((B, n, L), dtype=torch.int32, device="cuda")
+            out["spike_mask"] = torch.empty((B, n, L), dtype=torch.uint8, device="cuda")
+            out["event_ms"] = torch.empty((B, n, L), dtype=torch.float32, device="cuda")
+        rec = None
+        if per_neuron:
+            names = [f for f, _ in _lib.NeuronTrace._fields_]
+            for f in names:
+                out[f] = torch.empty((B, n), dtype=torch.float32 if f == "time_ms" else
+                                     torch.int32, device="cuda")
+            rec = _lib.NeuronTrace(*[ptr(out[f]) for f in names])
+        sin = _lib.StreamIn(ptr(dstream.times), ptr(dstream.src), ptr(dstream.n_real), E,
+                            int(dstream.virtual_pads))
+        desc = conv_desc(layer) if conv else fc_desc(layer)
+        fn = lib.salt_conv_layer_trace if conv else lib.salt_fc_layer_trace
+        _lib.check(fn(_lib.byref(desc), _lib.byref(qd), ptr(q_dev), ptr(lut_dev), ptr(vth_dev), B,
+                      _lib.byref(sin), ptr(out.get("v_steps")), ptr(out.get("spike_mask")),
+                      ptr(out.get("event_ms")), _lib.byref(rec) if rec is not None else None,
+                      current_stream()))
+        return out
+
+    @staticmethod
+    def _layer_trace(tr: dict):
+        from .trace import LayerForwardTrace
+        return LayerForwardTrace(spike_mask=tr["spike_mask"].cpu().numpy().astype(bool),
+                                 v_steps=tr["v_steps"].cpu().numpy(),
+                                 event_ms=tr["event_ms"].cpu().numpy())
+
     # ------------------------------------------------------------ host-level API
     @staticmethod
     def _host_layer(layer, run: _LayerRun, n_in: np.ndarray) -> tuple:
@@ -205,13 +250,13 @@ class QuantB200Backend:
 
     def forward_layer(self, layer, params, in_stream: EventStream, *, trace: bool = False
                       ) -> LayerOutput:
-        """ConvLayer.forward / FCLayer.forward with QuantBackend (batched or single sample)."""
-        if trace:
-            raise NotImplementedError("trace=True (per-step register trajectories) is not part of "
-                                      "the fused B200 pipeline")
+        """ConvLayer.forward / FCLayer.forward with QuantBackend (batched or single sample).
+        trace=True adds the per-column trajectories (LayerForwardTrace) from the trace kernels."""
         single = np.ndim(in_stream.event_times) == 1
         dstream = DeviceStream.from_host(in_stream)
         run = self.forward_layer_device(layer, params, dstream)
+        tr = self._layer_trace(self.trace_layer_device(layer, params, dstream, per_neuron=False)
+                               ) if trace else None
         n_in = np.atleast_1d(np.asarray(in_stream.n_real_events)).astype(np.int64)
         result, diag, _ = self._host_layer(layer, run, n_in)
         stream = run.out.to_host()
@@ -221,18 +266,22 @@ class QuantB200Backend:
                              {k: v[0] for k, v in diag.needed.items()})
             stream = EventStream(stream.event_times[0], stream.event_source_idx[0],
                                  stream.event_gain[0], stream.n_real_events[0])
-        return LayerOutput(stream=stream, result=result, diag=diag, trace=None)
+            if tr is not None:
+                tr = type(tr)(*(f[0] for f in tr))
+        return LayerOutput(stream=stream, result=result, diag=diag, trace=tr)
 
     def run_network(self, layers, weights, input_stream: EventStream, *, trace: bool = False,
                     keep_streams: bool = False) -> NetworkOutput:
-        """network.py:193-222 on the device; intermediate streams never leave the GPU."""
-        if trace:
-            raise NotImplementedError("trace=True is not part of the fused B200 pipeline")
+        """network.py:193-222 on the device; intermediate streams never leave the GPU.
+        trace=True also returns each layer's LayerForwardTrace (network.py:93-122)."""
         single = np.ndim(input_stream.event_times) == 1
         cur = DeviceStream.from_host(input_stream)
-        runs, n_ins = [], []
+        runs, n_ins, traces = [], [], []
         n_in = np.atleast_1d(np.asarray(input_stream.n_real_events)).astype(np.int64)
         for layer, p in zip(layers, weights):
+            if trace:
+                traces.append(self._layer_trace(self.trace_layer_device(layer, p, cur,
+                                                                        per_neuron=False)))
             run = self.forward_layer_device(layer, p, cur)
             runs.append((run, n_in, run.out if keep_streams else None))
             cur = run.out
@@ -247,13 +296,15 @@ class QuantB200Backend:
             fits = f if fits is None else (fits & f)
             if keep is not None:
                 streams.append(keep.to_host())
-        out = NetworkOutput(tuple(results), tuple(diags), None, fits, tuple(streams))
+        out = NetworkOutput(tuple(results), tuple(diags), tuple(traces) if trace else None, fits,
+                            tuple(streams))
         if single:
             out = NetworkOutput(
                 tuple(QuantLayerResult(*(np.asarray(f)[0] for f in r)) for r in out.results),
                 tuple(LayerDiag(d.spike_count[0], d.firing_rate[0],
                                 {k: v[0] for k, v in d.needed.items()}) for d in out.diags),
-                None, out.fits[0],
+                tuple(type(t)(*(f[0] for f in t)) for t in traces) if trace else None,
+                out.fits[0],
                 tuple(EventStream(s.event_times[0], s.event_source_idx[0], s.event_gain[0],
                                   s.n_real_events[0]) for s in out.streams))
         return out

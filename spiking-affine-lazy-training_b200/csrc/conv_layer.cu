@@ -274,7 +274,9 @@ conv_fused(ConvLaunch P) {
         k.ox_hi = min(k.ox_hi, ox0 + tw - 1);
       }
       // one candidate slot per round; lanes hitting the same position share one mask word,
-      // written by the group's first lane (no other warp writes this word)
+      // written by the group's first lane (no other warp writes this word).  Different lanes
+      // may lead the same position in different rounds, and the match gives no memory order
+      // between them, so the update is an atomic OR.
       const int wrd = e0 >> 5;
       for (int a = 0; a < P.ncand; ++a)
         for (int bb = 0; bb < P.ncand; ++bb) {
@@ -282,7 +284,7 @@ conv_fused(ConvLaunch P) {
           const bool ok = in && oy >= k.oy_lo && oy <= k.oy_hi && ox >= k.ox_lo && ox <= k.ox_hi;
           const int pl = ok ? (oy - oy0) * P.tile_w + (ox - ox0) : -1;
           const uint32_t same = __match_any_sync(0xffffffffu, pl);
-          if (ok && (__ffs(same) - 1) == lane) mask_s[pl * CHW + wrd] |= same;
+          if (ok && (__ffs(same) - 1) == lane) atomicOr(&mask_s[pl * CHW + wrd], same);
         }
     }
     __syncthreads();

@@ -756,6 +756,62 @@ salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc* layer,
                            (cudaStream_t)stream);
 }
 
+salt_status salt_conv_layer_trace(const salt_conv_desc* d, const salt_quant_desc* q,
+                                  const int32_t* qw, const int32_t* lut, const int32_t* vth,
+                                  int32_t B, const salt_stream_in* in, int32_t* v_steps,
+                                  uint8_t* spike_mask, float* event_ms,
+                                  const salt_neuron_trace* per_neuron, void* stream) {
+  salt_status rc = check_quant(q);
+  if (rc) return rc;
+  if ((rc = check_stream_in(in, B))) return rc;
+  if (!d || d->ic < 1 || d->oc < 1 || d->k < 1 || d->s < 1 || d->p < 0 || d->h_in < 1 ||
+      d->w_in < 1 || d->max_queue_len < 1)
+    return fail(SALT_BAD_ARG, "conv trace: bad geometry or max_queue_len");
+  const int32_t h_out = (d->h_in + 2 * d->p - d->k) / d->s + 1;
+  const int32_t w_out = (d->w_in + 2 * d->p - d->k) / d->s + 1;
+  if (h_out < 1 || w_out < 1) return fail(SALT_BAD_ARG, "conv trace: empty output plane");
+  if (!qw || (q->lut_len > 0 && !lut) || (q->has_vth && !vth))
+    return fail(SALT_BAD_ARG, "conv trace: NULL parameter pointer");
+  ConvLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.ic = d->ic; L.h_in = d->h_in; L.w_in = d->w_in; L.hw_in = d->h_in * d->w_in;
+  L.oc = d->oc; L.k = d->k; L.s = d->s; L.p = d->p;
+  L.h_out = h_out; L.w_out = w_out; L.n_sp = h_out * w_out;
+  L.n_neurons = (int64_t)d->oc * h_out * w_out;
+  L.L = d->max_queue_len;
+  L.in.times = in->times; L.in.src = in->src; L.in.capacity = in->capacity;
+  L.in.virtual_pads = in->virtual_pads;
+  L.in_nreal = in->n_real; L.batch = B;
+  L.q = qw; L.lut = lut; L.vth = vth; L.has_vth = q->has_vth != 0; L.qc = make_qc(q);
+  SALT_CUDA(conv_trace_launch(L, per_neuron, v_steps, spike_mask, event_ms, (cudaStream_t)stream));
+  ++g_launches;
+  return SALT_OK;
+}
+
+salt_status salt_fc_layer_trace(const salt_fc_desc* d, const salt_quant_desc* q, const int32_t* qw,
+                                const int32_t* lut, const int32_t* vth, int32_t B,
+                                const salt_stream_in* in, int32_t* v_steps, uint8_t* spike_mask,
+                                float* event_ms, const salt_neuron_trace* per_neuron,
+                                void* stream) {
+  salt_status rc = check_quant(q);
+  if (rc) return rc;
+  if ((rc = check_stream_in(in, B))) return rc;
+  if ((rc = check_fc(d))) return rc;
+  if (!qw || (q->lut_len > 0 && !lut) || (q->has_vth && !vth))
+    return fail(SALT_BAD_ARG, "fc trace: NULL parameter pointer");
+  FCLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.n_in = d->n_in; L.n_out = d->n_out; L.G = (d->n_out + 31) / 32;
+  L.in.times = in->times; L.in.src = in->src; L.in.capacity = in->capacity;
+  L.in.virtual_pads = in->virtual_pads;
+  L.in_nreal = in->n_real; L.batch = B;
+  L.qT = qw;  // the trace kernel reads the caller's (n_out, n_in) layout
+  L.lut = lut; L.vth = vth; L.has_vth = q->has_vth != 0; L.qc = make_qc(q);
+  SALT_CUDA(fc_trace_launch(L, per_neuron, v_steps, spike_mask, event_ms, (cudaStream_t)stream));
+  ++g_launches;
+  return SALT_OK;
+}
+
 salt_status salt_float_fc_layer_workspace_size(const salt_float_fc_desc* layer, int32_t batch,
                                                int32_t in_capacity, int32_t has_gain,
                                                size_t* bytes) {

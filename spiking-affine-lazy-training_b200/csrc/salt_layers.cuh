@@ -234,6 +234,12 @@ void* fc_scan_kernel(bool fires, bool saturate);
 // Device address of the fixed scratch behind salt_conv_layer_forward_noalloc (fixed_scratch.cu).
 cudaError_t fixed_scratch_address(void** ptr);
 
+// Per-column traces of the integer scan (trace.cu).
+cudaError_t conv_trace_launch(const ConvLaunch& P, const salt_neuron_trace* rec, int32_t* v_steps,
+                              uint8_t* spike_mask, float* event_ms, cudaStream_t st);
+cudaError_t fc_trace_launch(const FCLaunch& P, const salt_neuron_trace* rec, int32_t* v_steps,
+                            uint8_t* spike_mask, float* event_ms, cudaStream_t st);
+
 // Enqueues the float FC layer's kernels up to the final spike words (float_scan.cu); adds the
 // number of launches to *launches.  When given, seg_start/seg_stop are recorded around the
 // speculative segment kernel.

@@ -131,3 +131,103 @@ def check_quantized(model_path, reference_path, raw: InputEvents, batch_size: in
                               backend=backend)
     diffs = check_against_reference(out, reference)
     return int(any(len(v) for v in diffs.values())), diffs
+
+
+# ---------------------------------------------------------------- overflow analysis
+# example/quant_run.py:134-258
+
+MAX_OVERFLOW_EVENTS = 50
+
+
+def with_extra_i_V(params, extra: list[int]) -> list:
+    """example/quant_run.py:138-140: each layer's i_V plus extra[i] bits."""
+    return [p._replace(i_V=p.i_V + e) for p, e in zip(params, extra)]
+
+
+def headroom_bits(params, out: QuantSplitOutput) -> list[float | None]:
+    """example/quant_run.py:143-155: bits between each layer's unfitted extremes and its
+    register range (negative: overflow); None when every value was 0."""
+    import math
+    res = []
+    for i, p in enumerate(params):
+        peak = max(-int(out.v_unfitted_min[:, i].min()), int(out.v_unfitted_max[:, i].max()) + 1)
+        res.append(None if peak <= 0 else round(p.i_V + p.f_V - 1 - math.log2(peak), 3))
+    return res
+
+
+def min_extra_bits(network: Network, params, round_mode, raw: InputEvents, batch_size: int,
+                   policies: dict | None, out: QuantSplitOutput, *, backend=None
+                   ) -> tuple[list[int], int]:
+    """example/quant_run.py:158-176: widen the most upstream overflowing layer by one bit and
+    rerun until no sample overflows.  Returns (extra bits per layer, reruns)."""
+    extra = [0] * len(params)
+    rounds = 0
+    while out.overflowed.any():
+        extra[int(np.argmax(out.overflowed.any(axis=0)))] += 1
+        _, out, _ = run_until_fits(network, with_extra_i_V(params, extra), round_mode, raw,
+                                   batch_size, policies, backend=backend)
+        rounds += 1
+    return extra, rounds
+
+
+def _neuron_position(layer, neuron: int) -> tuple[int, int, int]:
+    shape = layer.unflatten_neurons(np.zeros(layer.n_neurons)).shape
+    return tuple(int(v) for v in np.unravel_index(neuron, shape))
+
+
+def overflow_events(network: Network, params, round_mode, raw: InputEvents,
+                    out: QuantSplitOutput, *, backend=None) -> list[dict]:
+    """example/quant_run.py:185-223: for each overflowing (sample, layer, neuron), its first
+    overflowing column — the time, the register before and after it, whether it fired — and the
+    neuron's unfitted extremes; at most MAX_OVERFLOW_EVENTS entries.  Each overflowing sample
+    runs once more on the GPU with the layer traces' per-neuron records."""
+    from .backend import QuantB200Backend
+    from .device import DeviceStream
+    backend = backend or QuantB200Backend(round_mode)
+    layers = list(network.layers)
+    events = []
+    for i in np.nonzero(out.overflowed.any(axis=1))[0]:
+        i = int(i)
+        one = InputEvents(np.asarray(raw.event_times)[i:i + 1], np.asarray(raw.source_idx)[i:i + 1],
+                          np.asarray(raw.n_real_events)[i:i + 1])
+        cur = DeviceStream.from_host(network.input_stream(one))
+        for layer, p in zip(layers, params):
+            tr = backend.trace_layer_device(layer, p, cur, dense=False)
+            first = tr["first_overflow"][0].cpu().numpy()
+            rec = {k: tr[k][0].cpu().numpy() for k in ("v_before", "v_after", "spiked", "time_ms",
+                                                        "v_min", "v_max")}
+            half = 2 ** (p.i_V + p.f_V - 1)
+            for neuron in np.nonzero(first >= 0)[0]:
+                ch, y, x = _neuron_position(layer, int(neuron))
+                events.append({"sample": i, "layer": layer.name, "channel": ch, "y": y, "x": x,
+                               "time_ms": float(rec["time_ms"][neuron]),
+                               "v_before": int(rec["v_before"][neuron]),
+                               "v_after": int(rec["v_after"][neuron]),
+                               "spiked": bool(rec["spiked"][neuron]),
+                               "true_min": int(rec["v_min"][neuron]),
+                               "true_max": int(rec["v_max"][neuron]),
+                               "register_range": [-half, half - 1]})
+                if len(events) >= MAX_OVERFLOW_EVENTS:
+                    return events
+            cur = backend.forward_layer_device(layer, p, cur).out
+    return events
+
+
+def overflow_summary(network: Network, params, round_mode, raw: InputEvents, batch_size: int,
+                     policies: dict | None, out: QuantSplitOutput, *, backend=None) -> dict:
+    """example/quant_run.py:226-258: overflowing samples per layer and headroom; without
+    saturating layers also the fewest extra bits and where the overflows happen."""
+    from .quant import OverflowMode
+    names = [l.name for l in network.layers]
+    summary = {"overflowed_samples": {n: int(out.overflowed[:, i].sum())
+                                      for i, n in enumerate(names)},
+               "headroom_bits": dict(zip(names, headroom_bits(params, out)))}
+    if any(OverflowMode(getattr(p, "overflow_mode", "wrap")) is OverflowMode.SATURATE
+           for p in params):
+        return summary
+    extra, rounds = min_extra_bits(network, params, round_mode, raw, batch_size, policies, out,
+                                   backend=backend)
+    return {**summary, "min_extra_bits": dict(zip(names, extra)),
+            "min_extra_bits_rounds": rounds,
+            "overflow_events": overflow_events(network, params, round_mode, raw, out,
+                                               backend=backend)}

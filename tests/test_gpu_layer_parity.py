@@ -47,6 +47,8 @@ CONV_GEOMS = [  # (ic, h, w, oc, k, s, p)
     (2, 8, 8, 48, 3, 2, 1),
     (1, 6, 5, 64, 2, 2, 0),
     (2, 9, 9, 5, 4, 3, 1),
+    (3, 9, 7, 5, 5, 1, 2),   # 5 candidate positions per axis
+    (2, 8, 8, 4, 4, 1, 1),   # 4 per axis
 ]
 
 

@@ -38,7 +38,8 @@ def test_struct_layouts_match_the_header(tmp_path):
                "salt_fc_desc": _lib.FCDesc, "salt_stream_in": _lib.StreamIn,
                "salt_stream_out": _lib.StreamOut, "salt_layer_stats": _lib.LayerStats,
                "salt_layer_spec": _lib.LayerSpec, "salt_float_fc_desc": _lib.FloatFCDesc,
-               "salt_float_layer_stats": _lib.FloatLayerStats}
+               "salt_float_layer_stats": _lib.FloatLayerStats,
+               "salt_neuron_trace": _lib.NeuronTrace}
     src = tmp_path / "sizes.c"
     src.write_text('#include <stdio.h>\n#include "salt_b200.h"\nint main(void){\n' + "".join(
         f'printf("{n} %zu\\n", sizeof({n}));\n' for n in structs) + "return 0;}\n")
