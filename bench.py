@@ -290,24 +290,24 @@ def run_b200(args):
     events_step = float(ev_all.item())
     value = events_step / (ms_max / 1000.0)
 
-    # ---- end to end through the public API with host buffers (pinned), per step:
-    # H2D of the batch, the forward (+ all-gather), D2H of the logits and fits.
+    # ---- end to end through the public API with host buffers (pinned), per step: the
+    # pipelined plan copies each sub-batch's real events host -> device while the previous
+    # sub-batch computes, and returns the logits and fits to the host; N > 1 also all-gathers
+    # the logits.
+    from salt_b200.plan import PipelinedForward
     t_h = torch.from_numpy(wl.times).pin_memory()
     s_h = torch.from_numpy(wl.src).pin_memory()
     n_h = torch.from_numpy(wl.n_real).pin_memory()
-    logits_h = torch.empty((B, n_out), dtype=torch.int32).pin_memory()
-    fits_h = torch.empty((B,), dtype=torch.int32).pin_memory()
+    chunks = 4 if B % 4 == 0 else 1
+    pf = PipelinedForward(layers, params, B, E, chunks=chunks)
+    logits_d = torch.empty((B, n_out), dtype=torch.int32, device="cuda")
     e2e_steps = max(1, min(args.steps, 20))
 
     def e2e_step():
-        t_d.copy_(t_h, non_blocking=True)
-        s_d.copy_(s_h, non_blocking=True)
-        n_d.copy_(n_h, non_blocking=True)
-        logits, _, fits = plan.forward_device(t_d, s_d, n_d)
+        logits_h, _ = pf(t_h, s_h, n_h)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, logits)
-        logits_h.copy_(logits, non_blocking=True)
-        fits_h.copy_(fits, non_blocking=True)
+            logits_d.copy_(logits_h, non_blocking=True)
+            dist.all_gather_into_tensor(gathered, logits_d)
 
     e2e_step()
     barrier()
@@ -322,8 +322,9 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_value = events_step / (float(e2e_ms.item()) / 1000.0)
-    h2d = int(t_h.numel() * 4 + s_h.numel() * 4 + n_h.numel() * 4)
-    d2h = int(logits_h.numel() * 4 + fits_h.numel() * 4)
+    h2d = pf.h2d_bytes(wl.n_real)
+    d2h = int(pf.logits.numel() * 4 + pf.fits.numel() * 4)
+    pf.close()
 
     # ---- roofline of the dominant kernel (the fused bucket+scan kernel of the busiest layer)
     dom = int(np.argmax(fused_ms))
@@ -362,7 +363,9 @@ def run_b200(args):
                          "note": "integer-ALU bound recurrence; see profiles/ for the "
                                  "integer-pipe utilisation"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "path": f"PipelinedForward, {chunks} sub-batches, real events only"
+                            + (" (whole rows)" if pf.full_rows else "")},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks.summary(),
         }

@@ -276,6 +276,19 @@ salt_status salt_float_fc_layer_forward(const salt_float_fc_desc *layer, const f
                                         const salt_float_layer_stats *stats, void *workspace,
                                         size_t workspace_bytes, void *stream);
 
+/* ---------------------------------------------------------------- stream transfer
+ * No reference counterpart (the reference's input lives in XLA buffers): copies a batch of event
+ * streams from PINNED host memory to the device, moving each sample's row only up to
+ * min(n_real, capacity).  host_times / host_src: (batch, host_pitch) rows in page-locked memory
+ * (cudaHostAlloc / cudaMallocHost / cudaHostRegister; rejected with SALT_BAD_ARG otherwise);
+ * n_real: (batch) DEVICE array (copy it first); dev_times / dev_src: (batch, capacity) device
+ * rows, whose pad entries are left as they were.  Exact whenever no layer reads pad entries: true
+ * unless the first layer has needs_tail set (then copy the full rows instead). */
+salt_status salt_stream_h2d_real(const float *host_times, const int32_t *host_src,
+                                 int64_t host_pitch, const int32_t *n_real, int32_t batch,
+                                 int32_t capacity, float *dev_times, int32_t *dev_src,
+                                 void *stream);
+
 /* Optional timing of the float FC layers that the calling thread enqueues: with profiling on,
  * CUDA events are recorded on the launching stream around each layer's speculative segment
  * kernel (the dominant kernel) and around the whole layer.  salt_float_fc_profile_read

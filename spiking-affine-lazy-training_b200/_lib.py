@@ -86,6 +86,7 @@ _SIGS = {
     "salt_conv_layer_trace": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
                                      _vp]),
     "salt_fc_layer_trace": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "salt_stream_h2d_real": (_i32, [_vp, _vp, ctypes.c_int64, _vp, _i32, _i32, _vp, _vp, _vp]),
     "salt_float_fc_layer_workspace_size": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "salt_float_fc_set_profiling": (_i32, [_i32]),
     "salt_float_fc_profile_read": (_i32, [_vp, _vp, _vp, _i32]),

@@ -474,12 +474,15 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   L.s_total = s.s_total; L.vmin = s.vmin; L.vmax = s.vmax; L.ovf = s.ovf; L.n_spk = s.n_spk;
   L.tail_mode = q->has_vth && q->needs_tail;
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
-  const int64_t warps = (int64_t)B * L.G;
+  // narrow layers (the membrane readouts) pack several samples into a warp
+  const int lpu = d->n_out <= 8 ? 8 : (d->n_out <= 16 ? 16 : 32);
+  const int64_t warps = ((int64_t)B * L.G + 32 / lpu - 1) / (32 / lpu);
   const int wpb = kFcThreads / 32;
   const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
   void* scan_args[] = {&L};
-  SALT_CUDA(cudaLaunchKernel(fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE), dim3(grid), dim3(kFcThreads),
-                             scan_args, 0, st));
+  SALT_CUDA(cudaLaunchKernel(
+      fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu), dim3(grid),
+      dim3(kFcThreads), scan_args, 0, st));
   SALT_LAUNCHED("fc_scan");
   if (q->has_vth) {
     spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
@@ -810,6 +813,29 @@ salt_status salt_fc_layer_trace(const salt_fc_desc* d, const salt_quant_desc* q,
   L.qT = qw;  // the trace kernel reads the caller's (n_out, n_in) layout
   L.lut = lut; L.vth = vth; L.has_vth = q->has_vth != 0; L.qc = make_qc(q);
   SALT_CUDA(fc_trace_launch(L, per_neuron, v_steps, spike_mask, event_ms, (cudaStream_t)stream));
+  ++g_launches;
+  return SALT_OK;
+}
+
+salt_status salt_stream_h2d_real(const float* host_times, const int32_t* host_src,
+                                 int64_t host_pitch, const int32_t* n_real, int32_t batch,
+                                 int32_t capacity, float* dev_times, int32_t* dev_src,
+                                 void* stream) {
+  if (!host_times || !host_src || !n_real || !dev_times || !dev_src)
+    return fail(SALT_BAD_ARG, "stream transfer: NULL pointer");
+  if (batch < 1 || batch > 65535 || capacity < 1 || host_pitch < capacity)
+    return fail(SALT_BAD_ARG, "stream transfer: bad batch, capacity or pitch");
+  // the host rows must be page-locked and mapped into the device address space
+  void* dt = nullptr;
+  void* ds = nullptr;
+  if (cudaHostGetDevicePointer(&dt, const_cast<float*>(host_times), 0) != cudaSuccess ||
+      cudaHostGetDevicePointer(&ds, const_cast<int32_t*>(host_src), 0) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SALT_BAD_ARG, "stream transfer: host rows are not pinned, mapped memory");
+  }
+  SALT_CUDA(gather_rows_launch(static_cast<const float*>(dt), static_cast<const int32_t*>(ds),
+                               n_real, batch, capacity, host_pitch, dev_times, dev_src,
+                               (cudaStream_t)stream));
   ++g_launches;
   return SALT_OK;
 }

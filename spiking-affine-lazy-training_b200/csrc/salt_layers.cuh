@@ -229,10 +229,16 @@ __global__ void fc_truncated(FCLaunch P, salt_stream_out out);
 void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate);
 // Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
-void* fc_scan_kernel(bool fires, bool saturate);
+// lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons.
+void* fc_scan_kernel(bool fires, bool saturate, int lpu);
 
 // Device address of the fixed scratch behind salt_conv_layer_forward_noalloc (fixed_scratch.cu).
 cudaError_t fixed_scratch_address(void** ptr);
+
+// Real-event rows of pinned host streams into device streams (stream_io.cu).
+cudaError_t gather_rows_launch(const float* ht, const int32_t* hs, const int32_t* n_real_dev,
+                               int32_t batch, int32_t capacity, int64_t host_pitch, float* dt,
+                               int32_t* ds, cudaStream_t st);
 
 // Per-column traces of the integer scan (trace.cu).
 cudaError_t conv_trace_launch(const ConvLaunch& P, const salt_neuron_trace* rec, int32_t* v_steps,

@@ -103,3 +103,76 @@ class NetworkPlan:
             self.close()
         except Exception:
             pass
+
+
+class PipelinedForward:
+    """Host in, host out, with the transfers overlapped: the batch runs as `chunks` sub-batches
+    on a NetworkPlan of batch/chunks samples; while sub-batch k computes on the current stream,
+    sub-batch k+1 is copied on a second stream into the other of two device buffers.  Each
+    sample's row is copied only up to its n_real (salt_stream_h2d_real) unless the first layer
+    may fire on pad entries (needs_tail), in which case whole rows are copied.
+
+    Host arrays must be pinned torch tensors: times (B, E) float32, src (B, E) int32, n_real
+    (B,) int32.  Returns pinned (logits (B, n_out) int32, fits (B,) int32) filled in place; with
+    sync=False the call returns once everything is enqueued, and the buffers hold the results
+    when the current stream reaches the end of the call (the next call reuses them)."""
+
+    def __init__(self, layers, weights, batch: int, in_capacity: int, chunks: int = 4,
+                 round_mode="round"):
+        require_cuda()
+        if batch % chunks:
+            raise ValueError(f"batch {batch} is not a multiple of chunks {chunks}")
+        self.batch, self.chunks, self.sub = int(batch), int(chunks), int(batch) // int(chunks)
+        self.capacity = int(in_capacity)
+        self.plan = NetworkPlan(layers, weights, self.sub, self.capacity, round_mode)
+        qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
+        self.full_rows = bool(qd.needs_tail)
+        E, sub = self.capacity, self.sub
+        self._t = [torch.empty((sub, E), dtype=torch.float32, device="cuda") for _ in range(2)]
+        self._s = [torch.empty((sub, E), dtype=torch.int32, device="cuda") for _ in range(2)]
+        self._n = [torch.empty((sub,), dtype=torch.int32, device="cuda") for _ in range(2)]
+        self._copy = torch.cuda.Stream()
+        self._ready = [torch.cuda.Event() for _ in range(2)]
+        self._free = [torch.cuda.Event() for _ in range(2)]
+        self._used = [False, False]   # buffer i was handed to a forward (this or an earlier call)
+        self.logits = torch.empty((batch, self.plan.n_out), dtype=torch.int32).pin_memory()
+        self.fits = torch.empty((batch,), dtype=torch.int32).pin_memory()
+
+    def h2d_bytes(self, n_real_host) -> int:
+        """Bytes one call moves host -> device for these event counts."""
+        n = np.minimum(np.maximum(np.asarray(n_real_host), 0), self.capacity)
+        rows = n.size * self.capacity if self.full_rows else int(n.sum())
+        return int(rows * 8 + n.size * 4)
+
+    def __call__(self, times_h, src_h, n_real_h, sync: bool = True):
+        lib = _lib.lib()
+        compute = torch.cuda.current_stream()
+        sub, E = self.sub, self.capacity
+        for k in range(self.chunks):
+            i = k % 2
+            rows = slice(k * sub, (k + 1) * sub)
+            with torch.cuda.stream(self._copy):
+                if self._used[i]:   # the forward that last read buffer i, in any call
+                    self._copy.wait_event(self._free[i])
+                self._n[i].copy_(n_real_h[rows], non_blocking=True)
+                if self.full_rows:
+                    self._t[i].copy_(times_h[rows], non_blocking=True)
+                    self._s[i].copy_(src_h[rows], non_blocking=True)
+                else:
+                    _lib.check(lib.salt_stream_h2d_real(
+                        ptr(times_h[rows]), ptr(src_h[rows]), ctypes.c_int64(times_h.shape[1]),
+                        ptr(self._n[i]), sub, E, ptr(self._t[i]), ptr(self._s[i]),
+                        ctypes.c_void_p(self._copy.cuda_stream)))
+                self._ready[i].record(self._copy)
+            compute.wait_event(self._ready[i])
+            logits, _, fits = self.plan.forward_device(self._t[i], self._s[i], self._n[i])
+            self.logits[rows].copy_(logits, non_blocking=True)
+            self.fits[rows].copy_(fits, non_blocking=True)
+            self._free[i].record(compute)
+            self._used[i] = True
+        if sync:
+            compute.synchronize()
+        return self.logits, self.fits
+
+    def close(self) -> None:
+        self.plan.close()

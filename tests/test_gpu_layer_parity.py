@@ -160,6 +160,20 @@ def test_fc_layer_matches_oracle(n_out, fires):
     _check_layer(layer, params, times, src, nr)
 
 
+@pytest.mark.parametrize("n_out,fires,batch", [(3, True, 7), (8, True, 5), (16, True, 9),
+                                               (12, False, 3), (16, False, 1), (9, True, 11)])
+def test_fc_packed_narrow_layers(n_out, fires, batch):
+    """Layers of at most 16 neurons run several samples per warp: odd batch sizes leave a warp
+    partly empty, and ragged n_real gives the packed samples different lengths."""
+    rng = np.random.default_rng(130 + n_out + batch)
+    layer = S.FCLayer(name="f", n_in=64, n_out=n_out, init_k=1.0, tau=20.0, max_out_spikes=400)
+    params = make_params(layer, rng, vth=(60, 200), fires=fires)
+    nr = rng.integers(0, 250, size=batch).astype(np.int32)
+    nr[0] = 250
+    times, src, _ = make_events(rng, batch, 250, 64, n_real=nr)
+    _check_layer(layer, params, times, src, nr)
+
+
 @pytest.mark.parametrize("M", [1, 5, 40])
 def test_fc_output_truncation(M):
     rng = np.random.default_rng(90 + M)

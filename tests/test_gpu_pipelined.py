@@ -1,0 +1,85 @@
+"""The pipelined host-in/host-out forward (sub-batches with overlapped transfers that move only
+each sample's real events) equals the plain batched plan, including a first layer that fires on
+pad entries (whole rows are then copied) and samples without events."""
+import numpy as np
+import pytest
+
+import salt_b200 as S
+from salt_b200.plan import NetworkPlan, PipelinedForward
+from _cases import make_events, make_params
+
+pytestmark = pytest.mark.gpu
+
+
+def _net(rng, vth):
+    net = S.Network.build((2, 12, 12), [
+        S.conv(8, k=3, s=2, p=0, init_k=5.0, tau=20.0, max_queue_len=96, max_out_spikes=900),
+        S.conv(16, k=3, s=2, p=1, init_k=5.0, tau=20.0, max_queue_len=96, max_out_spikes=600),
+        S.fc(7, init_k=5.0, tau=20.0, v_th=1e9, max_out_spikes=1)])
+    params = [make_params(l, rng, vth=vth, fires=i < 2) for i, l in enumerate(net.layers)]
+    return net, params
+
+
+@pytest.mark.parametrize("vth,chunks", [((60, 160), 4), ((60, 160), 2), ((-10, 30), 4)])
+def test_pipelined_equals_the_batched_plan(vth, chunks):
+    import torch
+    rng = np.random.default_rng(9)
+    net, params = _net(rng, vth)
+    B, E = 24, 400
+    times, src, nr = make_events(rng, B, E, 2 * 12 * 12, pad_time="big")
+    nr[3], nr[7] = 0, E + 50
+    plan = NetworkPlan(net.layers, params, B, E)
+    ref_logits, _, ref_fits = plan.forward_device(torch.from_numpy(times).cuda(),
+                                                  torch.from_numpy(src).cuda(),
+                                                  torch.from_numpy(nr.astype(np.int32)).cuda())
+    ref_logits, ref_fits = ref_logits.cpu().numpy(), ref_fits.cpu().numpy()
+    pf = PipelinedForward(net.layers, params, B, E, chunks=chunks)
+    assert pf.full_rows == (vth[0] <= 0)
+    t_h = torch.from_numpy(times).pin_memory()
+    s_h = torch.from_numpy(src).pin_memory()
+    n_h = torch.from_numpy(nr.astype(np.int32)).pin_memory()
+    for _ in range(2):   # twice: the second call starts from the first call's buffers
+        logits, fits = pf(t_h, s_h, n_h)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(logits.numpy(), ref_logits)
+        np.testing.assert_array_equal(fits.numpy(), ref_fits)
+    assert pf.h2d_bytes(nr) <= B * E * 8 + B * 4
+
+
+def test_back_to_back_calls_without_host_sync():
+    """Calls enqueued back to back (sync=False): a call's first sub-batches reuse the device
+    buffers that the previous call's last sub-batches still read."""
+    import torch
+    rng = np.random.default_rng(11)
+    net, params = _net(rng, (60, 160))
+    B, E = 32, 600
+    sets = []
+    for _ in range(3):
+        times, src, nr = make_events(rng, B, E, 2 * 12 * 12)
+        sets.append((torch.from_numpy(times).pin_memory(), torch.from_numpy(src).pin_memory(),
+                     torch.from_numpy(nr.astype(np.int32)).pin_memory()))
+    plan = NetworkPlan(net.layers, params, B, E)
+    refs = [plan.forward_device(t.cuda(), s.cuda(), n.cuda())[0].cpu().numpy() for t, s, n in sets]
+    pf = PipelinedForward(net.layers, params, B, E, chunks=4)
+    out = torch.empty((6, B, pf.plan.n_out), dtype=torch.int32, device="cuda")
+    for r in range(6):
+        logits, _ = pf(*sets[r % 3], sync=False)
+        out[r].copy_(logits, non_blocking=True)   # stream-ordered after the call's copies
+    torch.cuda.synchronize()
+    for r in range(6):
+        np.testing.assert_array_equal(out[r].cpu().numpy(), refs[r % 3])
+
+
+def test_unpinned_host_rows_are_rejected():
+    import ctypes
+    import torch
+    from salt_b200 import _lib
+    t = torch.zeros((2, 8), dtype=torch.float32)          # pageable
+    s = torch.zeros((2, 8), dtype=torch.int32)
+    n = torch.zeros((2,), dtype=torch.int32, device="cuda")
+    dt = torch.empty((2, 8), dtype=torch.float32, device="cuda")
+    ds = torch.empty((2, 8), dtype=torch.int32, device="cuda")
+    p = lambda x: ctypes.c_void_p(x.data_ptr())
+    rc = _lib.lib().salt_stream_h2d_real(p(t), p(s), ctypes.c_int64(8), p(n), 2, 8, p(dt), p(ds),
+                                         None)
+    assert rc == _lib.SALT_BAD_ARG
