@@ -15,94 +15,176 @@
 
 namespace salt {
 
+template <int WT> struct CodeType { using T = int32_t; };
+template <> struct CodeType<1> { using T = int8_t; };
+template <> struct CodeType<2> { using T = int16_t; };
+
+// Shared-memory layout of fc_scan: decay table (when short enough), then the per-warp event
+// records, then (WT > 0) the weight codes as (n_in + 1, n_out) with a zero row for masked entries.
+__host__ __device__ inline int fc_lut_words(int32_t lut_len) {
+  return lut_len <= kLutSmemMax ? ((lut_len + 3) & ~3) : 0;
+}
+__host__ __device__ inline int fc_ring(int wt) { return wt ? kFcRing : 1; }
+
+size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lpu) {
+  const size_t ev = (size_t)(kFcThreads / 32) * (32 / lpu) * lpu * fc_ring(wt) * sizeof(int2);
+  const size_t q = wt ? (((size_t)(n_in + 1) * n_out * wt + 15) & ~(size_t)15) : 0;
+  return (size_t)fc_lut_words(lut_len) * 4 + ev + q;
+}
+
 // LPU lanes (one per output neuron) form a group that runs one (sample, 32-neuron group) unit;
 // LPU < 32 packs 32 / LPU samples into a warp when the layer has at most LPU neurons (G == 1),
 // as the membrane readout layers do.
-template <bool FIRES, bool SAT, int LPU>
+//
+// The recurrence of one unit is a dependent chain of a few integer operations per event, so the
+// kernel is latency-bound; everything else is taken off the chain.  Events arrive in
+// super-batches of R * LPU (R events per lane, coalesced), and the next super-batch's loads are
+// in flight while the current one runs.  Each event's decay code and weight-row offset are
+// computed lane-parallel and parked as one int2 per event in shared memory, which every lane of
+// the group then reads with one broadcast load per step.  With WT > 0 the weight codes sit in
+// shared memory as WT-byte integers with a zero row that masked entries (pads, events past the
+// group's end) point at, so a step needs no predicate: past the end it is the identity.
+template <bool FIRES, bool SAT, int LPU, int WT>
 __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
+  using QT = typename CodeType<WT>::T;
   constexpr int SPW = 32 / LPU;
+  constexpr int R = WT ? kFcRing : 1;
+  constexpr int SB = R * LPU;
   constexpr uint32_t kAll = 0xffffffffu;
-  __shared__ int32_t lut_s[kLutSmemMax];
-  const bool lut_smem = P.qc.lut_len <= kLutSmemMax;
-  if (lut_smem)
+  extern __shared__ __align__(16) unsigned char fc_smem[];
+  const int lut_words = fc_lut_words(P.qc.lut_len);
+  int32_t* lut_s = reinterpret_cast<int32_t*>(fc_smem);
+  int2* ev_all = reinterpret_cast<int2*>(fc_smem + (size_t)lut_words * 4);
+  QT* q_s = reinterpret_cast<QT*>(ev_all + (kFcThreads / 32) * SPW * SB);
+  const int32_t zero_row = P.n_in * P.n_out;
+  if (lut_words)
     for (int i = threadIdx.x; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
+  if (WT) {
+    for (int32_t i = threadIdx.x; i < zero_row; i += blockDim.x) q_s[i] = (QT)__ldg(&P.qT[i]);
+    for (int32_t i = threadIdx.x; i < P.n_out; i += blockDim.x) q_s[zero_row + i] = 0;
+  }
   __syncthreads();
-  const int32_t* lut = lut_smem ? lut_s : P.lut;
+  const int32_t* lut = lut_words ? lut_s : P.lut;
   const int lane = threadIdx.x & 31, gi = lane / LPU, gl = lane % LPU;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t n_units = (int64_t)P.batch * P.G;
   if (gw * SPW >= n_units) return;  // the whole warp is past the last unit
+  int2* ev_s = ev_all + ((threadIdx.x >> 5) * SPW + gi) * SB;
   const int64_t unit = gw * SPW + gi;
   const bool unit_ok = unit < n_units;
   const int b = unit_ok ? (int)(unit / P.G) : 0, g = unit_ok ? (int)(unit % P.G) : 0;
   const int o = g * LPU + gl;
   const bool active = unit_ok && o < P.n_out;
+  const int oc = active ? o : 0;  // inactive lanes run column 0; their results are dropped
   const int32_t n_in = unit_ok ? P.in_nreal[b] : 0;
   const int32_t n_eff = unit_ok ? P.n_eff(b) : 0;
   const int32_t nproc = !unit_ok ? 0 : (P.tail_mode ? P.in.capacity : n_eff);
-  // lanes past n_out never fire (their register stays 0); registers stay below INT32_MAX
+  // lanes past n_out never fire (their register stays 0 or runs column 0 without firing);
+  // registers stay below INT32_MAX
   const int32_t vth = (FIRES && active) ? P.vth[o] : INT32_MAX;
   const StepConsts sc(P.qc);
   uint32_t* sw_b = FIRES ? P.sw + (int64_t)b * P.sw_stride : nullptr;
   int32_t* chunk_b = FIRES ? P.chunk_spikes + (int64_t)b * P.n_spk_chunks : nullptr;
   const int32_t nmax = __reduce_max_sync(kAll, nproc);
 
-  int32_t V = 0, vmin = 0, vmax = 0, nspk = 0;
-  float tprev = 0.0f;
-  for (int32_t base = 0; base < nmax; base += LPU) {
-    // Lane-parallel preparation of LPU events: time, source, Δt against the previous entry
-    // (connectivity/fc.py:26-29: the first against t=0, pads masked to 0) and decay code.
-    const int32_t jl = base + gl;
-    float t_l = 0.0f;
-    int32_t s_l = 0;
-    if (jl < nproc) {
-      t_l = P.in.time(b, jl, n_eff);
-      s_l = P.in.source(b, jl, n_eff);
-    }
-    float t_prev_l = __shfl_up_sync(kAll, t_l, 1, LPU);
-    if (gl == 0) t_prev_l = tprev;
-    const bool real_l = jl < n_in;
-    const int32_t dt_l = real_l ? dt_from_times(t_l, t_prev_l) : 0;
-    const int32_t a_l = dt_l == 0 ? sc.ident_a : decay_code(dt_l, lut, P.qc.lut_len);
-    const int cnt = min(LPU, nproc - base);  // this group's events in the batch (may be <= 0)
-    const float t_last = __shfl_sync(kAll, t_l, cnt > 0 ? cnt - 1 : 0, LPU);
-    if (cnt > 0) tprev = t_last;
-    int32_t qv[LPU];
+  float tn[R];
+  int32_t sn[R];
+  auto load = [&](int32_t base) {
 #pragma unroll
-    for (int e = 0; e < LPU; ++e) {
-      const int32_t s = __shfl_sync(kAll, s_l, e, LPU);
-      const bool real = (base + e) < n_in && e < cnt;  // fc.py:29 is_real = j < n_real
-      qv[e] = (real && active) ? __ldg(&P.qT[jax_index(s, P.n_in) * P.n_out + o]) : 0;
-    }
-    const int cntw = min(LPU, nmax - base);  // warp-uniform batch length
-#pragma unroll
-    for (int e = 0; e < LPU; ++e) {
-      if (e < cntw) {
-        const int32_t a = __shfl_sync(kAll, a_l, e, LPU);
-        bool spike = false;
-        if (e < cnt) {
-          int32_t u;
-          const int32_t w = sc.step<SAT>(V, a, qv[e], u);
-          spike = FIRES && w >= vth;
-          V = spike ? 0 : w;
-          // inactive lanes see q = 0 from V = 0, so u = 0 leaves the range untouched; overflow
-          // is read off the unfitted range at the end of the layer (layer_finish)
-          vmin = min(vmin, u);
-          vmax = max(vmax, u);
-          nspk += spike;
-        }
-        if (FIRES) {
-          const uint32_t bal = __ballot_sync(kAll, spike);
-          const uint32_t bits = LPU == 32 ? bal : (bal >> (gi * LPU)) & ((1u << LPU) - 1u);
-          if (gl == 0 && e < cnt) {
-            const int32_t j = base + e;
-            sw_b[(int64_t)j * P.G + g] = bits;
-            if (bits) atomicAdd(&chunk_b[j >> kSpkChunkShift], __popc(bits));
-          }
-        }
+    for (int r = 0; r < R; ++r) {
+      const int32_t j = base + r * LPU + gl;
+      tn[r] = 0.0f;
+      sn[r] = 0;
+      if (j < nproc) {
+        tn[r] = P.in.time(b, j, n_eff);
+        sn[r] = P.in.source(b, j, n_eff);
       }
     }
+  };
+  load(0);
+  int32_t V = 0, vmin = 0, vmax = 0, nspk = 0;
+  float tcarry = 0.0f;
+  for (int32_t base = 0; base < nmax; base += SB) {
+    float tc[R];
+    int32_t scur[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      tc[r] = tn[r];
+      scur[r] = sn[r];
+    }
+    if (base + SB < nmax) load(base + SB);  // in flight while this super-batch runs
+    // lane-parallel: Δt against the previous entry (connectivity/fc.py:26-29: the first
+    // against t = 0, pads masked to Δt = 0 and weight 0), decay code and weight-row offset
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int32_t j = base + r * LPU + gl;
+      float tp = __shfl_up_sync(kAll, tc[r], 1, LPU);
+      // the group's first lane continues from the previous row of events (or super-batch)
+      const float row_prev = r ? __shfl_sync(kAll, tc[r > 0 ? r - 1 : 0], LPU - 1, LPU) : tcarry;
+      if (gl == 0) tp = row_prev;
+      const bool real = j < n_in && j < nproc;
+      const int32_t dt = real ? dt_from_times(tc[r], tp) : 0;
+      const int32_t a = dt == 0 ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
+      int32_t qo;
+      if (WT) qo = real ? (int32_t)jax_index(scur[r], P.n_in) * P.n_out : zero_row;
+      else qo = real ? (int32_t)jax_index(scur[r], P.n_in) * P.n_out : -1;
+      ev_s[r * LPU + gl] = make_int2(a, qo);
+    }
+    tcarry = __shfl_sync(kAll, tc[R - 1], LPU - 1, LPU);
+    __syncwarp();
+    const int32_t cnt = nproc - base;  // this group's events in the super-batch (may be <= 0)
+    const int32_t cntw = min(SB, nmax - base);
+    uint32_t mybits[R];
+    int32_t sb_spk = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) mybits[r] = 0;
+    auto step = [&](int e) {
+      const int2 ev = ev_s[e];
+      int32_t qv;
+      if (WT) qv = (int32_t)q_s[ev.y + oc];
+      else qv = ev.y >= 0 ? __ldg(&P.qT[ev.y + oc]) : 0;
+      int32_t u;
+      const int32_t w = sc.step<SAT>(V, ev.x, qv, u);
+      vmin = min(vmin, u);
+      vmax = max(vmax, u);
+      if (FIRES) {
+        const bool spike = w >= vth;
+        V = spike ? 0 : w;
+        nspk += spike;
+        const uint32_t bal = __ballot_sync(kAll, spike);
+        const uint32_t bits = LPU == 32 ? bal : (bal >> (gi * LPU)) & ((1u << (LPU & 31)) - 1u);
+        if (gl == (e % LPU)) mybits[e / LPU] = bits;
+        sb_spk += __popc(bits);
+      } else {
+        V = w;
+      }
+    };
+    if (cntw == SB) {
+#pragma unroll
+      for (int e = 0; e < SB; ++e) step(e);
+    } else {
+#pragma unroll
+      for (int e = 0; e < SB; ++e)
+        if (e < cntw) step(e);
+    }
+    if (FIRES) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int32_t j = base + r * LPU + gl;
+        if (r * LPU + gl < cnt && unit_ok) sw_b[(int64_t)j * P.G + g] = mybits[r];
+      }
+      // a super-batch lies inside one spike-count chunk (SB divides kSpkChunk)
+      if (gl == 0 && sb_spk && unit_ok) atomicAdd(&chunk_b[base >> kSpkChunkShift], sb_spk);
+    }
+    __syncwarp();
   }
+  // pad columns the scan skipped are identity steps whose unfitted value is the register
+  // (quant/scan.py:40-42); steps past a group's end above were such identity steps too
+  if (!P.tail_mode && n_eff < P.in.capacity) {
+    vmin = min(vmin, V);
+    vmax = max(vmax, V);
+  }
+  if (!active) vmin = vmax = nspk = 0;
   if (active) P.v_final[(int64_t)b * P.n_out + o] = V;
   if (FIRES && active) P.n_spk[(int64_t)b * P.n_out + o] = nspk;
   // per-group reductions (lanes of other groups belong to other samples)
@@ -231,16 +313,27 @@ fc_truncated(FCLaunch P, salt_stream_out out) {
   }
 }
 
-template <int LPU>
+template <int LPU, int WT>
 static void* fc_scan_for(bool fires, bool saturate) {
-  if (saturate) return fires ? (void*)fc_scan<true, true, LPU> : (void*)fc_scan<false, true, LPU>;
-  return fires ? (void*)fc_scan<true, false, LPU> : (void*)fc_scan<false, false, LPU>;
+  if (saturate)
+    return fires ? (void*)fc_scan<true, true, LPU, WT> : (void*)fc_scan<false, true, LPU, WT>;
+  return fires ? (void*)fc_scan<true, false, LPU, WT> : (void*)fc_scan<false, false, LPU, WT>;
 }
 
-void* fc_scan_kernel(bool fires, bool saturate, int lpu) {
-  if (lpu == 8) return fc_scan_for<8>(fires, saturate);
-  if (lpu == 16) return fc_scan_for<16>(fires, saturate);
-  return fc_scan_for<32>(fires, saturate);
+template <int WT>
+static void* fc_scan_lpu(bool fires, bool saturate, int lpu) {
+  if (lpu == 8) return fc_scan_for<8, WT>(fires, saturate);
+  if (lpu == 16) return fc_scan_for<16, WT>(fires, saturate);
+  return fc_scan_for<32, WT>(fires, saturate);
+}
+
+void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt) {
+  switch (wt) {
+    case 1: return fc_scan_lpu<1>(fires, saturate, lpu);
+    case 2: return fc_scan_lpu<2>(fires, saturate, lpu);
+    case 4: return fc_scan_lpu<4>(fires, saturate, lpu);
+    default: return fc_scan_lpu<0>(fires, saturate, lpu);
+  }
 }
 
 }  // namespace salt

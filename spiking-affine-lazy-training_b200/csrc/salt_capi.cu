@@ -474,15 +474,20 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   L.s_total = s.s_total; L.vmin = s.vmin; L.vmax = s.vmax; L.ovf = s.ovf; L.n_spk = s.n_spk;
   L.tail_mode = q->has_vth && q->needs_tail;
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
-  // narrow layers (the membrane readouts) pack several samples into a warp
+  // narrow layers (the membrane readouts) pack several samples into a warp; weight tables that
+  // fit are staged in shared memory at the width of their codes
   const int lpu = d->n_out <= 8 ? 8 : (d->n_out <= 16 ? 16 : 32);
+  int wt = q->q_bits <= 8 ? 1 : (q->q_bits <= 16 ? 2 : 4);
+  if ((size_t)(d->n_in + 1) * d->n_out * wt > kFcQSmemMax) wt = 0;
+  const size_t smem = fc_scan_smem(d->n_in, d->n_out, q->lut_len, wt, lpu);
   const int64_t warps = ((int64_t)B * L.G + 32 / lpu - 1) / (32 / lpu);
   const int wpb = kFcThreads / 32;
   const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
+  void* scan_fn = fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu, wt);
+  if (smem > 48 * 1024)
+    SALT_CUDA(cudaFuncSetAttribute(scan_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* scan_args[] = {&L};
-  SALT_CUDA(cudaLaunchKernel(
-      fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu), dim3(grid),
-      dim3(kFcThreads), scan_args, 0, st));
+  SALT_CUDA(cudaLaunchKernel(scan_fn, dim3(grid), dim3(kFcThreads), scan_args, smem, st));
   SALT_LAUNCHED("fc_scan");
   if (q->has_vth) {
     spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);

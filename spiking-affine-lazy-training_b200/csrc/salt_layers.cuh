@@ -229,8 +229,11 @@ __global__ void fc_truncated(FCLaunch P, salt_stream_out out);
 void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate);
 // Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
-// lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons.
-void* fc_scan_kernel(bool fires, bool saturate, int lpu);
+// lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons;
+// wt: bytes per weight code staged in shared memory (1, 2, 4), 0 to read them from global.
+void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt);
+// Dynamic shared memory of fc_scan for these sizes.
+size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lpu);
 
 // Device address of the fixed scratch behind salt_conv_layer_forward_noalloc (fixed_scratch.cu).
 cudaError_t fixed_scratch_address(void** ptr);
@@ -252,5 +255,7 @@ cudaError_t fc_trace_launch(const FCLaunch& P, const salt_neuron_trace* rec, int
 cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches,
                             cudaEvent_t seg_start = nullptr, cudaEvent_t seg_stop = nullptr);
 constexpr int kFcThreads = 128;
+constexpr int kFcRing = 4;            // events per lane per fc_scan super-batch (smem codes)
+constexpr size_t kFcQSmemMax = 96 * 1024;  // largest staged weight table of fc_scan
 
 }  // namespace salt
