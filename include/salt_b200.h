@@ -276,6 +276,62 @@ salt_status salt_float_fc_layer_forward(const salt_float_fc_desc *layer, const f
                                         const salt_float_layer_stats *stats, void *workspace,
                                         size_t workspace_bytes, void *stream);
 
+/* ---------------------------------------------------------------- float conv layer
+ * Replaces ConvLayer.forward with FloatBackend (salt_core/layers/conv.py:124-149): the queue of
+ * build_conv_structure (connectivity/conv.py:128-172), conv_float_values (:187-206), the chunked
+ * scan (float/scan.py:100-131, float/affine.py:99-126), spike_step_upper_bound's need
+ * (affine.py:57-88) and extract_output_events_conv (stream.py:84-100).  The float forward of the
+ * quantisation pipeline: with chunk_size 1 it is the calibration forward of
+ * example/quant_run.py:30-44.  w is (oc, ic, k, k) float32; decay_base = float32(1 - 1/tau);
+ * in_gain (batch, capacity) may be NULL (all ones).  The output stream's real entries carry gain
+ * 1 (the forward value of s_spike), so it has no gain array.  v_th must be finite and > 0. */
+typedef struct {
+  int32_t ic, h_in, w_in, oc, k, s, p;
+  int32_t max_queue_len;    /* ConvLayer.max_queue_len */
+  int32_t max_out_spikes;   /* ConvLayer.max_out_spikes */
+  int32_t max_extra_steps;  /* ConvLayer.max_extra_steps */
+  int32_t chunk_size;       /* ConvLayer.chunk_size */
+  float v_th;               /* ConvLayer.v_th */
+} salt_float_conv_desc;
+
+typedef struct {
+  int32_t *spike_count;         /* (batch) spikes, not clipped to max_out_spikes */
+  int32_t *needed_queue;        /* (batch) largest real taps of a position + 1 */
+  int32_t *needed_extra_steps;  /* (batch) */
+  int32_t *fits;                /* (batch) every need within its knob */
+} salt_float_conv_stats;
+
+/* Per-step traces of a float layer (run_layer_traced, float/scan.py:53-64, with trace.py:13-60)
+ * and its potential ranges (quant/calibrate.py:16-36 reduces v_steps to these); any pointer may
+ * be NULL.  max_steps = ceil(L / chunk_size) + max_extra_steps, L = max_queue_len (conv) or the
+ * input capacity (FC).  Ranges are over every step and, for conv layers, every position of a
+ * channel; an FC neuron is its own channel. */
+typedef struct {
+  float *v_steps;       /* (batch, n_neurons, max_steps) potential after each step */
+  float *event_ms;      /* (batch, n_neurons, max_steps) first event time of the step; NaN idle */
+  uint8_t *spike_mask;  /* (batch, n_neurons, max_steps) */
+  float *v_max;         /* (batch, channels) */
+  float *v_min;         /* (batch, channels) */
+} salt_float_trace;
+
+salt_status salt_float_conv_layer_workspace_size(const salt_float_conv_desc *layer, int32_t batch,
+                                                 int32_t in_capacity, size_t *bytes);
+salt_status salt_float_conv_layer_forward(const salt_float_conv_desc *layer, const float *w,
+                                          float decay_base, int32_t batch,
+                                          const salt_stream_in *in, const float *in_gain,
+                                          salt_stream_out *out, float *v_final,
+                                          const salt_float_conv_stats *stats,
+                                          const salt_float_trace *trace, void *workspace,
+                                          size_t workspace_bytes, void *stream);
+
+/* Per-step traces and potential ranges of a float FC layer (FCLayer.forward with FloatBackend and
+ * trace=True, salt_core/layers/fc.py:84-106); v_final (batch, n_out) may be NULL.  The layer's
+ * output stream comes from salt_float_fc_layer_forward. */
+salt_status salt_float_fc_layer_trace(const salt_float_fc_desc *layer, const float *w,
+                                      const float *decay_base, int32_t batch,
+                                      const salt_stream_in *in, const float *in_gain,
+                                      float *v_final, const salt_float_trace *trace, void *stream);
+
 /* ---------------------------------------------------------------- stream transfer
  * No reference counterpart (the reference's input lives in XLA buffers): copies a batch of event
  * streams from PINNED host memory to the device, moving each sample's row only up to

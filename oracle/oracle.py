@@ -433,7 +433,7 @@ class _FloatOut(ctypes.Structure):
     _fields_ = [("v_final", _f32p), ("spike_mask", _u8p), ("spike_event_idx", _i32p),
                 ("out_times", _f32p), ("out_src", _i32p), ("out_gain", _f32p),
                 ("n_real_out", ctypes.c_int32), ("extra_steps_needed", ctypes.c_int32),
-                ("fits", ctypes.c_int32)]
+                ("fits", ctypes.c_int32), ("v_steps", _f32p), ("event_ms", _f32p)]
 
 
 class FloatResult(NamedTuple):
@@ -450,6 +450,8 @@ class FloatResult(NamedTuple):
     spike_count: int
     extra_steps_needed: int
     fits: bool
+    v_steps: np.ndarray | None = None   # (n_out, max_steps) with trace=True
+    event_ms: np.ndarray | None = None
 
 
 def decay_base(tau) -> np.ndarray:
@@ -459,7 +461,7 @@ def decay_base(tau) -> np.ndarray:
 
 
 def float_fc_forward(layer, w, times, src, n_real, gain=None, tau=None, *, dense=True,
-                     threads=1) -> FloatResult:
+                     threads=1, trace=False) -> FloatResult:
     """One float FC layer over one stream.  layer has the FCLayer fields n_in, n_out, tau,
     v_th, chunk_size, max_out_spikes, max_extra_steps; w is (n_out, n_in) float32; tau, when
     given, overrides layer.tau per neuron (n_out,).  dense=True also returns the
@@ -481,9 +483,12 @@ def float_fc_forward(layer, w, times, src, n_real, gain=None, tau=None, *, dense
     ot = np.empty(max(M, 1), np.float32)
     os_ = np.empty(max(M, 1), np.int32)
     og = np.empty(max(M, 1), np.float32)
+    vs = np.empty((n_out, steps), np.float32) if trace else None
+    ms = np.empty((n_out, steps), np.float32) if trace else None
     out = _FloatOut(_p(vf, _f32p), _p(mask, _u8p) if dense else None,
                     _p(eidx, _i32p) if dense else None, _p(ot, _f32p), _p(os_, _i32p),
-                    _p(og, _f32p), 0, 0, 0)
+                    _p(og, _f32p), 0, 0, 0, _p(vs, _f32p) if trace else None,
+                    _p(ms, _f32p) if trace else None)
     rc = lib().so_float_fc_forward(ctypes.byref(geom), _p(wf, _f32p), _p(base, _f32p),
                                    _p(t, _f32p), _p(s, _i32p),
                                    _p(g, _f32p) if g is not None else None, L, int(n_real),
@@ -492,7 +497,7 @@ def float_fc_forward(layer, w, times, src, n_real, gain=None, tau=None, *, dense
         raise ValueError(f"oracle float layer failed rc={rc}")
     return FloatResult(vf, mask.astype(bool) if dense else None, eidx, ot[:M], os_[:M], og[:M],
                        int(out.n_real_out), int(out.n_real_out), int(out.extra_steps_needed),
-                       bool(out.fits))
+                       bool(out.fits), vs, ms)
 
 
 def affine_scan(a, b):
@@ -505,3 +510,70 @@ def affine_scan(a, b):
     if rc:
         raise ValueError(f"oracle affine scan failed rc={rc}")
     return oa, ob
+
+
+class _FloatConvGeom(ctypes.Structure):
+    _fields_ = [("conv", _ConvGeom), ("chunk_size", ctypes.c_int32), ("v_th", ctypes.c_float)]
+
+
+class _FloatConvOut(ctypes.Structure):
+    _fields_ = [("v_final", _f32p), ("spike_mask", _u8p), ("spike_event_idx", _i32p),
+                ("v_steps", _f32p), ("event_ms", _f32p), ("out_times", _f32p),
+                ("out_src", _i32p), ("out_gain", _f32p), ("n_real_out", ctypes.c_int32),
+                ("needed_queue", ctypes.c_int32), ("extra_steps_needed", ctypes.c_int32),
+                ("fits", ctypes.c_int32)]
+
+
+class FloatConvResult(NamedTuple):
+    """ConvLayer.forward with FloatBackend (layers/conv.py:124-149) for one sample: the forward
+    values, output EventStream, needs, and (trace=True) LayerForwardTrace's per-step arrays
+    (trace.py:13-22; pointer resolved to ms as resolve_ms_conv does)."""
+    v_final: np.ndarray            # (n_neurons,) float32
+    spike_mask: np.ndarray | None  # (n_neurons, max_steps) bool
+    spike_event_idx: np.ndarray | None
+    v_steps: np.ndarray | None     # (n_neurons, max_steps) float32
+    event_ms: np.ndarray | None
+    event_times: np.ndarray
+    event_source_idx: np.ndarray
+    event_gain: np.ndarray
+    n_real_events: int
+    needed_queue: int
+    extra_steps_needed: int
+    fits: bool
+
+
+def float_conv_forward(layer, w, times, src, n_real, gain=None, *, trace=False
+                       ) -> FloatConvResult:
+    """One float conv layer over one stream.  layer has the ConvLayer fields (geometry, tau,
+    v_th, chunk_size, max_queue_len, max_out_spikes, max_extra_steps); w is (oc, ic, k, k)."""
+    t = np.ascontiguousarray(np.asarray(times, dtype=np.float32))
+    s = np.ascontiguousarray(np.asarray(src), dtype=np.int32)
+    E = int(t.shape[0])
+    wf = np.ascontiguousarray(np.asarray(w, dtype=np.float32).reshape(layer.weight_shape))
+    g = None if gain is None else np.ascontiguousarray(np.asarray(gain, dtype=np.float32))
+    L, C = int(layer.max_queue_len), int(layer.chunk_size)
+    steps = -(-L // C) + int(layer.max_extra_steps)
+    n = int(layer.n_neurons)
+    M = int(layer.max_out_spikes)
+    geom = _FloatConvGeom(_conv_geom(layer), C, float(layer.v_th))
+    vf = np.empty(n, np.float32)
+    mask = np.empty((n, steps), np.uint8)
+    eidx = np.empty((n, steps), np.int32)
+    vs = np.empty((n, steps), np.float32) if trace else None
+    ms = np.empty((n, steps), np.float32) if trace else None
+    ot = np.empty(max(M, 1), np.float32)
+    os_ = np.empty(max(M, 1), np.int32)
+    og = np.empty(max(M, 1), np.float32)
+    out = _FloatConvOut(_p(vf, _f32p), _p(mask, _u8p), _p(eidx, _i32p),
+                        _p(vs, _f32p) if trace else None, _p(ms, _f32p) if trace else None,
+                        _p(ot, _f32p), _p(os_, _i32p), _p(og, _f32p), 0, 0, 0, 0)
+    base = float(decay_base(layer.tau))
+    rc = lib().so_float_conv_forward(ctypes.byref(geom), _p(wf, _f32p), ctypes.c_float(base),
+                                     _p(t, _f32p), _p(s, _i32p),
+                                     _p(g, _f32p) if g is not None else None, E, int(n_real),
+                                     ctypes.byref(out))
+    if rc:
+        raise ValueError(f"oracle float conv layer failed rc={rc}")
+    return FloatConvResult(vf, mask.astype(bool), eidx, vs, ms, ot[:M], os_[:M], og[:M],
+                           int(out.n_real_out), int(out.needed_queue),
+                           int(out.extra_steps_needed), bool(out.fits))

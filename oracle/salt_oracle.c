@@ -757,12 +757,18 @@ static int float_neuron(float_ctx *c, int32_t i, float *a_pad, float *b_pad, flo
   int32_t *eidx = c->out->spike_event_idx ? c->out->spike_event_idx + (int64_t)i * c->max_steps
                                           : NULL;
   const int64_t id_from = L < c->n_real ? L : (c->n_real > 0 ? c->n_real : 0);
+  float *vst = c->out->v_steps ? c->out->v_steps + (int64_t)i * c->max_steps : NULL;
+  float *ems = c->out->event_ms ? c->out->event_ms + (int64_t)i * c->max_steps : NULL;
   for (int32_t step = 0; step < c->max_steps; ++step) {
+    /* trace.py:24-40 resolve_ms_fc: the step's start pointer, idle from n_real on */
+    if (ems) ems[step] = ptr >= c->n_real ? NAN : c->times[ptr < L - 1 ? ptr : L - 1];
     if (ptr >= id_from && !(v - v_th >= 0.0f)) {
       /* Every map from here on is the identity (1, 0), which composes to exactly (1, 0): each
        * remaining step leaves v unchanged, does not fire and consumes a whole chunk. */
       for (; step < c->max_steps; ++step) {
         const int32_t ev = (int32_t)(ptr + C < INT32_MAX ? ptr + C : INT32_MAX);
+        if (ems) ems[step] = ptr >= c->n_real ? NAN : c->times[ptr < L - 1 ? ptr : L - 1];
+        if (vst) vst[step] = v;
         if (mask) mask[step] = 0;
         if (eidx) eidx[step] = ev;
         if (step == 0) {
@@ -793,6 +799,7 @@ static int float_neuron(float_ctx *c, int32_t i, float *a_pad, float *b_pad, flo
     const int spiked = sidx < C;
     v = spiked ? (1.0f - 1.0f) * v_spk : A[C - 1] * v + B[C - 1];
     const int32_t ev = (int32_t)(ptr + sidx);
+    if (vst) vst[step] = v;
     if (mask) mask[step] = (uint8_t)spiked;
     if (eidx) eidx[step] = ev;
     if (step == 0) {
@@ -922,5 +929,170 @@ int so_float_fc_forward(const so_float_fc_geom *g, const float *w, const float *
   free(nidx);
   free(jdx);
   free(sraw);
+  return rc;
+}
+
+/* ================================================================ float conv layer */
+
+/* float/scan.py:100-131: max_steps steps over one neuron's padded queue (Lp = L + C maps).  Per
+ * step it records the spike flag, the queue column of the step's spike (pointer + spike_idx,
+ * scan.py:114; pointer + C on a silent step), the potential after the step and the pointer at
+ * the step's start (run_layer_traced's v_steps / pointer_steps, scan.py:118-119); any output
+ * may be NULL.  Maps from column id_from on are identities.  Returns v_final. */
+static float float_chunk_scan(const float *a_pad, const float *b_pad, int32_t L, int32_t C,
+                              int64_t id_from, int32_t max_steps, float v_th, float *ca,
+                              float *cb, float *A, float *B, float *work, uint8_t *mask,
+                              int32_t *eidx, float *v_steps, int32_t *ptr_steps) {
+  const int64_t Lp = (int64_t)L + C;
+  float v = 0.0f;
+  int64_t ptr = 0;
+  for (int32_t step = 0; step < max_steps; ++step) {
+    const int32_t p32 = (int32_t)(ptr < INT32_MAX ? ptr : INT32_MAX);
+    if (ptr >= id_from && !(v - v_th >= 0.0f)) {
+      /* identities compose to (1, 0): v stays, nothing fires, a whole chunk per step */
+      if (mask) mask[step] = 0;
+      if (eidx) eidx[step] = (int32_t)(ptr + C < INT32_MAX ? ptr + C : INT32_MAX);
+      if (v_steps) v_steps[step] = v;
+      if (ptr_steps) ptr_steps[step] = p32;
+      ptr += C;
+      continue;
+    }
+    for (int32_t k = 0; k < C; ++k) { /* take_chunk: jnp.take(..., mode='clip') */
+      int64_t idx = ptr + k;
+      if (idx > Lp - 1) idx = Lp - 1;
+      ca[k] = a_pad[idx];
+      cb[k] = b_pad[idx];
+    }
+    affine_scan_rec(ca, cb, C, A, B, work);
+    int32_t sidx = C; /* process_chunk (affine.py:99-126) */
+    float v_spk = 0.0f;
+    for (int32_t k = 0; k < C; ++k) {
+      const float vs = A[k] * v + B[k];
+      if (vs - v_th >= 0.0f) {
+        sidx = k;
+        v_spk = vs;
+        break;
+      }
+    }
+    const int spiked = sidx < C;
+    v = spiked ? (1.0f - 1.0f) * v_spk : A[C - 1] * v + B[C - 1];
+    if (mask) mask[step] = (uint8_t)spiked;
+    if (eidx) eidx[step] = (int32_t)(ptr + sidx);
+    if (v_steps) v_steps[step] = v;
+    if (ptr_steps) ptr_steps[step] = p32;
+    ptr += spiked ? sidx + 1 : C;
+  }
+  return v;
+}
+
+int so_float_conv_forward(const so_float_conv_geom *fg, const float *w, float decay_base,
+                          const float *times, const int32_t *src, const float *gain,
+                          int32_t E_len, int32_t n_in, so_float_conv_out *out) {
+  if (!fg || !out) return -1;
+  const so_conv_geom *g = &fg->conv;
+  const int32_t L = g->max_queue_len, C = fg->chunk_size, K = g->k;
+  if (C < 1 || L < 1 || E_len < 1 || g->max_extra_steps < 0 || g->max_out_spikes < 0)
+    return -1;
+  const int32_t h_out = conv_h_out(g), w_out = conv_w_out(g), n_sp = h_out * w_out;
+  const int64_t n = (int64_t)g->oc * n_sp;
+  const int32_t max_steps = (L + C - 1) / C + g->max_extra_steps;
+  const int64_t nL = (int64_t)n_sp * L;
+  int32_t *l2g = (int32_t *)malloc(sizeof(int32_t) * (size_t)nL * 4);
+  int32_t *n_real = (int32_t *)malloc(sizeof(int32_t) * (size_t)n_sp);
+  float *dt = (float *)malloc(sizeof(float) * (size_t)nL * 2);
+  uint8_t *mask = out->spike_mask ? out->spike_mask
+                                  : (uint8_t *)malloc((size_t)(n * max_steps));
+  int32_t *eidx = out->spike_event_idx
+                      ? out->spike_event_idx
+                      : (int32_t *)malloc(sizeof(int32_t) * (size_t)(n * max_steps));
+  int32_t *ptr_steps = out->event_ms ? (int32_t *)malloc(sizeof(int32_t) * (size_t)(n * max_steps))
+                                     : NULL;
+  const int32_t Lp = L + C;
+  float *a_pad = (float *)malloc(sizeof(float) * (size_t)Lp * 2);
+  float *buf = (float *)malloc(sizeof(float) * (size_t)(8 * C + 8));
+  int rc = 0;
+  if (!l2g || !n_real || !dt || !mask || !eidx || (out->event_ms && !ptr_steps) || !a_pad || !buf) {
+    rc = -2;
+    goto done;
+  }
+  {
+    int32_t *tc = l2g + nL, *tky = l2g + 2 * nL, *tkx = l2g + 3 * nL;
+    float *a_pos = dt + nL;
+    float *b_pad = a_pad + Lp;
+    rc = so_conv_structure(g, times, src, E_len, n_in, l2g, n_real, dt, tc, tky, tkx);
+    if (rc) goto done;
+    /* conv_float_values (connectivity/conv.py:187-206): a per position, tiled over channels */
+    for (int64_t e = 0; e < nL; ++e) a_pos[e] = powf(decay_base, dt[e]);
+    int32_t nq_max = 0, extra = (int32_t)0x80000000u;
+    for (int32_t pos = 0; pos < n_sp; ++pos)
+      if (n_real[pos] > nq_max) nq_max = n_real[pos];
+    for (int64_t i = 0; i < n; ++i) {
+      const int32_t oc = (int32_t)(i / n_sp), pos = (int32_t)(i % n_sp);
+      const int32_t nr = n_real[pos];
+      int32_t m_pos = 0;
+      float sum_pos = 0.0f;
+      for (int32_t col = 0; col < Lp; ++col) {
+        float a = 1.0f, b = 0.0f;
+        if (col < L) {
+          const int64_t e = (int64_t)pos * L + col;
+          a = a_pos[e];
+          if (col < nr) { /* _real_tap_mask; weight gather with JAX clamping */
+            const int64_t c = jidx(tc[e], g->ic);
+            b = w[(((int64_t)oc * g->ic + c) * K + tky[e]) * K + tkx[e]];
+            if (gain) {
+              const int32_t ej = l2g[e] < n_in - 1 ? l2g[e] : n_in - 1;
+              b = b * gain[jidx(ej, E_len)];
+            }
+          }
+          m_pos += b > 0.0f; /* spike_step_upper_bound over the (n, L) b */
+          sum_pos += b > 0.0f ? b : 0.0f;
+        }
+        a_pad[col] = a;
+        b_pad[col] = b;
+      }
+      const float m_star = fminf((float)m_pos, floorf(sum_pos / fg->v_th));
+      const float steps_f = m_star + ceilf(((float)L - m_star) / (float)C);
+      const int32_t ex = f32_to_i32(steps_f) - (L + C - 1) / C;
+      if (ex > extra) extra = ex;
+      /* from the column after the catch-up column on, every map is the identity */
+      const int64_t id_from = nr < L ? nr + 1 : L;
+      const int64_t row = i * max_steps;
+      out->v_final[i] = float_chunk_scan(
+          a_pad, b_pad, L, C, id_from, max_steps, fg->v_th, buf, buf + C, buf + 2 * C,
+          buf + 3 * C, buf + 4 * C, mask + row, eidx + row,
+          out->v_steps ? out->v_steps + row : NULL, ptr_steps ? ptr_steps + row : NULL);
+      if (out->event_ms) /* trace.py:43-60 resolve_ms_conv */
+        for (int32_t s = 0; s < max_steps; ++s) {
+          const int32_t p = ptr_steps[row + s];
+          if (p >= nr) {
+            out->event_ms[row + s] = NAN;
+          } else {
+            const int32_t col = p < L - 1 ? p : L - 1;
+            const int32_t gj = l2g[(int64_t)pos * L + col];
+            out->event_ms[row + s] = times[gj < E_len - 1 ? gj : E_len - 1];
+          }
+        }
+    }
+    /* layers/conv.py:133-141: output stream and needs */
+    const int32_t M = g->max_out_spikes;
+    int32_t nr_out = 0;
+    so_extract_output_events(mask, eidx, (int32_t)n, max_steps, l2g, n_sp, L, times, E_len, M,
+                             out->out_times, out->out_src, &nr_out);
+    for (int32_t q = 0; q < M; ++q) /* s_spike: 1 on a fire; the fill entry is (neuron 0, step 0) */
+      out->out_gain[q] = q < nr_out ? 1.0f : (mask[0] ? 1.0f : 0.0f);
+    out->n_real_out = nr_out;
+    out->needed_queue = nq_max + 1;
+    out->extra_steps_needed = extra;
+    out->fits = nq_max + 1 <= L && nr_out <= M && extra <= g->max_extra_steps;
+  }
+done:
+  if (!out->spike_mask) free(mask);
+  if (!out->spike_event_idx) free(eidx);
+  free(ptr_steps);
+  free(l2g);
+  free(n_real);
+  free(dt);
+  free(a_pad);
+  free(buf);
   return rc;
 }

@@ -153,6 +153,8 @@ typedef struct {
   int32_t n_real_out;        /* spikes in the layer (not clipped to max_out_spikes) */
   int32_t extra_steps_needed;
   int32_t fits;
+  float *v_steps;            /* (n_out, max_steps) potential after each step, or NULL */
+  float *event_ms;           /* (n_out, max_steps) trace.py resolve_ms_fc, or NULL */
 } so_float_out;
 
 /* max_steps = ceil(L / chunk_size) + max_extra_steps (layers/fc.py:128-130).  gain may be NULL
@@ -160,6 +162,34 @@ typedef struct {
 int so_float_fc_forward(const so_float_fc_geom *g, const float *w, const float *decay_base,
                         const float *times, const int32_t *src, const float *gain, int32_t L,
                         int32_t n_real, int32_t threads, so_float_out *out);
+
+/* ConvLayer.forward with FloatBackend (layers/conv.py:124-149): build_conv_structure, then
+ * conv_float_values (connectivity/conv.py:187-206: a = decay_base ** Δt per position, b = the
+ * weight tap times the event gain on real columns), the chunked scan of float/scan.py:100-131 and
+ * extract_output_events_conv (stream.py:84-100).  w is (oc, ic, k, k); gain may be NULL (ones).
+ * max_steps = ceil(L / chunk_size) + max_extra_steps.  The per-step arrays (spike_mask,
+ * spike_event_idx = queue column, v_steps, event_ms = trace.py:43-60) may be NULL. */
+typedef struct {
+  so_conv_geom conv;
+  int32_t chunk_size;
+  float v_th;
+} so_float_conv_geom;
+
+typedef struct {
+  float *v_final;            /* (n_neurons) */
+  uint8_t *spike_mask;       /* (n_neurons, max_steps) or NULL */
+  int32_t *spike_event_idx;  /* (n_neurons, max_steps) or NULL */
+  float *v_steps;            /* (n_neurons, max_steps) or NULL */
+  float *event_ms;           /* (n_neurons, max_steps) or NULL */
+  float *out_times;          /* (max_out_spikes) */
+  int32_t *out_src;
+  float *out_gain;
+  int32_t n_real_out, needed_queue, extra_steps_needed, fits;
+} so_float_conv_out;
+
+int so_float_conv_forward(const so_float_conv_geom *g, const float *w, float decay_base,
+                          const float *times, const int32_t *src, const float *gain,
+                          int32_t E_len, int32_t n_in, so_float_conv_out *out);
 
 /* lax.associative_scan(combine, maps) of float/affine.py:20-24 over n maps (exposed for tests). */
 int so_affine_scan(const float *a, const float *b, int64_t n, float *out_a, float *out_b);

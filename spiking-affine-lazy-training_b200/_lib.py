@@ -49,6 +49,22 @@ class FloatFCDesc(ctypes.Structure):
                 ("max_extra_steps", _i32), ("v_th", ctypes.c_float)]
 
 
+class FloatConvDesc(ctypes.Structure):
+    _fields_ = [("ic", _i32), ("h_in", _i32), ("w_in", _i32), ("oc", _i32), ("k", _i32),
+                ("s", _i32), ("p", _i32), ("max_queue_len", _i32), ("max_out_spikes", _i32),
+                ("max_extra_steps", _i32), ("chunk_size", _i32), ("v_th", ctypes.c_float)]
+
+
+class FloatConvStats(ctypes.Structure):
+    _fields_ = [("spike_count", _vp), ("needed_queue", _vp), ("needed_extra_steps", _vp),
+                ("fits", _vp)]
+
+
+class FloatTrace(ctypes.Structure):
+    _fields_ = [("v_steps", _vp), ("event_ms", _vp), ("spike_mask", _vp), ("v_max", _vp),
+                ("v_min", _vp)]
+
+
 class FloatLayerStats(ctypes.Structure):
     _fields_ = [(n, _vp) for n in ("spike_count", "needed_extra_steps", "fits")]
 
@@ -88,6 +104,10 @@ _SIGS = {
     "salt_fc_layer_trace": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "salt_stream_h2d_real": (_i32, [_vp, _vp, ctypes.c_int64, _vp, _i32, _i32, _vp, _vp, _vp]),
     "salt_float_fc_layer_workspace_size": (_i32, [_vp, _i32, _i32, _i32, _vp]),
+    "salt_float_conv_layer_workspace_size": (_i32, [_vp, _i32, _i32, _vp]),
+    "salt_float_conv_layer_forward": (_i32, [_vp, _vp, ctypes.c_float, _i32, _vp, _vp, _vp, _vp,
+                                             _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "salt_float_fc_layer_trace": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
     "salt_float_fc_set_profiling": (_i32, [_i32]),
     "salt_float_fc_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "salt_float_fc_layer_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -866,6 +866,199 @@ salt_status salt_float_fc_layer_forward(const salt_float_fc_desc* layer, const f
                             workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+// ---------------------------------------------------------------- float conv layer
+
+struct FConvPlan {
+  int32_t h_out, w_out, n_sp, ncand, nslots, lpu, G, ocp, taps, n_spk_chunks, max_steps, base;
+  int64_t n_neurons;
+};
+
+static salt_status plan_float_conv(const salt_float_conv_desc* d, int32_t E, FConvPlan& p) {
+  if (!d) return fail(SALT_BAD_ARG, "float conv descriptor is NULL");
+  if (d->ic < 1 || d->h_in < 1 || d->w_in < 1 || d->oc < 1 || d->k < 1 || d->s < 1 || d->p < 0)
+    return fail(SALT_BAD_ARG, "conv geometry: ic,h_in,w_in,oc,k,s must be >= 1 and p >= 0");
+  if (d->h_in + d->p > 32000 || d->w_in + d->p > 32000)
+    return fail(SALT_BAD_ARG, "conv input plane too large (h_in + p and w_in + p <= 32000)");
+  p.h_out = (d->h_in + 2 * d->p - d->k) / d->s + 1;
+  p.w_out = (d->w_in + 2 * d->p - d->k) / d->s + 1;
+  if (d->h_in + 2 * d->p - d->k < 0 || p.h_out < 1 || p.w_out < 1)
+    return fail(SALT_BAD_ARG, "conv geometry degenerates to an empty output plane");
+  if (d->max_queue_len < 1) return fail(SALT_BAD_ARG, "max_queue_len must be >= 1");
+  if (d->max_out_spikes < 1) return fail(SALT_BAD_ARG, "max_out_spikes must be >= 1");
+  if (d->max_extra_steps < 0) return fail(SALT_BAD_ARG, "max_extra_steps must be >= 0");
+  if (d->chunk_size < 1) return fail(SALT_BAD_ARG, "chunk_size must be >= 1");
+  if (!(d->v_th > 0.0f) || d->v_th == INFINITY)
+    return fail(SALT_BAD_ARG, "float conv: v_th must be a finite value > 0 (a threshold <= 0 "
+                              "fires on identity columns)");
+  p.n_sp = p.h_out * p.w_out;
+  p.n_neurons = (int64_t)d->oc * p.n_sp;
+  if (p.n_neurons > 0x7fffffffLL) return fail(SALT_BAD_ARG, "too many neurons");
+  p.ncand = (d->k - 1) / d->s + 1;
+  if (p.ncand > 16) return fail(SALT_BAD_ARG, "k / s too large (at most 16 candidates per axis)");
+  p.nslots = p.ncand * p.ncand;
+  int lpu = 1;
+  while (lpu < d->oc && lpu < 32) lpu <<= 1;
+  p.lpu = lpu;
+  p.G = (d->oc + lpu - 1) / lpu;
+  p.ocp = p.G * lpu;
+  p.taps = d->ic * d->k * d->k;
+  p.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
+  p.base = (d->max_queue_len + d->chunk_size - 1) / d->chunk_size;
+  const int64_t steps = (int64_t)p.base + d->max_extra_steps;
+  if (steps > (1 << 30)) return fail(SALT_BAD_ARG, "too many scan steps");
+  p.max_steps = (int32_t)steps;
+  return SALT_OK;
+}
+
+struct FConvScratch {
+  int32_t *stats, *s_total, *needed, *tail_total, *needed_extra, *oc_total, *chunk;
+  int32_t *vkey_max, *vkey_min, *tail_cnt, *hist;
+  size_t stats_bytes;
+  uint32_t* sw;
+  float* wT;
+};
+
+static size_t float_conv_carve(const salt_float_conv_desc* d, const FConvPlan& p, int32_t B,
+                               int32_t E, void* ws, FConvScratch& s) {
+  Carver c(ws);
+  const size_t nstat = (size_t)B * 4 + (size_t)B * d->oc + (size_t)B * p.n_spk_chunks;
+  s.stats = c.take<int32_t>(nstat);
+  s.stats_bytes = nstat * 4;
+  if (s.stats) {
+    s.s_total = s.stats;
+    s.needed = s.stats + B;
+    s.tail_total = s.stats + 2 * B;
+    s.needed_extra = s.stats + 3 * B;
+    s.oc_total = s.stats + 4 * B;
+    s.chunk = s.oc_total + (size_t)B * d->oc;
+  }
+  s.vkey_max = c.take<int32_t>((size_t)B * d->oc);
+  s.vkey_min = c.take<int32_t>((size_t)B * d->oc);
+  s.sw = c.take<uint32_t>((size_t)B * E * p.nslots * p.G);
+  s.tail_cnt = c.take<int32_t>((size_t)B * p.n_neurons);
+  s.hist = c.take<int32_t>((size_t)B * 2 * p.n_sp);
+  s.wT = c.take<float>((size_t)p.taps * p.ocp);
+  return c.size();
+}
+
+salt_status salt_float_conv_layer_workspace_size(const salt_float_conv_desc* layer, int32_t batch,
+                                                 int32_t in_capacity, size_t* bytes) {
+  if (!bytes || batch < 1 || in_capacity < 1) return fail(SALT_BAD_ARG, "bad batch/capacity");
+  FConvPlan p;
+  salt_status rc = plan_float_conv(layer, in_capacity, p);
+  if (rc) return rc;
+  FConvScratch s;
+  *bytes = float_conv_carve(layer, p, batch, in_capacity, nullptr, s);
+  return SALT_OK;
+}
+
+salt_status salt_float_conv_layer_forward(const salt_float_conv_desc* d, const float* w,
+                                          float decay_base, int32_t B, const salt_stream_in* in,
+                                          const float* in_gain, salt_stream_out* out,
+                                          float* v_final, const salt_float_conv_stats* stats,
+                                          const salt_float_trace* trace, void* ws,
+                                          size_t ws_bytes, void* stream) {
+  salt_status rc = check_stream_in(in, B);
+  if (rc) return rc;
+  if (!w || !out || !out->times || !out->src || !out->n_real || !v_final)
+    return fail(SALT_BAD_ARG, "float conv layer: NULL parameter or output pointer");
+  if (!(decay_base > 0.0f) || decay_base > 1.0f)
+    return fail(SALT_BAD_ARG, "float conv: decay_base must be in (0, 1] (tau >= 1)");
+  if (trace && ((trace->v_max == nullptr) != (trace->v_min == nullptr)))
+    return fail(SALT_BAD_ARG, "float conv trace: v_max and v_min go together");
+  const int32_t E = in->capacity;
+  FConvPlan p;
+  if ((rc = plan_float_conv(d, E, p))) return rc;
+  FConvScratch s;
+  const size_t need = float_conv_carve(d, p, B, E, nullptr, s);
+  if (!ws || ws_bytes < need) return fail(SALT_WORKSPACE_TOO_SMALL, "float conv workspace too small");
+  if (reinterpret_cast<uintptr_t>(ws) & 255) return fail(SALT_BAD_ARG, "workspace not 256-byte aligned");
+  float_conv_carve(d, p, B, E, ws, s);
+  cudaStream_t st = (cudaStream_t)stream;
+
+  ConvLaunch L;
+  memset(&L, 0, sizeof(L));
+  L.ic = d->ic; L.h_in = d->h_in; L.w_in = d->w_in; L.hw_in = d->h_in * d->w_in;
+  L.oc = d->oc; L.k = d->k; L.s = d->s; L.p = d->p;
+  L.h_out = p.h_out; L.w_out = p.w_out; L.n_sp = p.n_sp; L.n_neurons = p.n_neurons;
+  L.ncand = p.ncand; L.nslots = p.nslots;
+  L.L = d->max_queue_len; L.M = d->max_out_spikes; L.max_extra = d->max_extra_steps;
+  L.lpu = p.lpu; L.G = p.G; L.ocp = p.ocp;
+  L.tile_h = p.h_out; L.tile_w = p.w_out; L.tiles_x = 1; L.T = 1;
+  L.fd_hw = FastDiv((uint32_t)(d->h_in * d->w_in));
+  L.fd_w = FastDiv((uint32_t)d->w_in);
+  L.fd_s = FastDiv((uint32_t)d->s);
+  L.fd_G = FastDiv((uint32_t)p.G);
+  L.fd_tw = FastDiv((uint32_t)p.w_out);
+  L.in.times = in->times; L.in.src = in->src; L.in.capacity = E; L.in.virtual_pads = in->virtual_pads;
+  L.in_nreal = in->n_real; L.batch = B;
+  L.sw = s.sw; L.sw_stride = (int64_t)E * p.nslots * p.G;
+  L.chunk_spikes = s.chunk; L.chunk_off = s.chunk; L.n_spk_chunks = p.n_spk_chunks;
+  L.s_total = s.s_total; L.oc_total = s.oc_total; L.needed = s.needed;
+  L.tail_total = s.tail_total; L.tail_mode = 1; L.tail_cnt = s.tail_cnt;
+
+  FConvArgs X;
+  memset(&X, 0, sizeof(X));
+  X.wT = s.wT; X.gain = in_gain; X.base = decay_base; X.v_th = d->v_th;
+  X.C = d->chunk_size; X.max_steps = p.max_steps; X.base_steps = p.base;
+  X.v_final = v_final; X.needed_extra = s.needed_extra;
+  float *v_max = nullptr, *v_min = nullptr;
+  if (trace) {
+    X.v_steps = trace->v_steps; X.event_ms = trace->event_ms; X.spike_mask = trace->spike_mask;
+    if (trace->v_max) {
+      X.vkey_max = s.vkey_max; X.vkey_min = s.vkey_min;
+      v_max = trace->v_max; v_min = trace->v_min;
+    }
+  }
+  SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
+  if (v_max) {  // keys below / above every finite float: 0x80808080 and 0x7f7f7f7f
+    SALT_CUDA(cudaMemsetAsync(s.vkey_max, 0x80, sizeof(int32_t) * (size_t)B * d->oc, st));
+    SALT_CUDA(cudaMemsetAsync(s.vkey_min, 0x7f, sizeof(int32_t) * (size_t)B * d->oc, st));
+  }
+  SALT_CUDA(float_conv_launch(L, X, w, s.wT, out->n_real, stats, v_max, v_min, st));
+  g_launches += 3;
+  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
+  SALT_LAUNCHED("spike_chunk_scan");
+  conv_compact<<<dim3(std::min(p.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0,
+                 st>>>(L, *out);
+  SALT_LAUNCHED("conv_compact");
+  conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
+  SALT_LAUNCHED("conv_tail_append");
+  conv_truncated<<<B, kCompactThreads, 0, st>>>(L, *out, s.hist);
+  SALT_LAUNCHED("conv_truncated");
+  return SALT_OK;
+}
+
+salt_status salt_float_fc_layer_trace(const salt_float_fc_desc* d, const float* w,
+                                      const float* decay_base, int32_t B,
+                                      const salt_stream_in* in, const float* in_gain,
+                                      float* v_final, const salt_float_trace* trace,
+                                      void* stream) {
+  salt_status rc = check_float(d);
+  if (rc) return rc;
+  if ((rc = check_stream_in(in, B))) return rc;
+  if (!w || !decay_base) return fail(SALT_BAD_ARG, "float fc trace: NULL weights or decay base");
+  if (trace && ((trace->v_max == nullptr) != (trace->v_min == nullptr)))
+    return fail(SALT_BAD_ARG, "float fc trace: v_max and v_min go together");
+  const int64_t steps = (int64_t)(in->capacity + d->chunk_size - 1) / d->chunk_size +
+                        d->max_extra_steps;
+  if (steps > (1 << 30)) return fail(SALT_BAD_ARG, "too many scan steps");
+  FTraceArgs T;
+  memset(&T, 0, sizeof(T));
+  T.n_in = d->n_in; T.n_out = d->n_out; T.C = d->chunk_size; T.max_steps = (int32_t)steps;
+  T.batch = B; T.v_th = d->v_th;
+  T.in.times = in->times; T.in.src = in->src; T.in.capacity = in->capacity;
+  T.in.virtual_pads = in->virtual_pads; T.in_nreal = in->n_real;
+  T.w = w; T.decay_base = decay_base; T.gain = in_gain; T.v_final = v_final;
+  if (trace) {
+    T.v_max = trace->v_max; T.v_min = trace->v_min; T.v_steps = trace->v_steps;
+    T.event_ms = trace->event_ms; T.spike_mask = trace->spike_mask;
+  }
+  SALT_CUDA(float_fc_trace_launch(T, (cudaStream_t)stream));
+  ++g_launches;
+  return SALT_OK;
+}
+
 salt_status salt_float_fc_set_profiling(int32_t enable) {
   g_fprof.on = enable != 0;
   return SALT_OK;

@@ -254,6 +254,42 @@ cudaError_t fc_trace_launch(const FCLaunch& P, const salt_neuron_trace* rec, int
 // speculative segment kernel.
 cudaError_t float_fc_launch(const FloatLaunch& P, cudaStream_t st, int64_t* launches,
                             cudaEvent_t seg_start = nullptr, cudaEvent_t seg_stop = nullptr);
+// Float conv layer (float_conv.cu): per-warp arguments beyond the shared ConvLaunch geometry,
+// stream and spike-word scratch.
+constexpr int kFConvThreads = 128;
+struct FConvArgs {
+  const float* wT;            // (ic*k*k, ocp) weights, channels zero-padded
+  const float* gain;          // (B, E) event gains or null (ones)
+  float base, v_th;           // float32(1 - 1/tau), ConvLayer.v_th
+  int32_t C, max_steps, base_steps;
+  float* v_final;             // (B, n_neurons)
+  int32_t* needed_extra;      // (B)
+  int32_t *vkey_max, *vkey_min;  // (B, oc) order-preserving keys of the potential extremes
+  float* v_steps;             // (B, n_neurons, max_steps) traces, or null
+  float* event_ms;
+  uint8_t* spike_mask;
+};
+cudaError_t float_conv_launch(const ConvLaunch& P, const FConvArgs& X, const float* w, float* wT,
+                              int32_t* out_nreal, const salt_float_conv_stats* st, float* v_max,
+                              float* v_min, cudaStream_t stream);
+
+// Float FC per-step traces and potential ranges (float_conv.cu).
+struct FTraceArgs {
+  int32_t n_in, n_out, C, max_steps, batch;
+  float v_th;
+  StreamView in;
+  const int32_t* in_nreal;
+  const float* w;             // (n_out, n_in)
+  const float* decay_base;    // (n_out)
+  const float* gain;          // (B, E) or null
+  float* v_final;             // (B, n_out) or null
+  float *v_max, *v_min;       // (B, n_out) or null
+  float* v_steps;             // (B, n_out, max_steps) or null
+  float* event_ms;
+  uint8_t* spike_mask;
+};
+cudaError_t float_fc_trace_launch(const FTraceArgs& T, cudaStream_t stream);
+
 constexpr int kFcThreads = 128;
 constexpr int kFcRing = 4;            // events per lane per fc_scan super-batch (smem codes)
 constexpr size_t kFcQSmemMax = 96 * 1024;  // largest staged weight table of fc_scan
