@@ -39,7 +39,10 @@ def test_struct_layouts_match_the_header(tmp_path):
                "salt_stream_out": _lib.StreamOut, "salt_layer_stats": _lib.LayerStats,
                "salt_layer_spec": _lib.LayerSpec, "salt_float_fc_desc": _lib.FloatFCDesc,
                "salt_float_layer_stats": _lib.FloatLayerStats,
-               "salt_neuron_trace": _lib.NeuronTrace}
+               "salt_neuron_trace": _lib.NeuronTrace,
+               "salt_float_conv_desc": _lib.FloatConvDesc,
+               "salt_float_conv_stats": _lib.FloatConvStats,
+               "salt_float_trace": _lib.FloatTrace}
     src = tmp_path / "sizes.c"
     src.write_text('#include <stdio.h>\n#include "salt_b200.h"\nint main(void){\n' + "".join(
         f'printf("{n} %zu\\n", sizeof({n}));\n' for n in structs) + "return 0;}\n")
@@ -74,6 +77,21 @@ def test_bad_arguments_are_reported_before_any_device_work():
     f = _lib.FCDesc(0, 10, 1, 0)
     assert lib.salt_fc_layer_workspace_size(_lib.byref(f), _lib.byref(q), 4, 1000,
                                             _lib.byref(n)) == _lib.SALT_BAD_ARG
+
+
+def test_float_conv_arguments_are_checked_on_the_host():
+    lib = _lib.lib()
+    n = ctypes.c_size_t(0)
+    d = _lib.FloatConvDesc(2, 34, 34, 16, 3, 2, 0, 64, 100, 0, 1, 1.0)
+    assert lib.salt_float_conv_layer_workspace_size(_lib.byref(d), 4, 1000,
+                                                    _lib.byref(n)) == _lib.SALT_OK
+    assert n.value > 0
+    for bad in (_lib.FloatConvDesc(2, 34, 34, 16, 3, 2, 0, 64, 100, 0, 1, 0.0),    # v_th <= 0
+                _lib.FloatConvDesc(2, 34, 34, 16, 3, 2, 0, 64, 100, 0, 0, 1.0),    # chunk 0
+                _lib.FloatConvDesc(2, 34, 34, 16, 3, 2, 0, 0, 100, 0, 1, 1.0),     # no queue
+                _lib.FloatConvDesc(2, 2, 2, 16, 3, 2, 0, 64, 100, 0, 1, 1.0)):     # degenerate
+        assert lib.salt_float_conv_layer_workspace_size(_lib.byref(bad), 4, 1000,
+                                                        _lib.byref(n)) == _lib.SALT_BAD_ARG
 
 
 def test_workspace_is_independent_of_the_queue_capacity():
