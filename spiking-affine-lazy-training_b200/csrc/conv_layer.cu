@@ -420,7 +420,7 @@ conv_fused(ConvLaunch P) {
         if (e < nchunk)
           for (int i = 0; i < SWW; ++i) cnt += __popc(sw_s[e * SWW + i]);
         cnt = warp_sum(cnt);
-        if (lane == 0 && cnt) atomicAdd(&chunk_spk_b[(base + e0) >> kSpkChunkShift], cnt);
+        if (lane == 0 && cnt) atomicAdd(&chunk_spk_b[(base + e0) >> kConvGroupShift], cnt);
       }
     } else {
       // several tiles share an event: write only the slots whose position is in this tile
@@ -440,7 +440,7 @@ conv_fused(ConvLaunch P) {
               cnt += __popc(wd);
             }
           }
-        if (cnt) atomicAdd(&chunk_spk_b[j >> kSpkChunkShift], cnt);
+        if (cnt) atomicAdd(&chunk_spk_b[j >> kConvGroupShift], cnt);
       }
     }
     __syncthreads();
@@ -531,59 +531,163 @@ conv_fused(ConvLaunch P) {
 
 // ------------------------------------------------------------------ compaction
 
-// Emits sample b's spikes in (event, neuron) order; block x walks the sample's 256-event chunks
-// x, x + gridDim.x, ... (each chunk's output offset comes from the scanned per-chunk counts).
+// r-th spike (0-based) of an event whose candidate slots s < 4 hold spike words w[s] (bit = channel,
+// valid slots only), in neuron order: channel ascending, then slot.  The per-channel counts are
+// summed bit-sliced (lo + 2 mid + 4 hi, a carry-save add of the four words), the channel is found
+// by binary lifting over prefix counts, then the slot among that channel's set bits.
+__device__ __forceinline__ void rank_in_words(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                              int32_t r, int& channel, int& slot) {
+  const uint32_t s1 = w0 ^ w1, c1 = w0 & w1, s2 = w2 ^ w3, c2 = w2 & w3;
+  const uint32_t lo = s1 ^ s2, cl = s1 & s2;
+  const uint32_t mid = c1 ^ c2 ^ cl, hi = (c1 & c2) | (cl & (c1 ^ c2));
+  int c = 0, below = 0;  // channels [0, c) hold `below` spikes, below <= r
+#pragma unroll
+  for (int step = 16; step > 0; step >>= 1) {
+    const int t = c + step;
+    const uint32_t m = t >= 32 ? 0xffffffffu : ((1u << t) - 1u);
+    const int cum = __popc(lo & m) + 2 * __popc(mid & m) + 4 * __popc(hi & m);
+    if (cum <= r) {
+      c = t;
+      below = cum;
+    }
+  }
+  int rem = r - below, sl = 0;
+  const uint32_t bit = 1u << c;
+  const bool b0 = w0 & bit, b1 = w1 & bit, b2 = w2 & bit;
+  if (b0 && rem-- == 0) sl = 0;
+  else if (b1 && rem-- == 0) sl = 1;
+  else if (b2 && rem-- == 0) sl = 2;
+  else sl = 3;
+  channel = c;
+  slot = sl;
+}
+
+// Emits sample b's spikes in (event, neuron) order.  One warp per group of 32 input events (the
+// groups' output offsets come from the scanned per-group spike counts); the warps of block x take
+// groups x * warps + warp, stepping by the grid.  Within an event the order is channel group,
+// channel, then position (oy, ox) ascending, i.e. neuron index order.  Each lane counts its
+// event's spikes over the valid candidate slots; a warp scan gives every event its offset; then
+// the expansion is load-balanced: lane q of each 32-output round finds its event by a binary
+// search over the lanes' inclusive offsets, decodes which of the event's spikes it is and writes
+// it, so the warp writes consecutive entries and its work follows the spikes.  Warps never wait
+// on one another (no shared memory, no block barrier).  FOUR: at most 2 candidates per axis and
+// one channel group (the benchmark geometries): the event's four slot words stay in registers
+// and the decode is bit arithmetic on them (rank_in_words); otherwise the words are re-read.
+template <bool FOUR>
 __global__ void __launch_bounds__(kCompactThreads)
 conv_compact(ConvLaunch P, salt_stream_out out) {
-  __shared__ int32_t s_scan[kScanSmem];
-  const int b = blockIdx.y, tid = threadIdx.x;
+  constexpr uint32_t kAll = 0xffffffffu;
+  const int b = blockIdx.y, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
   const int32_t S = P.s_total[b];
   if (S > P.M) return;  // truncated samples go through conv_truncated
   const int32_t n_eff = P.n_eff(b);
   const int SWW = P.nslots * P.G;
+  const uint32_t* sw_b = P.sw + (int64_t)b * P.sw_stride;
   float* ot = out.times + (int64_t)b * P.M;
   int32_t* os = out.src + (int64_t)b * P.M;
-  for (int32_t c = blockIdx.x; c * kSpkChunk < n_eff; c += gridDim.x) {
-    const int32_t j = c * kSpkChunk + tid;
-    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
+  const int32_t n_groups = (n_eff + kConvGroup - 1) >> kConvGroupShift;
+  for (int32_t grp = blockIdx.x * wpb + (threadIdx.x >> 5); grp < n_groups;
+       grp += gridDim.x * wpb) {
+    const int32_t j = (grp << kConvGroupShift) + lane;
     int32_t cnt = 0;
-    EvCand k{0, 1, 0, 0, 1, 0};
+    uint32_t om = 0, rg = 0, w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+    float t = 0.0f;
     if (j < n_eff) {
       int32_t cc, y, x;
-      k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
-      for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
-        for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
-          const int slot = (oy - k.oy_min) * P.ncand + (ox - k.ox_min);
-          for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[slot * P.G + g]);
+      const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
+      const uint32_t* sw_j = sw_b + (int64_t)j * SWW;
+      if (FOUR) {  // slot s = (sy, sx) = (s / ncand, s % ncand), ncand <= 2, G == 1
+        const bool two = P.ncand == 2;
+        const bool y0 = k.oy_min >= k.oy_lo && k.oy_min <= k.oy_hi;
+        const bool y1 = two && k.oy_min + 1 >= k.oy_lo && k.oy_min + 1 <= k.oy_hi;
+        const bool x0 = k.ox_min >= k.ox_lo && k.ox_min <= k.ox_hi;
+        const bool x1 = two && k.ox_min + 1 >= k.ox_lo && k.ox_min + 1 <= k.ox_hi;
+        if (y0 && x0) w0 = sw_j[0];
+        if (two) {
+          if (y0 && x1) w1 = sw_j[1];
+          if (y1 && x0) w2 = sw_j[2];
+          if (y1 && x1) w3 = sw_j[3];
         }
-    }
-    int32_t total;
-    const int32_t off = block_exclusive_scan(cnt, s_scan, total);
-    if (cnt == 0) continue;
-    const int32_t base = P.chunk_off[(int64_t)b * P.n_spk_chunks + c] + off;
-    const float t = P.in.time(b, j, n_eff);
-    int32_t kk = 0;
-    for (int g = 0; g < P.G; ++g) {
-      uint32_t uni = 0;
-      for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
-        for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
-          uni |= sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
-      while (uni) {
-        const int bit = __ffs(uni) - 1;
-        uni &= uni - 1u;
-        const int oc = g * P.lpu + bit;
+        cnt = __popc(w0) + __popc(w1) + __popc(w2) + __popc(w3);
+      } else {
         for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
           for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
-            const uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
-            if (wd & (1u << bit)) {
-              ot[base + kk] = t;
-              os[base + kk] = oc * P.n_sp + oy * P.w_out + ox;
-              ++kk;
+            const int slot = (oy - k.oy_min) * P.ncand + (ox - k.ox_min);
+            for (int g = 0; g < P.G; ++g) cnt += __popc(sw_j[slot * P.G + g]);
+          }
+      }
+      if (cnt) {
+        om = ((uint32_t)(k.oy_min + 32768) << 16) | (uint32_t)(k.ox_min + 32768);
+        rg = (uint32_t)(k.oy_lo - k.oy_min) | ((uint32_t)(k.oy_hi - k.oy_min) << 4) |
+             ((uint32_t)(k.ox_lo - k.ox_min) << 8) | ((uint32_t)(k.ox_hi - k.ox_min) << 12);
+        t = P.in.time(b, j, n_eff);
+      }
+    }
+    int32_t incl = cnt;  // inclusive scan over the warp's events
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(kAll, incl, o);
+      if (lane >= o) incl += n;
+    }
+    const int32_t total = __shfl_sync(kAll, incl, 31);
+    if (total == 0) continue;
+    const int32_t base = P.chunk_off[(int64_t)b * P.n_spk_chunks + grp];
+    for (int32_t q0 = 0; q0 < total; q0 += 32) {
+      const int32_t q = q0 + lane;
+      int e = 0;  // lanes whose inclusive offset is <= q: the event holding output q
+#pragma unroll
+      for (int step = 16; step > 0; step >>= 1)
+        if (__shfl_sync(kAll, incl, e + step - 1) <= q) e += step;
+      const int32_t before = __shfl_sync(kAll, incl, e > 0 ? e - 1 : 0);
+      const uint32_t eom = __shfl_sync(kAll, om, e);
+      const float et = __shfl_sync(kAll, t, e);
+      const int oy_min = (int)(eom >> 16) - 32768, ox_min = (int)(eom & 0xffffu) - 32768;
+      int32_t r = q - (e > 0 ? before : 0);  // rank among the event's spikes
+      int32_t neuron = -1;
+      if (FOUR) {
+        const uint32_t e0 = __shfl_sync(kAll, w0, e), e1 = __shfl_sync(kAll, w1, e);
+        const uint32_t e2 = __shfl_sync(kAll, w2, e), e3 = __shfl_sync(kAll, w3, e);
+        int ch, sl;
+        rank_in_words(e0, e1, e2, e3, r, ch, sl);
+        const int sy = P.ncand == 2 ? sl >> 1 : 0, sx = P.ncand == 2 ? sl & 1 : 0;
+        neuron = ch * P.n_sp + (oy_min + sy) * P.w_out + (ox_min + sx);
+      }
+      if (!FOUR) {
+        const uint32_t erg = __shfl_sync(kAll, rg, e);
+        if (q < total) {
+          const int ylo = erg & 15, yhi = (erg >> 4) & 15, xlo = (erg >> 8) & 15;
+          const int xhi = (erg >> 12) & 15;
+          const uint32_t* sw_j = sw_b + (int64_t)((grp << kConvGroupShift) + e) * SWW;
+          for (int g = 0; g < P.G && neuron < 0; ++g) {
+            uint32_t uni = 0;
+            for (int sy = ylo; sy <= yhi; ++sy)
+              for (int sx = xlo; sx <= xhi; ++sx) uni |= sw_j[(sy * P.ncand + sx) * P.G + g];
+            while (uni && neuron < 0) {
+              const int bit = __ffs(uni) - 1;
+              uni &= uni - 1u;
+              for (int sy = ylo; sy <= yhi && neuron < 0; ++sy)
+                for (int sx = xlo; sx <= xhi; ++sx)
+                  if ((sw_j[(sy * P.ncand + sx) * P.G + g] >> bit) & 1u) {
+                    if (r == 0) {
+                      neuron = (g * P.lpu + bit) * P.n_sp + (oy_min + sy) * P.w_out + (ox_min + sx);
+                      break;
+                    }
+                    --r;
+                  }
             }
           }
+        }
+      }
+      if (q < total) {
+        ot[base + q] = et;
+        os[base + q] = neuron;
       }
     }
   }
+}
+
+void* conv_compact_kernel(int ncand, int G) {
+  return (ncand <= 2 && G == 1) ? (void*)conv_compact<true> : (void*)conv_compact<false>;
 }
 
 // Spikes on catch-up / identity columns (tail mode only): they map to the empty queue entry

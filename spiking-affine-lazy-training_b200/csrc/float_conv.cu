@@ -196,7 +196,7 @@ __global__ void __launch_bounds__(kFConvThreads) fconv_scan(ConvLaunch P, FConvA
         const int32_t jj = ev_j[warp][r];
         sw_b[(int64_t)jj * SWW + ev_slot[warp][r] * P.G + g] = bits;
         if (bits)
-          atomicAdd(&P.chunk_spikes[(int64_t)b * P.n_spk_chunks + (jj >> kSpkChunkShift)],
+          atomicAdd(&P.chunk_spikes[(int64_t)b * P.n_spk_chunks + (jj >> kConvGroupShift)],
                     __popc(bits));
       }
     }

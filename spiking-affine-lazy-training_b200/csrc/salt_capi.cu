@@ -38,6 +38,13 @@ static inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Compaction blocks per sample: the per-sample minimum, or enough to fill the GPU when the
 // batch is small.
+// Blocks per sample for conv_compact (8 warps each, one 32-event group per warp at a time):
+// about 16 K warps over the batch, no more than the groups need.
+static int conv_compact_blocks(int32_t n_groups, int32_t B) {
+  const int want = (2048 + B - 1) / std::max(B, 1);
+  return std::max(1, std::min((n_groups + 7) / 8, std::max(2, want)));
+}
+
 static int compact_blocks(int32_t B) {
   return std::max(kCompactBlocksPerSample, (1184 + B - 1) / std::max(B, 1));
 }
@@ -262,7 +269,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   const int per_x = p.tiles_x > 1 ? (p.ncand - 1 + p.tile_w - 1) / p.tile_w + 1 : 1;
   p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
   p.n_part_chunks = (E + kPartChunk - 1) / kPartChunk;
-  p.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
+  p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
   p.smem = fused_smem(d, q, p, p.tile_h, p.tile_w, p.T);
   if (p.smem > 227 * 1024)
     return fail(SALT_BAD_ARG, "conv layer weights do not fit in shared memory (ic*k*k*oc too "
@@ -382,8 +389,13 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   if (timer) SALT_CUDA(cudaEventRecord(timer->stop, st));
   spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
   SALT_LAUNCHED("spike_chunk_scan");
-  conv_compact<<<dim3(std::min(p.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0,
-                 st>>>(L, *out);
+  {
+    salt_stream_out so = *out;
+    void* cargs[] = {&L, &so};
+    SALT_CUDA(cudaLaunchKernel(conv_compact_kernel(p.ncand, p.G),
+                               dim3(conv_compact_blocks(p.n_spk_chunks, B), B),
+                               dim3(kCompactThreads), cargs, 0, st));
+  }
   SALT_LAUNCHED("conv_compact");
   if (p.tail_mode) {
     conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
@@ -902,7 +914,7 @@ static salt_status plan_float_conv(const salt_float_conv_desc* d, int32_t E, FCo
   p.G = (d->oc + lpu - 1) / lpu;
   p.ocp = p.G * lpu;
   p.taps = d->ic * d->k * d->k;
-  p.n_spk_chunks = (E + kSpkChunk - 1) / kSpkChunk;
+  p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
   p.base = (d->max_queue_len + d->chunk_size - 1) / d->chunk_size;
   const int64_t steps = (int64_t)p.base + d->max_extra_steps;
   if (steps > (1 << 30)) return fail(SALT_BAD_ARG, "too many scan steps");
@@ -1019,8 +1031,13 @@ salt_status salt_float_conv_layer_forward(const salt_float_conv_desc* d, const f
   g_launches += 3;
   spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
   SALT_LAUNCHED("spike_chunk_scan");
-  conv_compact<<<dim3(std::min(p.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0,
-                 st>>>(L, *out);
+  {
+    salt_stream_out so = *out;
+    void* cargs[] = {&L, &so};
+    SALT_CUDA(cudaLaunchKernel(conv_compact_kernel(p.ncand, p.G),
+                               dim3(conv_compact_blocks(p.n_spk_chunks, B), B),
+                               dim3(kCompactThreads), cargs, 0, st));
+  }
   SALT_LAUNCHED("conv_compact");
   conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
   SALT_LAUNCHED("conv_tail_append");

@@ -12,6 +12,9 @@ constexpr int kCompactThreads = 256; // compaction block size == events per spik
 constexpr int kSpkChunkShift = 8;
 constexpr int kSpkChunk = 1 << kSpkChunkShift;
 static_assert(kSpkChunk == kCompactThreads, "one compaction block per spike chunk");
+// Conv layers count spikes per group of 32 input events (one compaction warp per group).
+constexpr int kConvGroupShift = 5;
+constexpr int kConvGroup = 1 << kConvGroupShift;
 constexpr int kLutSmemMax = 4096;    // decay tables longer than this are read from global
 constexpr int kCompactBlocksPerSample = 8;  // compaction blocks per sample (grid-stride)
 constexpr int kScanSmem = 33;        // ints of shared memory block_exclusive_scan needs
@@ -220,7 +223,8 @@ __global__ void conv_tile_count(ConvLaunch P, int32_t* counts);
 __global__ void conv_tile_scan_offsets(ConvLaunch P, int32_t* counts, int32_t* tile_len,
                                        int32_t* tile_off);
 __global__ void conv_tile_scatter(ConvLaunch P, const int32_t* counts, int32_t* lists);
-__global__ void conv_compact(ConvLaunch P, salt_stream_out out);
+// conv_compact specialised for the geometry (ncand <= 2 and one channel group, or the rest).
+void* conv_compact_kernel(int ncand, int G);
 __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out);
 __global__ void conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* scratch_hist);
 __global__ void fc_compact(FCLaunch P, salt_stream_out out);
