@@ -41,6 +41,32 @@ __device__ __forceinline__ EvCand event_cand(const ConvLaunch& P, int32_t src, i
   return r;
 }
 
+// ------------------------------------------------------------------ schedule
+
+// Samples by decreasing event count: a stable-enough counting sort over 1024 bins of
+// min(n_real, capacity) (ties in any order; only the block schedule depends on it).
+__global__ void __launch_bounds__(kOrderThreads)
+sample_order_desc(const int32_t* __restrict__ n_real, int32_t capacity, int32_t batch,
+                  int32_t* __restrict__ order) {
+  __shared__ int32_t bins[kOrderThreads];
+  __shared__ int32_t s_scan[kScanSmem];
+  const int tid = threadIdx.x;
+  bins[tid] = 0;
+  __syncthreads();
+  auto bin_of = [&](int b) {
+    const int32_t n = min(max(n_real[b], 0), capacity);
+    const int bin = (int)(((int64_t)n * (kOrderThreads - 1)) / max(capacity, 1));
+    return kOrderThreads - 1 - bin;  // heaviest first
+  };
+  for (int b = tid; b < batch; b += blockDim.x) atomicAdd(&bins[bin_of(b)], 1);
+  __syncthreads();
+  int32_t total;
+  const int32_t off = block_exclusive_scan(bins[tid], s_scan, total);
+  bins[tid] = off;
+  __syncthreads();
+  for (int b = tid; b < batch; b += blockDim.x) order[atomicAdd(&bins[bin_of(b)], 1)] = b;
+}
+
 // ------------------------------------------------------------------ tile partition
 
 __global__ void conv_tile_count(ConvLaunch P, int32_t* __restrict__ counts) {
@@ -204,7 +230,8 @@ conv_fused(ConvLaunch P) {
   int32_t* ocspk_s = reinterpret_cast<int32_t*>(smem + L.ocspk);
   int32_t* misc_s = reinterpret_cast<int32_t*>(smem + L.misc);
 
-  const int b = blockIdx.y, tile = blockIdx.x;
+  // blocks run in launch order, so the heaviest samples start first (a longest-first schedule)
+  const int b = P.order ? P.order[blockIdx.y] : blockIdx.y, tile = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gi = lane / LPU, glane = lane % LPU;
   const uint32_t gmask_bits = LPU == 32 ? 0xffffffffu : ((1u << LPU) - 1u);

@@ -282,7 +282,7 @@ struct ConvScratch {
   int32_t *stats, *s_total, *needed, *vmin, *vmax, *ovf, *tail_total, *oc_total, *chunk;
   size_t stats_bytes;
   uint32_t* sw;
-  int32_t *tail_cnt, *counts, *tile_len, *tile_off, *lists, *hist;
+  int32_t *tail_cnt, *counts, *tile_len, *tile_off, *lists, *hist, *order;
 };
 
 static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, int32_t E,
@@ -312,6 +312,7 @@ static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, 
     s.counts = s.tile_len = s.tile_off = s.lists = nullptr;
   }
   s.hist = c.take<int32_t>((size_t)B * 2 * p.n_sp);
+  s.order = c.take<int32_t>((size_t)B);
   return c.size();
 }
 
@@ -367,8 +368,13 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.vmax = s.vmax; L.ovf = s.ovf; L.tail_total = s.tail_total;
   L.tail_mode = p.tail_mode; L.tail_cnt = s.tail_cnt;
   L.tile_len = s.tile_len; L.tile_off = s.tile_off; L.tile_lists = s.lists;
+  L.order = B > 1 ? s.order : nullptr;
 
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
+  if (L.order) {
+    sample_order_desc<<<1, kOrderThreads, 0, st>>>(in->n_real, E, B, s.order);
+    SALT_LAUNCHED("sample_order_desc");
+  }
   if (p.T > 1) {
     dim3 gp(p.n_part_chunks, B);
     conv_tile_count<<<gp, 256, p.T * sizeof(int32_t), st>>>(L, s.counts);

@@ -56,6 +56,7 @@ struct ConvLaunch {
   int32_t *s_total, *oc_total, *needed, *vmin, *vmax, *ovf, *tail_total;
   int32_t tail_mode;
   int32_t* tail_cnt;          // [B][n_neurons] (tail mode only)
+  const int32_t* order;       // [B] samples heaviest first (block y -> sample), or null
   const int32_t* tile_len;    // [B][T] events per tile
   const int32_t* tile_off;    // [B][T] start of each tile's list in the sample's region
   const int32_t* tile_lists;  // [B][list_stride] event indices, tile-major, arrival order
@@ -223,6 +224,10 @@ __global__ void conv_tile_count(ConvLaunch P, int32_t* counts);
 __global__ void conv_tile_scan_offsets(ConvLaunch P, int32_t* counts, int32_t* tile_len,
                                        int32_t* tile_off);
 __global__ void conv_tile_scatter(ConvLaunch P, const int32_t* counts, int32_t* lists);
+// order[0..B) = samples by decreasing min(n_real, capacity) (counting sort, one block).
+__global__ void sample_order_desc(const int32_t* __restrict__ n_real, int32_t capacity,
+                                  int32_t batch, int32_t* __restrict__ order);
+constexpr int kOrderThreads = 1024;
 // conv_compact specialised for the geometry (ncand <= 2 and one channel group, or the rest).
 void* conv_compact_kernel(int ncand, int G);
 __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out);
