@@ -69,25 +69,53 @@ sample_order_desc(const int32_t* __restrict__ n_real, int32_t capacity, int32_t 
 
 // ------------------------------------------------------------------ tile partition
 
-__global__ void conv_tile_count(ConvLaunch P, int32_t* __restrict__ counts) {
-  extern __shared__ int32_t s_cnt[];
-  const int b = blockIdx.y, ch = blockIdx.x;
-  for (int t = threadIdx.x; t < P.T; t += blockDim.x) s_cnt[t] = 0;
-  __syncthreads();
-  const int32_t n_eff = P.n_eff(b);
-  for (int32_t e = threadIdx.x; e < kPartChunk; e += blockDim.x) {
-    const int32_t jj = ch * kPartChunk + e;
-    if (jj >= n_eff) break;
-    int32_t c, y, x;
-    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + jj], c, y, x);
-    if (k.empty()) continue;
-    for (int ty = k.oy_lo / P.tile_h; ty <= k.oy_hi / P.tile_h; ++ty)
-      for (int tx = k.ox_lo / P.tile_w; tx <= k.ox_hi / P.tile_w; ++tx)
-        atomicAdd(&s_cnt[ty * P.tiles_x + tx], 1);
+// Partition chunks of a sample that hold real events; chunks past them are neither counted
+// nor scanned.  Blocks of a sample loop over its chunks (grid x = blocks per sample).
+__device__ __forceinline__ int32_t part_chunks(const ConvLaunch& P, int b) {
+  return (P.n_eff(b) + kPartChunk - 1) / kPartChunk;
+}
+
+// The kPartPer events of a thread in partition chunk ch, decoded (empty ranges past n_eff).  The
+// source loads are issued together so that their latencies overlap.
+__device__ __forceinline__ void part_events(const ConvLaunch& P, int b, int ch, int32_t n_eff,
+                                            EvCand (&k)[kPartPer]) {
+  int32_t src[kPartPer];
+#pragma unroll
+  for (int i = 0; i < kPartPer; ++i) {
+    const int32_t jj = ch * kPartChunk + i * kPartThreads + (int)threadIdx.x;
+    src[i] = jj < n_eff ? P.in.src[(int64_t)b * P.in.capacity + jj] : 0;
   }
-  __syncthreads();
-  for (int t = threadIdx.x; t < P.T; t += blockDim.x)
-    counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t] = s_cnt[t];
+#pragma unroll
+  for (int i = 0; i < kPartPer; ++i) {
+    const int32_t jj = ch * kPartChunk + i * kPartThreads + (int)threadIdx.x;
+    int32_t c, y, x;
+    k[i] = event_cand(P, src[i], c, y, x);
+    if (jj >= n_eff) k[i] = EvCand{0, 1, 0, 0, 1, 0};
+  }
+}
+
+__global__ void __launch_bounds__(kPartThreads)
+conv_tile_count(ConvLaunch P, int32_t* __restrict__ counts) {
+  extern __shared__ int32_t s_cnt[];
+  const int b = blockIdx.y;
+  const int32_t n_eff = P.n_eff(b), nch = part_chunks(P, b);
+  for (int ch = blockIdx.x; ch < nch; ch += gridDim.x) {
+    for (int t = threadIdx.x; t < P.T; t += blockDim.x) s_cnt[t] = 0;
+    __syncthreads();
+    EvCand k[kPartPer];
+    part_events(P, b, ch, n_eff, k);
+#pragma unroll
+    for (int i = 0; i < kPartPer; ++i) {
+      if (k[i].empty()) continue;
+      for (int ty = (int)P.fd_th.div(k[i].oy_lo), ty1 = (int)P.fd_th.div(k[i].oy_hi); ty <= ty1; ++ty)
+        for (int tx = (int)P.fd_tw.div(k[i].ox_lo), tx1 = (int)P.fd_tw.div(k[i].ox_hi); tx <= tx1; ++tx)
+          atomicAdd(&s_cnt[ty * P.tiles_x + tx], 1);
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < P.T; t += blockDim.x)
+      counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t] = s_cnt[t];
+    __syncthreads();
+  }
 }
 
 // One warp per sample: turns the per-(chunk, tile) counts into absolute offsets inside the
@@ -98,20 +126,21 @@ __global__ void conv_tile_scan_offsets(ConvLaunch P, int32_t* __restrict__ count
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= P.batch) return;
   const int b = warp;
+  const int32_t nch = part_chunks(P, b);
   int32_t tile_base = 0;
   for (int t = 0; t < P.T; ++t) {
     int32_t carry = 0;
-    for (int base = 0; base < P.n_part_chunks; base += 32) {
+    for (int base = 0; base < nch; base += 32) {
       const int c = base + lane;
       const int64_t idx = ((int64_t)b * P.n_part_chunks + c) * P.T + t;
-      const int32_t v = c < P.n_part_chunks ? counts[idx] : 0;
+      const int32_t v = c < nch ? counts[idx] : 0;
       int32_t incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += n;
       }
-      if (c < P.n_part_chunks) counts[idx] = tile_base + carry + incl - v;
+      if (c < nch) counts[idx] = tile_base + carry + incl - v;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) {
@@ -122,48 +151,55 @@ __global__ void conv_tile_scan_offsets(ConvLaunch P, int32_t* __restrict__ count
   }
 }
 
-__global__ void conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ counts,
-                                  int32_t* __restrict__ lists) {
+__global__ void __launch_bounds__(kPartThreads)
+conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ counts, int32_t* __restrict__ lists) {
   extern __shared__ uint32_t s_mask[];  // [T][kPartChunk/32] then word prefix [T][kPartChunk/32]
   constexpr int W = kPartChunk / 32;
+  static_assert(W == 32, "one warp scans one tile's words");
   uint32_t* s_pre = s_mask + P.T * W;
-  const int b = blockIdx.y, ch = blockIdx.x;
-  for (int i = threadIdx.x; i < P.T * W; i += blockDim.x) s_mask[i] = 0;
-  __syncthreads();
-  const int32_t n_eff = P.n_eff(b);
-  for (int32_t e = threadIdx.x; e < kPartChunk; e += blockDim.x) {
-    const int32_t jj = ch * kPartChunk + e;
-    if (jj >= n_eff) break;
-    int32_t c, y, x;
-    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + jj], c, y, x);
-    if (k.empty()) continue;
-    for (int ty = k.oy_lo / P.tile_h; ty <= k.oy_hi / P.tile_h; ++ty)
-      for (int tx = k.ox_lo / P.tile_w; tx <= k.ox_hi / P.tile_w; ++tx)
-        atomicOr(&s_mask[(ty * P.tiles_x + tx) * W + (e >> 5)], 1u << (e & 31));
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < P.T; t += blockDim.x) {  // word prefix per tile
-    uint32_t acc = 0;
-    for (int w = 0; w < W; ++w) {
-      s_pre[t * W + w] = acc;
-      acc += __popc(s_mask[t * W + w]);
-    }
-  }
-  __syncthreads();
+  const int b = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int32_t n_eff = P.n_eff(b), nch = part_chunks(P, b);
   int32_t* list_b = lists + (int64_t)b * P.list_stride;
-  for (int32_t e = threadIdx.x; e < kPartChunk; e += blockDim.x) {
-    const int32_t jj = ch * kPartChunk + e;
-    if (jj >= n_eff) break;
-    int32_t c, y, x;
-    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + jj], c, y, x);
-    if (k.empty()) continue;
-    for (int ty = k.oy_lo / P.tile_h; ty <= k.oy_hi / P.tile_h; ++ty)
-      for (int tx = k.ox_lo / P.tile_w; tx <= k.ox_hi / P.tile_w; ++tx) {
-        const int t = ty * P.tiles_x + tx;
-        const uint32_t m = s_mask[t * W + (e >> 5)] & ((1u << (e & 31)) - 1u);
-        const int32_t rank = (int32_t)(s_pre[t * W + (e >> 5)] + __popc(m));
-        list_b[counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t] + rank] = jj;
+  for (int ch = blockIdx.x; ch < nch; ch += gridDim.x) {
+    for (int i = threadIdx.x; i < P.T * W; i += blockDim.x) s_mask[i] = 0;
+    __syncthreads();
+    EvCand k[kPartPer];  // kept in registers for the write pass
+    part_events(P, b, ch, n_eff, k);
+#pragma unroll
+    for (int i = 0; i < kPartPer; ++i) {
+      if (k[i].empty()) continue;
+      const int e = i * kPartThreads + (int)threadIdx.x;
+      for (int ty = (int)P.fd_th.div(k[i].oy_lo), ty1 = (int)P.fd_th.div(k[i].oy_hi); ty <= ty1; ++ty)
+        for (int tx = (int)P.fd_tw.div(k[i].ox_lo), tx1 = (int)P.fd_tw.div(k[i].ox_hi); tx <= tx1; ++tx)
+          atomicOr(&s_mask[(ty * P.tiles_x + tx) * W + (e >> 5)], 1u << (e & 31));
+    }
+    __syncthreads();
+    for (int t = warp; t < P.T; t += nwarps) {  // word prefix per tile: one warp scan per tile
+      const int32_t v = __popc(s_mask[t * W + lane]);
+      int32_t incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
       }
+      s_pre[t * W + lane] = (uint32_t)(incl - v);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kPartPer; ++i) {
+      if (k[i].empty()) continue;
+      const int e = i * kPartThreads + (int)threadIdx.x;
+      const int32_t jj = ch * kPartChunk + e;
+      for (int ty = (int)P.fd_th.div(k[i].oy_lo), ty1 = (int)P.fd_th.div(k[i].oy_hi); ty <= ty1; ++ty)
+        for (int tx = (int)P.fd_tw.div(k[i].ox_lo), tx1 = (int)P.fd_tw.div(k[i].ox_hi); tx <= tx1; ++tx) {
+          const int t = ty * P.tiles_x + tx;
+          const uint32_t m = s_mask[t * W + (e >> 5)] & ((1u << (e & 31)) - 1u);
+          const int32_t rank = (int32_t)(s_pre[t * W + (e >> 5)] + __popc(m));
+          list_b[counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t] + rank] = jj;
+        }
+    }
+    __syncthreads();
   }
 }
 
@@ -604,7 +640,8 @@ template <bool FOUR>
 __global__ void __launch_bounds__(kCompactThreads)
 conv_compact(ConvLaunch P, salt_stream_out out) {
   constexpr uint32_t kAll = 0xffffffffu;
-  const int b = blockIdx.y, lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const int b = P.order ? P.order[blockIdx.y] : blockIdx.y;  // heaviest samples first
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
   const int32_t S = P.s_total[b];
   if (S > P.M) return;  // truncated samples go through conv_truncated
   const int32_t n_eff = P.n_eff(b);

@@ -356,6 +356,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.fd_s = FastDiv((uint32_t)d->s);
   L.fd_G = FastDiv((uint32_t)p.G);
   L.fd_tw = FastDiv((uint32_t)p.tile_w);
+  L.fd_th = FastDiv((uint32_t)p.tile_h);
   L.n_part_chunks = p.n_part_chunks; L.list_stride = p.list_stride;
   L.in.times = in->times; L.in.src = in->src; L.in.capacity = E; L.in.virtual_pads = in->virtual_pads;
   L.in_nreal = in->n_real; L.batch = B;
@@ -376,13 +377,14 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     SALT_LAUNCHED("sample_order_desc");
   }
   if (p.T > 1) {
-    dim3 gp(p.n_part_chunks, B);
-    conv_tile_count<<<gp, 256, p.T * sizeof(int32_t), st>>>(L, s.counts);
+    // a few blocks per sample loop over its chunks (chunks past its events are skipped)
+    dim3 gp(std::min(p.n_part_chunks, std::max(2, (4 * 1184 + B - 1) / B)), B);
+    conv_tile_count<<<gp, kPartThreads, p.T * sizeof(int32_t), st>>>(L, s.counts);
     SALT_LAUNCHED("conv_tile_count");
     conv_tile_scan_offsets<<<(B * 32 + 255) / 256, 256, 0, st>>>(L, s.counts, s.tile_len,
                                                                  s.tile_off);
     SALT_LAUNCHED("conv_tile_scan_offsets");
-    conv_tile_scatter<<<gp, 256, 2 * p.T * (kPartChunk / 32) * sizeof(uint32_t), st>>>(
+    conv_tile_scatter<<<gp, kPartThreads, 2 * p.T * (kPartChunk / 32) * sizeof(uint32_t), st>>>(
         L, s.counts, s.lists);
     SALT_LAUNCHED("conv_tile_scatter");
   }

@@ -8,6 +8,8 @@ namespace salt {
 constexpr int kFusedThreads = 256;   // conv_fused block size (8 warps)
 constexpr int kFusedChunk = 512;     // events bucketed per shared-memory chunk
 constexpr int kPartChunk = 1024;     // events per tile-partition block
+constexpr int kPartThreads = 256;    // tile-partition block size
+constexpr int kPartPer = kPartChunk / kPartThreads;  // events per partition thread
 constexpr int kCompactThreads = 256; // compaction block size == events per spike chunk
 constexpr int kSpkChunkShift = 8;
 constexpr int kSpkChunk = 1 << kSpkChunkShift;
@@ -29,7 +31,7 @@ struct ConvLaunch {
   int32_t L, M, max_extra;    // max_queue_len, max_out_spikes, max_extra_steps
   int32_t lpu, G, ocp;        // lanes per channel group, channel groups, padded channel stride
   // host-built divisors: h_in*w_in, w_in, stride, channel groups, tile width
-  FastDiv fd_hw, fd_w, fd_s, fd_G, fd_tw;
+  FastDiv fd_hw, fd_w, fd_s, fd_G, fd_tw, fd_th;
   // tiling of the output plane
   int32_t tile_h, tile_w, tiles_x, T;
   int32_t n_part_chunks;
