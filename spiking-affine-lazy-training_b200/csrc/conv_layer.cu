@@ -352,34 +352,42 @@ conv_fused(ConvLaunch P) {
     }
     __syncthreads();
 
-    // -------- phase 1.5: per-position event lists (arrival order) and the active positions
+    // -------- phase 1.5: per-position event lists (arrival order) and the active positions.
+    // The NPM x CHW mask words are dealt to all threads in position-major order (per = a power of
+    // two, so each position's words belong to tpp consecutive lanes); one block scan of
+    // (active-position flag << 20) + popcount gives every word its place in the position-major
+    // list and every active position its place in the active list, then all threads expand.
     int32_t n_active = 0;
     {
-      int32_t run = 0;
-      for (int p0 = 0; p0 < NPM; p0 += blockDim.x) {  // block-uniform trip count
-        const int p = p0 + tid;
-        int32_t c = 0;
-        if (p < NPM)
-          for (int w = 0; w < CHW; ++w) c += __popc(mask_s[p * CHW + w]);
-        int32_t tot, atot;
-        const int32_t off = run + block_exclusive_scan(c, s_scan, tot);
-        const int32_t aoff = n_active + block_exclusive_scan(c > 0, s_scan, atot);
-        if (p < NPM) {
-          posoff_s[p] = off;
-          poscnt_s[p] = c;
-          if (c > 0) act_s[aoff] = p;
-          int32_t k = off;
-          for (int w = 0; w < CHW && c > 0; ++w) {
-            uint32_t m = mask_s[p * CHW + w];
-            while (m) {
-              list_s[k++] = (uint16_t)(w * 32 + __ffs(m) - 1);
-              m &= m - 1u;
-            }
+      int per = 1;
+      while (per * (int)blockDim.x < NPM * CHW) per <<= 1;  // <= CHW since NPM <= blockDim
+      const int tpp = CHW / per;                              // threads per position
+      const int p = tid / tpp, wbase = (tid % tpp) * per;
+      int32_t c = 0;
+      if (p < NPM)
+        for (int i = 0; i < per; ++i) c += __popc(mask_s[p * CHW + wbase + i]);
+      int32_t cpos = c;
+      for (int o = 1; o < tpp; o <<= 1) cpos += __shfl_xor_sync(0xffffffffu, cpos, o);
+      const bool head = p < NPM && wbase == 0;
+      int32_t tot;
+      const int32_t pre =
+          block_exclusive_scan(((head && cpos > 0) ? (1 << 20) : 0) + c, s_scan, tot);
+      int32_t off = pre & 0xfffff;  // list entries per chunk stay below 2^20
+      n_active = tot >> 20;
+      if (head) {
+        posoff_s[p] = off;
+        poscnt_s[p] = cpos;
+        if (cpos > 0) act_s[pre >> 20] = p;
+      }
+      if (p < NPM)
+        for (int i = 0; i < per; ++i) {
+          const int w = wbase + i;
+          uint32_t m = mask_s[p * CHW + w];
+          while (m) {
+            list_s[off++] = (uint16_t)(w * 32 + __ffs(m) - 1);
+            m &= m - 1u;
           }
         }
-        run += tot;
-        n_active += atot;
-      }
     }
     __syncthreads();
 
