@@ -225,6 +225,22 @@ salt_status salt_network_forward(salt_network *net, int32_t batch, const salt_st
                                  int32_t *vmin, int32_t *vmax, int32_t *needed_queue,
                                  int32_t *fits, void *workspace, size_t workspace_bytes,
                                  void *stream);
+/* Part of a forward (no reference counterpart: lets a caller overlap the input transfer with the
+ * first layer): layers [layer_begin, layer_end) on rows [row0, row0 + rows) of a batch-`batch`
+ * forward planned for first-layer input capacity in_capacity, with that forward's workspace and
+ * full-batch output arrays (same layouts as salt_network_forward; only the rows' entries are
+ * written).  layer_begin == 0 reads `in` (rows rows, capacity in_capacity); otherwise the part
+ * reads what layer layer_begin - 1 left in the workspace for these rows, so parts run in layer
+ * order on one stream.  logits and fits are written when layer_end is the last layer.  Running
+ * layer 0 on row slices and then the remaining layers on all rows gives the results of
+ * salt_network_forward. */
+salt_status salt_network_forward_part(salt_network *net, int32_t batch, int32_t in_capacity,
+                                      int32_t row0, int32_t rows, int32_t layer_begin,
+                                      int32_t layer_end, const salt_stream_in *in,
+                                      int32_t *logits, int32_t *spike_count, int32_t *overflowed,
+                                      int32_t *vmin, int32_t *vmax, int32_t *needed_queue,
+                                      int32_t *fits, void *workspace, size_t workspace_bytes,
+                                      void *stream);
 /* Number of kernel launches the last salt_network_forward enqueued (for launch accounting). */
 int32_t salt_network_last_launch_count(const salt_network *net);
 /* Kernel timing of the forwards enqueued while profiling is on: CUDA events are recorded on the

@@ -94,6 +94,8 @@ _SIGS = {
     "salt_network_create": (_i32, [_vp, _i32, _vp]),
     "salt_network_destroy": (_i32, [_vp]),
     "salt_network_workspace_size": (_i32, [_vp, _i32, _i32, _vp]),
+    "salt_network_forward_part": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp,
+                                         _vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "salt_network_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                     ctypes.c_size_t, _vp]),
     "salt_network_last_launch_count": (_i32, [_vp]),

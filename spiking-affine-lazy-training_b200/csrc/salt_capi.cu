@@ -1315,36 +1315,58 @@ salt_status salt_network_workspace_size(const salt_network* net, int32_t batch,
   return SALT_OK;
 }
 
-salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_stream_in* in,
-                                 int32_t* logits, int32_t* spike_count, int32_t* overflowed,
-                                 int32_t* vmin, int32_t* vmax, int32_t* needed_queue,
-                                 int32_t* fits, void* workspace, size_t workspace_bytes,
-                                 void* stream) {
-  if (!net || !logits) return fail(SALT_BAD_ARG, "network forward: NULL network or logits");
-  salt_status rc = check_stream_in(in, batch);
-  if (rc) return rc;
+// Layers [l0, l1) of a batch-`batch` forward on rows [row0, row0 + rows).  Layer l0 reads `in`
+// (those rows only) when l0 == 0, else the workspace stream layer l0 - 1 left for these rows;
+// outputs and per-layer stats land at the rows' places in the full-batch arrays.  When l1 is the
+// last layer, fits (AND over all layers) is written for the rows.
+static salt_status network_run(salt_network* net, int32_t batch, int32_t in_capacity,
+                               int32_t row0, int32_t rows, int32_t l0, int32_t l1,
+                               const salt_stream_in* in, int32_t* logits,
+                               int32_t* spike_count, int32_t* overflowed, int32_t* vmin,
+                               int32_t* vmax, int32_t* needed_queue, int32_t* fits,
+                               void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  const int nl = (int)net->layers.size();
+  if (!logits && l1 == nl) return fail(SALT_BAD_ARG, "network forward: NULL logits");
+  if (batch < 1 || row0 < 0 || rows < 1 || row0 + rows > batch || l0 < 0 || l1 > nl || l0 >= l1)
+    return fail(SALT_BAD_ARG, "network forward: bad row or layer range");
+  if (l0 == 0) {
+    salt_status rc = check_stream_in(in, rows);
+    if (rc) return rc;
+    if (in->capacity != in_capacity)
+      return fail(SALT_BAD_ARG, "network forward: input capacity differs from the planned one");
+  }
+  if (in_capacity < 1) return fail(SALT_BAD_ARG, "network forward: in_capacity must be >= 1");
+  // the workspace layout depends only on the full batch and the first layer's input capacity
   NetLayout o;
-  if ((rc = net_layout(net, batch, in->capacity, nullptr, o))) return rc;
+  salt_status rc = net_layout(net, batch, in_capacity, nullptr, o);
+  if (rc) return rc;
   if (!workspace || workspace_bytes < o.total)
     return fail(SALT_WORKSPACE_TOO_SMALL, "network workspace too small");
-  net_layout(net, batch, in->capacity, workspace, o);
-  cudaStream_t st = (cudaStream_t)stream;
+  net_layout(net, batch, in_capacity, workspace, o);
   const int64_t launches0 = g_launches;
-  const int nl = (int)net->layers.size();
   const int B = batch;
-  salt_stream_in cur = *in;
-  for (int l = 0; l < nl; ++l) {
+  salt_stream_in cur{};
+  if (l0 == 0) {
+    cur = *in;
+  } else {
+    const LayerRec& prev = net->layers[l0 - 1];
+    cur.times = o.st_t[(l0 - 1) & 1] + (size_t)row0 * prev.M;
+    cur.src = o.st_s[(l0 - 1) & 1] + (size_t)row0 * prev.M;
+    cur.n_real = o.st_n[(l0 - 1) & 1] + row0;
+    cur.capacity = prev.M;
+    cur.virtual_pads = 1;
+  }
+  for (int l = l0; l < l1; ++l) {
     LayerRec& r = net->layers[l];
     const bool last = l == nl - 1;
-    salt_stream_out so{o.st_t[l & 1], o.st_s[l & 1], o.st_n[l & 1]};
-    int32_t* vf = last ? logits : o.vtmp;
-    int32_t* sb = o.stats + (size_t)6 * l * B;
-    salt_layer_stats ls{spike_count ? spike_count + (size_t)l * B : sb,
-                        needed_queue ? needed_queue + (size_t)l * B : sb + B,
-                        overflowed ? overflowed + (size_t)l * B : sb + 2 * B,
-                        vmin ? vmin + (size_t)l * B : sb + 3 * B,
-                        vmax ? vmax + (size_t)l * B : sb + 4 * B,
-                        sb + 5 * B};
+    salt_stream_out so{o.st_t[l & 1] + (size_t)row0 * r.M, o.st_s[l & 1] + (size_t)row0 * r.M,
+                       o.st_n[l & 1] + row0};
+    int32_t* vf = last ? logits + (size_t)row0 * r.n_neurons : o.vtmp + (size_t)row0 * r.n_neurons;
+    int32_t* sb = o.stats + (size_t)6 * l * B + row0;
+    auto at = [&](int32_t* a) { return a ? a + (size_t)l * B + row0 : nullptr; };
+    salt_layer_stats ls{spike_count ? at(spike_count) : sb, needed_queue ? at(needed_queue) : sb + B,
+                        overflowed ? at(overflowed) : sb + 2 * B, vmin ? at(vmin) : sb + 3 * B,
+                        vmax ? at(vmax) : sb + 4 * B, sb + 5 * B};
     KernelTimer timer, whole;
     auto take = [&](KernelTimer& t) -> salt_status {
       if (net->pool.empty()) {
@@ -1366,12 +1388,12 @@ salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_st
       }
     }
     if (r.spec.kind == 0)
-      rc = conv_forward_impl(&r.spec.conv, &r.spec.quant, r.d_q, r.d_lut, r.d_vth, B, &cur, &so,
-                             vf, &ls, o.scratch, o.scratch_bytes, st,
+      rc = conv_forward_impl(&r.spec.conv, &r.spec.quant, r.d_q, r.d_lut, r.d_vth, rows, &cur,
+                             &so, vf, &ls, o.scratch, o.scratch_bytes, st,
                              timer.start ? &timer : nullptr);
     else
-      rc = fc_forward_impl(&r.spec.fc, &r.spec.quant, r.d_q, true, r.d_lut, r.d_vth, B, &cur, &so,
-                           vf, &ls, o.scratch, o.scratch_bytes, st);
+      rc = fc_forward_impl(&r.spec.fc, &r.spec.quant, r.d_q, true, r.d_lut, r.d_vth, rows, &cur,
+                           &so, vf, &ls, o.scratch, o.scratch_bytes, st);
     if (rc) return rc;
     if (whole.stop) SALT_CUDA(cudaEventRecord(whole.stop, st));
     cur.times = so.times;
@@ -1380,12 +1402,40 @@ salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_st
     cur.capacity = r.M;
     cur.virtual_pads = 1;
   }
-  if (fits) {  // per-layer fits sit at offset 5*B of each layer's (6, B) stats block
-    fits_and<<<(B + 255) / 256, 256, 0, st>>>(o.stats + 5 * B, nl, (int64_t)6 * B, B, fits);
+  if (fits && l1 == nl) {  // per-layer fits sit at offset 5*B of each layer's (6, B) stats block
+    fits_and<<<(rows + 255) / 256, 256, 0, st>>>(o.stats + 5 * B + row0, nl, (int64_t)6 * B, rows,
+                                                 fits + row0);
     SALT_LAUNCHED("fits_and");
   }
   net->last_launches = (int32_t)(g_launches - launches0);
   return SALT_OK;
+}
+
+salt_status salt_network_forward(salt_network* net, int32_t batch, const salt_stream_in* in,
+                                 int32_t* logits, int32_t* spike_count, int32_t* overflowed,
+                                 int32_t* vmin, int32_t* vmax, int32_t* needed_queue,
+                                 int32_t* fits, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  if (!net || !logits) return fail(SALT_BAD_ARG, "network forward: NULL network or logits");
+  if (!in) return fail(SALT_BAD_ARG, "input stream pointers must be non-NULL");
+  return network_run(net, batch, in->capacity, 0, batch, 0, (int32_t)net->layers.size(), in,
+                     logits,
+                     spike_count, overflowed, vmin, vmax, needed_queue, fits, workspace,
+                     workspace_bytes, (cudaStream_t)stream);
+}
+
+salt_status salt_network_forward_part(salt_network* net, int32_t batch, int32_t in_capacity,
+                                      int32_t row0, int32_t rows, int32_t layer_begin,
+                                      int32_t layer_end, const salt_stream_in* in,
+                                      int32_t* logits, int32_t* spike_count, int32_t* overflowed,
+                                      int32_t* vmin, int32_t* vmax, int32_t* needed_queue,
+                                      int32_t* fits, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+  if (!net) return fail(SALT_BAD_ARG, "network forward: NULL network");
+  return network_run(net, batch, in_capacity, row0, rows, layer_begin, layer_end, in, logits,
+                     spike_count,
+                     overflowed, vmin, vmax, needed_queue, fits, workspace, workspace_bytes,
+                     (cudaStream_t)stream);
 }
 
 int32_t salt_network_last_launch_count(const salt_network* net) {

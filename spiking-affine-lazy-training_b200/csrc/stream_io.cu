@@ -12,32 +12,31 @@
 
 namespace salt {
 
-// One block per (row, slice of the row): 16-byte loads where both rows allow them.
-__global__ void gather_rows_kernel(const float* __restrict__ ht, const int32_t* __restrict__ hs,
-                                   const int32_t* __restrict__ n_real, int32_t capacity,
-                                   int64_t host_pitch, float* __restrict__ dt,
-                                   int32_t* __restrict__ ds) {
-  const int b = blockIdx.y;
-  const int32_t nr = n_real[b];
-  const int32_t n = nr < 0 ? 0 : (nr < capacity ? nr : capacity);
-  const float* trow = ht + (int64_t)b * host_pitch;
-  const int32_t* srow = hs + (int64_t)b * host_pitch;
-  float* drow_t = dt + (int64_t)b * capacity;
-  int32_t* drow_s = ds + (int64_t)b * capacity;
+// A few persistent blocks loop over the rows (16-byte loads where both rows allow them): the
+// host link is saturated by a small share of the GPU, so a layer running on the compute stream
+// keeps the rest of the SMs while the next rows arrive.
+__global__ void __launch_bounds__(kGatherThreads)
+gather_rows_kernel(const float* __restrict__ ht, const int32_t* __restrict__ hs,
+                   const int32_t* __restrict__ n_real, int32_t batch, int32_t capacity,
+                   int64_t host_pitch, float* __restrict__ dt, int32_t* __restrict__ ds) {
   const bool vec = (host_pitch % 4 == 0) && (capacity % 4 == 0);
-  const int32_t step = gridDim.x * blockDim.x;
-  if (vec) {
-    const int32_t n4 = n >> 2;
-    for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step) {
-      reinterpret_cast<float4*>(drow_t)[i] = reinterpret_cast<const float4*>(trow)[i];
-      reinterpret_cast<int4*>(drow_s)[i] = reinterpret_cast<const int4*>(srow)[i];
+  for (int32_t b = blockIdx.x; b < batch; b += gridDim.x) {
+    const int32_t nr = n_real[b];
+    const int32_t n = nr < 0 ? 0 : (nr < capacity ? nr : capacity);
+    const float* trow = ht + (int64_t)b * host_pitch;
+    const int32_t* srow = hs + (int64_t)b * host_pitch;
+    float* drow_t = dt + (int64_t)b * capacity;
+    int32_t* drow_s = ds + (int64_t)b * capacity;
+    int32_t done = 0;
+    if (vec) {
+      const int32_t n4 = n >> 2;
+      for (int32_t i = threadIdx.x; i < n4; i += blockDim.x) {
+        reinterpret_cast<float4*>(drow_t)[i] = reinterpret_cast<const float4*>(trow)[i];
+        reinterpret_cast<int4*>(drow_s)[i] = reinterpret_cast<const int4*>(srow)[i];
+      }
+      done = n4 << 2;
     }
-    for (int32_t i = (n4 << 2) + blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
-      drow_t[i] = trow[i];
-      drow_s[i] = srow[i];
-    }
-  } else {
-    for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    for (int32_t i = done + threadIdx.x; i < n; i += blockDim.x) {
       drow_t[i] = trow[i];
       drow_s[i] = srow[i];
     }
@@ -47,9 +46,9 @@ __global__ void gather_rows_kernel(const float* __restrict__ ht, const int32_t* 
 cudaError_t gather_rows_launch(const float* ht, const int32_t* hs, const int32_t* n_real_dev,
                                int32_t batch, int32_t capacity, int64_t host_pitch, float* dt,
                                int32_t* ds, cudaStream_t st) {
-  const int slices = std::max(1, std::min(8, capacity / 2048));
-  gather_rows_kernel<<<dim3(slices, batch), 256, 0, st>>>(ht, hs, n_real_dev, capacity,
-                                                          host_pitch, dt, ds);
+  const int blocks = std::max(1, std::min(batch, kGatherBlocks));
+  gather_rows_kernel<<<blocks, kGatherThreads, 0, st>>>(ht, hs, n_real_dev, batch, capacity,
+                                                       host_pitch, dt, ds);
   return cudaGetLastError();
 }
 

@@ -68,6 +68,25 @@ class NetworkPlan:
             self.workspace_bytes, current_stream()))
         return self.logits, self.stats, self.fits
 
+    def forward_part(self, times, src, n_real, row0: int, rows: int, layer_begin: int,
+                     layer_end: int, virtual_pads: bool = False):
+        """Layers [layer_begin, layer_end) on rows [row0, row0 + rows) of this plan's batch
+        (salt_network_forward_part).  With layer_begin == 0 the inputs are that row slice
+        (rows, in_capacity); later parts read what the previous layer left in the workspace, so
+        parts are enqueued in layer order.  Outputs land in the full-batch (logits, stats, fits)
+        returned by forward_device; logits and fits only when layer_end is the last layer."""
+        sin = None
+        if layer_begin == 0:
+            sin = _lib.StreamIn(ptr(times), ptr(src), ptr(n_real), int(times.shape[1]),
+                                int(virtual_pads))
+        s = self.stats
+        _lib.check(_lib.lib().salt_network_forward_part(
+            self._net, self.batch, self.in_capacity, int(row0), int(rows), int(layer_begin),
+            int(layer_end), _lib.byref(sin) if sin is not None else None, ptr(self.logits),
+            ptr(s[0]), ptr(s[1]), ptr(s[2]), ptr(s[3]), ptr(s[4]), ptr(self.fits), ptr(self._ws),
+            self.workspace_bytes, current_stream()))
+        return self.logits, self.stats, self.fits
+
     def set_profiling(self, enable: bool) -> None:
         _lib.check(_lib.lib().salt_network_set_profiling(self._net, int(bool(enable))))
 
@@ -106,11 +125,12 @@ class NetworkPlan:
 
 
 class PipelinedForward:
-    """Host in, host out, with the transfers overlapped: the batch runs as `chunks` sub-batches
-    on a NetworkPlan of batch/chunks samples; while sub-batch k computes on the current stream,
-    sub-batch k+1 is copied on a second stream into the other of two device buffers.  Each
-    sample's row is copied only up to its n_real (salt_stream_h2d_real) unless the first layer
-    may fire on pad entries (needs_tail), in which case whole rows are copied.
+    """Host in, host out, with the transfer overlapped: the batch's first layer runs as `chunks`
+    row slices, each starting as soon as its rows are on the device, while the next slice is
+    copied on a second stream into the other of two device buffers; the remaining layers then run
+    on the whole batch (salt_network_forward_part).  Each sample's row is copied only up to its
+    n_real (salt_stream_h2d_real) unless the first layer may fire on pad entries (needs_tail), in
+    which case whole rows are copied.
 
     Host arrays must be pinned torch tensors: times (B, E) float32, src (B, E) int32, n_real
     (B,) int32.  Returns pinned (logits (B, n_out) int32, fits (B,) int32) filled in place; with
@@ -124,7 +144,8 @@ class PipelinedForward:
             raise ValueError(f"batch {batch} is not a multiple of chunks {chunks}")
         self.batch, self.chunks, self.sub = int(batch), int(chunks), int(batch) // int(chunks)
         self.capacity = int(in_capacity)
-        self.plan = NetworkPlan(layers, weights, self.sub, self.capacity, round_mode)
+        self.plan = NetworkPlan(layers, weights, self.batch, self.capacity, round_mode)
+        self.n_layers = len(self.plan.layers)
         qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
         self.full_rows = bool(qd.needs_tail)
         E, sub = self.capacity, self.sub
@@ -148,6 +169,7 @@ class PipelinedForward:
         lib = _lib.lib()
         compute = torch.cuda.current_stream()
         sub, E = self.sub, self.capacity
+        first_only = self.n_layers > 1   # layer 0 per slice, the rest on the whole batch
         for k in range(self.chunks):
             i = k % 2
             rows = slice(k * sub, (k + 1) * sub)
@@ -165,11 +187,14 @@ class PipelinedForward:
                         ctypes.c_void_p(self._copy.cuda_stream)))
                 self._ready[i].record(self._copy)
             compute.wait_event(self._ready[i])
-            logits, _, fits = self.plan.forward_device(self._t[i], self._s[i], self._n[i])
-            self.logits[rows].copy_(logits, non_blocking=True)
-            self.fits[rows].copy_(fits, non_blocking=True)
+            self.plan.forward_part(self._t[i], self._s[i], self._n[i], k * sub, sub, 0,
+                                   1 if first_only else self.n_layers)
             self._free[i].record(compute)
             self._used[i] = True
+        if first_only:
+            self.plan.forward_part(None, None, None, 0, self.batch, 1, self.n_layers)
+        self.logits.copy_(self.plan.logits, non_blocking=True)
+        self.fits.copy_(self.plan.fits, non_blocking=True)
         if sync:
             compute.synchronize()
         return self.logits, self.fits

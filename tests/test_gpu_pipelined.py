@@ -83,3 +83,26 @@ def test_unpinned_host_rows_are_rejected():
     rc = _lib.lib().salt_stream_h2d_real(p(t), p(s), ctypes.c_int64(8), p(n), 2, 8, p(dt), p(ds),
                                          None)
     assert rc == _lib.SALT_BAD_ARG
+
+
+def test_forward_parts_in_any_slicing_equal_the_full_forward():
+    """salt_network_forward_part: layer 0 on uneven row slices, layer 1 on two slices, the last
+    layer on all rows gives the full forward's logits, fits and per-layer stats."""
+    import torch
+    rng = np.random.default_rng(13)
+    net, params = _net(rng, (60, 160))
+    B, E = 10, 300
+    times, src, nr = make_events(rng, B, E, 2 * 12 * 12)
+    t, s, n = (torch.from_numpy(a).cuda() for a in (times, src, nr.astype(np.int32)))
+    full = NetworkPlan(net.layers, params, B, E)
+    lf, sf, ff = (x.clone() for x in full.forward_device(t, s, n))
+    part = NetworkPlan(net.layers, params, B, E)
+    for r0, r1 in ((0, 3), (3, 4), (4, 10)):
+        part.forward_part(t[r0:r1], s[r0:r1], n[r0:r1], r0, r1 - r0, 0, 1)
+    for r0, r1 in ((0, 6), (6, 10)):
+        part.forward_part(None, None, None, r0, r1 - r0, 1, 2)
+    lp, sp, fp = part.forward_part(None, None, None, 0, B, 2, 3)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(lp.cpu().numpy(), lf.cpu().numpy())
+    np.testing.assert_array_equal(fp.cpu().numpy(), ff.cpu().numpy())
+    np.testing.assert_array_equal(sp.cpu().numpy(), sf.cpu().numpy())
