@@ -448,7 +448,9 @@ conv_fused(ConvLaunch P) {
         if (nb > 0) tp = last_t;
         const int32_t nbw = min(nmax - b0, LPU);  // warp-uniform batch length
         uint32_t mybits = 0;
-        for (int32_t st = 0; st < nbw; ++st) {
+        // 16-lane groups: the walk is unrolled so that the broadcasts and weight loads of later
+        // steps are issued ahead of the dependent register updates
+        auto walk = [&](int st) {
           const int32_t as = __shfl_sync(0xffffffffu, a, st, LPU);
           const int32_t Ts = __shfl_sync(0xffffffffu, T, st, LPU);
           bool spike = false;
@@ -465,6 +467,18 @@ conv_fused(ConvLaunch P) {
           const uint32_t bits = (__ballot_sync(0xffffffffu, spike) >> (gi * LPU)) & gmask_bits;
           if (glane == st) mybits = bits;
           spk_visit += spike;
+        };
+        if (LPU <= 16) {
+          if (nbw == LPU) {
+#pragma unroll
+            for (int st = 0; st < LPU; ++st) walk(st);
+          } else {
+#pragma unroll
+            for (int st = 0; st < LPU; ++st)
+              if (st < nbw) walk(st);
+          }
+        } else {  // 32-lane groups: unrolling measured slower (by 8: +4 %, fully: +33 %)
+          for (int st = 0; st < nbw; ++st) walk(st);
         }
         if (has) sw_s[widx] = mybits;
         cn += max(nb, 0);
