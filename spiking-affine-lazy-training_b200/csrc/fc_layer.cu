@@ -72,7 +72,10 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   int2* ev_s = ev_all + ((threadIdx.x >> 5) * SPW + gi) * SB;
   const int64_t unit = gw * SPW + gi;
   const bool unit_ok = unit < n_units;
-  const int b = unit_ok ? (int)(unit / P.G) : 0, g = unit_ok ? (int)(unit % P.G) : 0;
+  // units in heaviest-first sample order: a warp's samples have similar lengths, and the
+  // longest chains start first
+  const int bu = unit_ok ? (int)(unit / P.G) : 0, g = unit_ok ? (int)(unit % P.G) : 0;
+  const int b = P.order ? P.order[bu] : bu;
   const int o = g * LPU + gl;
   const bool active = unit_ok && o < P.n_out;
   const int oc = active ? o : 0;  // inactive lanes run column 0; their results are dropped

@@ -422,7 +422,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
 // ---------------------------------------------------------------- fc
 
 struct FCScratch {
-  int32_t *stats, *s_total, *vmin, *vmax, *ovf, *chunk, *n_spk, *qT;
+  int32_t *stats, *s_total, *vmin, *vmax, *ovf, *chunk, *n_spk, *qT, *order;
   size_t stats_bytes;
   uint32_t* sw;
 };
@@ -445,6 +445,7 @@ static size_t fc_carve(const salt_fc_desc* d, const salt_quant_desc* q, int32_t 
   s.sw = q->has_vth ? c.take<uint32_t>((size_t)B * E * G) : nullptr;
   s.n_spk = q->has_vth ? c.take<int32_t>((size_t)B * d->n_out) : nullptr;
   s.qT = need_qT ? c.take<int32_t>((size_t)d->n_in * d->n_out) : nullptr;
+  s.order = c.take<int32_t>((size_t)B);
   return c.size();
 }
 
@@ -494,6 +495,11 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   L.s_total = s.s_total; L.vmin = s.vmin; L.vmax = s.vmax; L.ovf = s.ovf; L.n_spk = s.n_spk;
   L.tail_mode = q->has_vth && q->needs_tail;
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
+  L.order = B > 1 ? s.order : nullptr;
+  if (L.order) {
+    sample_order_desc<<<1, kOrderThreads, 0, st>>>(in->n_real, E, B, s.order);
+    SALT_LAUNCHED("sample_order_desc");
+  }
   // narrow layers (the membrane readouts) pack several samples into a warp; weight tables that
   // fit are staged in shared memory at the width of their codes
   const int lpu = d->n_out <= 8 ? 8 : (d->n_out <= 16 ? 16 : 32);

@@ -101,6 +101,7 @@ struct FCLaunch {
   StreamView in;
   const int32_t* in_nreal;
   int32_t batch;
+  const int32_t* order;       // [B] samples heaviest first (unit -> sample), or null
   const int32_t* qT;          // (n_in, n_out) int32, transposed weight codes
   const int32_t* lut;
   const int32_t* vth;
