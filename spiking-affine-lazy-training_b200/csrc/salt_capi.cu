@@ -369,7 +369,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.vmax = s.vmax; L.ovf = s.ovf; L.tail_total = s.tail_total;
   L.tail_mode = p.tail_mode; L.tail_cnt = s.tail_cnt;
   L.tile_len = s.tile_len; L.tile_off = s.tile_off; L.tile_lists = s.lists;
-  L.order = B > 1 ? s.order : nullptr;
+  L.order = B >= kOrderMinBatch ? s.order : nullptr;  // small batches: launch-bound anyway
 
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
   if (L.order) {
@@ -495,7 +495,7 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   L.s_total = s.s_total; L.vmin = s.vmin; L.vmax = s.vmax; L.ovf = s.ovf; L.n_spk = s.n_spk;
   L.tail_mode = q->has_vth && q->needs_tail;
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
-  L.order = B > 1 ? s.order : nullptr;
+  L.order = B >= kOrderMinBatch ? s.order : nullptr;  // small batches: launch-bound anyway
   if (L.order) {
     sample_order_desc<<<1, kOrderThreads, 0, st>>>(in->n_real, E, B, s.order);
     SALT_LAUNCHED("sample_order_desc");

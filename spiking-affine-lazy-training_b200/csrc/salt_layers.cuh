@@ -231,6 +231,7 @@ __global__ void conv_tile_scatter(ConvLaunch P, const int32_t* counts, int32_t* 
 __global__ void sample_order_desc(const int32_t* __restrict__ n_real, int32_t capacity,
                                   int32_t batch, int32_t* __restrict__ order);
 constexpr int kOrderThreads = 1024;
+constexpr int kOrderMinBatch = 128;  // below this the sort costs more than the schedule gains
 // conv_compact specialised for the geometry (ncand <= 2 and one channel group, or the rest).
 void* conv_compact_kernel(int ncand, int G);
 __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out);
