@@ -125,10 +125,10 @@ class NetworkPlan:
 
 
 class PipelinedForward:
-    """Host in, host out, with the transfer overlapped: the batch's first layer runs as `chunks`
-    row slices, each starting as soon as its rows are on the device, while the next slice is
-    copied on a second stream into the other of two device buffers; the remaining layers then run
-    on the whole batch (salt_network_forward_part).  Each sample's row is copied only up to its
+    """Host in, host out, with the transfer overlapped: the batch's first `slice_layers` layers
+    run as `chunks` row slices, each starting as soon as its rows are on the device, while the
+    next slice is copied on a second stream into the other of two device buffers; the remaining
+    layers then run on the whole batch (salt_network_forward_part).  Each sample's row is copied only up to its
     n_real (salt_stream_h2d_real) unless the first layer may fire on pad entries (needs_tail), in
     which case whole rows are copied.
 
@@ -138,7 +138,7 @@ class PipelinedForward:
     when the current stream reaches the end of the call (the next call reuses them)."""
 
     def __init__(self, layers, weights, batch: int, in_capacity: int, chunks: int = 4,
-                 round_mode="round"):
+                 round_mode="round", slice_layers: int = 1):
         require_cuda()
         if batch % chunks:
             raise ValueError(f"batch {batch} is not a multiple of chunks {chunks}")
@@ -146,6 +146,8 @@ class PipelinedForward:
         self.capacity = int(in_capacity)
         self.plan = NetworkPlan(layers, weights, self.batch, self.capacity, round_mode)
         self.n_layers = len(self.plan.layers)
+        # layers run per slice as the slice arrives; the rest run once on the whole batch
+        self.slice_layers = max(1, min(int(slice_layers), self.n_layers))
         qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
         self.full_rows = bool(qd.needs_tail)
         E, sub = self.capacity, self.sub
@@ -169,7 +171,7 @@ class PipelinedForward:
         lib = _lib.lib()
         compute = torch.cuda.current_stream()
         sub, E = self.sub, self.capacity
-        first_only = self.n_layers > 1   # layer 0 per slice, the rest on the whole batch
+        per_slice = self.slice_layers
         for k in range(self.chunks):
             i = k % 2
             rows = slice(k * sub, (k + 1) * sub)
@@ -188,11 +190,11 @@ class PipelinedForward:
                 self._ready[i].record(self._copy)
             compute.wait_event(self._ready[i])
             self.plan.forward_part(self._t[i], self._s[i], self._n[i], k * sub, sub, 0,
-                                   1 if first_only else self.n_layers)
+                                   per_slice)
             self._free[i].record(compute)
             self._used[i] = True
-        if first_only:
-            self.plan.forward_part(None, None, None, 0, self.batch, 1, self.n_layers)
+        if per_slice < self.n_layers:
+            self.plan.forward_part(None, None, None, 0, self.batch, per_slice, self.n_layers)
         self.logits.copy_(self.plan.logits, non_blocking=True)
         self.fits.copy_(self.plan.fits, non_blocking=True)
         if sync:
