@@ -87,6 +87,22 @@ class NetworkPlan:
             self.workspace_bytes, current_stream()))
         return self.logits, self.stats, self.fits
 
+    def capture(self, times, src, n_real, virtual_pads: bool = False):
+        """Records forward_device on these device buffers as a CUDA graph and returns its replay
+        function: one launch per forward instead of one per kernel (launch-bound batches gain,
+        large ones do not).  Refill the same buffers between replays; the results appear in the
+        tensors forward_device returns.  Profiling must be off while capturing."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):   # first call outside the capture: kernel attributes set
+            self.forward_device(times, src, n_real, virtual_pads)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.forward_device(times, src, n_real, virtual_pads)
+        self._graph = graph   # kept alive with the plan
+        return graph.replay
+
     def set_profiling(self, enable: bool) -> None:
         _lib.check(_lib.lib().salt_network_set_profiling(self._net, int(bool(enable))))
 

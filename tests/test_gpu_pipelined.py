@@ -106,3 +106,30 @@ def test_forward_parts_in_any_slicing_equal_the_full_forward():
     np.testing.assert_array_equal(lp.cpu().numpy(), lf.cpu().numpy())
     np.testing.assert_array_equal(fp.cpu().numpy(), ff.cpu().numpy())
     np.testing.assert_array_equal(sp.cpu().numpy(), sf.cpu().numpy())
+
+
+def test_captured_graph_replays_the_forward():
+    """NetworkPlan.capture: a CUDA graph of the forward gives the eager results, and replays
+    pick up new contents of the captured input buffers."""
+    import torch
+    rng = np.random.default_rng(17)
+    net, params = _net(rng, (60, 160))
+    B, E = 12, 300
+    plan = NetworkPlan(net.layers, params, B, E)
+    t = torch.empty((B, E), dtype=torch.float32, device="cuda")
+    s = torch.empty((B, E), dtype=torch.int32, device="cuda")
+    n = torch.empty((B,), dtype=torch.int32, device="cuda")
+    sets = [make_events(rng, B, E, 2 * 12 * 12) for _ in range(2)]
+    t.copy_(torch.from_numpy(sets[0][0])); s.copy_(torch.from_numpy(sets[0][1]))
+    n.copy_(torch.from_numpy(sets[0][2].astype(np.int32)))
+    replay = plan.capture(t, s, n)
+    eager = NetworkPlan(net.layers, params, B, E)
+    for times, src, nr in sets:
+        t.copy_(torch.from_numpy(times)); s.copy_(torch.from_numpy(src))
+        n.copy_(torch.from_numpy(nr.astype(np.int32)))
+        replay()
+        lg, st, ft = eager.forward_device(t, s, n)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(plan.logits.cpu().numpy(), lg.cpu().numpy())
+        np.testing.assert_array_equal(plan.stats.cpu().numpy(), st.cpu().numpy())
+        np.testing.assert_array_equal(plan.fits.cpu().numpy(), ft.cpu().numpy())
