@@ -341,13 +341,22 @@ def run_b200(args):
     d2h = int(pf.logits.numel() * 4 + pf.fits.numel() * 4)
     pf.close()
 
-    # ---- roofline of the dominant kernel (the fused bucket+scan kernel of the busiest layer)
-    dom = int(np.argmax(fused_ms))
-    avg_ms = float(fused_ms[dom] / max(int(fused_n[dom]), 1))
-    alg_bytes = algorithmic_bytes(backend, wl, dom)
+    # ---- roofline of the dominant kernel (the fused bucket+scan kernel of the busiest conv
+    # layer; a network of FC layers only: the busiest FC layer, scan and compaction together)
+    conv_dominant = float(np.max(fused_ms)) > 0.0
+    if conv_dominant:
+        dom = int(np.argmax(fused_ms))
+        avg_ms = float(fused_ms[dom] / max(int(fused_n[dom]), 1))
+        alg_bytes = algorithmic_bytes(backend, wl, dom)
+        kernel_name = f"conv_fused (layer {layers[dom].name})"
+    else:
+        dom = int(np.argmax(layer_ms))
+        avg_ms = float(layer_ms[dom] / max(int(fused_n[dom]), 1))
+        alg_bytes = fc_algorithmic_bytes(backend, wl, dom)
+        kernel_name = f"fc_scan + compaction (layer {layers[dom].name})"
     peak, peak_kind = peak_hbm()
     achieved = alg_bytes / (avg_ms / 1000.0) / 1e9
-    traffic = traffic_from_profile(wl, dom)
+    traffic = traffic_from_profile(wl, dom) if conv_dominant else None
 
     if rank == 0:
         line = {
@@ -368,7 +377,7 @@ def run_b200(args):
                              f"{wl.times.nbytes * 2 / 2**20:.0f} MiB > 126 MB), no flush"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": f"conv_fused (layer {layers[dom].name})",
+                         "kernel": kernel_name,
                          "kernel_ms": avg_ms, "algorithmic_bytes": alg_bytes,
                          "per_layer_ms": {l.name: {"layer": float(layer_ms[i] / max(fused_n[i], 1)),
                                                    "fused_kernel": float(fused_ms[i] /
@@ -418,6 +427,22 @@ def algorithmic_bytes(backend, wl, layer_index):
     real = np.arange(E)[None, :] < n_eff[:, None]
     C = int(np.where(real, W.candidates_per_event(layer, src), 0).sum())
     return float(8 * int(n_eff.sum()) + 16 * C + 4 * layer.n_neurons * wl.batch)
+
+
+def fc_algorithmic_bytes(backend, wl, layer_index):
+    """Per-launch algorithmic bytes of one integer FC layer with the FC byte model: 8 B per input
+    event (time, source), 24 B per output spike (spike word, scan, stream entry), 4 B per neuron
+    (v_final)."""
+    layers = list(wl.network.layers)
+    out = backend.run_network(layers[:layer_index + 1], wl.params[:layer_index + 1],
+                              wl.network.input_stream(wl.raw()), keep_streams=True)
+    if layer_index == 0:
+        n_in = np.minimum(wl.n_real, wl.src.shape[1])
+    else:
+        prev = out.streams[layer_index - 1]
+        n_in = np.minimum(prev.n_real_events, prev.event_source_idx.shape[1])
+    S = int(np.sum(out.results[layer_index].spike_count))
+    return float(8 * int(np.sum(n_in)) + 24 * S + 4 * layers[layer_index].n_neurons * wl.batch)
 
 
 def traffic_from_profile(wl, layer_index):

@@ -1272,12 +1272,13 @@ struct NetLayout {
 static salt_status net_layout(const salt_network* net, int32_t B, int32_t E0, void* ws,
                               NetLayout& o) {
   const int nl = (int)net->layers.size();
+  // every layer writes its output stream into the ping-pong buffers, the last one too (a firing
+  // last layer compacts up to its max_out_spikes per sample); v_final of all but the last layer
+  // goes to vtmp (the last one's is the logits)
   int32_t maxM = 1;
   int64_t maxN = 1;
-  for (int l = 0; l + 1 < nl; ++l) {
-    maxM = std::max(maxM, net->layers[l].M);
-    maxN = std::max(maxN, net->layers[l].n_neurons);
-  }
+  for (int l = 0; l < nl; ++l) maxM = std::max(maxM, net->layers[l].M);
+  for (int l = 0; l + 1 < nl; ++l) maxN = std::max(maxN, net->layers[l].n_neurons);
   size_t scratch = 0;
   int32_t E = E0;
   for (int l = 0; l < nl; ++l) {

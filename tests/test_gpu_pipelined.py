@@ -133,3 +133,31 @@ def test_captured_graph_replays_the_forward():
         np.testing.assert_array_equal(plan.logits.cpu().numpy(), lg.cpu().numpy())
         np.testing.assert_array_equal(plan.stats.cpu().numpy(), st.cpu().numpy())
         np.testing.assert_array_equal(plan.fits.cpu().numpy(), ft.cpu().numpy())
+
+
+def test_network_whose_last_layer_fires():
+    """A firing last layer compacts its full output stream inside the network workspace (the
+    single firing FC layer of configuration 1; a conv net ending in a firing conv)."""
+    import torch
+    import oracle as O
+    rng = np.random.default_rng(19)
+    for net in (S.Network.build((2, 12, 12), [
+                    S.fc(128, init_k=5.0, tau=20.0, max_out_spikes=700)]),
+                S.Network.build((2, 12, 12), [
+                    S.conv(8, k=3, s=2, p=0, init_k=5.0, tau=20.0, max_queue_len=96,
+                           max_out_spikes=900),
+                    S.conv(16, k=3, s=2, p=1, init_k=5.0, tau=20.0, max_queue_len=96,
+                           max_out_spikes=500)])):
+        params = [make_params(l, rng, vth=(60, 160)) for l in net.layers]
+        B, E = 3, 400
+        times, src, nr = make_events(rng, B, E, 2 * 12 * 12)
+        plan = NetworkPlan(net.layers, params, B, E)
+        logits, stats, fits = plan.forward_device(torch.from_numpy(times).cuda(),
+                                                  torch.from_numpy(src).cuda(),
+                                                  torch.from_numpy(nr.astype(np.int32)).cuda())
+        torch.cuda.synchronize()
+        for b in range(B):
+            refs = O.network_forward(net.layers, params, times[b], src[b], nr[b])
+            np.testing.assert_array_equal(logits[b].cpu().numpy(), refs[-1].v_final)
+            assert [int(v) for v in stats[0, :, b].cpu().numpy()] == \
+                [r.n_real_events for r in refs]
