@@ -20,15 +20,27 @@ template <> struct CodeType<1> { using T = int8_t; };
 template <> struct CodeType<2> { using T = int16_t; };
 
 // Shared-memory layout of fc_scan: decay table (when short enough), then the per-warp event
-// records, then (WT > 0) the weight codes as (n_in + 1, n_out) with a zero row for masked entries.
+// records, then (WT > 0) the block's neuron group's weight codes, (n_in, q_cols) followed by a
+// zero row that masked entries point at.
 __host__ __device__ inline int fc_lut_words(int32_t lut_len) {
   return lut_len <= kLutSmemMax ? ((lut_len + 3) & ~3) : 0;
 }
 __host__ __device__ inline int fc_ring(int wt) { return wt ? kFcRing : 1; }
 
+// Columns of the staged weight table: a layer of one neuron group stages its whole (n_in, n_out)
+// table; otherwise each block stages the LPU columns of its own group.
+__host__ __device__ inline int32_t fc_q_cols(int32_t n_out, int lpu) {
+  return n_out <= lpu ? n_out : lpu;
+}
+
+size_t fc_scan_q_bytes(int32_t n_in, int32_t n_out, int wt, int lpu) {
+  // + one zero row of lpu entries: masked entries and lanes past n_out read it
+  return wt ? (((size_t)n_in * fc_q_cols(n_out, lpu) + lpu) * wt + 15) & ~(size_t)15 : 0;
+}
+
 size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lpu) {
   const size_t ev = (size_t)(kFcThreads / 32) * (32 / lpu) * lpu * fc_ring(wt) * sizeof(int2);
-  const size_t q = wt ? (((size_t)(n_in + 1) * n_out * wt + 15) & ~(size_t)15) : 0;
+  const size_t q = fc_scan_q_bytes(n_in, n_out, wt, lpu);
   return (size_t)fc_lut_words(lut_len) * 4 + ev + q;
 }
 
@@ -56,29 +68,35 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   int32_t* lut_s = reinterpret_cast<int32_t*>(fc_smem);
   int2* ev_all = reinterpret_cast<int2*>(fc_smem + (size_t)lut_words * 4);
   QT* q_s = reinterpret_cast<QT*>(ev_all + (kFcThreads / 32) * SPW * SB);
-  const int32_t zero_row = P.n_in * P.n_out;
+  const int g = blockIdx.y;  // the block's neuron group: neurons [g * LPU, g * LPU + LPU)
+  const int32_t qcols = fc_q_cols(P.n_out, LPU);
+  const int32_t zero_row = P.n_in * qcols;
   if (lut_words)
     for (int i = threadIdx.x; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
   if (WT) {
-    for (int32_t i = threadIdx.x; i < zero_row; i += blockDim.x) q_s[i] = (QT)__ldg(&P.qT[i]);
-    for (int32_t i = threadIdx.x; i < P.n_out; i += blockDim.x) q_s[zero_row + i] = 0;
+    if (P.G == 1) {  // the whole table, as laid out in global memory
+      for (int32_t i = threadIdx.x; i < zero_row; i += blockDim.x) q_s[i] = (QT)__ldg(&P.qT[i]);
+    } else {         // this group's LPU columns
+      for (int32_t i = threadIdx.x; i < zero_row; i += blockDim.x) {
+        const int32_t row = i / LPU, col = g * LPU + (i - row * LPU);
+        q_s[i] = col < P.n_out ? (QT)__ldg(&P.qT[(int64_t)row * P.n_out + col]) : (QT)0;
+      }
+    }
+    for (int32_t i = threadIdx.x; i < LPU; i += blockDim.x) q_s[zero_row + i] = 0;
   }
   __syncthreads();
   const int32_t* lut = lut_words ? lut_s : P.lut;
   const int lane = threadIdx.x & 31, gi = lane / LPU, gl = lane % LPU;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t n_units = (int64_t)P.batch * P.G;
-  if (gw * SPW >= n_units) return;  // the whole warp is past the last unit
+  if (gw * SPW >= P.batch) return;  // the whole warp is past the last sample
   int2* ev_s = ev_all + ((threadIdx.x >> 5) * SPW + gi) * SB;
-  const int64_t unit = gw * SPW + gi;
-  const bool unit_ok = unit < n_units;
-  // units in heaviest-first sample order: a warp's samples have similar lengths, and the
-  // longest chains start first
-  const int bu = unit_ok ? (int)(unit / P.G) : 0, g = unit_ok ? (int)(unit % P.G) : 0;
-  const int b = P.order ? P.order[bu] : bu;
+  const int64_t bs = gw * SPW + gi;  // sample slot
+  const bool unit_ok = bs < P.batch;
+  // samples in heaviest-first order: a warp's samples have similar lengths, and the longest
+  // chains start first
+  const int b = !unit_ok ? 0 : (P.order ? P.order[bs] : (int)bs);
   const int o = g * LPU + gl;
   const bool active = unit_ok && o < P.n_out;
-  const int oc = active ? o : 0;  // inactive lanes run column 0; their results are dropped
   const int32_t n_in = unit_ok ? P.in_nreal[b] : 0;
   const int32_t n_eff = unit_ok ? P.n_eff(b) : 0;
   const int32_t nproc = !unit_ok ? 0 : (P.tail_mode ? P.in.capacity : n_eff);
@@ -128,9 +146,9 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
       const bool real = j < n_in && j < nproc;
       const int32_t dt = real ? dt_from_times(tc[r], tp) : 0;
       const int32_t a = dt == 0 ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
-      int32_t qo;
-      if (WT) qo = real ? (int32_t)jax_index(scur[r], P.n_in) * P.n_out : zero_row;
-      else qo = real ? (int32_t)jax_index(scur[r], P.n_in) * P.n_out : -1;
+      int32_t qo;  // row offset of the event's weights (staged table, or the global codes)
+      if (WT) qo = real ? (int32_t)jax_index(scur[r], P.n_in) * qcols : zero_row;
+      else qo = real ? (int32_t)jax_index(scur[r], P.n_in) * P.n_out + g * LPU : -1;
       ev_s[r * LPU + gl] = make_int2(a, qo);
     }
     tcarry = __shfl_sync(kAll, tc[R - 1], LPU - 1, LPU);
@@ -144,8 +162,10 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
     auto step = [&](int e) {
       const int2 ev = ev_s[e];
       int32_t qv;
-      if (WT) qv = (int32_t)q_s[ev.y + oc];
-      else qv = ev.y >= 0 ? __ldg(&P.qT[ev.y + oc]) : 0;
+      // lanes past n_out read the row's tail (or the zero row's padding); their results are
+      // dropped
+      if (WT) qv = (int32_t)q_s[ev.y + gl];
+      else qv = (ev.y >= 0 && active) ? __ldg(&P.qT[ev.y + gl]) : 0;
       int32_t u;
       const int32_t w = sc.step<SAT>(V, ev.x, qv, u);
       vmin = min(vmin, u);

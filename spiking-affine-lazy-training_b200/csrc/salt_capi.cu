@@ -503,12 +503,14 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   // narrow layers (the membrane readouts) pack several samples into a warp; weight tables that
   // fit are staged in shared memory at the width of their codes
   const int lpu = d->n_out <= 8 ? 8 : (d->n_out <= 16 ? 16 : 32);
+  // every block serves one neuron group (grid y) for 4 warps of samples (grid x) and stages
+  // that group's weight columns
   int wt = q->q_bits <= 8 ? 1 : (q->q_bits <= 16 ? 2 : 4);
-  if ((size_t)(d->n_in + 1) * d->n_out * wt > kFcQSmemMax) wt = 0;
+  if (fc_scan_q_bytes(d->n_in, d->n_out, wt, lpu) > kFcQSmemMax) wt = 0;
   const size_t smem = fc_scan_smem(d->n_in, d->n_out, q->lut_len, wt, lpu);
-  const int64_t warps = ((int64_t)B * L.G + 32 / lpu - 1) / (32 / lpu);
+  const int64_t warps = ((int64_t)B + 32 / lpu - 1) / (32 / lpu);
   const int wpb = kFcThreads / 32;
-  const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
+  const dim3 grid((unsigned)((warps + wpb - 1) / wpb), (unsigned)L.G);
   void* scan_fn = fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu, wt);
   if (smem > 48 * 1024)
     SALT_CUDA(cudaFuncSetAttribute(scan_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -247,6 +247,8 @@ size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt);
 // Dynamic shared memory of fc_scan for these sizes.
 size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lpu);
+// Bytes of the weight table fc_scan stages in shared memory (0 when wt == 0).
+size_t fc_scan_q_bytes(int32_t n_in, int32_t n_out, int wt, int lpu);
 
 // Device address of the fixed scratch behind salt_conv_layer_forward_noalloc (fixed_scratch.cu).
 cudaError_t fixed_scratch_address(void** ptr);

@@ -174,6 +174,17 @@ def test_fc_packed_narrow_layers(n_out, fires, batch):
     _check_layer(layer, params, times, src, nr)
 
 
+@pytest.mark.parametrize("n_in,n_out,q_max", [(2312, 128, 127), (4000, 40, 3000)])
+def test_fc_wide_inputs(n_in, n_out, q_max):
+    """Weight tables past the shared-memory stage (int16 codes over 4000 inputs, read from global
+    memory) and configuration 1's 2312x128 layer (int8 codes staged per neuron group)."""
+    rng = np.random.default_rng(140 + n_out)
+    layer = S.FCLayer(name="f", n_in=n_in, n_out=n_out, init_k=1.0, tau=20.0, max_out_spikes=900)
+    params = make_params(layer, rng, vth=(300, 900), q_max=q_max)
+    times, src, nr = make_events(rng, 3, 400, n_in)
+    _check_layer(layer, params, times, src, nr)
+
+
 @pytest.mark.parametrize("M", [1, 5, 40])
 def test_fc_output_truncation(M):
     rng = np.random.default_rng(90 + M)
