@@ -242,7 +242,7 @@ size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes) {
   return FusedSmem(P, wt_bytes).total;
 }
 
-template <typename WT, int LPU, bool SAT>
+template <typename WT, int LPU, bool SAT, bool WIDE>
 __global__ void __launch_bounds__(kFusedThreads)
 conv_fused(ConvLaunch P) {
   constexpr int UPW = 32 / LPU;  // units (position x channel group) per warp
@@ -457,7 +457,7 @@ conv_fused(ConvLaunch P) {
           if (Ts >= 0 && lane_ok) {
             const int32_t qv = (int32_t)w_s[Ts + oc];
             int32_t u;
-            const int32_t w = sc.step<SAT>(V, as, qv, u);
+            const int32_t w = sc.step<SAT, WIDE>(V, as, qv, u);
             spike = w >= vth;
             V = spike ? 0 : w;
             // overflow is read off the unfitted range at the end of the layer (layer_finish)
@@ -969,29 +969,31 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   }
 }
 
-// Host-side dispatch over the (weight width, lanes per channel group, overflow mode)
-// instantiations.
-template <typename WT, bool SAT>
+// Host-side dispatch over the (weight width, lanes per channel group, overflow mode, decay
+// product form) instantiations.
+template <typename WT, bool SAT, bool WIDE>
 static void* fused_for_lpu(int lpu) {
   switch (lpu) {
-    case 1: return (void*)conv_fused<WT, 1, SAT>;
-    case 2: return (void*)conv_fused<WT, 2, SAT>;
-    case 4: return (void*)conv_fused<WT, 4, SAT>;
-    case 8: return (void*)conv_fused<WT, 8, SAT>;
-    case 16: return (void*)conv_fused<WT, 16, SAT>;
-    default: return (void*)conv_fused<WT, 32, SAT>;
+    case 1: return (void*)conv_fused<WT, 1, SAT, WIDE>;
+    case 2: return (void*)conv_fused<WT, 2, SAT, WIDE>;
+    case 4: return (void*)conv_fused<WT, 4, SAT, WIDE>;
+    case 8: return (void*)conv_fused<WT, 8, SAT, WIDE>;
+    case 16: return (void*)conv_fused<WT, 16, SAT, WIDE>;
+    default: return (void*)conv_fused<WT, 32, SAT, WIDE>;
   }
 }
 
-void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate) {
-  if (saturate) {
-    if (wt_bytes == 1) return fused_for_lpu<int8_t, true>(lpu);
-    if (wt_bytes == 2) return fused_for_lpu<int16_t, true>(lpu);
-    return fused_for_lpu<int32_t, true>(lpu);
-  }
-  if (wt_bytes == 1) return fused_for_lpu<int8_t, false>(lpu);
-  if (wt_bytes == 2) return fused_for_lpu<int16_t, false>(lpu);
-  return fused_for_lpu<int32_t, false>(lpu);
+template <bool SAT, bool WIDE>
+static void* fused_for_wt(int wt_bytes, int lpu) {
+  if (wt_bytes == 1) return fused_for_lpu<int8_t, SAT, WIDE>(lpu);
+  if (wt_bytes == 2) return fused_for_lpu<int16_t, SAT, WIDE>(lpu);
+  return fused_for_lpu<int32_t, SAT, WIDE>(lpu);
+}
+
+void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate, bool wide) {
+  if (saturate)
+    return wide ? fused_for_wt<true, true>(wt_bytes, lpu) : fused_for_wt<true, false>(wt_bytes, lpu);
+  return wide ? fused_for_wt<false, true>(wt_bytes, lpu) : fused_for_wt<false, false>(wt_bytes, lpu);
 }
 
 }  // namespace salt

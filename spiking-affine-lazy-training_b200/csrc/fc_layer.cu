@@ -56,7 +56,7 @@ size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lp
 // the group then reads with one broadcast load per step.  With WT > 0 the weight codes sit in
 // shared memory as WT-byte integers with a zero row that masked entries (pads, events past the
 // group's end) point at, so a step needs no predicate: past the end it is the identity.
-template <bool FIRES, bool SAT, int LPU, int WT>
+template <bool FIRES, bool SAT, int LPU, int WT, bool WIDE>
 __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   using QT = typename CodeType<WT>::T;
   constexpr int SPW = 32 / LPU;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
       if (WT) qv = (int32_t)q_s[ev.y + gl];
       else qv = (ev.y >= 0 && active) ? __ldg(&P.qT[ev.y + gl]) : 0;
       int32_t u;
-      const int32_t w = sc.step<SAT>(V, ev.x, qv, u);
+      const int32_t w = sc.step<SAT, WIDE>(V, ev.x, qv, u);
       vmin = min(vmin, u);
       vmax = max(vmax, u);
       if (FIRES) {
@@ -336,27 +336,35 @@ fc_truncated(FCLaunch P, salt_stream_out out) {
   }
 }
 
-template <int LPU, int WT>
+template <int LPU, int WT, bool WIDE>
 static void* fc_scan_for(bool fires, bool saturate) {
   if (saturate)
-    return fires ? (void*)fc_scan<true, true, LPU, WT> : (void*)fc_scan<false, true, LPU, WT>;
-  return fires ? (void*)fc_scan<true, false, LPU, WT> : (void*)fc_scan<false, false, LPU, WT>;
+    return fires ? (void*)fc_scan<true, true, LPU, WT, WIDE>
+                 : (void*)fc_scan<false, true, LPU, WT, WIDE>;
+  return fires ? (void*)fc_scan<true, false, LPU, WT, WIDE>
+               : (void*)fc_scan<false, false, LPU, WT, WIDE>;
 }
 
-template <int WT>
+template <int WT, bool WIDE>
 static void* fc_scan_lpu(bool fires, bool saturate, int lpu) {
-  if (lpu == 8) return fc_scan_for<8, WT>(fires, saturate);
-  if (lpu == 16) return fc_scan_for<16, WT>(fires, saturate);
-  return fc_scan_for<32, WT>(fires, saturate);
+  if (lpu == 8) return fc_scan_for<8, WT, WIDE>(fires, saturate);
+  if (lpu == 16) return fc_scan_for<16, WT, WIDE>(fires, saturate);
+  return fc_scan_for<32, WT, WIDE>(fires, saturate);
 }
 
-void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt) {
+template <bool WIDE>
+static void* fc_scan_wt(bool fires, bool saturate, int lpu, int wt) {
   switch (wt) {
-    case 1: return fc_scan_lpu<1>(fires, saturate, lpu);
-    case 2: return fc_scan_lpu<2>(fires, saturate, lpu);
-    case 4: return fc_scan_lpu<4>(fires, saturate, lpu);
-    default: return fc_scan_lpu<0>(fires, saturate, lpu);
+    case 1: return fc_scan_lpu<1, WIDE>(fires, saturate, lpu);
+    case 2: return fc_scan_lpu<2, WIDE>(fires, saturate, lpu);
+    case 4: return fc_scan_lpu<4, WIDE>(fires, saturate, lpu);
+    default: return fc_scan_lpu<0, WIDE>(fires, saturate, lpu);
   }
+}
+
+void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt, bool wide) {
+  return wide ? fc_scan_wt<true>(fires, saturate, lpu, wt)
+              : fc_scan_wt<false>(fires, saturate, lpu, wt);
 }
 
 }  // namespace salt

@@ -388,7 +388,9 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
         L, s.counts, s.lists);
     SALT_LAUNCHED("conv_tile_scatter");
   }
-  void* fn = conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE);
+  // without needs_tail every decay code lies in [0, 2^f_a): the one-multiply decay form is exact
+  void* fn = conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE,
+                               q->needs_tail == 0);
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
   void* args[] = {&L};
   if (timer) SALT_CUDA(cudaEventRecord(timer->start, st));
@@ -511,7 +513,8 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   const int64_t warps = ((int64_t)B + 32 / lpu - 1) / (32 / lpu);
   const int wpb = kFcThreads / 32;
   const dim3 grid((unsigned)((warps + wpb - 1) / wpb), (unsigned)L.G);
-  void* scan_fn = fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu, wt);
+  void* scan_fn = fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu, wt,
+                                 q->needs_tail == 0);
   if (smem > 48 * 1024)
     SALT_CUDA(cudaFuncSetAttribute(scan_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* scan_args[] = {&L};

@@ -71,11 +71,21 @@ __device__ __forceinline__ int32_t quant_step(int32_t v, int32_t a, bool is_iden
 // + lo, the rounding term is (2^f_a * lo + half) >> f_a = lo) for every register value of at
 // most 30 bits; a decay code equal to 2^f_a likewise leaves v unchanged.  The overflow mode is a
 // compile-time choice; ovf is "the fitted value differs from the unfitted one".
-template <bool SAT>
+//
+// WIDE computes the decay as one 64-bit product: with v = hi * 2^f_a + lo (0 <= lo < 2^f_a),
+// a * hi + floor((a * lo + half) / 2^f_a) = floor((a * v + half) / 2^f_a) in the integers, so the
+// two agree modulo 2^32 whenever the reference's int32 term a * lo + round_half does not wrap.
+// That holds for every decay code in [0, 2^f_a] with f_a <= 15 (a * lo + half < 2^30), which is
+// what a layer without needs_tail guarantees; other tables take the split form.
+template <bool SAT, bool WIDE = false>
 __device__ __forceinline__ int32_t quant_step_a(int32_t v, int32_t a, int32_t q_shifted,
                                                 int32_t f_a, int32_t lo_mask, int32_t round_half,
                                                 int32_t half, int32_t wrap_shift, int32_t& u) {
-  const int32_t dec = wadd(wmul(a, v >> f_a), wadd(wmul(a, v & lo_mask), round_half) >> f_a);
+  int32_t dec;
+  if (WIDE)
+    dec = (int32_t)(uint32_t)(uint64_t)(((int64_t)a * v + round_half) >> f_a);
+  else
+    dec = wadd(wmul(a, v >> f_a), wadd(wmul(a, v & lo_mask), round_half) >> f_a);
   u = wadd(dec, q_shifted);
   if (SAT) return min(max(u, -half), half - 1);
   return (int32_t)((uint32_t)u << wrap_shift) >> wrap_shift;
@@ -88,10 +98,10 @@ struct StepConsts {
       : f_a(c.f_a), f_V(c.f_V), lo_mask((int32_t)((1u << c.f_a) - 1u)), round_half(c.round_half),
         half((int32_t)(1u << (c.total_bits - 1))), wrap_shift(32 - c.total_bits),
         ident_a((int32_t)(1u << c.f_a)) {}
-  template <bool SAT>
+  template <bool SAT, bool WIDE = false>
   __device__ __forceinline__ int32_t step(int32_t v, int32_t a, int32_t q, int32_t& u) const {
-    return quant_step_a<SAT>(v, a, wmul(q, (int32_t)(1u << f_V)), f_a, lo_mask, round_half, half,
-                             wrap_shift, u);
+    return quant_step_a<SAT, WIDE>(v, a, wmul(q, (int32_t)(1u << f_V)), f_a, lo_mask, round_half,
+                                   half, wrap_shift, u);
   }
 };
 
