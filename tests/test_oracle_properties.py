@@ -20,6 +20,33 @@ def test_wide_mul_shift_equals_exact_integer_arithmetic():
         assert O.wide_mul_shift(int(a), int(v), shift, "truncate") == exact >> shift
 
 
+def _wrap32(x):
+    return ((np.asarray(x, np.int64) + 2 ** 31) % 2 ** 32) - 2 ** 31
+
+
+def test_split_decay_equals_one_wide_product_for_in_range_codes():
+    """The kernels' one-multiply decay, low 32 bits of (a*V + half) >> f_a, against the
+    reference's int32 split a*(V>>f_a) + ((a*(V & mask) + half) >> f_a) (fixed_point.py:47-65),
+    for every f_a <= 15, decay codes in [0, 2^f_a] and register values over the whole int32
+    range; out-of-range codes can make the split form's a*lo term wrap, which is why a layer with
+    needs_tail keeps the split form."""
+    rng = np.random.default_rng(11)
+    edge_v = np.array([0, 1, -1, 2 ** 29 - 1, -(2 ** 29), 2 ** 31 - 1, -(2 ** 31)], np.int64)
+    for f_a in range(16):
+        for half in ({0, (1 << (f_a - 1))} if f_a else {0}):
+            a = np.concatenate([rng.integers(0, 2 ** f_a + 1, 4000),
+                                [0, 1, 2 ** f_a - 1, 2 ** f_a]]).astype(np.int64)
+            v = np.concatenate([rng.integers(-(2 ** 31), 2 ** 31, a.size - edge_v.size), edge_v])
+            lo = v & ((1 << f_a) - 1)
+            split = _wrap32(_wrap32(a * (v >> f_a)) + (_wrap32(a * lo + half) >> f_a))
+            wide = _wrap32((a * v + half) >> f_a)
+            np.testing.assert_array_equal(split, wide)
+    # a code beyond the range: the split form's inner term wraps and the two differ
+    f_a, a, v = 15, 2 ** 20, 2 ** 15 - 1
+    lo = v & ((1 << f_a) - 1)
+    assert _wrap32(_wrap32(a * (v >> f_a)) + (_wrap32(a * lo) >> f_a)) != _wrap32((a * v) >> f_a)
+
+
 def test_decay_step_never_grows_magnitude():
     """salt_core/tests/test_fixed_point.py:49-58"""
     rng = np.random.default_rng(0)
