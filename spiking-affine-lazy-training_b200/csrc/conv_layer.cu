@@ -215,7 +215,7 @@ struct __align__(16) EvRec {
 
 // Shared-memory layout of conv_fused; the host sizes it with the same function.
 struct FusedSmem {
-  size_t w, lut, v, tprev, cnt, mask, ev, ej, sw, list, posoff, poscnt, act, ocspk, misc, total;
+  size_t w, lut, v, tprev, cnt, mask, ev, ej, sw, list, posoff, poscnt, act, misc, total;
   __host__ __device__ FusedSmem(const ConvLaunch& P, int wt_bytes) {
     const size_t npm = (size_t)P.tile_h * P.tile_w;
     size_t o = 0;
@@ -232,7 +232,6 @@ struct FusedSmem {
     posoff = o; o += align16(npm * 4);
     poscnt = o; o += align16(npm * 4);
     act = o;   o += align16(npm * 4);
-    ocspk = o; o += align16((size_t)P.ocp * 4);
     misc = o;  o += 64;
     total = o;
   }
@@ -263,7 +262,6 @@ conv_fused(ConvLaunch P) {
   int32_t* poscnt_s = reinterpret_cast<int32_t*>(smem + L.poscnt);
   int32_t* act_s = reinterpret_cast<int32_t*>(smem + L.act);
   __shared__ int32_t s_scan[kScanSmem];
-  int32_t* ocspk_s = reinterpret_cast<int32_t*>(smem + L.ocspk);
   int32_t* misc_s = reinterpret_cast<int32_t*>(smem + L.misc);
 
   // blocks run in launch order, so the heaviest samples start first (a longest-first schedule)
@@ -289,7 +287,6 @@ conv_fused(ConvLaunch P) {
     tprev_s[i] = 0.0f;
     cnt_s[i] = 0;
   }
-  for (int i = tid; i < OCP; i += blockDim.x) ocspk_s[i] = 0;
   if (tid < 8) misc_s[tid] = 0;
   const int32_t* lut = P.lut_in_smem ? lut_s : P.lut;
 
@@ -424,7 +421,6 @@ conv_fused(ConvLaunch P) {
       vth = INT32_MAX;
       if (lane_ok && P.has_vth) vth = __ldg(&P.vth[(int64_t)oc * P.n_sp + oy * P.w_out + ox]);
       const int32_t nmax = __reduce_max_sync(0xffffffffu, n);
-      int32_t spk_visit = 0;
       for (int32_t b0 = 0; b0 < nmax; b0 += LPU) {
         const int32_t idx = b0 + glane;
         const bool has = idx < n;
@@ -447,7 +443,7 @@ conv_fused(ConvLaunch P) {
         const float last_t = __shfl_sync(0xffffffffu, r.t, nb > 0 ? nb - 1 : 0, LPU);
         if (nb > 0) tp = last_t;
         const int32_t nbw = min(nmax - b0, LPU);  // warp-uniform batch length
-        uint32_t mybits = 0;
+        uint32_t myvote = 0;  // the warp's spike ballot of this lane's step
         // 16-lane groups: the walk is unrolled so that the broadcasts and weight loads of later
         // steps are issued ahead of the dependent register updates
         auto walk = [&](int st) {
@@ -464,9 +460,8 @@ conv_fused(ConvLaunch P) {
             acc_min = min(acc_min, u);
             acc_max = max(acc_max, u);
           }
-          const uint32_t bits = (__ballot_sync(0xffffffffu, spike) >> (gi * LPU)) & gmask_bits;
-          if (glane == st) mybits = bits;
-          spk_visit += spike;
+          const uint32_t vote = __ballot_sync(0xffffffffu, spike);
+          if (glane == st) myvote = vote;
         };
         if (LPU <= 16) {
           if (nbw == LPU) {
@@ -481,7 +476,7 @@ conv_fused(ConvLaunch P) {
                   // software pipeline (+12 %) all measured slower than the plain loop
           for (int st = 0; st < nbw; ++st) walk(st);
         }
-        if (has) sw_s[widx] = mybits;
+        if (has) sw_s[widx] = (myvote >> (gi * LPU)) & gmask_bits;
         cn += max(nb, 0);
       }
       if (unit_ok) {
@@ -490,9 +485,7 @@ conv_fused(ConvLaunch P) {
           tprev_s[pl * P.G + g] = tp;
           cnt_s[pl * P.G + g] = cn;
         }
-        if (spk_visit && oc < P.oc) atomicAdd(&ocspk_s[oc], spk_visit);
       }
-      acc_spk += spk_visit;
     }
     __syncthreads();
 
@@ -585,7 +578,6 @@ conv_fused(ConvLaunch P) {
       P.v_final[(int64_t)b * P.n_neurons + neuron] = V;
       if (P.tail_mode) P.tail_cnt[(int64_t)b * P.n_neurons + neuron] = tail;
       if (tail) {
-        atomicAdd(&ocspk_s[oc], tail);
         atomicAdd(&P.tail_total[b], tail);
         acc_spk += tail;
       }
@@ -609,10 +601,8 @@ conv_fused(ConvLaunch P) {
     atomicMin(&P.vmin[b], misc_s[1]);
     atomicMax(&P.vmax[b], misc_s[2]);
     if (misc_s[3]) atomicOr(&P.ovf[b], 1);
-    if (misc_s[4]) atomicAdd(&P.s_total[b], misc_s[4]);
-  }
-  for (int oc = tid; oc < P.oc; oc += blockDim.x)
-    if (ocspk_s[oc]) atomicAdd(&P.oc_total[(int64_t)b * P.oc + oc], ocspk_s[oc]);
+    if (misc_s[4]) atomicAdd(&P.s_total[b], misc_s[4]);  // tail spikes; spike_chunk_scan
+  }                                                      // adds the spike words' count
 }
 
 // ------------------------------------------------------------------ compaction
@@ -814,11 +804,34 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   const int32_t n_eff = P.n_eff(b);
   const int SWW = P.nslots * P.G;
   int32_t* hist = scratch_hist + (int64_t)b * P.n_sp * 2;  // [n_sp] real, [n_sp] tail
-  // 1. channel cut: the channel holding the M-th spike in neuron-major order
+  // 1. spikes per channel (spike words of the valid candidate slots, then catch-up/identity
+  // spikes) into the zeroed oc_total row, and the channel cut: the channel holding the M-th
+  // spike in neuron-major order
+  int32_t* oct = P.oc_total + (int64_t)b * P.oc;
+  for (int32_t j = tid; j < n_eff; j += blockDim.x) {
+    int32_t cc, y, x;
+    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
+    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
+        for (int g = 0; g < P.G; ++g) {
+          uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
+          while (wd) {
+            atomicAdd(&oct[g * P.lpu + __ffs(wd) - 1], 1);
+            wd &= wd - 1u;
+          }
+        }
+  }
+  if (P.tail_mode)
+    for (int64_t n = tid; n < P.n_neurons; n += blockDim.x) {
+      const int32_t c = P.tail_cnt[(int64_t)b * P.n_neurons + n];
+      if (c) atomicAdd(&oct[n / P.n_sp], c);
+    }
+  __syncthreads();
   if (tid == 0) {
     int32_t cum = 0, occ = P.oc - 1;
     for (int oc = 0; oc < P.oc; ++oc) {
-      const int32_t t = P.oc_total[(int64_t)b * P.oc + oc];
+      const int32_t t = oct[oc];
       if (cum + t >= M) {
         occ = oc;
         break;

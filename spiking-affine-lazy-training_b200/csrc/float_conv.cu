@@ -226,7 +226,6 @@ __global__ void __launch_bounds__(kFConvThreads) fconv_scan(ConvLaunch P, FConvA
   if (act) {
     X.v_final[(int64_t)b * P.n_neurons + neuron] = s.v0;
     P.tail_cnt[(int64_t)b * P.n_neurons + neuron] = tail;
-    if (nspk + tail) atomicAdd(&P.oc_total[(int64_t)b * P.oc + oc], nspk + tail);
     if (tail) atomicAdd(&P.tail_total[b], tail);
     atomicMax(&X.needed_extra[b],
               extra_steps_bound(m_pos, sum_pos, X.v_th, L, C, X.base_steps));

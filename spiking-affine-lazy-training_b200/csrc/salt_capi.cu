@@ -66,8 +66,10 @@ struct Carver {
 
 // ---------------------------------------------------------------- small kernels
 
-// One warp per sample: exclusive scan in place of the spike counts per event chunk.
-__global__ void spike_chunk_scan(int32_t* __restrict__ chunk, int32_t n_chunks, int32_t batch) {
+// One warp per sample: exclusive scan in place of the spike counts per event chunk; with
+// total_add, the sample's total is also added to total_add[sample].
+__global__ void spike_chunk_scan(int32_t* __restrict__ chunk, int32_t n_chunks, int32_t batch,
+                                 int32_t* __restrict__ total_add) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= batch) return;
   int32_t* c = chunk + (int64_t)warp * n_chunks;
@@ -84,6 +86,7 @@ __global__ void spike_chunk_scan(int32_t* __restrict__ chunk, int32_t n_chunks, 
     if (i < n_chunks) c[i] = carry + incl - v;
     carry += __shfl_sync(0xffffffffu, incl, 31);
   }
+  if (total_add && lane == 0 && carry) total_add[warp] += carry;
 }
 
 struct FinishArgs {
@@ -397,7 +400,9 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   SALT_CUDA(cudaLaunchKernel(fn, dim3(p.T, B), dim3(kFusedThreads), args, p.smem, st));
   SALT_LAUNCHED("conv_fused");
   if (timer) SALT_CUDA(cudaEventRecord(timer->stop, st));
-  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
+  // conv_fused counts only catch-up/identity spikes into s_total: the spike words' count is the
+  // scan's total
+  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B, s.s_total);
   SALT_LAUNCHED("spike_chunk_scan");
   {
     salt_stream_out so = *out;
@@ -521,7 +526,7 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   SALT_CUDA(cudaLaunchKernel(scan_fn, dim3(grid), dim3(kFcThreads), scan_args, smem, st));
   SALT_LAUNCHED("fc_scan");
   if (q->has_vth) {
-    spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
+    spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B, nullptr);
     SALT_LAUNCHED("spike_chunk_scan");
     fc_compact<<<dim3(std::min(L.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0,
                  st>>>(L, *out);
@@ -703,7 +708,7 @@ static salt_status float_forward_impl(const salt_float_fc_desc* d, const float* 
   L.sw = s.sw; L.sw_stride = P.sw_stride;
   L.chunk_spikes = s.chunk; L.chunk_off = s.chunk; L.n_spk_chunks = P.n_spk_chunks;
   L.s_total = s.s_total; L.n_spk = s.n_spk; L.tail_mode = 0;
-  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B);
+  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, L.n_spk_chunks, B, nullptr);
   SALT_LAUNCHED("spike_chunk_scan");
   fc_compact<<<dim3(std::min(L.n_spk_chunks, compact_blocks(B)), B), kCompactThreads, 0, st>>>(
       L, *out);
@@ -1048,7 +1053,7 @@ salt_status salt_float_conv_layer_forward(const salt_float_conv_desc* d, const f
   }
   SALT_CUDA(float_conv_launch(L, X, w, s.wT, out->n_real, stats, v_max, v_min, st));
   g_launches += 3;
-  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B);
+  spike_chunk_scan<<<(B * 32 + 255) / 256, 256, 0, st>>>(s.chunk, p.n_spk_chunks, B, nullptr);
   SALT_LAUNCHED("spike_chunk_scan");
   {
     salt_stream_out so = *out;
