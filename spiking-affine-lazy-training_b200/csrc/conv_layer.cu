@@ -307,19 +307,24 @@ conv_fused(ConvLaunch P) {
   for (int32_t base = 0; base < nev; base += kFusedChunk) {
     const int32_t nchunk = min(kFusedChunk, nev - base);
     // -------- phase 1: decode the chunk and bucket its candidates by position
+    auto load_ev = [&](int e, int32_t& j, float& t, int32_t& sv) {
+      j = e < nchunk ? (list ? list[base + e] : base + e) : -1;
+      if (j >= 0) {
+        t = P.in.times[row * P.in.capacity + j];
+        sv = P.in.src[row * P.in.capacity + j];
+      }
+    };
     for (int i = tid; i < NPM * CHW; i += blockDim.x) mask_s[i] = 0;
     for (int i = tid; i < kFusedChunk * SWW; i += blockDim.x) sw_s[i] = 0;
     if (tid == 0) misc_s[0] = 0;
     __syncthreads();
-    for (int e0 = warp * 32; e0 < kFusedChunk; e0 += blockDim.x) {  // warp-uniform trip count
+    auto decode = [&](int e0, int32_t j, float t, int32_t srcv) {  // warp-uniform e0
       const int e = e0 + lane;
-      const bool in = e < nchunk;
+      const bool in = j >= 0;
       EvCand k{0, 1, 0, 0, 1, 0};
       if (in) {
-        const int32_t j = list ? list[base + e] : base + e;
-        const float t = P.in.times[row * P.in.capacity + j];
         int32_t c, y, x;
-        k = event_cand(P, P.in.src[row * P.in.capacity + j], c, y, x);
+        k = event_cand(P, srcv, c, y, x);
         EvRec r;
         r.t = t;
         r.ckk = c * KK;
@@ -338,14 +343,47 @@ conv_fused(ConvLaunch P) {
       // may lead the same position in different rounds, and the match gives no memory order
       // between them, so the update is an atomic OR.
       const int wrd = e0 >> 5;
-      for (int a = 0; a < P.ncand; ++a)
-        for (int bb = 0; bb < P.ncand; ++bb) {
-          const int oy = k.oy_min + a, ox = k.ox_min + bb;
-          const bool ok = in && oy >= k.oy_lo && oy <= k.oy_hi && ox >= k.ox_lo && ox <= k.ox_hi;
-          const int pl = ok ? (oy - oy0) * P.tile_w + (ox - ox0) : -1;
-          const uint32_t same = __match_any_sync(0xffffffffu, pl);
-          if (ok && (__ffs(same) - 1) == lane) atomicOr(&mask_s[pl * CHW + wrd], same);
+      if (P.ncand == 2) {
+        // 2x2 windows: one match per event.  Lanes whose windows start at the same position with
+        // the same valid slots share all their candidate positions, so the group's first lane
+        // sets the group's bits in every one of them (tile sides are at most 64 positions, so
+        // the tile-local origin, offset by 2, fits in 7 bits per axis).
+        uint32_t vb = 0;
+        if (in) {
+          const bool y0 = k.oy_min >= k.oy_lo && k.oy_min <= k.oy_hi;
+          const bool y1 = k.oy_min + 1 >= k.oy_lo && k.oy_min + 1 <= k.oy_hi;
+          const bool x0 = k.ox_min >= k.ox_lo && k.ox_min <= k.ox_hi;
+          const bool x1 = k.ox_min + 1 >= k.ox_lo && k.ox_min + 1 <= k.ox_hi;
+          vb = (uint32_t)(y0 && x0) | ((uint32_t)(y0 && x1) << 1) | ((uint32_t)(y1 && x0) << 2) |
+               ((uint32_t)(y1 && x1) << 3);
         }
+        const int ly = k.oy_min - oy0, lx = k.ox_min - ox0;
+        const int32_t key = vb ? (((ly + 2) << 11) | ((lx + 2) << 4) | (int32_t)vb) : -1;
+        const uint32_t same = __match_any_sync(0xffffffffu, key);
+        if (vb && (__ffs(same) - 1) == lane) {
+          const int i0 = (ly * P.tile_w + lx) * CHW + wrd;  // slot (0, 0); used only if valid
+          if (vb & 1u) atomicOr(&mask_s[i0], same);
+          if (vb & 2u) atomicOr(&mask_s[i0 + CHW], same);
+          if (vb & 4u) atomicOr(&mask_s[i0 + P.tile_w * CHW], same);
+          if (vb & 8u) atomicOr(&mask_s[i0 + (P.tile_w + 1) * CHW], same);
+        }
+      } else {
+        for (int a = 0; a < P.ncand; ++a)
+          for (int bb = 0; bb < P.ncand; ++bb) {
+            const int oy = k.oy_min + a, ox = k.ox_min + bb;
+            const bool ok = in && oy >= k.oy_lo && oy <= k.oy_hi && ox >= k.ox_lo && ox <= k.ox_hi;
+            const int pl = ok ? (oy - oy0) * P.tile_w + (ox - ox0) : -1;
+            const uint32_t same = __match_any_sync(0xffffffffu, pl);
+            if (ok && (__ffs(same) - 1) == lane) atomicOr(&mask_s[pl * CHW + wrd], same);
+          }
+      }
+    };
+#pragma unroll 1
+    for (int e0 = warp * 32; e0 < kFusedChunk; e0 += kFusedThreads) {  // warp-uniform trip count
+      int32_t j, sv = 0;
+      float t = 0.0f;
+      load_ev(e0 + lane, j, t, sv);
+      decode(e0, j, t, sv);
     }
     __syncthreads();
 

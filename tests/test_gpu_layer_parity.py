@@ -85,6 +85,19 @@ def test_conv_output_truncation(M):
     assert np.any(out.stream.n_real_events > M)
 
 
+@pytest.mark.parametrize("M", [3, 60])
+def test_conv_output_truncation_two_channel_groups_several_tiles(M):
+    """40 channels (two 32-lane channel groups) over a 14x14 plane (several tiles): the channel
+    cut of the truncated samples counts each group's spike words at channel g * 32 + bit."""
+    rng = np.random.default_rng(25 + M)
+    layer = S.ConvLayer(name="c", ic=2, h_in=14, w_in=14, oc=40, k=3, s=1, p=1, init_k=1.0,
+                        tau=8.0, max_queue_len=64, max_out_spikes=M)
+    params = make_params(layer, rng, vth=(5, 30), f_a=6)
+    times, src, nr = make_events(rng, 3, 120, 2 * 14 * 14, t_max=60)
+    out = _check_layer(layer, params, times, src, nr)
+    assert np.any(out.stream.n_real_events > M)
+
+
 @pytest.mark.parametrize("vth", [(-20, 0), (-5, 5)])
 def test_conv_tail_columns_fire_when_threshold_not_positive(vth):
     rng = np.random.default_rng(30)
