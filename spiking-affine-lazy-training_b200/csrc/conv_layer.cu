@@ -215,7 +215,8 @@ struct __align__(16) EvRec {
 
 // Shared-memory layout of conv_fused; the host sizes it with the same function.
 struct FusedSmem {
-  size_t w, lut, v, tprev, cnt, mask, ev, ej, sw, list, posoff, poscnt, act, misc, total;
+  size_t w, lut, v, tprev, cnt, mask, ev, ej, sw, list, posoff, poscnt, act, park, vote, misc,
+      total;
   __host__ __device__ FusedSmem(const ConvLaunch& P, int wt_bytes) {
     const size_t npm = (size_t)P.tile_h * P.tile_w;
     size_t o = 0;
@@ -232,6 +233,9 @@ struct FusedSmem {
     posoff = o; o += align16(npm * 4);
     poscnt = o; o += align16(npm * 4);
     act = o;   o += align16(npm * 4);
+    // 32-lane groups park each batch's (decay code, weight row) pairs and step ballots per warp
+    park = o;  o += align16((size_t)(P.lpu == 32 ? kFusedThreads : 0) * sizeof(int2));
+    vote = o;  o += align16((size_t)(P.lpu == 32 ? kFusedThreads : 0) * 4);
     misc = o;  o += 64;
     total = o;
   }
@@ -263,6 +267,12 @@ conv_fused(ConvLaunch P) {
   int32_t* act_s = reinterpret_cast<int32_t*>(smem + L.act);
   __shared__ int32_t s_scan[kScanSmem];
   int32_t* misc_s = reinterpret_cast<int32_t*>(smem + L.misc);
+  // 32-lane groups: per-warp parking of the batch's (a, T) pairs and of the step ballots (one
+  // broadcast load per step instead of two shuffles, one store instead of a select); the
+  // 16-lane walk keeps them in registers, where it needs fewer
+  constexpr bool PARK = LPU == 32;
+  int2* park_w = reinterpret_cast<int2*>(smem + L.park) + (threadIdx.x & ~31);
+  uint32_t* vote_w = reinterpret_cast<uint32_t*>(smem + L.vote) + (threadIdx.x & ~31);
 
   // blocks run in launch order, so the heaviest samples start first (a longest-first schedule)
   const int b = P.order ? P.order[blockIdx.y] : blockIdx.y, tile = blockIdx.x;
@@ -482,11 +492,23 @@ conv_fused(ConvLaunch P) {
         if (nb > 0) tp = last_t;
         const int32_t nbw = min(nmax - b0, LPU);  // warp-uniform batch length
         uint32_t myvote = 0;  // the warp's spike ballot of this lane's step
+        if (PARK) {
+          __syncwarp();
+          park_w[lane] = make_int2(a, T);
+          __syncwarp();
+        }
         // 16-lane groups: the walk is unrolled so that the broadcasts and weight loads of later
         // steps are issued ahead of the dependent register updates
         auto walk = [&](int st) {
-          const int32_t as = __shfl_sync(0xffffffffu, a, st, LPU);
-          const int32_t Ts = __shfl_sync(0xffffffffu, T, st, LPU);
+          int32_t as, Ts;
+          if (PARK) {
+            const int2 at = park_w[st];
+            as = at.x;
+            Ts = at.y;
+          } else {
+            as = __shfl_sync(0xffffffffu, a, st, LPU);
+            Ts = __shfl_sync(0xffffffffu, T, st, LPU);
+          }
           bool spike = false;
           if (Ts >= 0 && lane_ok) {
             const int32_t qv = (int32_t)w_s[Ts + oc];
@@ -499,7 +521,11 @@ conv_fused(ConvLaunch P) {
             acc_max = max(acc_max, u);
           }
           const uint32_t vote = __ballot_sync(0xffffffffu, spike);
-          if (glane == st) myvote = vote;
+          if (PARK) {
+            if (lane == 0) vote_w[st] = vote;
+          } else if (glane == st) {
+            myvote = vote;
+          }
         };
         if (LPU <= 16) {
           if (nbw == LPU) {
@@ -513,6 +539,11 @@ conv_fused(ConvLaunch P) {
         } else {  // 32-lane groups: unrolling (by 8: +4 %, fully: +33 %) and a one-step
                   // software pipeline (+12 %) all measured slower than the plain loop
           for (int st = 0; st < nbw; ++st) walk(st);
+        }
+        if (PARK) {
+          __syncwarp();
+          myvote = vote_w[lane];
+          __syncwarp();
         }
         if (has) sw_s[widx] = (myvote >> (gi * LPU)) & gmask_bits;
         cn += max(nb, 0);

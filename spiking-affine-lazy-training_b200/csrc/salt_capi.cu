@@ -213,6 +213,7 @@ static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, cons
   L.ic = d->ic;
   L.k = d->k;
   L.ocp = p.ocp;
+  L.lpu = p.lpu;
   L.G = p.G;
   L.nslots = p.nslots;
   L.tile_h = tile_h;
