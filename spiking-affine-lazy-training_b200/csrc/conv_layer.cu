@@ -863,7 +863,7 @@ __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out) {
 // Samples with more spikes than max_out_spikes: keep the first M in neuron-major order
 // (jnp.nonzero(size=M) over the (neuron, column) grid, stream.py:60), then emit them in
 // (event, neuron) order.  One block per sample; only truncated samples do any work.
-__global__ void __launch_bounds__(kCompactThreads)
+__global__ void __launch_bounds__(kTruncThreads)
 conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_hist) {
   __shared__ int32_t s_scan[kScanSmem];
   __shared__ int32_t s_cut[8];
@@ -1030,6 +1030,7 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
       }
     }
     written += total;
+    if (written >= M) break;  // all M kept spikes are real ones and have been written
   }
   // 5. kept tail spikes (neurons before nstar, plus s_cut[3] of nstar), in neuron order
   if (P.tail_mode) {

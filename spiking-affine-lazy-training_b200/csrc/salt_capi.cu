@@ -417,7 +417,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
     SALT_LAUNCHED("conv_tail_append");
   }
-  conv_truncated<<<B, kCompactThreads, 0, st>>>(L, *out, s.hist);
+  conv_truncated<<<B, kTruncThreads, 0, st>>>(L, *out, s.hist);
   SALT_LAUNCHED("conv_truncated");
   FinishArgs fa{s.s_total, s.needed, s.vmin, s.vmax, s.ovf, d->max_queue_len, d->max_out_spikes,
                 d->max_extra_steps, 1, B, 1 << (q->i_V + q->f_V - 1)};
@@ -1066,7 +1066,7 @@ salt_status salt_float_conv_layer_forward(const salt_float_conv_desc* d, const f
   SALT_LAUNCHED("conv_compact");
   conv_tail_append<<<B, kCompactThreads, 0, st>>>(L, *out);
   SALT_LAUNCHED("conv_tail_append");
-  conv_truncated<<<B, kCompactThreads, 0, st>>>(L, *out, s.hist);
+  conv_truncated<<<B, kTruncThreads, 0, st>>>(L, *out, s.hist);
   SALT_LAUNCHED("conv_truncated");
   return SALT_OK;
 }

@@ -19,6 +19,9 @@ constexpr int kConvGroupShift = 5;
 constexpr int kConvGroup = 1 << kConvGroupShift;
 constexpr int kLutSmemMax = 4096;    // decay tables longer than this are read from global
 constexpr int kCompactBlocksPerSample = 8;  // compaction blocks per sample (grid-stride)
+// conv_truncated: one block per truncated sample walks all its events several times, so it runs
+// as wide as a block goes (each pass is latency-bound, 4x fewer rounds than 256 threads)
+constexpr int kTruncThreads = 1024;
 constexpr int kScanSmem = 33;        // ints of shared memory block_exclusive_scan needs
 
 __host__ __device__ __forceinline__ size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
