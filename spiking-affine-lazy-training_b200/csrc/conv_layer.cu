@@ -94,6 +94,16 @@ __device__ __forceinline__ void part_events(const ConvLaunch& P, int b, int ch, 
   }
 }
 
+// Tile rows and columns an event's valid candidates reach (an empty range for empty events).
+struct TileRange {
+  int32_t ty0, ty1, tx0, tx1;
+};
+__device__ __forceinline__ TileRange tile_range(const ConvLaunch& P, const EvCand& k) {
+  if (k.empty()) return TileRange{1, 0, 1, 0};
+  return TileRange{(int32_t)P.fd_th.div(k.oy_lo), (int32_t)P.fd_th.div(k.oy_hi),
+                   (int32_t)P.fd_tw.div(k.ox_lo), (int32_t)P.fd_tw.div(k.ox_hi)};
+}
+
 __global__ void __launch_bounds__(kPartThreads)
 conv_tile_count(ConvLaunch P, int32_t* __restrict__ counts) {
   extern __shared__ int32_t s_cnt[];
@@ -153,10 +163,12 @@ __global__ void conv_tile_scan_offsets(ConvLaunch P, int32_t* __restrict__ count
 
 __global__ void __launch_bounds__(kPartThreads)
 conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ counts, int32_t* __restrict__ lists) {
-  extern __shared__ uint32_t s_mask[];  // [T][kPartChunk/32] then word prefix [T][kPartChunk/32]
+  // [T][kPartChunk/32] masks, then the word prefix [T][kPartChunk/32], then the chunk's [T] bases
+  extern __shared__ uint32_t s_mask[];
   constexpr int W = kPartChunk / 32;
   static_assert(W == 32, "one warp scans one tile's words");
   uint32_t* s_pre = s_mask + P.T * W;
+  int32_t* s_base = reinterpret_cast<int32_t*>(s_pre + P.T * W);
   const int b = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
   const int32_t n_eff = P.n_eff(b), nch = part_chunks(P, b);
@@ -164,14 +176,18 @@ conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ counts, int32_t* __r
   for (int ch = blockIdx.x; ch < nch; ch += gridDim.x) {
     for (int i = threadIdx.x; i < P.T * W; i += blockDim.x) s_mask[i] = 0;
     __syncthreads();
-    EvCand k[kPartPer];  // kept in registers for the write pass
-    part_events(P, b, ch, n_eff, k);
+    TileRange r[kPartPer];  // kept in registers for the write pass
+    {
+      EvCand k[kPartPer];
+      part_events(P, b, ch, n_eff, k);
+#pragma unroll
+      for (int i = 0; i < kPartPer; ++i) r[i] = tile_range(P, k[i]);
+    }
 #pragma unroll
     for (int i = 0; i < kPartPer; ++i) {
-      if (k[i].empty()) continue;
       const int e = i * kPartThreads + (int)threadIdx.x;
-      for (int ty = (int)P.fd_th.div(k[i].oy_lo), ty1 = (int)P.fd_th.div(k[i].oy_hi); ty <= ty1; ++ty)
-        for (int tx = (int)P.fd_tw.div(k[i].ox_lo), tx1 = (int)P.fd_tw.div(k[i].ox_hi); tx <= tx1; ++tx)
+      for (int ty = r[i].ty0; ty <= r[i].ty1; ++ty)
+        for (int tx = r[i].tx0; tx <= r[i].tx1; ++tx)
           atomicOr(&s_mask[(ty * P.tiles_x + tx) * W + (e >> 5)], 1u << (e & 31));
     }
     __syncthreads();
@@ -185,18 +201,19 @@ conv_tile_scatter(ConvLaunch P, const int32_t* __restrict__ counts, int32_t* __r
       }
       s_pre[t * W + lane] = (uint32_t)(incl - v);
     }
+    for (int t = threadIdx.x; t < P.T; t += blockDim.x)
+      s_base[t] = counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t];
     __syncthreads();
 #pragma unroll
     for (int i = 0; i < kPartPer; ++i) {
-      if (k[i].empty()) continue;
       const int e = i * kPartThreads + (int)threadIdx.x;
       const int32_t jj = ch * kPartChunk + e;
-      for (int ty = (int)P.fd_th.div(k[i].oy_lo), ty1 = (int)P.fd_th.div(k[i].oy_hi); ty <= ty1; ++ty)
-        for (int tx = (int)P.fd_tw.div(k[i].ox_lo), tx1 = (int)P.fd_tw.div(k[i].ox_hi); tx <= tx1; ++tx) {
+      for (int ty = r[i].ty0; ty <= r[i].ty1; ++ty)
+        for (int tx = r[i].tx0; tx <= r[i].tx1; ++tx) {
           const int t = ty * P.tiles_x + tx;
           const uint32_t m = s_mask[t * W + (e >> 5)] & ((1u << (e & 31)) - 1u);
           const int32_t rank = (int32_t)(s_pre[t * W + (e >> 5)] + __popc(m));
-          list_b[counts[((int64_t)b * P.n_part_chunks + ch) * P.T + t] + rank] = jj;
+          list_b[s_base[t] + rank] = jj;
         }
     }
     __syncthreads();

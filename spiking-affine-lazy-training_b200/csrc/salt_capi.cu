@@ -274,6 +274,9 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
   p.n_part_chunks = (E + kPartChunk - 1) / kPartChunk;
   p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
+  if (p.T > 1 && conv_scatter_smem(p.T) > 227 * 1024)
+    return fail(SALT_BAD_ARG, "conv output plane too large: its tile partition needs more shared "
+                              "memory than a block has (at most 894 tiles)");
   p.smem = fused_smem(d, q, p, p.tile_h, p.tile_w, p.T);
   if (p.smem > 227 * 1024)
     return fail(SALT_BAD_ARG, "conv layer weights do not fit in shared memory (ic*k*k*oc too "
@@ -388,8 +391,11 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     conv_tile_scan_offsets<<<(B * 32 + 255) / 256, 256, 0, st>>>(L, s.counts, s.tile_len,
                                                                  s.tile_off);
     SALT_LAUNCHED("conv_tile_scan_offsets");
-    conv_tile_scatter<<<gp, kPartThreads, 2 * p.T * (kPartChunk / 32) * sizeof(uint32_t), st>>>(
-        L, s.counts, s.lists);
+    const size_t scatter_smem = conv_scatter_smem(p.T);
+    if (scatter_smem > 48 * 1024)
+      SALT_CUDA(cudaFuncSetAttribute((const void*)conv_tile_scatter,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scatter_smem));
+    conv_tile_scatter<<<gp, kPartThreads, scatter_smem, st>>>(L, s.counts, s.lists);
     SALT_LAUNCHED("conv_tile_scatter");
   }
   // without needs_tail every decay code lies in [0, 2^f_a): the one-multiply decay form is exact

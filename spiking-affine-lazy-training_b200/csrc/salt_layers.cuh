@@ -244,6 +244,11 @@ __global__ void fc_truncated(FCLaunch P, salt_stream_out out);
 // Kernel entry points of the templated kernels, for cudaLaunchKernel.  wide: decay products in
 // the one-multiply 64-bit form, exact when every decay code lies in [0, 2^f_a] (no needs_tail).
 void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate, bool wide);
+// Dynamic shared memory of conv_tile_scatter: per tile a mask and a word prefix per
+// 1024-event chunk, plus the chunk's list base.
+inline size_t conv_scatter_smem(int T) {
+  return (size_t)T * (2 * (kPartChunk / 32) * sizeof(uint32_t) + sizeof(int32_t));
+}
 // Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 // lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons;

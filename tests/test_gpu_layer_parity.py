@@ -98,6 +98,17 @@ def test_conv_output_truncation_two_channel_groups_several_tiles(M):
     assert np.any(out.stream.n_real_events > M)
 
 
+def test_conv_many_tiles():
+    """A 64x240 output plane: 240 tiles of 16x4 positions, whose partition needs more than the
+    default 48 KB of shared memory per block."""
+    rng = np.random.default_rng(27)
+    layer = S.ConvLayer(name="c", ic=1, h_in=64, w_in=240, oc=4, k=3, s=1, p=1, init_k=1.0,
+                        tau=8.0, max_queue_len=64, max_out_spikes=3000)
+    params = make_params(layer, rng, vth=(5, 30), f_a=6)
+    times, src, nr = make_events(rng, 2, 1500, 64 * 240, t_max=200)
+    _check_layer(layer, params, times, src, nr)
+
+
 @pytest.mark.parametrize("vth", [(-20, 0), (-5, 5)])
 def test_conv_tail_columns_fire_when_threshold_not_positive(vth):
     rng = np.random.default_rng(30)

@@ -77,6 +77,15 @@ def test_bad_arguments_are_reported_before_any_device_work():
     f = _lib.FCDesc(0, 10, 1, 0)
     assert lib.salt_fc_layer_workspace_size(_lib.byref(f), _lib.byref(q), 4, 1000,
                                             _lib.byref(n)) == _lib.SALT_BAD_ARG
+    # the tile partition holds per-tile masks in one block's shared memory: a 226x226 output
+    # plane (15 x 57 = 855 tiles of 16 x 4) fits, a 3999x3999 one is refused before any launch
+    big_ok = _lib.ConvDesc(1, 453, 453, 16, 3, 2, 0, 64, 100, 0)
+    assert lib.salt_conv_layer_workspace_size(_lib.byref(big_ok), _lib.byref(q), 1, 1000,
+                                              _lib.byref(n)) == _lib.SALT_OK
+    too_big = _lib.ConvDesc(1, 8000, 8000, 16, 3, 2, 0, 64, 100, 0)
+    assert lib.salt_conv_layer_workspace_size(_lib.byref(too_big), _lib.byref(q), 1, 1000,
+                                              _lib.byref(n)) == _lib.SALT_BAD_ARG
+    assert b"tile" in lib.salt_last_error()
 
 
 def test_float_conv_arguments_are_checked_on_the_host():
