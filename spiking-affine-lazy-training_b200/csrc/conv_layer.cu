@@ -735,14 +735,40 @@ __device__ __forceinline__ void rank_in_words(uint32_t w0, uint32_t w1, uint32_t
 // on one another (no shared memory, no block barrier).  FOUR: at most 2 candidates per axis and
 // one channel group (the benchmark geometries): the event's four slot words stay in registers
 // and the decode is bit arithmetic on them (rank_in_words); otherwise the words are re-read.
+// Spikes per channel of a truncated sample (its spike words over the valid candidate slots),
+// added into the sample's zeroed oc_total row by all of the sample's compaction blocks; the
+// catch-up/identity spikes are added by conv_truncated, which then places the channel cut.
+__device__ __forceinline__ void count_channels(const ConvLaunch& P, int b) {
+  const int32_t n_eff = P.n_eff(b);
+  const int SWW = P.nslots * P.G;
+  int32_t* oct = P.oc_total + (int64_t)b * P.oc;
+  for (int32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < n_eff; j += gridDim.x * blockDim.x) {
+    int32_t cc, y, x;
+    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
+    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
+    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
+      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
+        for (int g = 0; g < P.G; ++g) {
+          uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
+          while (wd) {
+            atomicAdd(&oct[g * P.lpu + __ffs(wd) - 1], 1);
+            wd &= wd - 1u;
+          }
+        }
+  }
+}
+
 template <bool FOUR>
-__global__ void __launch_bounds__(kCompactThreads)
+__global__ void __launch_bounds__(kCompactThreads, 6)
 conv_compact(ConvLaunch P, salt_stream_out out) {
   constexpr uint32_t kAll = 0xffffffffu;
   const int b = P.order ? P.order[blockIdx.y] : blockIdx.y;  // heaviest samples first
   const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
   const int32_t S = P.s_total[b];
-  if (S > P.M) return;  // truncated samples go through conv_truncated
+  if (S > P.M) {  // truncated samples are emitted by conv_truncated; count their channels for it
+    count_channels(P, b);
+    return;
+  }
   const int32_t n_eff = P.n_eff(b);
   const int SWW = P.nslots * P.G;
   const uint32_t* sw_b = P.sw + (int64_t)b * P.sw_stride;
@@ -890,24 +916,10 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   const int32_t n_eff = P.n_eff(b);
   const int SWW = P.nslots * P.G;
   int32_t* hist = scratch_hist + (int64_t)b * P.n_sp * 2;  // [n_sp] real, [n_sp] tail
-  // 1. spikes per channel (spike words of the valid candidate slots, then catch-up/identity
-  // spikes) into the zeroed oc_total row, and the channel cut: the channel holding the M-th
-  // spike in neuron-major order
+  // 1. spikes per channel: conv_compact counted the spike words into the oc_total row; the
+  // catch-up/identity spikes are added here.  Then the channel cut: the channel holding the
+  // M-th spike in neuron-major order
   int32_t* oct = P.oc_total + (int64_t)b * P.oc;
-  for (int32_t j = tid; j < n_eff; j += blockDim.x) {
-    int32_t cc, y, x;
-    const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
-    const uint32_t* sw_j = P.sw + (int64_t)b * P.sw_stride + (int64_t)j * SWW;
-    for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
-      for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox)
-        for (int g = 0; g < P.G; ++g) {
-          uint32_t wd = sw_j[((oy - k.oy_min) * P.ncand + (ox - k.ox_min)) * P.G + g];
-          while (wd) {
-            atomicAdd(&oct[g * P.lpu + __ffs(wd) - 1], 1);
-            wd &= wd - 1u;
-          }
-        }
-  }
   if (P.tail_mode)
     for (int64_t n = tid; n < P.n_neurons; n += blockDim.x) {
       const int32_t c = P.tail_cnt[(int64_t)b * P.n_neurons + n];
