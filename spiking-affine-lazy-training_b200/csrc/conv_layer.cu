@@ -373,8 +373,8 @@ conv_fused(ConvLaunch P) {
       if (P.ncand == 2) {
         // 2x2 windows: one match per event.  Lanes whose windows start at the same position with
         // the same valid slots share all their candidate positions, so the group's first lane
-        // sets the group's bits in every one of them (tile sides are at most 64 positions, so
-        // the tile-local origin, offset by 2, fits in 7 bits per axis).
+        // sets the group's bits in every one of them (a tile holds at most 256 positions, so
+        // the tile-local origin, offset by 2, fits in 9 bits per axis).
         uint32_t vb = 0;
         if (in) {
           const bool y0 = k.oy_min >= k.oy_lo && k.oy_min <= k.oy_hi;
@@ -385,7 +385,7 @@ conv_fused(ConvLaunch P) {
                ((uint32_t)(y1 && x1) << 3);
         }
         const int ly = k.oy_min - oy0, lx = k.ox_min - ox0;
-        const int32_t key = vb ? (((ly + 2) << 11) | ((lx + 2) << 4) | (int32_t)vb) : -1;
+        const int32_t key = vb ? (((ly + 2) << 13) | ((lx + 2) << 4) | (int32_t)vb) : -1;
         const uint32_t same = __match_any_sync(0xffffffffu, key);
         if (vb && (__ffs(same) - 1) == lane) {
           const int i0 = (ly * P.tile_w + lx) * CHW + wrd;  // slot (0, 0); used only if valid

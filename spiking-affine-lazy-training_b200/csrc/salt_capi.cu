@@ -253,9 +253,13 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   // Positions per block: at most 64 (fewer positions per block means more of each position's
   // events per 512-event chunk, so the per-position setup of the recurrence is shared by more
   // events, and more, smaller blocks), within a ~100 KB shared-memory budget, never fewer than
-  // one candidate window.  Measured against 256: configuration 3 1.07x, 2 1.86x, 4 1.48x.
+  // one candidate window.  Measured against 256: configuration 3 1.07x, 2 1.86x, 4 1.48x; 32
+  // and 128 were slower on configuration 3 too.  A layer whose input capacity is below its
+  // position count has few events per position whatever the tiling, and its blocks' fixed work
+  // (weight staging, register init, catch-up) dominates: it takes tiles of up to 256 positions
+  // (configuration 4's conv2, 36 events over 1024 positions: 0.50 -> 0.36 ms at 128).
   const size_t budget = 100 * 1024;
-  int npm_cap = 64;
+  int npm_cap = E < p.n_sp ? 256 : 64;
   while (npm_cap > 1 && fused_smem(d, q, p, 1, npm_cap, 2) > budget) npm_cap >>= 1;
   if (p.n_sp <= npm_cap) {
     p.tile_h = p.h_out;

@@ -99,13 +99,26 @@ def test_conv_output_truncation_two_channel_groups_several_tiles(M):
 
 
 def test_conv_many_tiles():
-    """A 64x240 output plane: 240 tiles of 16x4 positions, whose partition needs more than the
-    default 48 KB of shared memory per block."""
+    """A 64x200 output plane with rows of 13000 events (no fewer than its 12800 positions, so
+    64-position tiles): 208 tiles of 16x4 positions, whose partition needs more than the default
+    48 KB of shared memory per block."""
     rng = np.random.default_rng(27)
-    layer = S.ConvLayer(name="c", ic=1, h_in=64, w_in=240, oc=4, k=3, s=1, p=1, init_k=1.0,
-                        tau=8.0, max_queue_len=64, max_out_spikes=3000)
+    layer = S.ConvLayer(name="c", ic=1, h_in=64, w_in=200, oc=4, k=3, s=1, p=1, init_k=1.0,
+                        tau=8.0, max_queue_len=64, max_out_spikes=20000)
     params = make_params(layer, rng, vth=(5, 30), f_a=6)
-    times, src, nr = make_events(rng, 2, 1500, 64 * 240, t_max=200)
+    times, src, nr = make_events(rng, 2, 13000, 64 * 200, t_max=2000)
+    _check_layer(layer, params, times, src, nr)
+
+
+@pytest.mark.parametrize("ic,h,w", [(8, 64, 64), (2, 1, 400)])
+def test_conv_sparse_input_takes_large_tiles(ic, h, w):
+    """Input rows shorter than the output plane: the layer is planned with tiles of up to 256
+    positions (32x32 plane: four 16x16 tiles; 1x200 plane: one tile 200 positions wide)."""
+    rng = np.random.default_rng(28 + h)
+    layer = S.ConvLayer(name="c", ic=ic, h_in=h, w_in=w, oc=24, k=3, s=2, p=1, init_k=1.0,
+                        tau=8.0, max_queue_len=16, max_out_spikes=400)
+    params = make_params(layer, rng, vth=(3, 20), f_a=6)
+    times, src, nr = make_events(rng, 6, 40, ic * h * w, t_max=100)
     _check_layer(layer, params, times, src, nr)
 
 
