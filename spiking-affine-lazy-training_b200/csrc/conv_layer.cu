@@ -262,7 +262,7 @@ size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes) {
   return FusedSmem(P, wt_bytes).total;
 }
 
-template <typename WT, int LPU, bool SAT, bool WIDE>
+template <typename WT, int LPU, bool SAT, int FORM>
 __global__ void __launch_bounds__(kFusedThreads)
 conv_fused(ConvLaunch P) {
   constexpr int UPW = 32 / LPU;  // units (position x channel group) per warp
@@ -530,7 +530,7 @@ conv_fused(ConvLaunch P) {
           if (Ts >= 0 && lane_ok) {
             const int32_t qv = (int32_t)w_s[Ts + oc];
             int32_t u;
-            const int32_t w = sc.step<SAT, WIDE>(V, as, qv, u);
+            const int32_t w = sc.step<SAT, FORM != kStepSplit, FORM != kStepWideNoFit>(V, as, qv, u);
             spike = w >= vth;
             V = spike ? 0 : w;
             // overflow is read off the unfitted range at the end of the layer (layer_finish)
@@ -1081,31 +1081,34 @@ conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* __restrict__ scratch_
   }
 }
 
-// Host-side dispatch over the (weight width, lanes per channel group, overflow mode, decay
-// product form) instantiations.
-template <typename WT, bool SAT, bool WIDE>
+// Host-side dispatch over the (weight width, lanes per channel group, overflow mode, step form)
+// instantiations; the no-fit form ignores the overflow mode.
+template <typename WT, bool SAT, int FORM>
 static void* fused_for_lpu(int lpu) {
   switch (lpu) {
-    case 1: return (void*)conv_fused<WT, 1, SAT, WIDE>;
-    case 2: return (void*)conv_fused<WT, 2, SAT, WIDE>;
-    case 4: return (void*)conv_fused<WT, 4, SAT, WIDE>;
-    case 8: return (void*)conv_fused<WT, 8, SAT, WIDE>;
-    case 16: return (void*)conv_fused<WT, 16, SAT, WIDE>;
-    default: return (void*)conv_fused<WT, 32, SAT, WIDE>;
+    case 1: return (void*)conv_fused<WT, 1, SAT, FORM>;
+    case 2: return (void*)conv_fused<WT, 2, SAT, FORM>;
+    case 4: return (void*)conv_fused<WT, 4, SAT, FORM>;
+    case 8: return (void*)conv_fused<WT, 8, SAT, FORM>;
+    case 16: return (void*)conv_fused<WT, 16, SAT, FORM>;
+    default: return (void*)conv_fused<WT, 32, SAT, FORM>;
   }
 }
 
-template <bool SAT, bool WIDE>
+template <bool SAT, int FORM>
 static void* fused_for_wt(int wt_bytes, int lpu) {
-  if (wt_bytes == 1) return fused_for_lpu<int8_t, SAT, WIDE>(lpu);
-  if (wt_bytes == 2) return fused_for_lpu<int16_t, SAT, WIDE>(lpu);
-  return fused_for_lpu<int32_t, SAT, WIDE>(lpu);
+  if (wt_bytes == 1) return fused_for_lpu<int8_t, SAT, FORM>(lpu);
+  if (wt_bytes == 2) return fused_for_lpu<int16_t, SAT, FORM>(lpu);
+  return fused_for_lpu<int32_t, SAT, FORM>(lpu);
 }
 
-void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate, bool wide) {
+void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate, int form) {
+  if (form == kStepWideNoFit) return fused_for_wt<false, kStepWideNoFit>(wt_bytes, lpu);
   if (saturate)
-    return wide ? fused_for_wt<true, true>(wt_bytes, lpu) : fused_for_wt<true, false>(wt_bytes, lpu);
-  return wide ? fused_for_wt<false, true>(wt_bytes, lpu) : fused_for_wt<false, false>(wt_bytes, lpu);
+    return form == kStepWide ? fused_for_wt<true, kStepWide>(wt_bytes, lpu)
+                             : fused_for_wt<true, kStepSplit>(wt_bytes, lpu);
+  return form == kStepWide ? fused_for_wt<false, kStepWide>(wt_bytes, lpu)
+                           : fused_for_wt<false, kStepSplit>(wt_bytes, lpu);
 }
 
 }  // namespace salt

@@ -56,7 +56,7 @@ size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lp
 // the group then reads with one broadcast load per step.  With WT > 0 the weight codes sit in
 // shared memory as WT-byte integers with a zero row that masked entries (pads, events past the
 // group's end) point at, so a step needs no predicate: past the end it is the identity.
-template <bool FIRES, bool SAT, int LPU, int WT, bool WIDE>
+template <bool FIRES, bool SAT, int LPU, int WT, int FORM>
 __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   using QT = typename CodeType<WT>::T;
   constexpr int SPW = 32 / LPU;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
       if (WT) qv = (int32_t)q_s[ev.y + gl];
       else qv = (ev.y >= 0 && active) ? __ldg(&P.qT[ev.y + gl]) : 0;
       int32_t u;
-      const int32_t w = sc.step<SAT, WIDE>(V, ev.x, qv, u);
+      const int32_t w = sc.step<SAT, FORM != kStepSplit, FORM != kStepWideNoFit>(V, ev.x, qv, u);
       vmin = min(vmin, u);
       vmax = max(vmax, u);
       if (FIRES) {
@@ -336,35 +336,39 @@ fc_truncated(FCLaunch P, salt_stream_out out) {
   }
 }
 
-template <int LPU, int WT, bool WIDE>
+template <int LPU, int WT, int FORM>
 static void* fc_scan_for(bool fires, bool saturate) {
+  if (FORM == kStepWideNoFit)  // the overflow mode does not matter
+    return fires ? (void*)fc_scan<true, false, LPU, WT, FORM>
+                 : (void*)fc_scan<false, false, LPU, WT, FORM>;
   if (saturate)
-    return fires ? (void*)fc_scan<true, true, LPU, WT, WIDE>
-                 : (void*)fc_scan<false, true, LPU, WT, WIDE>;
-  return fires ? (void*)fc_scan<true, false, LPU, WT, WIDE>
-               : (void*)fc_scan<false, false, LPU, WT, WIDE>;
+    return fires ? (void*)fc_scan<true, true, LPU, WT, FORM>
+                 : (void*)fc_scan<false, true, LPU, WT, FORM>;
+  return fires ? (void*)fc_scan<true, false, LPU, WT, FORM>
+               : (void*)fc_scan<false, false, LPU, WT, FORM>;
 }
 
-template <int WT, bool WIDE>
+template <int WT, int FORM>
 static void* fc_scan_lpu(bool fires, bool saturate, int lpu) {
-  if (lpu == 8) return fc_scan_for<8, WT, WIDE>(fires, saturate);
-  if (lpu == 16) return fc_scan_for<16, WT, WIDE>(fires, saturate);
-  return fc_scan_for<32, WT, WIDE>(fires, saturate);
+  if (lpu == 8) return fc_scan_for<8, WT, FORM>(fires, saturate);
+  if (lpu == 16) return fc_scan_for<16, WT, FORM>(fires, saturate);
+  return fc_scan_for<32, WT, FORM>(fires, saturate);
 }
 
-template <bool WIDE>
+template <int FORM>
 static void* fc_scan_wt(bool fires, bool saturate, int lpu, int wt) {
   switch (wt) {
-    case 1: return fc_scan_lpu<1, WIDE>(fires, saturate, lpu);
-    case 2: return fc_scan_lpu<2, WIDE>(fires, saturate, lpu);
-    case 4: return fc_scan_lpu<4, WIDE>(fires, saturate, lpu);
-    default: return fc_scan_lpu<0, WIDE>(fires, saturate, lpu);
+    case 1: return fc_scan_lpu<1, FORM>(fires, saturate, lpu);
+    case 2: return fc_scan_lpu<2, FORM>(fires, saturate, lpu);
+    case 4: return fc_scan_lpu<4, FORM>(fires, saturate, lpu);
+    default: return fc_scan_lpu<0, FORM>(fires, saturate, lpu);
   }
 }
 
-void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt, bool wide) {
-  return wide ? fc_scan_wt<true>(fires, saturate, lpu, wt)
-              : fc_scan_wt<false>(fires, saturate, lpu, wt);
+void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt, int form) {
+  if (form == kStepWideNoFit) return fc_scan_wt<kStepWideNoFit>(fires, saturate, lpu, wt);
+  return form == kStepWide ? fc_scan_wt<kStepWide>(fires, saturate, lpu, wt)
+                           : fc_scan_wt<kStepSplit>(fires, saturate, lpu, wt);
 }
 
 }  // namespace salt

@@ -224,6 +224,17 @@ static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, cons
   return conv_fused_smem_bytes(L, p.wt_bytes);
 }
 
+// Step form of a layer's hot loop (salt_common.cuh).  Without needs_tail every decay code lies
+// in [0, 2^f_a]: the one-multiply product is exact, and a decay never grows |v|, so a neuron that
+// sees at most max_steps weighted steps with |q| <= 2^(q_bits - 1) stays inside its register
+// range when max_steps < 2^(i_V - q_bits), and the fit can be left out.
+static int step_form(const salt_quant_desc* q, int64_t max_steps) {
+  if (q->needs_tail) return kStepSplit;
+  const int headroom = q->i_V - q->q_bits;
+  if (headroom > 0 && headroom < 62 && max_steps < (int64_t(1) << headroom)) return kStepWideNoFit;
+  return kStepWide;
+}
+
 static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, int32_t batch,
                              int32_t E, ConvPlan& p) {
   if (!d) return fail(SALT_BAD_ARG, "conv descriptor is NULL");
@@ -402,9 +413,9 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     conv_tile_scatter<<<gp, kPartThreads, scatter_smem, st>>>(L, s.counts, s.lists);
     SALT_LAUNCHED("conv_tile_scatter");
   }
-  // without needs_tail every decay code lies in [0, 2^f_a): the one-multiply decay form is exact
+  // a neuron sees at most max_queue_len weighted steps
   void* fn = conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE,
-                               q->needs_tail == 0);
+                               step_form(q, d->max_queue_len));
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
   void* args[] = {&L};
   if (timer) SALT_CUDA(cudaEventRecord(timer->start, st));
@@ -529,8 +540,9 @@ static salt_status fc_forward_impl(const salt_fc_desc* d, const salt_quant_desc*
   const int64_t warps = ((int64_t)B + 32 / lpu - 1) / (32 / lpu);
   const int wpb = kFcThreads / 32;
   const dim3 grid((unsigned)((warps + wpb - 1) / wpb), (unsigned)L.G);
+  // a neuron sees at most one weighted step per input entry
   void* scan_fn = fc_scan_kernel(q->has_vth != 0, q->overflow_mode == SALT_SATURATE, lpu, wt,
-                                 q->needs_tail == 0);
+                                 step_form(q, E));
   if (smem > 48 * 1024)
     SALT_CUDA(cudaFuncSetAttribute(scan_fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   void* scan_args[] = {&L};

@@ -77,7 +77,13 @@ __device__ __forceinline__ int32_t quant_step(int32_t v, int32_t a, bool is_iden
 // two agree modulo 2^32 whenever the reference's int32 term a * lo + round_half does not wrap.
 // That holds for every decay code in [0, 2^f_a] with f_a <= 15 (a * lo + half < 2^30), which is
 // what a layer without needs_tail guarantees; other tables take the split form.
-template <bool SAT, bool WIDE = false>
+//
+// Without FIT the fitted value is the unfitted one.  That is exact when the host has shown that
+// no register can leave its range: with decay codes in [0, 2^f_a] a decay never grows |v|
+// (floor((a*v + half) / 2^f_a) lies between 0 and v), so after n weighted steps
+// |v| <= n * max|q| * 2^f_V, and n * 2^(q_bits - 1) < 2^(i_V - 1) keeps every value inside
+// [-2^(i_V + f_V - 1), 2^(i_V + f_V - 1)), where wrap and saturate are both the identity.
+template <bool SAT, bool WIDE = false, bool FIT = true>
 __device__ __forceinline__ int32_t quant_step_a(int32_t v, int32_t a, int32_t q_shifted,
                                                 int32_t f_a, int32_t lo_mask, int32_t round_half,
                                                 int32_t half, int32_t wrap_shift, int32_t& u) {
@@ -87,6 +93,7 @@ __device__ __forceinline__ int32_t quant_step_a(int32_t v, int32_t a, int32_t q_
   else
     dec = wadd(wmul(a, v >> f_a), wadd(wmul(a, v & lo_mask), round_half) >> f_a);
   u = wadd(dec, q_shifted);
+  if (!FIT) return u;
   if (SAT) return min(max(u, -half), half - 1);
   return (int32_t)((uint32_t)u << wrap_shift) >> wrap_shift;
 }
@@ -98,12 +105,17 @@ struct StepConsts {
       : f_a(c.f_a), f_V(c.f_V), lo_mask((int32_t)((1u << c.f_a) - 1u)), round_half(c.round_half),
         half((int32_t)(1u << (c.total_bits - 1))), wrap_shift(32 - c.total_bits),
         ident_a((int32_t)(1u << c.f_a)) {}
-  template <bool SAT, bool WIDE = false>
+  template <bool SAT, bool WIDE = false, bool FIT = true>
   __device__ __forceinline__ int32_t step(int32_t v, int32_t a, int32_t q, int32_t& u) const {
-    return quant_step_a<SAT, WIDE>(v, a, wmul(q, (int32_t)(1u << f_V)), f_a, lo_mask, round_half,
-                                   half, wrap_shift, u);
+    return quant_step_a<SAT, WIDE, FIT>(v, a, wmul(q, (int32_t)(1u << f_V)), f_a, lo_mask,
+                                        round_half, half, wrap_shift, u);
   }
 };
+
+// Step forms of the hot loops, chosen per layer on the host (step_form): the reference's split
+// product; one 64-bit product (every decay code in [0, 2^f_a]); one 64-bit product and no fit
+// (no register can leave its range either).
+constexpr int kStepSplit = 0, kStepWide = 1, kStepWideNoFit = 2;
 
 // apply_decay_table_int (salt_core/quant/codes.py:87-105) on an integer Δt.
 __device__ __forceinline__ int32_t decay_code(int32_t dt, const int32_t* lut, int32_t lut_len) {

@@ -241,9 +241,9 @@ __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out);
 __global__ void conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* scratch_hist);
 __global__ void fc_compact(FCLaunch P, salt_stream_out out);
 __global__ void fc_truncated(FCLaunch P, salt_stream_out out);
-// Kernel entry points of the templated kernels, for cudaLaunchKernel.  wide: decay products in
-// the one-multiply 64-bit form, exact when every decay code lies in [0, 2^f_a] (no needs_tail).
-void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate, bool wide);
+// Kernel entry points of the templated kernels, for cudaLaunchKernel.  form: kStepSplit,
+// kStepWide or kStepWideNoFit (salt_common.cuh), as step_form chooses it for the layer.
+void* conv_fused_kernel(int wt_bytes, int lpu, bool saturate, int form);
 // Dynamic shared memory of conv_tile_scatter: per tile a mask and a word prefix per
 // 1024-event chunk, plus the chunk's list base.
 inline size_t conv_scatter_smem(int T) {
@@ -253,7 +253,7 @@ inline size_t conv_scatter_smem(int T) {
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 // lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons;
 // wt: bytes per weight code staged in shared memory (1, 2, 4), 0 to read them from global.
-void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt, bool wide);
+void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt, int form);
 // Dynamic shared memory of fc_scan for these sizes.
 size_t fc_scan_smem(int32_t n_in, int32_t n_out, int32_t lut_len, int wt, int lpu);
 // Bytes of the weight table fc_scan stages in shared memory (0 when wt == 0).
