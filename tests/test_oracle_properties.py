@@ -47,6 +47,35 @@ def test_split_decay_equals_one_wide_product_for_in_range_codes():
     assert _wrap32(_wrap32(a * (v >> f_a)) + (_wrap32(a * lo) >> f_a)) != _wrap32((a * v) >> f_a)
 
 
+def test_register_stays_in_range_when_steps_are_below_the_headroom():
+    """The kernels leave the register fit out when every decay code lies in [0, 2^f_a] and a
+    neuron sees fewer than 2^(i_V - q_bits) weighted steps: the unfitted value after n steps is
+    within n * 2^(q_bits - 1) * 2^f_V, below half the register range.  Checked on the
+    reference's integer update (split product, int32 wrap) with worst-case weights."""
+    rng = np.random.default_rng(12)
+    for f_a, f_V, i_V, q_bits in [(10, 0, 24, 8), (6, 2, 20, 8), (15, 0, 30, 16), (8, 3, 14, 4)]:
+        half = 1 << (i_V + f_V - 1)
+        n = (1 << (i_V - q_bits)) - 1
+        qmax = 1 << (q_bits - 1)
+        for trial in range(3):
+            a = rng.integers(0, (1 << f_a) + 1, n).astype(np.int64)
+            a[rng.random(n) < 0.3] = 1 << f_a                  # identity steps (dt = 0)
+            sign = 1 if trial == 0 else (-1 if trial == 1 else None)
+            q = (np.full(n, sign * qmax) if sign else
+                 rng.choice([-qmax, qmax - 1], n)).astype(np.int64)
+            v, peak = 0, 0
+            rh = 1 << (f_a - 1) if f_a else 0
+            for k in range(n):
+                lo = v & ((1 << f_a) - 1)
+                dec = int(_wrap32(_wrap32(a[k] * (v >> f_a)) + (_wrap32(a[k] * lo + rh) >> f_a)))
+                u = int(_wrap32(dec + (int(q[k]) << f_V)))
+                assert abs(u) <= (k + 1) * qmax * (1 << f_V)
+                assert -half <= u < half
+                peak = max(peak, abs(u))
+                v = u                                             # no fit needed
+            assert peak < half
+
+
 def test_decay_step_never_grows_magnitude():
     """salt_core/tests/test_fixed_point.py:49-58"""
     rng = np.random.default_rng(0)
