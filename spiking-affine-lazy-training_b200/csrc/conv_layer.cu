@@ -237,7 +237,8 @@ struct FusedSmem {
   __host__ __device__ FusedSmem(const ConvLaunch& P, int wt_bytes) {
     const size_t npm = (size_t)P.tile_h * P.tile_w;
     size_t o = 0;
-    w = o;     o += align16((size_t)P.ic * P.k * P.k * P.ocp * wt_bytes);
+    // weights [ic*k*k][ocp], then one zero row (the padding steps of the no-fit walk)
+    w = o;     o += align16((size_t)(P.ic * P.k * P.k + 1) * P.ocp * wt_bytes);
     lut = o;   o += align16((size_t)(P.lut_in_smem ? P.qc.lut_len : 0) * 4);
     v = o;     o += align16(npm * P.ocp * 4);
     tprev = o; o += align16(npm * P.G * 4);   // one copy per (position, channel group)
@@ -303,9 +304,10 @@ conv_fused(ConvLaunch P) {
   const int oy0 = ty * P.tile_h, ox0 = tx * P.tile_w;
   const int th = min(P.tile_h, P.h_out - oy0), tw = min(P.tile_w, P.w_out - ox0);
 
-  for (int i = tid; i < P.ic * KK * OCP; i += blockDim.x) {
+  const int zero_row = P.ic * KK * OCP;
+  for (int i = tid; i < zero_row + OCP; i += blockDim.x) {
     const int tap = i / OCP, oc = i - tap * OCP;
-    w_s[i] = oc < P.oc ? (WT)P.q[(int64_t)oc * P.ic * KK + tap] : (WT)0;
+    w_s[i] = (oc < P.oc && i < zero_row) ? (WT)P.q[(int64_t)oc * P.ic * KK + tap] : (WT)0;
   }
   if (P.lut_in_smem)
     for (int i = tid; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
@@ -495,12 +497,16 @@ conv_fused(ConvLaunch P) {
         if (glane == 0) tpv = tp;
         const bool kept = has && (cn + glane) < P.L;  // cn already counts earlier batches
         const int32_t dt = dt_from_times(r.t, tpv);
-        const int32_t a = dt == 0 ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
         const int32_t ky = (int32_t)(r.yx >> 16) - oys;
         const int32_t kx = (int32_t)(r.yx & 0xffffu) - oxs;
-        // weight row offset of the event's tap; -1 marks lanes without a kept event (their
-        // placeholder record may give a negative tap)
-        const int32_t T = kept ? (r.ckk + ky * P.k + kx) * OCP : -1;
+        // weight row offset of the event's tap; lanes without a kept event (their placeholder
+        // record may give a negative tap) get -1, or in the no-fit form an identity step on the
+        // zero row: there it changes nothing (V stays, already inside the tracked range, and
+        // below every threshold, all positive without needs_tail), so the walk needs no guard
+        constexpr bool kPadIdentity = FORM == kStepWideNoFit && LPU <= 16;  // 32 lanes: +16 regs
+        const int32_t a = (dt == 0 || (kPadIdentity && !kept))
+                              ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
+        const int32_t T = kept ? (r.ckk + ky * P.k + kx) * OCP : (kPadIdentity ? zero_row : -1);
         const int sy = oy - ((int32_t)(r.omin >> 16) - 32768);
         const int sx = ox - ((int32_t)(r.omin & 0xffffu) - 32768);
         const int widx = e * SWW + (sy * P.ncand + sx) * P.G + g;
@@ -527,7 +533,7 @@ conv_fused(ConvLaunch P) {
             Ts = __shfl_sync(0xffffffffu, T, st, LPU);
           }
           bool spike = false;
-          if (Ts >= 0 && lane_ok) {
+          if (kPadIdentity || (Ts >= 0 && lane_ok)) {
             const int32_t qv = (int32_t)w_s[Ts + oc];
             int32_t u;
             const int32_t w = sc.step<SAT, FORM != kStepSplit, FORM != kStepWideNoFit>(V, as, qv, u);
