@@ -263,8 +263,14 @@ size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes) {
   return FusedSmem(P, wt_bytes).total;
 }
 
+// The 32-lane no-fit walk is held to 5 blocks per SM (48 registers; as many blocks as its shared
+// memory allows at the benchmark sizes), which it would otherwise trade for registers; the other
+// variants keep the compiler's choice (a minimum of 0 blocks sets no bound).
+template <int LPU, int FORM>
+constexpr int fused_min_blocks() { return (LPU == 32 && FORM == kStepWideNoFit) ? 5 : 0; }
+
 template <typename WT, int LPU, bool SAT, int FORM>
-__global__ void __launch_bounds__(kFusedThreads)
+__global__ void __launch_bounds__(kFusedThreads, fused_min_blocks<LPU, FORM>())
 conv_fused(ConvLaunch P) {
   constexpr int UPW = 32 / LPU;  // units (position x channel group) per warp
   constexpr int CHW = kFusedChunk / 32;
@@ -503,7 +509,7 @@ conv_fused(ConvLaunch P) {
         // record may give a negative tap) get -1, or in the no-fit form an identity step on the
         // zero row: there it changes nothing (V stays, already inside the tracked range, and
         // below every threshold, all positive without needs_tail), so the walk needs no guard
-        constexpr bool kPadIdentity = FORM == kStepWideNoFit && LPU <= 16;  // 32 lanes: +16 regs
+        constexpr bool kPadIdentity = FORM == kStepWideNoFit;
         const int32_t a = (dt == 0 || (kPadIdentity && !kept))
                               ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
         const int32_t T = kept ? (r.ckk + ky * P.k + kx) * OCP : (kPadIdentity ? zero_row : -1);
