@@ -7,7 +7,9 @@ One step = one batched forward of the whole network (every conv/FC layer, spike 
 diagnostics and fits) over one batch of synthetic input resident in HBM, plus the NCCL
 all-gather of the int32 logits when N > 1.  Metric: input events/s over all ranks.  Prints one
 JSON line on rank 0.  The default workload is configuration 3 of the benchmark (the conv network
-on 4096 blob samples, the configuration quoted at 1/2/4/8 GPUs); --config selects another.
+on 4096 blob samples, the configuration quoted at 1/2/4/8 GPUs), as one batch sharded across the
+ranks (strong scaling); --config selects another (run as replicas, one batch per rank).  Every
+arm uses the fixed capacities of workloads.CAPACITY_TABLE.
 --config 5 measures the float FC layer (4096->4096, one stream of 10^6 events, chunk 4096): one
 step = one layer forward; N > 1 runs one independent stream per rank (weak scaling, no
 collective on the data path).
@@ -40,7 +42,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--config", type=int, default=3, choices=[1, 2, 3, 4, 5])
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default=None,
+                    help="default: strong for configuration 3 (one batch sharded across the "
+                         "ranks), weak (replicas) otherwise")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-rank batch (profiling on a small case)")
@@ -50,7 +54,10 @@ def parse():
                          "times then come from an eager profiled pass after the timed region")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target duration of the bounded CPU-baseline sample")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.scaling is None:
+        args.scaling = default_scaling(args.config)
+    return args
 
 
 def rank_info():
@@ -58,29 +65,39 @@ def rank_info():
             int(os.environ.get("LOCAL_RANK", 0)))
 
 
-def make_workload(config, seed, rank, world, scaling, backend=None, batch=None):
-    """Weak scaling: every rank generates its own batch (seed + rank).  Strong scaling: every
-    rank generates the same global batch and keeps its event-balanced shard of it."""
+def default_scaling(config):
+    """Configuration 3 is stated as one 4096-sample batch sharded across 1/2/4/8 GPUs (strong
+    scaling); the others run as replicas, one batch per rank (weak scaling)."""
+    return "strong" if config == 3 else "weak"
+
+
+def make_workload(config, seed, rank, world, scaling, batch=None):
+    """(global workload, this rank's workload): the configuration's seeded batch with the fixed
+    benchmark capacities (workloads.CAPACITY_TABLE).  Strong scaling: every rank builds the same
+    global batch and keeps its event-balanced shard.  Weak scaling: every rank runs the whole
+    batch (replicas)."""
     from salt_b200 import workloads as W
     from salt_b200.sharding import balanced_shards, take_shard
-    kw = {}
-    if config == 3:
-        kw["batch"] = batch or 4096
-    if config == 4:
-        kw["batch"] = batch or 256
-    s = seed + (rank if (scaling == "weak" and world > 1) else 0)
-    wl = W.CONFIGS[config](seed=s, **kw)
+    wl = W.benchmark(config, seed=seed, batch=batch)
     if scaling == "strong" and world > 1:
         sh = balanced_shards(np.minimum(wl.n_real, wl.times.shape[1]), world)
         t, src, n = take_shard([wl.times, wl.src, wl.n_real], sh, rank)
         n = np.where(sh.of(rank) == sh.pad_index, 0, n).astype(np.int32)
-        wl = W.Workload(f"{wl.name}_shard{rank}of{world}", wl.network, wl.params, t, src, n)
-    if backend is not None:
-        if config == 4:
-            wl = W.size_capacities(wl, backend, expected_factor=4.0)
-        elif config in (2, 3):
-            wl = W.size_capacities(wl, backend)
-    return wl
+        return wl, W.Workload(f"{wl.name}_shard{rank}of{world}", wl.network, wl.params, t, src, n)
+    return wl, wl
+
+
+def job_config(args, wl, world):
+    """The `config` object of both arms' JSON lines: the whole job's workload (identical for the
+    same flags, whichever arm prints it)."""
+    copies = world if args.scaling == "weak" else 1
+    B, E = wl.batch, wl.times.shape[1]
+    return {"workload": wl.name, "global_batch": int(B * copies),
+            "events_per_step": int(wl.events * copies), "stream_capacity": int(E),
+            "capacities": {l.name: dict(l.capacity) for l in wl.network.layers},
+            "scaling": args.scaling,
+            "l2": "inputs larger than L2 (the input stream alone is "
+                  f"{B * copies * E * 8 / 2**20:.0f} MiB > 126 MB), no flush"}
 
 
 def peak_hbm():
@@ -141,9 +158,12 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "source": "nvml, 10 ms"}
 
 
-def cpu_baseline(wl, seconds, threads=None):
+def cpu_baseline(wl, seconds, threads=None, gpu=None):
     """The oracle port (literal C restatement of the reference path, all host threads) on a
-    bounded sample of the same workload."""
+    bounded sample of the same workload: the first m samples, m sized for about `seconds` of
+    CPU work.  With gpu = (logits (B, n_out), spike counts (n_layers, B), fits (B,)) of this
+    workload's forward, the oracle's logits, per-layer spike counts and fits of those m samples
+    are compared with the GPU's: the returned dict's "parity" counts the samples that differ."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     threads = threads or os.cpu_count() or 1
@@ -151,34 +171,39 @@ def cpu_baseline(wl, seconds, threads=None):
     n = min(wl.batch, max(threads, 1))
     t0 = time.perf_counter()
     O.network_batch(layers, params, wl.times[:n], wl.src[:n], wl.n_real[:n], threads=threads)
-    dt = time.perf_counter() - t0
-    per_sample = dt / n
-    m = int(min(wl.batch, max(n, seconds / max(per_sample, 1e-6) * 1.0)))
-    idx = np.arange(m) % wl.batch
+    per_sample = (time.perf_counter() - t0) / n
+    m = int(min(wl.batch, max(n, seconds / max(per_sample, 1e-6))))
+    idx = np.arange(m)
     t0 = time.perf_counter()
-    O.network_batch(layers, params, wl.times[idx], wl.src[idx], wl.n_real[idx], threads=threads)
+    vf, sc, fits = O.network_batch(layers, params, wl.times[idx], wl.src[idx], wl.n_real[idx],
+                                   threads=threads)
     dt = time.perf_counter() - t0
     ev = int(np.minimum(wl.n_real[idx], wl.times.shape[1]).sum())
-    return {"value": ev / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{m} samples of {wl.name} ({ev} events) through the C oracle, "
-                      f"{threads} threads, {dt:.1f} s"}
+    out = {"value": ev / dt, "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": f"the first {m} samples of {wl.name} ({ev} events) through the C oracle, "
+                     f"{threads} threads, {dt:.1f} s"}
+    if gpu is not None:
+        g_logits, g_spikes, g_fits = gpu
+        bad = (np.any(g_logits[idx] != vf, axis=1) | np.any(g_spikes[:, idx].T != sc, axis=1)
+               | ((g_fits[idx] != 0) != fits))
+        out["parity"] = {"samples": m, "mismatches": int(bad.sum()),
+                         "compared": "logits (last layer v_final), per-layer spike counts, fits"}
+    return out
 
 
 def run_reference(args):
+    """The reference arm: the reference's algorithm on the host cores (the C oracle port, all
+    threads; the reference itself needs JAX, absent here), on the same workload and capacities
+    as the GPU arm, each step a bounded sample of consecutive samples of the batch."""
     rank, world, _ = rank_info()
     if rank != 0:
         return
-    wl = make_workload(args.config, args.seed, 0, 1, args.scaling, batch=args.batch)
-    # capacities: the oracle path needs the sized knobs; size them without a GPU by the same
-    # rule on the CPU port (one generous pass) — or reuse generous values when sizing is costly
-    from salt_b200 import workloads as W
-    if args.config in (2, 3, 4):
-        wl = _cpu_sized(wl, args.config)
+    wl, _ = make_workload(args.config, args.seed, 0, 1, args.scaling, batch=args.batch)
     threads = os.cpu_count() or 1
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     layers, params = list(wl.network.layers), wl.params
-    n = max(1, min(wl.batch, threads))
+    n = max(1, min(wl.batch, 4 * threads))   # several samples per thread: balanced threads
     per_step = []
     cursor = 0
     for step in range(args.warmup + args.steps):
@@ -193,44 +218,24 @@ def run_reference(args):
     ev = sum(e for e, _ in per_step)
     tt = sum(d for _, d in per_step)
     value = ev / tt
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 0,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tt / args.steps,
-            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
-            "dtype": "int32", "data": "synthetic",
-            "config": {"workload": wl.name, "samples_per_step": n},
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * tt / args.steps, "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+            "config": job_config(args, wl, args.gpus),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{n} samples per step of {wl.name} through the C "
-                                       f"restatement of the reference path (oracle/), "
-                                       f"{threads} threads"},
+                             "sample": f"{n} consecutive samples per step of {wl.name} through "
+                                       f"the C restatement of the reference path (oracle/), "
+                                       f"{threads} threads, rank 0 only"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def _cpu_sized(wl, config):
-    """Capacities for the CPU-only arm: the queue knob from the candidates per position (its
-    largest per sample, x1.5) and generous output knobs; the CPU port allocates (n, L) arrays,
-    so L must be finite."""
-    from dataclasses import replace
-    from salt_b200 import workloads as W
-    from salt_b200.layers import ConvLayer
-    layers = list(wl.network.layers)
-    sub = min(wl.batch, 8)
-    E = wl.times.shape[1]
-    real = np.arange(E)[None, :] < np.minimum(wl.n_real[:sub], E)[:, None]
-    new = []
-    for i, layer in enumerate(layers):
-        if isinstance(layer, ConvLayer):
-            if i == 0:
-                cand = np.where(real, W.candidates_per_event(layer, wl.src[:sub]), 0).sum(1)
-                L = int(math.ceil(1.5 * cand.max() / (layer.h_out * layer.w_out) * 4))
-            else:
-                L = 256
-            new.append(replace(layer, max_queue_len=max(L, 8),
-                               max_out_spikes=min(layer.max_out_spikes, 4 * E)))
-        else:
-            new.append(layer)
-    return replace(wl, network=wl.network.replace_layers(new))
+# DRAM bytes (read + write) per input event of conv1's conv_fused launch, measured by ncu on the
+# 1024-sample configuration-3 case of the current kernel (profiles/conv_fused_config3.md, "v17"
+# rows: 185.0 + 143.4 MB for 7.77 M input events); reported scaled by the launch's input events.
+CONV_FUSED_DRAM_BYTES_PER_EVENT = (185.0e6 + 143.4e6) / 7.772496e6
 
 
 def run_b200(args):
@@ -242,10 +247,9 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     import salt_b200 as S
-    from salt_b200 import workloads as W
     backend = S.QuantB200Backend("round")
-    wl = make_workload(args.config, args.seed, rank, world, args.scaling, backend,
-                       batch=args.batch)
+    wl_all, wl = make_workload(args.config, args.seed, rank, world, args.scaling,
+                               batch=args.batch)
     layers, params = list(wl.network.layers), wl.params
     B, E = wl.batch, wl.times.shape[1]
     plan = backend.compile(layers, params, batch=B, in_capacity=E)
@@ -296,6 +300,9 @@ def run_b200(args):
     fused_ms, layer_ms, fused_n = plan.profile_read(reset=True)
     launches_per_step = plan.last_launch_count()
     ms = start.elapsed_time(stop) / args.steps
+    # the last forward's results, for the parity check against the oracle (rank 0, N = 1)
+    gpu_results = (plan.logits.cpu().numpy(), plan.stats[0].cpu().numpy(),
+                   plan.fits.cpu().numpy())
     t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
     ev_all = torch.tensor([events_rank], dtype=torch.float64, device="cuda")
     if world > 1:
@@ -341,22 +348,33 @@ def run_b200(args):
     d2h = int(pf.logits.numel() * 4 + pf.fits.numel() * 4)
     pf.close()
 
-    # ---- roofline of the dominant kernel (the fused bucket+scan kernel of the busiest conv
-    # layer; a network of FC layers only: the busiest FC layer, scan and compaction together)
+    # ---- roofline: the dominant kernel (the fused bucket+scan kernel of the busiest conv layer;
+    # a network of FC layers only: the busiest FC layer, scan and compaction together) and the
+    # whole network (the layer byte model over every layer, against the step time)
+    vol = layer_volumes(backend, wl)
     conv_dominant = float(np.max(fused_ms)) > 0.0
     if conv_dominant:
         dom = int(np.argmax(fused_ms))
         avg_ms = float(fused_ms[dom] / max(int(fused_n[dom]), 1))
-        alg_bytes = algorithmic_bytes(backend, wl, dom)
+        v = vol[dom]
+        alg_bytes = float(8 * v["E"] + 16 * v["C"] + 4 * v["N"])
         kernel_name = f"conv_fused (layer {layers[dom].name})"
+        traffic = CONV_FUSED_DRAM_BYTES_PER_EVENT * v["E"] if dom == 0 else None
     else:
         dom = int(np.argmax(layer_ms))
         avg_ms = float(layer_ms[dom] / max(int(fused_n[dom]), 1))
-        alg_bytes = fc_algorithmic_bytes(backend, wl, dom)
+        v = vol[dom]
+        alg_bytes = float(8 * v["E"] + 24 * v["S"] + 4 * v["N"])
         kernel_name = f"fc_scan + compaction (layer {layers[dom].name})"
+        traffic = None
+    net_bytes = torch.tensor([sum(layer_bytes(l, v, np.size(p.decay_table_int))
+                                  for l, v, p in zip(layers, vol, params))],
+                             dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(net_bytes, op=dist.ReduceOp.SUM)
     peak, peak_kind = peak_hbm()
     achieved = alg_bytes / (avg_ms / 1000.0) / 1e9
-    traffic = traffic_from_profile(wl, dom) if conv_dominant else None
+    net_achieved = float(net_bytes.item()) / (ms_max / 1000.0) / 1e9
 
     if rank == 0:
         line = {
@@ -364,21 +382,24 @@ def run_b200(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "int32", "data": "synthetic",
-            "config": {"workload": wl.name,
-                       "global_batch": B * world if args.scaling == "weak"
-                       else (args.batch or {3: 4096, 4: 256}.get(args.config, B)),
-                       "per_rank_batch": B, "events_per_step": int(events_step),
-                       "stream_capacity": E,
+            "config": job_config(args, wl_all, world),
+            "layout": {"per_rank_batch": B, "events_rank0": int(events_rank),
                        "parallelism": f"dp{world} (" + ("one batch per rank" if args.scaling ==
                                                         "weak" else "event-balanced shards of "
-                                                        "one batch") + ")",
-                       "capacities": {l.name: dict(l.capacity) for l in layers},
-                       "l2": "inputs larger than L2 (per-rank stream "
-                             f"{wl.times.nbytes * 2 / 2**20:.0f} MiB > 126 MB), no flush"},
+                                                        "one batch") + ")"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
+                         "traffic_source": ("ncu DRAM bytes per input event of the captured "
+                                            "1024-sample case, scaled by this launch's events"
+                                            if traffic is not None else None),
                          "kernel": kernel_name,
                          "kernel_ms": avg_ms, "algorithmic_bytes": alg_bytes,
+                         "network": {"achieved": net_achieved, "frac": net_achieved / peak,
+                                     "frac_of_8tbs": net_achieved / 8000.0,
+                                     "bytes_per_step": float(net_bytes.item()),
+                                     "model": "sum over layers and ranks of the conv/FC layer "
+                                              "byte model (8E + 16C + 16S + 8S_out + 4N; FC "
+                                              "8E + 24S + 4N; weights and LUT once) / step"},
                          "per_layer_ms": {l.name: {"layer": float(layer_ms[i] / max(fused_n[i], 1)),
                                                    "fused_kernel": float(fused_ms[i] /
                                                                          max(fused_n[i], 1))}
@@ -397,9 +418,10 @@ def run_b200(args):
             "clocks": clocks.summary(),
         }
         if replay is not None:
-            line["config"]["launch"] = "CUDA graph replay of the forward"
+            line["layout"]["launch"] = "CUDA graph replay of the forward"
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds, gpu=gpu_results)
+            line["parity"] = line["cpu_baseline"].pop("parity")
         print(json.dumps(line), flush=True)
     plan.close()
     if world > 1:
@@ -407,57 +429,42 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
-def algorithmic_bytes(backend, wl, layer_index):
-    """Per-launch algorithmic bytes of the fused bucket+scan kernel of one conv layer, with the
-    per-sample terms of the conv-layer byte model: 8 B per input event (time, source), 16 B per
-    receptive-field candidate (the bucketed record written and read once), 4 B per neuron
-    (v_final)."""
+def layer_volumes(backend, wl, sub=512):
+    """Per layer, summed over the workload's samples: real input events E (min(n_real,
+    capacity)), valid receptive-field candidates C (conv layers), spikes S (the true count),
+    output entries written S_out = min(S, max_out_spikes) and neurons N (per sample x batch).
+    One forward of the batch in sub-batches, keeping the host streams of each sub-batch."""
     from salt_b200 import workloads as W
+    from salt_b200.layers import ConvLayer
     layers = list(wl.network.layers)
-    layer = layers[layer_index]
-    if layer_index == 0:
-        src, n_real = wl.src, wl.n_real
-    else:
-        out = backend.run_network(layers[:layer_index], wl.params[:layer_index],
-                                  wl.network.input_stream(wl.raw()), keep_streams=True)
-        st = out.streams[-1]
-        src, n_real = st.event_source_idx, st.n_real_events
-    E = src.shape[1]
-    n_eff = np.minimum(n_real, E)
-    real = np.arange(E)[None, :] < n_eff[:, None]
-    C = int(np.where(real, W.candidates_per_event(layer, src), 0).sum())
-    return float(8 * int(n_eff.sum()) + 16 * C + 4 * layer.n_neurons * wl.batch)
+    vol = [dict(E=0, C=0, S=0, S_out=0, N=l.n_neurons * wl.batch) for l in layers]
+    for b0 in range(0, wl.batch, sub):
+        part = wl.subset(np.arange(b0, min(wl.batch, b0 + sub)))
+        out = backend.run_network(layers, part.params, part.network.input_stream(part.raw()),
+                                  keep_streams=True)
+        src, n_real = part.src, part.n_real
+        for li, layer in enumerate(layers):
+            cap = src.shape[1]
+            n_eff = np.minimum(n_real, cap)
+            vol[li]["E"] += int(n_eff.sum())
+            if isinstance(layer, ConvLayer):
+                real = np.arange(cap)[None, :] < n_eff[:, None]
+                vol[li]["C"] += int(np.where(real, W.candidates_per_event(layer, src), 0).sum())
+            S = out.results[li].spike_count.astype(np.int64)
+            vol[li]["S"] += int(S.sum())
+            vol[li]["S_out"] += int(np.minimum(S, layer.max_out_spikes).sum())
+            src, n_real = out.streams[li].event_source_idx, out.streams[li].n_real_events
+    return vol
 
 
-def fc_algorithmic_bytes(backend, wl, layer_index):
-    """Per-launch algorithmic bytes of one integer FC layer with the FC byte model: 8 B per input
-    event (time, source), 24 B per output spike (spike word, scan, stream entry), 4 B per neuron
-    (v_final)."""
-    layers = list(wl.network.layers)
-    out = backend.run_network(layers[:layer_index + 1], wl.params[:layer_index + 1],
-                              wl.network.input_stream(wl.raw()), keep_streams=True)
-    if layer_index == 0:
-        n_in = np.minimum(wl.n_real, wl.src.shape[1])
-    else:
-        prev = out.streams[layer_index - 1]
-        n_in = np.minimum(prev.n_real_events, prev.event_source_idx.shape[1])
-    S = int(np.sum(out.results[layer_index].spike_count))
-    return float(8 * int(np.sum(n_in)) + 24 * S + 4 * layers[layer_index].n_neurons * wl.batch)
-
-
-def traffic_from_profile(wl, layer_index):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, scaled from
-    the captured case to this launch by input events (null when no summary exists)."""
-    path = os.path.join(ROOT, "profiles", "conv_fused_config3.md")
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.startswith("dram_bytes_per_input_event:"):
-                    per_ev = float(line.split(":", 1)[1])
-                    return per_ev * wl.events if layer_index == 0 else None
-    except OSError:
-        pass
-    return None
+def layer_bytes(layer, v, lut_len):
+    """The conv / FC layer byte model for one layer's volumes, plus its weights and LUT once."""
+    from salt_b200.layers import ConvLayer
+    weights = 4 * int(np.prod(layer.weight_shape)) + 4 * int(lut_len)
+    if isinstance(layer, ConvLayer):
+        return float(8 * v["E"] + 16 * v["C"] + 16 * v["S"] + 8 * v["S_out"] + 4 * v["N"]
+                     + weights)
+    return float(8 * v["E"] + 16 * v["S"] + 8 * v["S_out"] + 4 * v["N"] + weights)
 
 
 # ---------------------------------------------------------------- configuration 5 (float)
@@ -639,12 +646,13 @@ def run_b200_float(args):
                        "l2": "256 MiB written between timed steps (L2 flush, outside the "
                              "layer's timed events)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": float_traffic_from_profile(wl),
+                         "frac": achieved / peak, "traffic": FFC_SEGMENT_DRAM_BYTES_PER_EVENT * wl.events,
                          "kernel": "ffc_segment (speculative segment scan)",
                          "kernel_ms": seg_avg, "algorithmic_bytes": alg,
                          "layer_ms": ms, "peak_source": peak_kind,
-                         "note": "the 64 MB weight matrix is re-read per event from L2; "
-                                 "achieved counts those bytes against the HBM peak"},
+                         "note": "L2-served: the 64 MB weight matrix stays in L2 and is re-read "
+                                 "per event from there (DRAM sees ~3 KB per event); achieved "
+                                 "counts those L2 bytes against the HBM peak"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "gpu_launches": launches_per_step * args.steps,
@@ -658,17 +666,9 @@ def run_b200_float(args):
         dist.destroy_process_group()
 
 
-def float_traffic_from_profile(wl):
-    """DRAM bytes per segment-kernel launch from the committed ncu summary, scaled by events."""
-    path = os.path.join(ROOT, "profiles", "ffc_segment_config5.md")
-    try:
-        with open(path) as f:
-            for line in f:
-                if line.startswith("dram_bytes_per_input_event:"):
-                    return float(line.split(":", 1)[1]) * wl.events
-    except OSError:
-        pass
-    return None
+# DRAM bytes (read + write) per input event of ffc_segment, measured by ncu on the full
+# configuration-5 launch (profiles/ffc_segment_config5.md: 1.850 + 1.131 GB for 10^6 events).
+FFC_SEGMENT_DRAM_BYTES_PER_EVENT = (1.850e9 + 1.131e9) / 1.0e6
 
 
 def main():

@@ -11,7 +11,7 @@
  *   - All array pointers are DEVICE pointers unless a comment says "host".
  *   - Batch-major layouts: a stream is (batch, capacity) row-major; per-neuron arrays are
  *     (batch, n_neurons) with neuron = oc * h_out * w_out + oy * w_out + ox for conv layers
- *     (salt_core/layers/conv.py:189-197).
+ *     (salt_core/layers/conv.py:104-112).
  *   - Every call is asynchronous on `stream` (a cudaStream_t) and returns a status; argument
  *     errors are reported before anything is enqueued.  Capacity overflow is NOT an error: it
  *     is reported through `fits` / `needed_queue` / `n_real`, as salt_core/capacity.py:60-63.
@@ -56,13 +56,13 @@ typedef struct {
                               every column).  Setting it when not needed is always correct. */
 } salt_quant_desc;
 
-/* ConvLayer geometry and capacity (salt_core/layers/conv.py:107-138). */
+/* ConvLayer geometry and capacity (salt_core/layers/conv.py:23-99). */
 typedef struct {
   int32_t ic, h_in, w_in, oc, k, s, p;
   int32_t max_queue_len, max_out_spikes, max_extra_steps;
 } salt_conv_desc;
 
-/* FCLayer geometry and capacity (salt_core/layers/fc.py:323-341). */
+/* FCLayer geometry and capacity (salt_core/layers/fc.py:23-41). */
 typedef struct {
   int32_t n_in, n_out;
   int32_t max_out_spikes, max_extra_steps;
@@ -88,7 +88,7 @@ typedef struct {
 
 /* Per-sample diagnostics of one layer (batch entries each).  Any pointer may be NULL.
  *   spike_count  LayerDiag.spike_count (layers/base.py:73-79)
- *   needed_queue LayerDiag.needed["max_queue_len"] = max n_real + 1 (layers/conv.py:222-224)
+ *   needed_queue LayerDiag.needed["max_queue_len"] = max n_real + 1 (layers/conv.py:137-141)
  *   overflowed   any(QuantLayerResult.overflowed) (example/quant_run.py:88-89)
  *   vmin / vmax  min/max of v_unfitted_min/max over neurons (example/quant_run.py:90-93)
  *   fits         Capacity.fits (capacity.py:60-63) */
@@ -97,7 +97,7 @@ typedef struct {
 } salt_layer_stats;
 
 /* ---------------------------------------------------------------- conv layer
- * Replaces ConvLayer.forward with QuantBackend (salt_core/layers/conv.py:209-234 calling
+ * Replaces ConvLayer.forward with QuantBackend (salt_core/layers/conv.py:124-149 calling
  * build_conv_structure connectivity/conv.py:128-172, QuantBackend.scan quant/backend.py:31-53,
  * extract_output_events_conv stream.py:84-100, _layer_diag layers/base.py:73-79).
  *   q    (oc, ic, k, k) int32 weight codes      lut (lut_len) int32 decay_table_int
@@ -140,7 +140,7 @@ salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc *layer,
 
 /* ---------------------------------------------------------------- traces
  * Replace QuantBackend.scan with trace=True (salt_core/quant/backend.py:31-53 ->
- * run_layer_traced quant/scan.py:83-94) and the event times of salt_core/trace.py:24-60: for
+ * run_layer_traced quant/scan.py:83-94) and the event times of salt_core/trace.py:25-55: for
  * every neuron of every sample, the register after each of its L queue columns (conv: L =
  * max_queue_len; fc: L = the input stream capacity), whether it fired there and the time of the
  * column's event (NaN for columns at or past the neuron's real events).  v_steps / spike_mask /
@@ -170,7 +170,7 @@ salt_status salt_fc_layer_trace(const salt_fc_desc *layer, const salt_quant_desc
                                 const salt_neuron_trace *per_neuron, void *stream);
 
 /* ---------------------------------------------------------------- fc layer
- * Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:385-402 calling
+ * Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:84-101 calling
  * build_fc_structure connectivity/fc.py:20-33, fc_weight_codes :54-61, QuantBackend.scan,
  * extract_output_events_fc stream.py:67-81).
  *   q (n_out, n_in) int32 weight codes; vth (n_out) or NULL; v_final (batch, n_out). */
@@ -193,8 +193,18 @@ salt_status salt_quant_scan_dense(const salt_quant_desc *quant, int32_t n, int32
                                   uint8_t *overflowed, int32_t *v_final, int32_t *vmin,
                                   int32_t *vmax, void *stream);
 
+/* The same scan with trace=True (run_layer_traced, salt_core/quant/scan.py:83-94, as
+ * QuantBackend.scan calls it, salt_core/quant/backend.py:41-43): v_steps (n, L) int32 receives
+ * the register after each column (after a spike's reset); its last column equals v_final. */
+salt_status salt_quant_scan_dense_trace(const salt_quant_desc *quant, int32_t n, int32_t L,
+                                        const int32_t *a_int, const uint8_t *is_identity,
+                                        const int32_t *q_int, const int32_t *vth,
+                                        uint8_t *spike_mask, uint8_t *overflowed,
+                                        int32_t *v_final, int32_t *vmin, int32_t *vmax,
+                                        int32_t *v_steps, void *stream);
+
 /* ---------------------------------------------------------------- network plan
- * A native runtime object that chains layers on the device (salt_core/network.py:193-222
+ * A native runtime object that chains layers on the device (salt_core/network.py:93-122
  * run_network, vmapped over the batch as Network.apply_batched :279-283) with every
  * intermediate stream kept in the workspace, optionally replayed as one CUDA graph.
  * Layer parameters are HOST pointers copied to the device at creation. */
@@ -219,7 +229,7 @@ salt_status salt_network_workspace_size(const salt_network *net, int32_t batch,
  *   logits      (batch, n_last) int32: v_final of the last layer (register values)
  *   spike_count (n_layers, batch) int32, overflowed (n_layers, batch) int32,
  *   vmin/vmax   (n_layers, batch) int32, needed_queue (n_layers, batch) int32,
- *   fits        (batch) int32: AND of Capacity.fits over layers (network.py:216-219). */
+ *   fits        (batch) int32: AND of Capacity.fits over layers (network.py:116-119). */
 salt_status salt_network_forward(salt_network *net, int32_t batch, const salt_stream_in *in,
                                  int32_t *logits, int32_t *spike_count, int32_t *overflowed,
                                  int32_t *vmin, int32_t *vmax, int32_t *needed_queue,
@@ -295,7 +305,7 @@ salt_status salt_float_fc_layer_forward(const salt_float_fc_desc *layer, const f
 /* ---------------------------------------------------------------- float conv layer
  * Replaces ConvLayer.forward with FloatBackend (salt_core/layers/conv.py:124-149): the queue of
  * build_conv_structure (connectivity/conv.py:128-172), conv_float_values (:187-206), the chunked
- * scan (float/scan.py:100-131, float/affine.py:99-126), spike_step_upper_bound's need
+ * scan (float/scan.py:67-116, float/affine.py:99-126), spike_step_upper_bound's need
  * (affine.py:57-88) and extract_output_events_conv (stream.py:84-100).  The float forward of the
  * quantisation pipeline: with chunk_size 1 it is the calibration forward of
  * example/quant_run.py:30-44.  w is (oc, ic, k, k) float32; decay_base = float32(1 - 1/tau);
@@ -317,7 +327,7 @@ typedef struct {
   int32_t *fits;                /* (batch) every need within its knob */
 } salt_float_conv_stats;
 
-/* Per-step traces of a float layer (run_layer_traced, float/scan.py:53-64, with trace.py:13-60)
+/* Per-step traces of a float layer (run_layer_traced, float/scan.py:53-64, with trace.py:13-55)
  * and its potential ranges (quant/calibrate.py:16-36 reduces v_steps to these); any pointer may
  * be NULL.  max_steps = ceil(L / chunk_size) + max_extra_steps, L = max_queue_len (conv) or the
  * input capacity (FC).  Ranges are over every step and, for conv layers, every position of a
@@ -369,6 +379,46 @@ salt_status salt_stream_h2d_real(const float *host_times, const int32_t *host_sr
 salt_status salt_float_fc_set_profiling(int32_t enable);
 salt_status salt_float_fc_profile_read(float *segment_ms, float *layer_ms, int32_t *layers,
                                        int32_t reset);
+
+/* ---------------------------------------------------------------- runtime plumbing
+ * No reference counterpart: under JAX, XLA owns the buffers, streams and executables.  A host
+ * that calls this library without XLA (the Python package, a C or cgo caller) takes device
+ * memory, pinned host memory, streams, events and graph replay from these thin wrappers of the
+ * CUDA runtime, so that nothing else on the host side needs a GPU framework.
+ *   - salt_malloc / salt_free: stream-ordered device memory (cudaMallocAsync / cudaFreeAsync on
+ *     `stream`; the device's default pool keeps freed memory cached for reuse).  A pointer may
+ *     be used on another stream only after that stream waits for `stream`.
+ *   - salt_host_alloc / salt_host_free: page-locked host memory, mapped into the device's address
+ *     space (what salt_stream_h2d_real reads).
+ *   - salt_memcpy_async: any direction (cudaMemcpyDefault: unified addressing tells host from
+ *     device); salt_memset_async: bytes.
+ *   - streams are created non-blocking (no implicit ordering with the legacy default stream,
+ *     which is `stream` = NULL).
+ *   - salt_graph_*: records everything enqueued on `stream` between begin and end (a
+ *     non-default stream; nothing may synchronise meanwhile) and replays it with one launch. */
+salt_status salt_malloc(size_t bytes, void *stream, void **ptr);
+salt_status salt_free(void *ptr, void *stream);
+salt_status salt_host_alloc(size_t bytes, void **ptr);
+salt_status salt_host_free(void *ptr);
+salt_status salt_memcpy_async(void *dst, const void *src, size_t bytes, void *stream);
+salt_status salt_memset_async(void *ptr, int32_t value, size_t bytes, void *stream);
+salt_status salt_device_count(int32_t *count);
+salt_status salt_set_device(int32_t device);
+salt_status salt_get_device(int32_t *device);
+salt_status salt_device_synchronize(void);
+salt_status salt_stream_create(void **stream);
+salt_status salt_stream_destroy(void *stream);
+salt_status salt_stream_synchronize(void *stream);
+salt_status salt_stream_wait_event(void *stream, void *event);
+salt_status salt_event_create(int32_t timing, void **event);
+salt_status salt_event_destroy(void *event);
+salt_status salt_event_record(void *event, void *stream);
+salt_status salt_event_synchronize(void *event);
+salt_status salt_event_elapsed_ms(void *start, void *stop, float *ms);
+salt_status salt_graph_begin_capture(void *stream);
+salt_status salt_graph_end_capture(void *stream, void **graph_exec);
+salt_status salt_graph_launch(void *graph_exec, void *stream);
+salt_status salt_graph_destroy(void *graph_exec);
 
 /* Library facts and errors (host). */
 const char *salt_last_error(void);

@@ -295,12 +295,12 @@ def _run(layer, params, times, src, n_in, round_mode, kind, trace=False):
 
 def conv_forward(layer, params, times, src, n_in, round_mode="round", trace=False
                  ) -> LayerResult:
-    """salt_core/layers/conv.py:209-234 with salt_core/quant/backend.py:31-53."""
+    """salt_core/layers/conv.py:124-149 with salt_core/quant/backend.py:31-53."""
     return _run(layer, params, times, src, n_in, round_mode, "conv", trace)
 
 
 def fc_forward(layer, params, times, src, n_in, round_mode="round", trace=False) -> LayerResult:
-    """salt_core/layers/fc.py:385-402 with salt_core/quant/backend.py:31-53."""
+    """salt_core/layers/fc.py:84-101 with salt_core/quant/backend.py:31-53."""
     return _run(layer, params, times, src, n_in, round_mode, "fc", trace)
 
 
@@ -438,7 +438,7 @@ class _FloatOut(ctypes.Structure):
 
 class FloatResult(NamedTuple):
     """FCLayer.forward with FloatBackend (layers/fc.py:84-106): FloatLayerResult's forward
-    values (float/scan.py:10-16; s_spike and s_value equal spike_mask there), the output
+    values (float/scan.py:15-22; s_spike and s_value equal spike_mask there), the output
     EventStream (stream.py:16-21) and the layer's needs (LayerDiag.needed)."""
     v_final: np.ndarray           # (n_out,) float32
     spike_mask: np.ndarray | None  # (n_out, max_steps) bool
@@ -498,6 +498,29 @@ def float_fc_forward(layer, w, times, src, n_real, gain=None, tau=None, *, dense
     return FloatResult(vf, mask.astype(bool) if dense else None, eidx, ot[:M], os_[:M], og[:M],
                        int(out.n_real_out), int(out.n_real_out), int(out.extra_steps_needed),
                        bool(out.fits), vs, ms)
+
+
+def float_seq64(layer, w, times, src, n_real, gain=None, tau=None, near=1e-6):
+    """Float64 yardstick of a float FC layer's sequential semantics (so_float_seq64): returns
+    (v_final (n_out,) float64, first_near (n_out,) int32: the first event whose value came within
+    near * |v_th| of the threshold, len(times) when none did)."""
+    n_out, n_in = int(layer.n_out), int(layer.n_in)
+    t = np.ascontiguousarray(np.asarray(times, dtype=np.float32))
+    s = np.ascontiguousarray(np.asarray(src), dtype=np.int32)
+    wf = np.ascontiguousarray(np.asarray(w, dtype=np.float32).reshape(n_out, n_in))
+    base = decay_base(np.broadcast_to(layer.tau if tau is None else tau, (n_out,)))
+    g = None if gain is None else np.ascontiguousarray(np.asarray(gain, dtype=np.float32))
+    vf = np.empty(n_out, np.float64)
+    fn = np.empty(n_out, np.int32)
+    rc = lib().so_float_seq64(n_in, n_out, _p(wf, _f32p), _p(base, _f32p), _p(t, _f32p),
+                              _p(s, _i32p), _p(g, _f32p) if g is not None else None,
+                              int(t.shape[0]), int(n_real), int(layer.chunk_size),
+                              int(layer.max_extra_steps), ctypes.c_double(float(layer.v_th)),
+                              ctypes.c_double(float(near)),
+                              vf.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), _p(fn, _i32p))
+    if rc:
+        raise ValueError(f"oracle float64 yardstick failed rc={rc}")
+    return vf, fn
 
 
 def affine_scan(a, b):

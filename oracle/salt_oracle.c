@@ -419,7 +419,7 @@ static void reduce_layer(so_layer_out *out, int32_t n, int32_t L, const uint8_t 
   out->vmax_all = hi;
 }
 
-/* layers/conv.py:209-234 ConvLayer.forward with QuantBackend.scan (quant/backend.py:31-53). */
+/* layers/conv.py:124-149 ConvLayer.forward with QuantBackend.scan (quant/backend.py:31-53). */
 int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const float *times,
                     const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out) {
   const int32_t L = g->max_queue_len, h_out = conv_h_out(g), w_out = conv_w_out(g);
@@ -436,7 +436,7 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
   int rc = so_conv_structure(g, times, src, E_len, n_in, l2g, nreal, dt, tc, tky, tkx);
   if (rc) return rc;
 
-  /* neuron_delta_t = tile_channels(delta_t) (layers/conv.py:252-254); codes per conv.py:209-218 */
+  /* neuron_delta_t = tile_channels(delta_t) (layers/conv.py:167-169); codes per connectivity/conv.py:210-219 */
   size_t NL = (size_t)n * L;
   int32_t *a = (int32_t *)malloc(sizeof(int32_t) * NL);
   uint8_t *isid = (uint8_t *)malloc(NL);
@@ -460,7 +460,7 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
   run_layer_traced(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
                    qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax,
                    out->v_steps);
-  if (out->event_ms) /* trace.py:44-60 resolve_ms_conv with pointer = column */
+  if (out->event_ms) /* trace.py:40-55 resolve_ms_conv with pointer = column */
     for (int32_t o = 0; o < OC; ++o)
       for (int32_t pos = 0; pos < n_sp; ++pos)
         for (int32_t col = 0; col < L; ++col) {
@@ -475,7 +475,7 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
   int32_t mx = 0;
   for (int32_t pos = 0; pos < n_sp; ++pos)
     if (nreal[pos] > mx) mx = nreal[pos];
-  out->needed_queue = mx + 1; /* layers/conv.py:222-224 */
+  out->needed_queue = mx + 1; /* layers/conv.py:137-141 */
   reduce_layer(out, n, L, ovf);
   out->fits = out->needed_queue <= L && out->n_real_out <= g->max_out_spikes &&
               0 <= g->max_extra_steps; /* capacity.py:60-63 */
@@ -493,7 +493,7 @@ int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const floa
   return 0;
 }
 
-/* layers/fc.py:385-402 FCLayer.forward with QuantBackend; structure per connectivity/fc.py:20-33,
+/* layers/fc.py:84-101 FCLayer.forward with QuantBackend; structure per connectivity/fc.py:20-33,
  * codes per fc.py:54-61. */
 int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *times,
                   const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out) {
@@ -525,7 +525,7 @@ int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *t
   run_layer_traced(a, isid, qi, qp->vth, n, L, qp->f_a, qp->f_V, qp->i_V, qp->round_mode,
                    qp->overflow_mode, mask, ovf, out->v_final, out->vmin, out->vmax,
                    out->v_steps);
-  if (out->event_ms) /* trace.py:24-41 resolve_ms_fc: the column is the global event index */
+  if (out->event_ms) /* trace.py:25-37 resolve_ms_fc: the column is the global event index */
     for (int32_t o = 0; o < n; ++o)
       for (int32_t j = 0; j < L; ++j)
         out->event_ms[(size_t)o * L + j] = j >= n_in ? (float)NAN : times[j];
@@ -718,7 +718,7 @@ static int push_spike(fneuron_t *r, int32_t step, int32_t j) {
   return 0;
 }
 
-/* One neuron: fc_float_values (connectivity/fc.py:36-51) + float/scan.py:100-131 step loop +
+/* One neuron: fc_float_values (connectivity/fc.py:36-51) + float/scan.py:67-116 step loop +
  * affine.py:57-88 bound. */
 static int float_neuron(float_ctx *c, int32_t i, float *a_pad, float *b_pad, float *ca, float *cb,
                         float *A, float *B, float *work) {
@@ -760,7 +760,7 @@ static int float_neuron(float_ctx *c, int32_t i, float *a_pad, float *b_pad, flo
   float *vst = c->out->v_steps ? c->out->v_steps + (int64_t)i * c->max_steps : NULL;
   float *ems = c->out->event_ms ? c->out->event_ms + (int64_t)i * c->max_steps : NULL;
   for (int32_t step = 0; step < c->max_steps; ++step) {
-    /* trace.py:24-40 resolve_ms_fc: the step's start pointer, idle from n_real on */
+    /* trace.py:25-37 resolve_ms_fc: the step's start pointer, idle from n_real on */
     if (ems) ems[step] = ptr >= c->n_real ? NAN : c->times[ptr < L - 1 ? ptr : L - 1];
     if (ptr >= id_from && !(v - v_th >= 0.0f)) {
       /* Every map from here on is the identity (1, 0), which composes to exactly (1, 0): each
@@ -934,7 +934,7 @@ int so_float_fc_forward(const so_float_fc_geom *g, const float *w, const float *
 
 /* ================================================================ float conv layer */
 
-/* float/scan.py:100-131: max_steps steps over one neuron's padded queue (Lp = L + C maps).  Per
+/* float/scan.py:67-116: max_steps steps over one neuron's padded queue (Lp = L + C maps).  Per
  * step it records the spike flag, the queue column of the step's spike (pointer + spike_idx,
  * scan.py:114; pointer + C on a silent step), the potential after the step and the pointer at
  * the step's start (run_layer_traced's v_steps / pointer_steps, scan.py:118-119); any output
@@ -1061,7 +1061,7 @@ int so_float_conv_forward(const so_float_conv_geom *fg, const float *w, float de
           a_pad, b_pad, L, C, id_from, max_steps, fg->v_th, buf, buf + C, buf + 2 * C,
           buf + 3 * C, buf + 4 * C, mask + row, eidx + row,
           out->v_steps ? out->v_steps + row : NULL, ptr_steps ? ptr_steps + row : NULL);
-      if (out->event_ms) /* trace.py:43-60 resolve_ms_conv */
+      if (out->event_ms) /* trace.py:40-55 resolve_ms_conv */
         for (int32_t s = 0; s < max_steps; ++s) {
           const int32_t p = ptr_steps[row + s];
           if (p >= nr) {
@@ -1095,4 +1095,47 @@ done:
   free(a_pad);
   free(buf);
   return rc;
+}
+
+/* ---------------------------------------------------------------- float64 yardstick */
+
+int so_float_seq64(int32_t n_in, int32_t n_out, const float *w, const float *decay_base,
+                   const float *times, const int32_t *src, const float *gain, int32_t E_len,
+                   int32_t n_real, int32_t chunk_size, int32_t max_extra_steps, double v_th,
+                   double near, double *v_final, int32_t *first_near) {
+  if (n_in < 1 || n_out < 1 || E_len < 0 || chunk_size < 1) return 1;
+  const int32_t n_eff = n_real < 0 ? 0 : (n_real > E_len ? E_len : n_real);
+  const int64_t max_steps = (E_len + chunk_size - 1) / chunk_size + (int64_t)max_extra_steps;
+  const double band = near * fabs(v_th);
+  for (int32_t o = 0; o < n_out; ++o) {
+    double v = 0.0;
+    int64_t phase = 0, steps = 0;
+    int run = max_steps > 0;
+    float tprev = 0.0f;
+    int32_t fn = E_len;
+    const double base = (double)decay_base[o];
+    for (int32_t j = 0; j < n_eff && run; ++j) {
+      const float t = times[j];
+      const double dt = (double)(float)(t - tprev);
+      tprev = t;
+      int32_t s = src[j];
+      if (s < 0) s += n_in;
+      if (s < 0) s = 0;
+      if (s >= n_in) s = n_in - 1;
+      const double b = (double)w[(int64_t)o * n_in + s] * (gain ? (double)gain[j] : 1.0);
+      v = pow(base, dt) * v + b;
+      if (fn == E_len && fabs(v - v_th) < band) fn = j;
+      const int spike = v >= v_th;
+      if (spike) v = 0.0;
+      phase += 1;
+      if (spike || phase == chunk_size) {
+        steps += 1;
+        phase = 0;
+      }
+      run = steps < max_steps;
+    }
+    v_final[o] = v;
+    first_near[o] = fn;
+  }
+  return 0;
 }

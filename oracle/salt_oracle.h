@@ -61,7 +61,7 @@ typedef struct {
   int32_t any_overflow;
   int32_t vmin_all, vmax_all;
   int32_t fits;
-  /* trace (quant/scan.py:83-94 run_layer_traced, trace.py:32-60 resolve_ms_*), may be NULL:
+  /* trace (quant/scan.py:83-94 run_layer_traced, trace.py:25-55 resolve_ms_*), may be NULL:
    *   v_steps  (n_neurons, L) register value after each column (after the reset)
    *   event_ms (n_neurons, L) time of the column's event, NaN for columns at or past n_real */
   int32_t *v_steps;
@@ -109,7 +109,7 @@ void so_extract_output_events(const uint8_t *mask, const int32_t *event_idx, int
                               const float *times, int32_t E_len, int32_t max_out, float *out_times,
                               int32_t *out_src, int32_t *n_real_out);
 
-/* Whole layers (layers/conv.py:209-234, layers/fc.py:385-402 with QuantBackend). */
+/* Whole layers (layers/conv.py:124-149, layers/fc.py:84-101 with QuantBackend). */
 int so_conv_forward(const so_conv_geom *g, const so_quant_params *qp, const float *times,
                     const int32_t *src, int32_t E_len, int32_t n_in, so_layer_out *out);
 int so_fc_forward(const so_fc_geom *g, const so_quant_params *qp, const float *times,
@@ -165,10 +165,10 @@ int so_float_fc_forward(const so_float_fc_geom *g, const float *w, const float *
 
 /* ConvLayer.forward with FloatBackend (layers/conv.py:124-149): build_conv_structure, then
  * conv_float_values (connectivity/conv.py:187-206: a = decay_base ** Δt per position, b = the
- * weight tap times the event gain on real columns), the chunked scan of float/scan.py:100-131 and
+ * weight tap times the event gain on real columns), the chunked scan of float/scan.py:67-116 and
  * extract_output_events_conv (stream.py:84-100).  w is (oc, ic, k, k); gain may be NULL (ones).
  * max_steps = ceil(L / chunk_size) + max_extra_steps.  The per-step arrays (spike_mask,
- * spike_event_idx = queue column, v_steps, event_ms = trace.py:43-60) may be NULL. */
+ * spike_event_idx = queue column, v_steps, event_ms = trace.py:40-55) may be NULL. */
 typedef struct {
   so_conv_geom conv;
   int32_t chunk_size;
@@ -190,6 +190,17 @@ typedef struct {
 int so_float_conv_forward(const so_float_conv_geom *g, const float *w, float decay_base,
                           const float *times, const int32_t *src, const float *gain,
                           int32_t E_len, int32_t n_in, so_float_conv_out *out);
+
+/* Float64 yardstick of a float FC layer (test infrastructure): the layer's sequential semantics
+ * (v = a*v + b with fire-and-reset at every event, a = base^dt with base = float32(1 - 1/tau)
+ * widened to double; the step accounting of float/scan.py:67-116: a step ends at a fire or
+ * after chunk_size events, events after max_steps steps are dropped) in double precision.
+ * Outputs per neuron: v_final (double) and first_near, the first event at which the value came
+ * within `near` of v_th (E_len when never).  gain may be NULL (all ones). */
+int so_float_seq64(int32_t n_in, int32_t n_out, const float *w, const float *decay_base,
+                   const float *times, const int32_t *src, const float *gain, int32_t E_len,
+                   int32_t n_real, int32_t chunk_size, int32_t max_extra_steps, double v_th,
+                   double near, double *v_final, int32_t *first_near);
 
 /* lax.associative_scan(combine, maps) of float/affine.py:20-24 over n maps (exposed for tests). */
 int so_affine_scan(const float *a, const float *b, int64_t n, float *out_a, float *out_b);

@@ -6,7 +6,8 @@ specs, Network/run_network, QuantizedLayerParams and the offline integer codes. 
 in libsalt_b200.so (CUDA kernels behind a C ABI, include/salt_b200.h); there is no CPU fallback.
 """
 from .capacity import Capacity, GrowthPolicy, LayerDiag, grown_to_fit, reduce_over_batch
-from .layers import ConvLayer, ConvSpec, FCLayer, FCSpec, LayerOutput, conv, fc
+from .layers import (ConvLayer, ConvQueueStructure, ConvSpec, FCLayer, FCQueueStructure, FCSpec,
+                     LayerOutput, conv, fc)
 from .network import InputEvents, Network, check_layer_connections, input_stream, run_network
 from .quant import (MAX_REGISTER_BITS, MAX_SHIFT_BITS, OverflowMode, QuantizedLayerParams,
                     RoundMode, build_decay_table_int, delta_t_max, quantize_to_int,
@@ -34,7 +35,7 @@ def __getattr__(name):  # the CUDA-backed objects load the library lazily
 __all__ = ["REFERENCE_FIELDS", "QuantSplitOutput", "QuantizedModel", "check_quantized",
            "load_quantized", "load_weights", "network_from_dict", "network_to_dict",
            "quant_forward_split", "reference_arrays", "run_until_fits", "save_quantized",
-           "save_weights", "Capacity", "ConvLayer", "ConvSpec", "EventStream", "FCLayer", "FCSpec", "GrowthPolicy",
+           "save_weights", "Capacity", "ConvLayer", "ConvQueueStructure", "ConvSpec", "FCQueueStructure", "EventStream", "FCLayer", "FCSpec", "GrowthPolicy",
            "FloatB200Backend", "FloatLayerResult", "InputEvents", "LayerDiag", "LayerOutput", "MAX_REGISTER_BITS", "MAX_SHIFT_BITS",
            "Network", "NetworkPlan", "OverflowMode", "PAD_TIME", "QuantB200Backend",
            "QuantizedLayerParams", "RoundMode", "build_decay_table_int", "check_layer_connections",

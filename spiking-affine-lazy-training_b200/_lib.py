@@ -91,6 +91,8 @@ _SIGS = {
                                      ctypes.c_size_t, _vp]),
     "salt_quant_scan_dense": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                      _vp, _vp]),
+    "salt_quant_scan_dense_trace": (_i32, [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                           _vp, _vp, _vp, _vp]),
     "salt_network_create": (_i32, [_vp, _i32, _vp]),
     "salt_network_destroy": (_i32, [_vp]),
     "salt_network_workspace_size": (_i32, [_vp, _i32, _i32, _vp]),
@@ -114,6 +116,29 @@ _SIGS = {
     "salt_float_fc_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "salt_float_fc_layer_forward": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                            ctypes.c_size_t, _vp]),
+    "salt_malloc": (_i32, [ctypes.c_size_t, _vp, _vp]),
+    "salt_free": (_i32, [_vp, _vp]),
+    "salt_host_alloc": (_i32, [ctypes.c_size_t, _vp]),
+    "salt_host_free": (_i32, [_vp]),
+    "salt_memcpy_async": (_i32, [_vp, _vp, ctypes.c_size_t, _vp]),
+    "salt_memset_async": (_i32, [_vp, _i32, ctypes.c_size_t, _vp]),
+    "salt_device_count": (_i32, [_vp]),
+    "salt_set_device": (_i32, [_i32]),
+    "salt_get_device": (_i32, [_vp]),
+    "salt_device_synchronize": (_i32, []),
+    "salt_stream_create": (_i32, [_vp]),
+    "salt_stream_destroy": (_i32, [_vp]),
+    "salt_stream_synchronize": (_i32, [_vp]),
+    "salt_stream_wait_event": (_i32, [_vp, _vp]),
+    "salt_event_create": (_i32, [_i32, _vp]),
+    "salt_event_destroy": (_i32, [_vp]),
+    "salt_event_record": (_i32, [_vp, _vp]),
+    "salt_event_synchronize": (_i32, [_vp]),
+    "salt_event_elapsed_ms": (_i32, [_vp, _vp, _vp]),
+    "salt_graph_begin_capture": (_i32, [_vp]),
+    "salt_graph_end_capture": (_i32, [_vp, _vp]),
+    "salt_graph_launch": (_i32, [_vp, _vp]),
+    "salt_graph_destroy": (_i32, [_vp]),
     "salt_last_error": (ctypes.c_char_p, []),
     "salt_version": (ctypes.c_char_p, []),
     "salt_launch_counter": (ctypes.c_int64, [_i32]),

@@ -8,8 +8,8 @@ Two entry levels, both on the CUDA kernels of libsalt_b200 (no CPU fallback):
   (layer.neuron_delta_t / layer.gather_weight_codes) and runs the integer recurrence on the GPU.
 * ``forward_layer`` / ``run_network`` / ``compile`` — the fused per-layer pipeline (fan-out,
   stable bucketing, recurrence, compaction, diagnostics) that replaces ConvLayer.forward /
-  FCLayer.forward / run_network (salt_core/layers/conv.py:209-234, fc.py:385-402,
-  network.py:193-222) without materialising any (n, L) array.
+  FCLayer.forward / run_network (salt_core/layers/conv.py:124-149, layers/fc.py:84-101,
+  network.py:93-122) without materialising any (n, L) array.
 """
 from __future__ import annotations
 
@@ -68,7 +68,7 @@ class ScanOutput(NamedTuple):
 
 
 class NetworkOutput(NamedTuple):
-    """salt_core/network.py:157-167, batched (leading batch axis on every array)."""
+    """salt_core/network.py:57-67, batched (leading batch axis on every array)."""
     results: tuple
     diags: tuple
     traces: tuple | None
@@ -272,7 +272,7 @@ class QuantB200Backend:
 
     def run_network(self, layers, weights, input_stream: EventStream, *, trace: bool = False,
                     keep_streams: bool = False) -> NetworkOutput:
-        """network.py:193-222 on the device; intermediate streams never leave the GPU.
+        """network.py:93-122 on the device; intermediate streams never leave the GPU.
         trace=True also returns each layer's LayerForwardTrace (network.py:93-122)."""
         single = np.ndim(input_stream.event_times) == 1
         cur = DeviceStream.from_host(input_stream)
@@ -317,23 +317,30 @@ class QuantB200Backend:
 
     # ------------------------------------------------------------ Backend.scan plug-in
     def scan(self, layer, structure, params, event_gain, *, trace: bool) -> ScanOutput:
-        """salt_core/quant/backend.py:31-53 on materialised queues, integer scan on the GPU."""
-        if trace:
-            raise NotImplementedError("trace=True is not supported by the B200 dense scan")
+        """salt_core/quant/backend.py:31-53 on materialised queues, integer scan on the GPU.
+        The layer supplies the queue's Δt and weight codes through its ScanLayer accessors
+        (neuron_delta_t, gather_weight_codes); event_gain is unused (the integer path's gain is
+        1).  trace=True adds v_steps, the register after every column, and pointer_steps, the
+        column index (quant/backend.py:41-43)."""
         check_weight_codes(params.q)
         delta_t = np.asarray(layer.neuron_delta_t(structure), dtype=np.float32)
         a_int, is_identity = apply_decay_table_int(delta_t, params.decay_table_int)
         q_int = np.asarray(layer.gather_weight_codes(structure, params.q), dtype=np.int32)
         res = self.scan_dense(a_int, is_identity, q_int, params.v_th_int, f_a=params.f_a,
                               f_V=params.f_V, i_V=params.i_V,
-                              overflow_mode=getattr(params, "overflow_mode", "wrap"))
+                              overflow_mode=getattr(params, "overflow_mode", "wrap"),
+                              trace=trace)
+        v_steps = None
+        if trace:
+            res, v_steps = res
         return ScanOutput(result=res, spike_gain=np.ones_like(res.spike_mask, dtype=np.float32),
-                          extra_steps_needed=np.zeros((), np.int32), v_steps=None,
-                          pointer_steps=None)
+                          extra_steps_needed=np.zeros((), np.int32), v_steps=v_steps,
+                          pointer_steps=res.spike_event_idx if trace else None)
 
     def scan_dense(self, a_int, is_identity, q_int, v_th_int, *, f_a, f_V, i_V,
-                   overflow_mode="wrap") -> DenseQuantLayerResult:
-        """quant/scan.py:65-80 run_layer on the GPU."""
+                   overflow_mode="wrap", trace: bool = False):
+        """quant/scan.py:65-80 run_layer on the GPU; with trace=True, run_layer_traced
+        (:83-94): returns (result, v_steps (n, L))."""
         require_cuda()
         check_bit_widths(int(f_a), int(f_V), int(i_V))
         a = np.ascontiguousarray(a_int, dtype=np.int32)
@@ -349,15 +356,22 @@ class QuantB200Backend:
         mask = torch.empty((n, L), dtype=torch.uint8, device="cuda")
         ovf = torch.empty((n, L), dtype=torch.uint8, device="cuda")
         vf, lo, hi = (torch.empty((n,), dtype=torch.int32, device="cuda") for _ in range(3))
-        _lib.check(_lib.lib().salt_quant_scan_dense(
-            _lib.byref(qd), n, L, ptr(a_d), ptr(id_d), ptr(q_d), ptr(vth_d), ptr(mask), ptr(ovf),
-            ptr(vf), ptr(lo), ptr(hi), current_stream()))
+        args = (_lib.byref(qd), n, L, ptr(a_d), ptr(id_d), ptr(q_d), ptr(vth_d), ptr(mask),
+                ptr(ovf), ptr(vf), ptr(lo), ptr(hi))
+        steps = None
+        if trace:
+            steps = torch.empty((n, L), dtype=torch.int32, device="cuda")
+            _lib.check(_lib.lib().salt_quant_scan_dense_trace(*args, ptr(steps),
+                                                              current_stream()))
+        else:
+            _lib.check(_lib.lib().salt_quant_scan_dense(*args, current_stream()))
         m = mask.cpu().numpy().astype(bool)
-        return DenseQuantLayerResult(spike_mask=m,
-                                     spike_event_idx=np.broadcast_to(np.arange(L), (n, L)),
-                                     v_final=vf.cpu().numpy(), overflowed=ovf.cpu().numpy() != 0,
-                                     v_unfitted_min=lo.cpu().numpy(),
-                                     v_unfitted_max=hi.cpu().numpy())
+        res = DenseQuantLayerResult(spike_mask=m,
+                                    spike_event_idx=np.broadcast_to(np.arange(L), (n, L)),
+                                    v_final=vf.cpu().numpy(), overflowed=ovf.cpu().numpy() != 0,
+                                    v_unfitted_min=lo.cpu().numpy(),
+                                    v_unfitted_max=hi.cpu().numpy())
+        return (res, steps.cpu().numpy()) if trace else res
 
     # ------------------------------------------------------------ compiled network
     def compile(self, layers, weights, batch: int, in_capacity: int):

@@ -1,7 +1,7 @@
 // Integer conv layer pipeline for B200 (sm_100a).
 //
 // Replaces, for a batch of samples, ConvLayer.forward with QuantBackend
-// (salt_core/layers/conv.py:209-234): queue construction (connectivity/conv.py:128-172), the
+// (salt_core/layers/conv.py:124-149): queue construction (connectivity/conv.py:128-172), the
 // integer LIF scan over every queue column (quant/scan.py:97-132), spike compaction into the
 // next EventStream (stream.py:24-64, :84-100) and the layer diagnostics (layers/base.py:73-79).
 //

@@ -1,6 +1,6 @@
 // Integer FC layer for B200 (sm_100a).
 //
-// Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:385-402): every output
+// Replaces FCLayer.forward with QuantBackend (salt_core/layers/fc.py:84-101): every output
 // neuron scans the whole input stream (connectivity/fc.py:20-33 — Δt against the previous
 // entry, the first against t=0, pads masked to Δt=0 and weight 0), applying
 // quant/scan.py:22-52 per entry; spikes leave as per-event neuron bitmasks and are compacted

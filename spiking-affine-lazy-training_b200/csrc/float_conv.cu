@@ -4,7 +4,7 @@
 // build_conv_structure (connectivity/conv.py:128-172, the first max_queue_len candidates of each
 // output position in event order, then the catch-up column and identity columns of :102-125),
 // conv_float_values (:187-206: a = (1 - 1/tau)^Δt per position, b = w[oc, c, ky, kx] times the
-// event gain on real columns), the chunked scan of float/scan.py:100-131 with process_chunk
+// event gain on real columns), the chunked scan of float/scan.py:67-116 with process_chunk
 // (float/affine.py:99-126), and the spike_step_upper_bound need (affine.py:57-88).  The output
 // stream goes through the integer conv layer's compaction kernels (same per-event spike words).
 //
@@ -34,7 +34,7 @@ __device__ __forceinline__ float key_float(int32_t k) {
   return __int_as_float(k >= 0 ? k : k ^ 0x7fffffff);
 }
 
-// One neuron's chunked scan, streamed column by column (float/scan.py:100-131).
+// One neuron's chunked scan, streamed column by column (float/scan.py:67-116).
 struct ChunkLane {
   float v0 = 0.0f, A = 1.0f, B = 0.0f, vs = 0.0f;  // potential at the chunk start, prefix map
   float vmax = -INFINITY, vmin = INFINITY;         // over the potentials after each step
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kFConvThreads) fconv_scan(ConvLaunch P, FConvA
                                         X.max_steps);
     next_col = nr + 1;
   }
-  // trace time of an identity step starting at column p (trace.py:43-60 resolve_ms_conv)
+  // trace time of an identity step starting at column p (trace.py:40-55 resolve_ms_conv)
   const float nan = __int_as_float(0x7fc00000);
   auto ms_at = [&](int32_t p) { return p >= nr ? nan : tlast; };
   if (act) s.finish(next_col, C, X.max_steps, ms_at);
@@ -318,7 +318,7 @@ __global__ void ffc_trace(FTraceArgs T) {
     s.column(col, a, w, t, T.v_th, T.C, T.max_steps);
   }
   const float nan = __int_as_float(0x7fc00000);
-  // trace.py:24-40 resolve_ms_fc: idle from n_real on, times clipped to the stream
+  // trace.py:25-37 resolve_ms_fc: idle from n_real on, times clipped to the stream
   auto ms_at = [&](int32_t p) {
     return p >= n_in ? nan : T.in.time(b, p < E - 1 ? p : E - 1, n_eff);
   };

@@ -598,7 +598,7 @@ __global__ void __launch_bounds__(128) ffc_fixup(FloatLaunch P) {
 
 // ------------------------------------------------------------------ 3. exact step accounting
 
-// float/scan.py:100-131 for the groups that ffc_fixup flagged: per neuron, the number of
+// float/scan.py:67-116 for the groups that ffc_fixup flagged: per neuron, the number of
 // events in the open step (phase) and the steps used; a step ends at a fire or after C
 // events, and once max_steps steps have ended the remaining events are dropped.
 template <bool GAIN>

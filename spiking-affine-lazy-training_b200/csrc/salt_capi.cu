@@ -95,8 +95,8 @@ struct FinishArgs {
   int32_t half;  // 2^(i_V + f_V - 1): the register range is [-half, half)
 };
 
-// Per-sample diagnostics and Capacity.fits (salt_core/capacity.py:60-63; layers/conv.py:222-226,
-// layers/fc.py:393-395).
+// Per-sample diagnostics and Capacity.fits (salt_core/capacity.py:60-63; layers/conv.py:137-141,
+// layers/fc.py:92-94).
 __global__ void layer_finish(FinishArgs A, int32_t* out_nreal, salt_layer_stats st) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= A.batch) return;
@@ -134,11 +134,13 @@ __global__ void fits_and(const int32_t* __restrict__ per_layer, int n_layers, in
 }
 
 // quant/scan.py:97-132 on materialised (n, L) inputs: one thread per neuron, every column.
+// v_steps (optional): the register after each column (run_layer_traced, quant/scan.py:83-94).
 __global__ void dense_scan(QuantCfg qc, int32_t n, int32_t L, const int32_t* __restrict__ a_int,
                            const uint8_t* __restrict__ is_id, const int32_t* __restrict__ q_int,
                            const int32_t* __restrict__ vth, uint8_t* __restrict__ mask,
                            uint8_t* __restrict__ ovf_out, int32_t* __restrict__ v_final,
-                           int32_t* __restrict__ vmin, int32_t* __restrict__ vmax) {
+                           int32_t* __restrict__ vmin, int32_t* __restrict__ vmax,
+                           int32_t* __restrict__ v_steps) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   int32_t v = 0, lo = 0, hi = 0;
@@ -154,6 +156,7 @@ __global__ void dense_scan(QuantCfg qc, int32_t n, int32_t L, const int32_t* __r
     hi = max(hi, u);
     if (mask) mask[e] = spike;
     if (ovf_out) ovf_out[e] = ovf;
+    if (v_steps) v_steps[e] = v;
   }
   v_final[i] = v;
   vmin[i] = lo;
@@ -775,6 +778,167 @@ struct salt_network {
 
 extern "C" {
 
+// ---------------------------------------------------------------- runtime plumbing
+
+// The current device's default memory pool keeps what cudaFreeAsync returns instead of handing
+// it back to the driver at the next synchronisation (a per-process pool attribute).
+static salt_status keep_pool_cached() {
+  int dev = 0;
+  SALT_CUDA(cudaGetDevice(&dev));
+  static thread_local uint64_t done_mask = 0;
+  if (dev < 64 && (done_mask >> dev) & 1u) return SALT_OK;
+  cudaMemPool_t pool;
+  SALT_CUDA(cudaDeviceGetDefaultMemPool(&pool, dev));
+  uint64_t keep = UINT64_MAX;
+  SALT_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  if (dev < 64) done_mask |= uint64_t(1) << dev;
+  return SALT_OK;
+}
+
+salt_status salt_malloc(size_t bytes, void* stream, void** ptr) {
+  if (!ptr) return fail(SALT_BAD_ARG, "salt_malloc: ptr is NULL");
+  *ptr = nullptr;
+  if (bytes == 0) return SALT_OK;
+  salt_status rc = keep_pool_cached();
+  if (rc) return rc;
+  SALT_CUDA(cudaMallocAsync(ptr, bytes, (cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_free(void* ptr, void* stream) {
+  if (ptr) SALT_CUDA(cudaFreeAsync(ptr, (cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_host_alloc(size_t bytes, void** ptr) {
+  if (!ptr) return fail(SALT_BAD_ARG, "salt_host_alloc: ptr is NULL");
+  *ptr = nullptr;
+  SALT_CUDA(cudaHostAlloc(ptr, bytes ? bytes : 1, cudaHostAllocPortable | cudaHostAllocMapped));
+  return SALT_OK;
+}
+
+salt_status salt_host_free(void* ptr) {
+  if (ptr) SALT_CUDA(cudaFreeHost(ptr));
+  return SALT_OK;
+}
+
+salt_status salt_memcpy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return SALT_OK;
+  if (!dst || !src) return fail(SALT_BAD_ARG, "salt_memcpy_async: NULL pointer");
+  SALT_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_memset_async(void* ptr, int32_t value, size_t bytes, void* stream) {
+  if (bytes == 0) return SALT_OK;
+  if (!ptr) return fail(SALT_BAD_ARG, "salt_memset_async: NULL pointer");
+  SALT_CUDA(cudaMemsetAsync(ptr, value, bytes, (cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_device_count(int32_t* count) {
+  if (!count) return fail(SALT_BAD_ARG, "salt_device_count: NULL");
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  *count = e == cudaSuccess ? n : 0;
+  if (e != cudaSuccess) cudaGetLastError();  // no driver or no device: report 0 devices
+  return SALT_OK;
+}
+
+salt_status salt_set_device(int32_t device) {
+  SALT_CUDA(cudaSetDevice(device));
+  return SALT_OK;
+}
+
+salt_status salt_get_device(int32_t* device) {
+  int d = 0;
+  SALT_CUDA(cudaGetDevice(&d));
+  *device = d;
+  return SALT_OK;
+}
+
+salt_status salt_device_synchronize(void) {
+  SALT_CUDA(cudaDeviceSynchronize());
+  return SALT_OK;
+}
+
+salt_status salt_stream_create(void** stream) {
+  cudaStream_t s;
+  SALT_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  *stream = (void*)s;
+  return SALT_OK;
+}
+
+salt_status salt_stream_destroy(void* stream) {
+  if (stream) SALT_CUDA(cudaStreamDestroy((cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_stream_synchronize(void* stream) {
+  SALT_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_stream_wait_event(void* stream, void* event) {
+  SALT_CUDA(cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0));
+  return SALT_OK;
+}
+
+salt_status salt_event_create(int32_t timing, void** event) {
+  cudaEvent_t e;
+  SALT_CUDA(cudaEventCreateWithFlags(&e, timing ? cudaEventDefault : cudaEventDisableTiming));
+  *event = (void*)e;
+  return SALT_OK;
+}
+
+salt_status salt_event_destroy(void* event) {
+  if (event) SALT_CUDA(cudaEventDestroy((cudaEvent_t)event));
+  return SALT_OK;
+}
+
+salt_status salt_event_record(void* event, void* stream) {
+  SALT_CUDA(cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_event_synchronize(void* event) {
+  SALT_CUDA(cudaEventSynchronize((cudaEvent_t)event));
+  return SALT_OK;
+}
+
+salt_status salt_event_elapsed_ms(void* start, void* stop, float* ms) {
+  SALT_CUDA(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)stop));
+  return SALT_OK;
+}
+
+salt_status salt_graph_begin_capture(void* stream) {
+  if (!stream) return fail(SALT_BAD_ARG, "graph capture needs a non-default stream");
+  SALT_CUDA(cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal));
+  return SALT_OK;
+}
+
+salt_status salt_graph_end_capture(void* stream, void** graph_exec) {
+  cudaGraph_t g = nullptr;
+  SALT_CUDA(cudaStreamEndCapture((cudaStream_t)stream, &g));
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess)
+    return fail(SALT_CUDA_ERROR, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
+  *graph_exec = (void*)ex;
+  return SALT_OK;
+}
+
+salt_status salt_graph_launch(void* graph_exec, void* stream) {
+  SALT_CUDA(cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream));
+  return SALT_OK;
+}
+
+salt_status salt_graph_destroy(void* graph_exec) {
+  if (graph_exec) SALT_CUDA(cudaGraphExecDestroy((cudaGraphExec_t)graph_exec));
+  return SALT_OK;
+}
+
 const char* salt_last_error(void) { return g_err.c_str(); }
 const char* salt_version(void) { return "salt_b200 0.1 (sm_100a)"; }
 int64_t salt_launch_counter(int32_t reset) {
@@ -1177,21 +1341,41 @@ salt_status salt_fc_layer_forward(const salt_fc_desc* layer, const salt_quant_de
                          workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
-salt_status salt_quant_scan_dense(const salt_quant_desc* quant, int32_t n, int32_t L,
-                                  const int32_t* a_int, const uint8_t* is_identity,
-                                  const int32_t* q_int, const int32_t* vth, uint8_t* spike_mask,
-                                  uint8_t* overflowed, int32_t* v_final, int32_t* vmin,
-                                  int32_t* vmax, void* stream) {
+static salt_status dense_scan_impl(const salt_quant_desc* quant, int32_t n, int32_t L,
+                                   const int32_t* a_int, const uint8_t* is_identity,
+                                   const int32_t* q_int, const int32_t* vth, uint8_t* spike_mask,
+                                   uint8_t* overflowed, int32_t* v_final, int32_t* vmin,
+                                   int32_t* vmax, int32_t* v_steps, cudaStream_t stream) {
   salt_status rc = check_quant(quant);
   if (rc) return rc;
   if (n < 1 || L < 1 || !a_int || !is_identity || !q_int || !v_final || !vmin || !vmax ||
       (quant->has_vth && !vth))
     return fail(SALT_BAD_ARG, "dense scan: bad sizes or NULL pointers");
-  dense_scan<<<(unsigned)((n + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
+  dense_scan<<<(unsigned)((n + 127) / 128), 128, 0, stream>>>(
       make_qc(quant), n, L, a_int, is_identity, q_int, quant->has_vth ? vth : nullptr, spike_mask,
-      overflowed, v_final, vmin, vmax);
+      overflowed, v_final, vmin, vmax, v_steps);
   SALT_LAUNCHED("dense_scan");
   return SALT_OK;
+}
+
+salt_status salt_quant_scan_dense(const salt_quant_desc* quant, int32_t n, int32_t L,
+                                  const int32_t* a_int, const uint8_t* is_identity,
+                                  const int32_t* q_int, const int32_t* vth, uint8_t* spike_mask,
+                                  uint8_t* overflowed, int32_t* v_final, int32_t* vmin,
+                                  int32_t* vmax, void* stream) {
+  return dense_scan_impl(quant, n, L, a_int, is_identity, q_int, vth, spike_mask, overflowed,
+                         v_final, vmin, vmax, nullptr, (cudaStream_t)stream);
+}
+
+salt_status salt_quant_scan_dense_trace(const salt_quant_desc* quant, int32_t n, int32_t L,
+                                        const int32_t* a_int, const uint8_t* is_identity,
+                                        const int32_t* q_int, const int32_t* vth,
+                                        uint8_t* spike_mask, uint8_t* overflowed,
+                                        int32_t* v_final, int32_t* vmin, int32_t* vmax,
+                                        int32_t* v_steps, void* stream) {
+  if (!v_steps) return fail(SALT_BAD_ARG, "dense scan trace: v_steps is NULL");
+  return dense_scan_impl(quant, n, L, a_int, is_identity, q_int, vth, spike_mask, overflowed,
+                         v_final, vmin, vmax, v_steps, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------- network plan

@@ -27,7 +27,7 @@ constexpr int kScanSmem = 33;        // ints of shared memory block_exclusive_sc
 __host__ __device__ __forceinline__ size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
 struct ConvLaunch {
-  // geometry (salt_core/layers/conv.py:107-167)
+  // geometry (salt_core/layers/conv.py:23-91)
   int32_t ic, h_in, w_in, hw_in, oc, k, s, p, h_out, w_out, n_sp;
   int64_t n_neurons;
   int32_t ncand, nslots;      // candidates per axis (k-1)//s+1 and per event (ncand^2)

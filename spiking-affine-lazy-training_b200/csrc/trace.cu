@@ -1,10 +1,10 @@
 // Per-column traces of the integer layer scan (the analysis path, not the hot path).
 //
 // Replaces QuantBackend.scan with trace=True (salt_core/quant/backend.py:31-53 calling
-// run_layer_traced quant/scan.py:83-94) together with the event times of trace.py:24-60
+// run_layer_traced quant/scan.py:83-94) together with the event times of trace.py:25-55
 // (resolve_ms_conv / resolve_ms_fc with pointer = column): for every neuron, the register after
 // each of its L queue columns, whether it fired there and the time of the column's event, plus a
-// per-neuron record of its first overflowing column (example/quant_run.py:191-223 reads those
+// per-neuron record of its first overflowing column (example/quant_run.py:189-214 reads those
 // for overflow forensics).
 //
 // One thread per (sample, neuron) rebuilds that neuron's queue straight from the stream: the

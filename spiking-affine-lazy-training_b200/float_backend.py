@@ -1,13 +1,13 @@
 """FloatB200Backend: the float forward (FloatBackend) of FC and conv layers on B200.
 
 Mirrors FCLayer.forward / ConvLayer.forward with FloatBackend (salt_core/layers/fc.py:84-106,
-layers/conv.py:124-149, float/backend.py:16-31, float/scan.py:34-131, float/affine.py:57-126,
+layers/conv.py:124-149, float/backend.py:16-31, float/scan.py:34-116, float/affine.py:57-126,
 connectivity/conv.py:128-206, stream.py:67-100) for the forward values:
 ``FloatLayerResult.v_final``, the output EventStream (gain 1 on every real entry, the forward value
 of s_spike) and LayerDiag with the reference's ``needed``.  FC layers run
 ``salt_float_fc_layer_forward``, conv layers ``salt_float_conv_layer_forward`` (libsalt_b200,
 include/salt_b200.h); no CPU fallback.  ``trace=True`` adds the per-step LayerForwardTrace
-(trace.py:13-60) and ``v_range=True`` each layer's per-(sample, channel) potential extremes over all
+(trace.py:13-55) and ``v_range=True`` each layer's per-(sample, channel) potential extremes over all
 steps, which calibration (quant/calibrate.py) reduces to M.
 
 Extension beyond the reference API: an FC layer's ``tau`` may be given per neuron (an (n_out,)
@@ -36,7 +36,7 @@ except ImportError:  # pragma: no cover
 
 
 class FloatLayerResult(NamedTuple):
-    """Forward values of float/scan.py:10-16, batched.  The per-step arrays of the reference
+    """Forward values of float/scan.py:15-22, batched.  The per-step arrays of the reference
     (spike_mask, spike_event_idx, s_spike, s_value of shape (n, max_steps)) carry no more than the
     output stream does in a forward pass (s_spike = s_value = spike_mask there), so the layer
     returns the stream instead; spike_count = Σ spike_mask."""
@@ -45,7 +45,7 @@ class FloatLayerResult(NamedTuple):
 
 
 class NetworkOutput(NamedTuple):
-    """salt_core/network.py:157-167 for a chain of float layers, batched.  traces: per layer a
+    """salt_core/network.py:57-67 for a chain of float layers, batched.  traces: per layer a
     LayerForwardTrace (trace=True); v_ranges: per layer (v_max, v_min), each (B, channels)
     (v_range=True)."""
     results: tuple

@@ -22,6 +22,32 @@ def uniform_init(rng: np.random.Generator, shape, fan_in: int, init_k: float) ->
     return rng.uniform(-limit, limit, size=shape).astype(np.float32)
 
 
+class ConvQueueStructure(NamedTuple):
+    """A conv layer's materialised queue (salt_core/connectivity/conv.py:46-54), one row per
+    output position oy*w_out+ox, shared by every output channel; the input of the dense
+    Backend.scan plug-in.  Built by the caller (the reference builds it with XLA)."""
+    local_to_global_j: np.ndarray  # (n_spatial, L) int32; empty columns hold n_events
+    n_real_events: np.ndarray      # (n_spatial,) int32; may exceed L
+    delta_t: np.ndarray            # (n_spatial, L) float32 integer ms
+    tap_c: np.ndarray              # (n_spatial, L) int32, clamped kernel coordinates
+    tap_ky: np.ndarray
+    tap_kx: np.ndarray
+    n_input_events: int = 0
+
+
+class FCQueueStructure(NamedTuple):
+    """An FC layer's queue (salt_core/connectivity/fc.py:13-17): every neuron sees the stream."""
+    delta_t: np.ndarray            # (E,) float32; pads 0
+    source_idx: np.ndarray         # (E,) int
+    n_real_events: int
+
+
+def _jax_take(n: int, idx) -> np.ndarray:
+    """Gather indices as XLA resolves them: negative ones wrap once, then clamp into [0, n)."""
+    idx = np.asarray(idx, dtype=np.int64)
+    return np.clip(np.where(idx < 0, idx + n, idx), 0, n - 1)
+
+
 class LayerOutput(NamedTuple):
     """layers/base.py:65-70"""
     stream: Any       # EventStream (host) of the layer's output spikes
@@ -38,7 +64,7 @@ def _check_leading_axis(values, expected: int, what: str) -> None:
 
 @dataclass(frozen=True)
 class ConvLayer:
-    """salt_core/layers/conv.py:107-186.  Output geometry (h_in + 2p - k) // s + 1."""
+    """salt_core/layers/conv.py:23-187.  Output geometry (h_in + 2p - k) // s + 1."""
     name: str
     ic: int
     h_in: int
@@ -114,19 +140,39 @@ class ConvLayer:
     def scan_steps(self, structure=None) -> int:
         return base_scan_steps(self.max_queue_len, self.chunk_size) + self.max_extra_steps
 
+    # ScanLayer accessors of the dense Backend.scan plug-in (salt_core/backend.py:36-61)
+    def neuron_delta_t(self, structure) -> np.ndarray:
+        """(n_neurons, L): each position's Δt row, repeated for every output channel
+        (layers/conv.py:167-169, tile_channels of connectivity/conv.py:221-225)."""
+        return np.tile(np.asarray(structure.delta_t), (self.oc, 1))
+
+    def neuron_n_real(self, structure) -> np.ndarray:
+        """(n_neurons,): real taps per neuron (layers/conv.py:171-173)."""
+        return np.tile(np.asarray(structure.n_real_events), self.oc)
+
+    def gather_weight_codes(self, structure, q) -> np.ndarray:
+        """(n_neurons, L) int32: q[oc, tap_c, tap_ky, tap_kx] on real-tap columns, 0 elsewhere
+        (layers/conv.py:163-165 -> connectivity/conv.py:175-179, :210-219)."""
+        q = np.asarray(q).reshape(self.weight_shape)
+        tc, ky, kx = (np.asarray(getattr(structure, f)) for f in ("tap_c", "tap_ky", "tap_kx"))
+        n_sp, L = tc.shape
+        real = np.arange(L)[None, :] < np.asarray(structure.n_real_events)[:, None]
+        codes = q[:, tc, ky, kx]                       # (oc, n_sp, L)
+        return np.where(real[None], codes, 0).astype(np.int32).reshape(self.oc * n_sp, L)
+
     def with_chunk_size(self, chunk_size: int) -> "ConvLayer":
         return replace(self, chunk_size=chunk_size,
                        max_extra_steps=safe_extra_steps(self.max_queue_len, chunk_size))
 
     def forward(self, params, in_stream, *, backend=None, trace: bool = False) -> LayerOutput:
-        """layers/conv.py:209-234 on the B200 backend."""
+        """layers/conv.py:124-149 on the B200 backend."""
         from .backend import default_backend
         return (backend or default_backend()).forward_layer(self, params, in_stream, trace=trace)
 
 
 @dataclass(frozen=True)
 class FCLayer:
-    """salt_core/layers/fc.py:323-437."""
+    """salt_core/layers/fc.py:23-137."""
     name: str
     n_in: int
     n_out: int
@@ -179,18 +225,36 @@ class FCLayer:
     def scan_steps(self, stream_len: int) -> int:
         return base_scan_steps(stream_len, self.chunk_size) + self.max_extra_steps
 
+    # ScanLayer accessors of the dense Backend.scan plug-in (salt_core/backend.py:36-61)
+    def neuron_delta_t(self, structure) -> np.ndarray:
+        """(n_out, E): the stream's Δt, the same row for every neuron (layers/fc.py:117-120)."""
+        dt = np.asarray(structure.delta_t)
+        return np.broadcast_to(dt[None, :], (self.n_out, dt.shape[0]))
+
+    def neuron_n_real(self, structure) -> np.ndarray:
+        """(n_out,) (layers/fc.py:122-124)."""
+        return np.full(self.n_out, int(structure.n_real_events), np.int32)
+
+    def gather_weight_codes(self, structure, q) -> np.ndarray:
+        """(n_out, E) int32: q[:, source] on real events, 0 on pads (layers/fc.py:113-115 ->
+        connectivity/fc.py:54-61; sources resolved as XLA's gather does)."""
+        q = np.asarray(q).reshape(self.weight_shape)
+        src = _jax_take(self.n_in, structure.source_idx)
+        real = np.arange(src.shape[0]) < int(structure.n_real_events)
+        return np.where(real[None, :], q[:, src], 0).astype(np.int32)
+
     def with_chunk_size(self, chunk_size: int) -> "FCLayer":
         return replace(self, chunk_size=chunk_size)
 
     def forward(self, params, in_stream, *, backend=None, trace: bool = False) -> LayerOutput:
-        """layers/fc.py:385-402 on the B200 backend."""
+        """layers/fc.py:84-101 on the B200 backend."""
         from .backend import default_backend
         return (backend or default_backend()).forward_layer(self, params, in_stream, trace=trace)
 
 
 @dataclass(frozen=True)
 class ConvSpec:
-    """layers/conv.py:274-296"""
+    """layers/conv.py:189-211"""
     oc: int
     k: int
     s: int
@@ -208,13 +272,13 @@ class ConvSpec:
 
 
 def conv(oc: int, k: int, s: int, p: int, *, name: str | None = None, **options) -> ConvSpec:
-    """layers/conv.py:299-301"""
+    """layers/conv.py:214-216"""
     return ConvSpec(oc=oc, k=k, s=s, p=p, name=name, options=options)
 
 
 @dataclass(frozen=True)
 class FCSpec:
-    """layers/fc.py:440-454"""
+    """layers/fc.py:139-153"""
     n_out: int
     name: str | None = None
     options: Mapping[str, Any] = field(default_factory=dict)
@@ -225,7 +289,7 @@ class FCSpec:
 
 
 def fc(n_out: int, *, name: str | None = None, **options) -> FCSpec:
-    """layers/fc.py:457-459"""
+    """layers/fc.py:156-158"""
     return FCSpec(n_out=n_out, name=name, options=options)
 
 

@@ -12,18 +12,18 @@ import numpy as np
 from .layers import ConvLayer, FCLayer
 from .stream import EventStream
 
-_MAX_EVENT_TIME = 2 ** 31  # network.py:123
+_MAX_EVENT_TIME = 2 ** 31  # network.py:23
 
 
 class InputEvents(NamedTuple):
-    """network.py:126-154.  Single sample: (E,) arrays and a scalar; batched: (B, E), (B,)."""
+    """network.py:26-54.  Single sample: (E,) arrays and a scalar; batched: (B, E), (B,)."""
     event_times: np.ndarray
     source_idx: np.ndarray
     n_real_events: np.ndarray
 
     @staticmethod
     def checked(event_times, source_idx, n_real_events) -> "InputEvents":
-        """Host check of the real events' times (network.py:133-154): integer ms in
+        """Host check of the real events' times (network.py:33-54): integer ms in
         [0, 2^31), non-decreasing.  Raises ValueError otherwise."""
         times = np.asarray(event_times)
         n_real = np.asarray(n_real_events)
@@ -41,7 +41,7 @@ class InputEvents(NamedTuple):
 
 
 def _check_connected(out_shape, in_shape, out_name, in_name) -> None:
-    """network.py:170-184"""
+    """network.py:70-84"""
     out_shape, in_shape = tuple(out_shape), tuple(in_shape)
     connected = (math.prod(out_shape) == in_shape[0]) if len(in_shape) == 1 else out_shape == in_shape
     if connected:
@@ -53,13 +53,13 @@ def _check_connected(out_shape, in_shape, out_name, in_name) -> None:
 
 
 def check_layer_connections(layers: Sequence) -> None:
-    """network.py:187-190"""
+    """network.py:87-90"""
     for prev, nxt in zip(layers, layers[1:]):
         _check_connected(prev.output_shape, nxt.input_shape, prev.name, nxt.name)
 
 
 def input_stream(raw: InputEvents) -> EventStream:
-    """network.py:265-271: source_idx as int32, event_gain all ones."""
+    """network.py:165-171: source_idx as int32, event_gain all ones."""
     t = np.asarray(raw.event_times, dtype=np.float32)
     return EventStream(t, np.asarray(raw.source_idx, dtype=np.int32), np.ones_like(t),
                        np.asarray(raw.n_real_events, dtype=np.int32))
@@ -67,7 +67,7 @@ def input_stream(raw: InputEvents) -> EventStream:
 
 def run_network(layers: Sequence, weights: Sequence, input_stream: EventStream, *, backend=None,
                 trace: bool = False, keep_streams: bool = False):
-    """network.py:193-222 — chain the layers; fits = AND of every layer's Capacity.fits."""
+    """network.py:93-122 — chain the layers; fits = AND of every layer's Capacity.fits."""
     from .backend import default_backend
     check_layer_connections(layers)
     return (backend or default_backend()).run_network(layers, weights, input_stream, trace=trace,
@@ -76,7 +76,7 @@ def run_network(layers: Sequence, weights: Sequence, input_stream: EventStream, 
 
 @dataclass(frozen=True)
 class Network:
-    """network.py:225-287"""
+    """network.py:125-187"""
     input_shape: tuple[int, ...]
     layers: tuple
 
@@ -115,7 +115,7 @@ class Network:
 
     def apply_batched(self, weights, raw_batch: InputEvents, *, backend=None, trace: bool = False,
                       keep_streams: bool = False):
-        """Batched forward (the reference vmaps apply over axis 0, network.py:279-283)."""
+        """Batched forward (the reference vmaps apply over axis 0, network.py:179-183)."""
         if np.ndim(raw_batch.event_times) != 2:
             raise ValueError("apply_batched expects (B, E) event arrays")
         return run_network(self.layers, weights, self.input_stream(raw_batch), backend=backend,

@@ -1,6 +1,6 @@
 """Whole-split integer forward, capacity growth and the reference-file check, on the B200 backend.
 
-Mirrors example/quant_run.py:58-132 and the check of example/quantize.py:306-330: a split of
+Mirrors example/quant_run.py:54-136 and the check of example/quantize.py:306-330: a split of
 input samples runs through the quantised network batch by batch; the per-sample fields that the
 reference records in ``reference.npz`` (REFERENCE_FIELDS) come back for comparison, and
 ``run_until_fits`` grows the capacities until no sample overflows.  Capacities are runtime sizes
@@ -20,7 +20,7 @@ _ARRAY_FIELDS = REFERENCE_FIELDS + ("v_unfitted_min", "v_unfitted_max")
 
 
 class QuantSplitOutput(NamedTuple):
-    """example/quant_run.py:53-63, N samples."""
+    """example/quant_run.py:54-64, N samples."""
     v_final_int: np.ndarray     # (N, n_out) output-layer registers
     preds: np.ndarray           # (N,)
     spike_count: np.ndarray     # (N, n_layers)
@@ -89,7 +89,7 @@ def grown_for_needed(layers, policies, needed: dict) -> list:
 def run_until_fits(network: Network, params, round_mode, raw: InputEvents, batch_size: int,
                    policies: dict | None = None, *, backend=None, max_rounds: int = 16
                    ) -> tuple[Network, QuantSplitOutput, int]:
-    """example/quant_run.py:122-132: rerun with grown capacities while a sample overflows.
+    """example/quant_run.py:122-136: rerun with grown capacities while a sample overflows.
     Returns (the network that fits, its output, the number of reruns)."""
     policies = policies or {l.name: GrowthPolicy() for l in network.layers}
     n = 0
@@ -134,18 +134,18 @@ def check_quantized(model_path, reference_path, raw: InputEvents, batch_size: in
 
 
 # ---------------------------------------------------------------- overflow analysis
-# example/quant_run.py:134-258
+# example/quant_run.py:139-240
 
 MAX_OVERFLOW_EVENTS = 50
 
 
 def with_extra_i_V(params, extra: list[int]) -> list:
-    """example/quant_run.py:138-140: each layer's i_V plus extra[i] bits."""
+    """example/quant_run.py:139-141: each layer's i_V plus extra[i] bits."""
     return [p._replace(i_V=p.i_V + e) for p, e in zip(params, extra)]
 
 
 def headroom_bits(params, out: QuantSplitOutput) -> list[float | None]:
-    """example/quant_run.py:143-155: bits between each layer's unfitted extremes and its
+    """example/quant_run.py:144-154: bits between each layer's unfitted extremes and its
     register range (negative: overflow); None when every value was 0."""
     import math
     res = []
@@ -158,7 +158,7 @@ def headroom_bits(params, out: QuantSplitOutput) -> list[float | None]:
 def min_extra_bits(network: Network, params, round_mode, raw: InputEvents, batch_size: int,
                    policies: dict | None, out: QuantSplitOutput, *, backend=None
                    ) -> tuple[list[int], int]:
-    """example/quant_run.py:158-176: widen the most upstream overflowing layer by one bit and
+    """example/quant_run.py:157-174: widen the most upstream overflowing layer by one bit and
     rerun until no sample overflows.  Returns (extra bits per layer, reruns)."""
     extra = [0] * len(params)
     rounds = 0
@@ -177,7 +177,7 @@ def _neuron_position(layer, neuron: int) -> tuple[int, int, int]:
 
 def overflow_events(network: Network, params, round_mode, raw: InputEvents,
                     out: QuantSplitOutput, *, backend=None) -> list[dict]:
-    """example/quant_run.py:185-223: for each overflowing (sample, layer, neuron), its first
+    """example/quant_run.py:183-214: for each overflowing (sample, layer, neuron), its first
     overflowing column — the time, the register before and after it, whether it fired — and the
     neuron's unfitted extremes; at most MAX_OVERFLOW_EVENTS entries.  Each overflowing sample
     runs once more on the GPU with the layer traces' per-neuron records."""
@@ -215,7 +215,7 @@ def overflow_events(network: Network, params, round_mode, raw: InputEvents,
 
 def overflow_summary(network: Network, params, round_mode, raw: InputEvents, batch_size: int,
                      policies: dict | None, out: QuantSplitOutput, *, backend=None) -> dict:
-    """example/quant_run.py:226-258: overflowing samples per layer and headroom; without
+    """example/quant_run.py:217-240: overflowing samples per layer and headroom; without
     saturating layers also the fewest extra bits and where the overflows happen."""
     from .quant import OverflowMode
     names = [l.name for l in network.layers]

@@ -1,7 +1,7 @@
 """Data-parallel sample sharding across ranks (one process per GPU).
 
 Samples are independent (the reference vmaps the network over the batch,
-salt_core/network.py:279-283), so a batch is split into per-rank shards with no data-path
+salt_core/network.py:179-183), so a batch is split into per-rank shards with no data-path
 collective; the only exchange is the gather of the int32 logits (the last layer's v_final) back
 into the caller's sample order.
 

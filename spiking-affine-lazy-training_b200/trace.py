@@ -1,4 +1,4 @@
-"""Per-step trajectories of a forward (salt_core/trace.py:13-100).
+"""Per-step trajectories of a forward (salt_core/trace.py:13-81).
 
 ``forward_layer(..., trace=True)`` and ``run_network(..., trace=True)`` on the B200 integer
 backend fill ``LayerOutput.trace`` with a LayerForwardTrace computed by the trace kernels
@@ -13,7 +13,7 @@ import numpy as np
 
 
 class LayerForwardTrace(NamedTuple):
-    """trace.py:13-21: (n, L) per neuron and queue column (leading batch axis when batched).
+    """trace.py:13-22: (n, L) per neuron and queue column (leading batch axis when batched).
 
     spike_mask: the forward's spike mask.  v_steps: the register after each column (after the
     reset); the last column equals v_final.  event_ms: the time of each column's event, NaN for
@@ -24,7 +24,7 @@ class LayerForwardTrace(NamedTuple):
 
 
 class TraceSummary(TypedDict):
-    """trace.py:64-72"""
+    """trace.py:58-66"""
     n: int
     steps: int
     total_spikes: int
@@ -35,7 +35,7 @@ class TraceSummary(TypedDict):
 
 
 def summarize_trace_scalars(trace: LayerForwardTrace) -> TraceSummary:
-    """trace.py:75-88: one sample's one layer as scalars."""
+    """trace.py:69-81: one sample's one layer as scalars."""
     sm = np.asarray(trace.spike_mask)
     vs = np.asarray(trace.v_steps)
     ms = np.asarray(trace.event_ms)

@@ -4,7 +4,7 @@ src = c*H*W + y*W + x, integer-ms timestamps — shape configs 1-3).
 
 Every generator is deterministic given its seed (numpy PCG64).  Capacities that the
 configurations leave open are sized like the reference's run_until_fits
-(example/quant_run.py:122-132): run once with room to spare, then grow each knob to
+(example/quant_run.py:122-136): run once with room to spare, then grow each knob to
 ceil(1.5 x the largest need) (capacity.py GrowthPolicy factor 1.5), or to 4x the expected need
 where a configuration says so.
 """
@@ -230,6 +230,63 @@ def size_float_capacity(wl: FloatWorkload, backend, factor: float = 1.5) -> Floa
 
 
 CONFIGS = {1: config1, 2: config2, 3: config3, 4: config4, 5: config5}
+
+# Capacity knobs of the benchmark workloads at seed 0, per layer name, fixed so that the GPU arm,
+# the CPU reference arm and the parity tests run the same layers.  They are what size_capacities
+# gives for the full seed-0 batch: configurations 2 and 3 grow every knob to ceil(1.5 x the
+# largest need) until every sample fits (configuration 2's table was also reproduced by the same
+# loop on the CPU oracle); configuration 4 takes 4 x the expected need (queue: mean receptive-field
+# candidates per position; output: mean spike count), under which some samples' conv1 output is
+# truncated by design (154 of 256 fit).  Configuration 1 keeps its layer's own 8192.
+CAPACITY_TABLE = {
+    (1, 0): {"fc1": {"max_out_spikes": 8192}},
+    (2, 0): {"conv1": {"max_queue_len": 102, "max_out_spikes": 2},
+             "conv2": {"max_queue_len": 3, "max_out_spikes": 1},
+             "fc1": {"max_out_spikes": 1}},
+    (2, 1): {"conv1": {"max_queue_len": 107, "max_out_spikes": 5},
+             "conv2": {"max_queue_len": 3, "max_out_spikes": 1},
+             "fc1": {"max_out_spikes": 1}},
+    (3, 0): {"conv1": {"max_queue_len": 3752, "max_out_spikes": 23450},
+             "conv2": {"max_queue_len": 4467, "max_out_spikes": 10322},
+             "fc1": {"max_out_spikes": 1}},
+    (4, 0): {"conv1": {"max_queue_len": 274, "max_out_spikes": 36},
+             "conv2": {"max_queue_len": 2, "max_out_spikes": 1},
+             "conv3": {"max_queue_len": 2, "max_out_spikes": 1},
+             "conv4": {"max_queue_len": 2, "max_out_spikes": 1},
+             "fc1": {"max_out_spikes": 1}},
+}
+
+
+def with_capacities(wl: Workload, table: dict) -> Workload:
+    """The workload with each named layer's capacity knobs set from `table` (max_extra_steps
+    follows the reference's default for the new queue length)."""
+    layers = []
+    for layer in wl.network.layers:
+        knobs = dict(table.get(layer.name, {}))
+        if isinstance(layer, ConvLayer) and "max_queue_len" in knobs:
+            layer = replace(layer, max_extra_steps=None, **knobs)
+        elif knobs:
+            layer = replace(layer, **knobs)
+        layers.append(layer)
+    return replace(wl, network=wl.network.replace_layers(layers))
+
+
+def benchmark(config: int, seed: int = 0, batch: int | None = None, p1: int = 0) -> Workload:
+    """A benchmark configuration's seeded workload with the fixed capacities of CAPACITY_TABLE.
+    `batch` (configurations 3 and 4) keeps the first `batch` samples of the seed's batch: the
+    generators draw the parameters first and then sample after sample, so a smaller batch is a
+    prefix of the full one and fits the same capacities."""
+    kw = {}
+    if config in (3, 4) and batch is not None:
+        kw["batch"] = int(batch)
+    if config in (2, 3):
+        kw["p1"] = p1
+    wl = CONFIGS[config](seed=seed, **kw)
+    table = CAPACITY_TABLE.get((config, p1))
+    if table is None or seed != 0:
+        raise ValueError(f"no fixed capacities for configuration {config} (p1={p1}, seed={seed}); "
+                         "size them with size_capacities")
+    return with_capacities(wl, table)
 
 
 def candidates_per_event(layer: ConvLayer, src: np.ndarray) -> np.ndarray:

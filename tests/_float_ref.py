@@ -1,7 +1,7 @@
 """Independent float64 restatement of a float FC layer's sequential semantics (test-only).
 
 Runs v = a*v + b with fire-and-reset at every event and the chunk step accounting of
-salt_core/float/scan.py:100-131 (a step ends at a fire or after chunk_size events; after
+salt_core/float/scan.py:67-116 (a step ends at a fire or after chunk_size events; after
 max_steps steps the remaining events are dropped).  In float64 it serves as the exact-math
 yardstick: it reports, per neuron, how close any processed value came to v_th, so that tests can
 set apart the fire decisions that float32 rounding may legitimately flip: `first_near[o]` is the

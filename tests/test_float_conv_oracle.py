@@ -111,7 +111,7 @@ def test_trace_rows_end_at_v_final_and_mark_idle_steps():
 
 
 def test_calibration_ranges_match_hand_computation():
-    """test_quant_calibrate.py:13-66: per-channel (max, min) over steps and positions."""
+    """test_quant_calibrate.py:13-65: per-channel (max, min) over steps and positions."""
     from salt_b200.calibrate import merge_v_ranges, v_abs_max_per_channel, v_range_per_channel
     conv = S.ConvLayer(name="conv", ic=1, h_in=1, w_in=2, oc=2, k=1, s=1, p=0, init_k=5.0,
                        chunk_size=1, max_queue_len=3)

@@ -1,0 +1,163 @@
+"""Bit-exact parity on the benchmark configurations themselves, with the capacities the benchmark
+runs (workloads.CAPACITY_TABLE), against the CPU oracle — the regression loop of the reference
+(example/quant_run.py:67,71-103 records every REFERENCE_FIELDS entry of a split and
+example/quantize.py:306-330 compares them exactly).
+
+Configuration 1 and 2 run in full; configuration 3 as 64 samples of the benchmark's 4096-sample
+batch (its 32 heaviest and 32 others, the same rows the bench times); configuration 4 as 8
+samples at the stated 2x128x128 shapes with 4x capacities.  Per sample and layer the GPU must
+reproduce the oracle's v_final, output stream (times, sources, n_real), spike count, overflow
+flag, unfitted extremes, needed queue length and fits.  The native network plan (the benchmark's
+timed path) must give the same logits, per-layer statistics and fits.
+
+At the full configuration-3 size (4096 samples) the checks are size-independent: two forwards are
+bit-identical, every sample fits the committed capacities, and each sample's results do not depend
+on the batch it runs in (the full batch's rows equal those of the oracle-checked slices run on
+their own)."""
+from concurrent.futures import ThreadPoolExecutor
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import salt_b200 as S
+from salt_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+THREADS = max(1, min(16, os.cpu_count() or 1))
+
+
+def _oracle_rows(wl, rows):
+    layers = list(wl.network.layers)
+
+    def one(b):
+        return O.network_forward(layers, wl.params, wl.times[b], wl.src[b], int(wl.n_real[b]))
+
+    with ThreadPoolExecutor(THREADS) as ex:   # the oracle's ctypes calls release the GIL
+        return list(ex.map(one, rows))
+
+
+def _check_layerwise(wl, refs, rows):
+    """backend.run_network (per-layer device pipeline) against the oracle, every field."""
+    layers = list(wl.network.layers)
+    sub = wl.subset(rows)
+    out = S.QuantB200Backend("round").run_network(layers, wl.params,
+                                                  sub.network.input_stream(sub.raw()),
+                                                  keep_streams=True)
+    for i, b in enumerate(rows):
+        for li, (layer, ref) in enumerate(zip(layers, refs[i])):
+            where = f"sample {b} layer {layer.name}"
+            r, d, st = out.results[li], out.diags[li], out.streams[li]
+            np.testing.assert_array_equal(r.v_final[i], ref.v_final, err_msg=where)
+            assert int(r.spike_count[i]) == ref.spike_count, where
+            assert int(st.n_real_events[i]) == ref.n_real_events, where
+            np.testing.assert_array_equal(st.event_times[i], ref.event_times, err_msg=where)
+            np.testing.assert_array_equal(st.event_source_idx[i], ref.event_source_idx,
+                                          err_msg=where)
+            assert bool(r.overflowed[i]) == ref.any_overflow, where
+            assert int(r.v_unfitted_min[i]) == ref.vmin_all, where
+            assert int(r.v_unfitted_max[i]) == ref.vmax_all, where
+            if isinstance(layer, S.ConvLayer):
+                assert int(d.needed["max_queue_len"][i]) == ref.needed_queue, where
+            fits = bool(layer.capacity.fits(S.LayerDiag(
+                d.spike_count[i], d.firing_rate[i], {k: v[i] for k, v in d.needed.items()})))
+            assert fits == ref.fits, where
+        assert bool(out.fits[i]) == all(x.fits for x in refs[i]), f"sample {b} fits"
+    return out
+
+
+def _plan_rows(wl, rows=None):
+    """The benchmark's timed path (NetworkPlan.forward_device) on rows of the workload."""
+    import torch
+    sub = wl if rows is None else wl.subset(rows)
+    plan = S.QuantB200Backend("round").compile(list(wl.network.layers), wl.params,
+                                               batch=sub.batch, in_capacity=sub.times.shape[1])
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    logits, stats, fits = plan.forward_device(dev(sub.times), dev(sub.src),
+                                              dev(sub.n_real.astype(np.int32)))
+    res = (logits.cpu().numpy().copy(), stats.cpu().numpy().copy(), fits.cpu().numpy().copy())
+    plan.close()
+    return res
+
+
+def _check_plan(wl, refs, rows):
+    logits, stats, fits = _plan_rows(wl, rows)
+    for i, b in enumerate(rows):
+        np.testing.assert_array_equal(logits[i], refs[i][-1].v_final, err_msg=f"logits {b}")
+        for li, ref in enumerate(refs[i]):
+            where = f"plan sample {b} layer {li}"
+            assert stats[0, li, i] == ref.spike_count, where
+            assert bool(stats[1, li, i]) == ref.any_overflow, where
+            assert stats[2, li, i] == ref.vmin_all, where
+            assert stats[3, li, i] == ref.vmax_all, where
+            if isinstance(wl.network.layers[li], S.ConvLayer):
+                assert stats[4, li, i] == ref.needed_queue, where
+        assert bool(fits[i]) == all(x.fits for x in refs[i]), f"plan fits {b}"
+    return logits, stats, fits
+
+
+def test_config1_in_full():
+    wl = W.benchmark(1)
+    rows = list(range(wl.batch))
+    refs = _oracle_rows(wl, rows)
+    assert refs[0][0].spike_count > 0          # the single FC layer fires at v_th_int = 256
+    _check_layerwise(wl, refs, rows)
+    _check_plan(wl, refs, rows)
+
+
+@pytest.mark.parametrize("p1", [0, 1])
+def test_config2_in_full(p1):
+    """p1 = 0 is the stated geometry (FC 32*8*8); p1 = 1 the reference's production padding."""
+    wl = W.benchmark(2, p1=p1)
+    rows = list(range(wl.batch))
+    refs = _oracle_rows(wl, rows)
+    assert sum(r[0].spike_count for r in refs) > 0   # conv1 fires on some samples (rarely)
+    _check_layerwise(wl, refs, rows)
+    _check_plan(wl, refs, rows)
+
+
+def _config3_rows(wl, k=32):
+    n = np.minimum(wl.n_real, wl.times.shape[1])
+    heavy = np.argsort(-n, kind="stable")[:k]
+    others = np.setdiff1d(np.arange(0, wl.batch, wl.batch // k), heavy)[:k]
+    return sorted(int(b) for b in np.concatenate([heavy, others]))
+
+
+@pytest.fixture(scope="module")
+def config3():
+    return W.benchmark(3)
+
+
+def test_config3_slice_matches_oracle(config3):
+    rows = _config3_rows(config3)
+    refs = _oracle_rows(config3, rows)
+    _check_layerwise(config3, refs, rows)
+    _check_plan(config3, refs, rows)
+
+
+def test_config3_full_batch_properties(config3):
+    """Full 4096-sample batch: deterministic, everything fits the committed capacities, and the
+    oracle-checked slice's rows are the same inside the full batch as on their own."""
+    a = _plan_rows(config3)
+    b = _plan_rows(config3)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x, y)
+    logits, stats, fits = a
+    assert np.all(fits != 0), f"{int(np.sum(fits == 0))} samples do not fit"
+    rows = _config3_rows(config3)
+    l_s, s_s, f_s = _plan_rows(config3, rows)
+    np.testing.assert_array_equal(logits[rows], l_s)
+    np.testing.assert_array_equal(stats[:, :, rows], s_s)
+    np.testing.assert_array_equal(fits[rows], f_s)
+    assert np.mean(stats[0, 0] > 0) > 0.9   # the blob drives conv1 to fire on most samples
+
+
+def test_config4_samples_match_oracle():
+    """8 samples of the deep configuration (2x128x128, 50k-200k bursty events, four conv layers
+    with 4x the expected capacities: output truncation happens on these rows)."""
+    wl = W.benchmark(4, batch=8)
+    rows = list(range(wl.batch))
+    refs = _oracle_rows(wl, rows)
+    _check_layerwise(wl, refs, rows)
+    _check_plan(wl, refs, rows)

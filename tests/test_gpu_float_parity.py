@@ -1,13 +1,15 @@
 """GPU parity of the float FC layer (salt_float_fc_layer_forward) against the float oracle (the
 chunk-by-chunk restatement of salt_core/float) and the reference's own known answers.
 
-Tolerance: v_final within 1e-5 relative (atol 1e-5 for values near 0), identical spike sets and
-output streams.  A neuron's spikes may differ from the oracle's only after its value came within
-1e-4·v_th of the threshold in exact (float64) arithmetic, where float32 rounding (the oracle
-composes chunks in associative-scan order, the kernel runs events in order) may flip a fire
-decision; such neurons are bounded in number and their later values are not compared.  needed
-max_extra_steps may differ by one where Σb⁺/v_th sits on an integer (the reference sums in
-float32 in XLA's order)."""
+Tolerance (the north star's): v_final within 1e-5 relative (1e-6 absolute near 0), and identical
+spike sets except where a value lies within +-1e-6 * v_th of the threshold.  The kernel runs
+each chunk's events in order with fused multiply-adds where the reference composes the chunk's
+maps in associative-scan order, so float32 rounding may flip a fire decision only there: a
+neuron's spikes may differ from the oracle's only at or after an event whose exact (float64)
+value came within the band (oracle.float_seq64), and such a neuron's later values are not
+compared; every other neuron's v_final is.  There is no cap on their number: the band alone
+decides.  needed max_extra_steps may differ by one where sum(b+)/v_th sits on an integer (the
+reference sums in float32 in XLA's order)."""
 import json
 import os
 
@@ -16,7 +18,6 @@ import pytest
 
 import oracle as O
 import salt_b200 as S
-from _float_ref import sequential_float64
 from test_oracle_known_answers import check_float_result, float_layer_from_case
 
 pytestmark = pytest.mark.gpu
@@ -53,43 +54,59 @@ def _batch(seed, B, n_in, n_out, E, chunk, extra, t_max, w_sd, M=None, tau=20.0,
     return layer, w, t, s, nr, g, taus
 
 
-def _check_against_oracle(layer, w, t, s, nr, g, taus, out):
+BAND = 1e-6          # spike decisions may differ only within +-BAND * v_th of the threshold
+RTOL, ATOL = 1e-5, 1e-6
+
+
+def _ref_spike_times(ref, o, t):
+    if ref.spike_mask is not None:
+        return [float(t[j]) for j in ref.spike_event_idx[o][ref.spike_mask[o]]]
+    k = min(ref.n_real_events, ref.event_times.shape[0])
+    return sorted(float(x) for x in ref.event_times[:k][ref.event_source_idx[:k] == o])
+
+
+def _check_against_oracle(layer, w, t, s, nr, g, taus, out, dense=True, threads=1):
     gain_used = not np.all(g == 1.0)
     for b in range(t.shape[0]):
         gb = g[b] if gain_used else None
-        ref = O.float_fc_forward(layer, w, t[b], s[b], int(nr[b]), gain=gb, tau=taus)
-        _, _, _, first_near = sequential_float64(layer, w, t[b], s[b], int(nr[b]), gain=gb,
-                                                 tau=taus)
+        ref = O.float_fc_forward(layer, w, t[b], s[b], int(nr[b]), gain=gb, tau=taus,
+                                 dense=dense, threads=threads)
+        _, first_near = O.float_seq64(layer, w, t[b], s[b], int(nr[b]), gain=gb, tau=taus,
+                                      near=BAND)
+        E = len(t[b])
         vf = np.asarray(out.result.v_final[b])
         S_gpu = int(out.result.spike_count[b])
         k = min(S_gpu, layer.max_out_spikes)
         times = out.stream.event_times[b][:k]
         src = out.stream.event_source_idx[b][:k]
         complete = S_gpu <= layer.max_out_spikes  # the stream holds every spike
+        if not dense:
+            assert ref.n_real_events <= layer.max_out_spikes, "oracle stream must be complete"
         diverged = 0
         for o in range(layer.n_out):
-            ref_t = [float(t[b][j]) for j in ref.spike_event_idx[o][ref.spike_mask[o]]]
+            ref_t = _ref_spike_times(ref, o, t[b])
             if complete:
                 got_t = sorted(float(x) for x in times[src == o])
                 if got_t != ref_t:
-                    # allowed only after a value within rounding distance of v_th
                     i = next(i for i in range(min(len(got_t), len(ref_t)) + 1)
                              if i == min(len(got_t), len(ref_t)) or got_t[i] != ref_t[i])
                     t_diff = min(got_t[i] if i < len(got_t) else np.inf,
                                  ref_t[i] if i < len(ref_t) else np.inf)
-                    assert first_near[o] < len(t[b]) and t[b][first_near[o]] <= t_diff, \
-                        f"b={b} neuron {o}: spikes differ at t={t_diff} with no near-threshold value"
+                    assert first_near[o] < E and t[b][first_near[o]] <= t_diff, \
+                        f"b={b} neuron {o}: spikes differ at t={t_diff} with no value within " \
+                        f"{BAND} of v_th before it"
                     diverged += 1
                     continue
-            if first_near[o] == len(t[b]) or complete:
-                np.testing.assert_allclose(vf[o], ref.v_final[o], rtol=1e-5, atol=1e-5,
-                                           err_msg=f"v_final b={b} neuron {o}")
-        assert diverged <= 0.25 * layer.n_out, f"b={b}: {diverged} neurons diverged"
-        if diverged == 0 and (complete or np.all(first_near == len(t[b]))):
+            elif first_near[o] < E:
+                continue   # truncated stream: a flipped decision here cannot be told apart
+            np.testing.assert_allclose(vf[o], ref.v_final[o], rtol=RTOL, atol=ATOL,
+                                       err_msg=f"v_final b={b} neuron {o}")
+        if diverged == 0 and (complete or np.all(first_near == E)):
             assert S_gpu == ref.n_real_events, f"spike count b={b}"
             np.testing.assert_array_equal(src, ref.event_source_idx[:k], err_msg=f"src b={b}")
             np.testing.assert_array_equal(times, ref.event_times[:k], err_msg=f"times b={b}")
         assert abs(int(out.diag.needed["max_extra_steps"][b]) - ref.extra_steps_needed) <= 1
+    return diverged
 
 
 PARITY = [
@@ -161,3 +178,19 @@ def test_float_rejects_non_positive_threshold():
                            np.ones(3, np.float32), np.int32(3))
     with pytest.raises(ValueError):
         S.FloatB200Backend().forward_layer(layer, np.ones((2, 2), np.float32), stream)
+
+
+def test_config5_neuron_subset_full_stream():
+    """Configuration 5's layer (4096 -> 4096, per-neuron tau, chunk 4096, one stream of 10^6
+    events) on a 64-neuron subset over the full stream: neurons are independent, so the first 64
+    neurons of the full layer see exactly what they see here."""
+    from dataclasses import replace
+    from salt_b200 import workloads as W
+    wl = W.config5(seed=0)
+    k = 64
+    layer = replace(wl.layer, n_out=k, max_out_spikes=200_000)
+    out = S.FloatB200Backend().forward_layer(layer, wl.w[:k], S.EventStream(
+        wl.times, wl.src, np.ones_like(wl.times), wl.n_real), tau=wl.tau[:k])
+    assert int(out.result.spike_count[0]) > 1000
+    _check_against_oracle(layer, wl.w[:k], wl.times, wl.src, wl.n_real, np.ones_like(wl.times),
+                          wl.tau[:k], out, dense=False, threads=8)

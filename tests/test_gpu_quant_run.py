@@ -1,5 +1,5 @@
 """The whole-split integer forward, capacity growth and the saved-reference check on the GPU
-(example/quant_run.py:71-132, example/quantize.py:306-330), against the oracle."""
+(example/quant_run.py:71-136, example/quantize.py:306-330), against the oracle."""
 import numpy as np
 import pytest
 

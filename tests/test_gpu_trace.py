@@ -1,5 +1,5 @@
 """Per-column traces (trace=True) and overflow forensics on the GPU against the oracle:
-run_layer_traced's v_steps, the spike mask, event_ms (quant/scan.py:83-94, trace.py:24-60), and
+run_layer_traced's v_steps, the spike mask, event_ms (quant/scan.py:83-94, trace.py:25-55), and
 the first-overflow records that example/quant_run.py's overflow analysis reports."""
 import numpy as np
 import pytest

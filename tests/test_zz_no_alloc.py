@@ -11,6 +11,7 @@ import re
 import numpy as np
 import pytest
 
+import oracle as O
 import salt_b200 as S
 from salt_b200 import _lib
 from salt_b200.backend import conv_desc, quant_desc
@@ -97,6 +98,16 @@ def test_noalloc_matches_the_workspace_entry_on_consecutive_calls():
         for b in range(B):
             np.testing.assert_array_equal(got["times"][b], ref["times"][b])
             np.testing.assert_array_equal(got["src"][b], ref["src"][b])
+        # and pinned to the CPU oracle directly (the stream is read with virtual pads: entries
+        # past n_real are time 1e12, source 0)
+        for b in range(B):
+            t, s = times[b].copy(), src[b].copy()
+            t[nr[b]:], s[nr[b]:] = np.float32(1e12), 0
+            o = O.conv_forward(layer, params, t, s, int(nr[b]))
+            np.testing.assert_array_equal(got["v_final"][b], o.v_final)
+            assert int(got["n_real"][b]) == o.n_real_events
+            np.testing.assert_array_equal(got["times"][b], o.event_times[:len(got["times"][b])])
+            np.testing.assert_array_equal(got["src"][b], o.event_source_idx[:len(got["src"][b])])
 
 
 def test_noalloc_rejects_layers_beyond_the_fixed_scratch():
