@@ -238,27 +238,52 @@ def run_reference(args):
 CONV_FUSED_DRAM_BYTES_PER_EVENT = (185.0e6 + 143.4e6) / 7.772496e6
 
 
-def run_b200(args):
+def _init_ranks(world, local):
+    """torch.distributed (barriers, timing reductions) and the package's own NCCL communicator
+    for the data path's logits all-gather, on this rank's GPU."""
+    from salt_b200 import device as D
+    D.set_device(local)
+    if world == 1:
+        return None, None
+    import datetime
     import torch
     import torch.distributed as dist
+    from salt_b200.comm import NcclComm, new_unique_id
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    uid = [new_unique_id() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    return dist, NcclComm(dist.get_rank(), world, uid[0])
+
+
+def _reduce(dist, value, op):
+    """A float reduced over the ranks (max or sum); the value itself on one rank."""
+    if dist is None:
+        return float(value)
+    import torch
+    t = torch.tensor([float(value)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "sum": dist.ReduceOp.SUM}[op])
+    return float(t.item())
+
+
+def run_b200(args):
     rank, world, local = rank_info()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    dist, comm = _init_ranks(world, local)
     import salt_b200 as S
+    from salt_b200 import device as D
     backend = S.QuantB200Backend("round")
     wl_all, wl = make_workload(args.config, args.seed, rank, world, args.scaling,
                                batch=args.batch)
     layers, params = list(wl.network.layers), wl.params
     B, E = wl.batch, wl.times.shape[1]
     plan = backend.compile(layers, params, batch=B, in_capacity=E)
-    t_d = torch.from_numpy(wl.times).cuda()
-    s_d = torch.from_numpy(wl.src).cuda()
-    n_d = torch.from_numpy(wl.n_real).cuda()
+    t_d = D.to_device(wl.times, np.float32)
+    s_d = D.to_device(wl.src, np.int32)
+    n_d = D.to_device(wl.n_real, np.int32)
     events_rank = wl.events
     n_out = plan.n_out
-    gathered = torch.empty((world * B, n_out), dtype=torch.int32, device="cuda")
+    gathered = D.empty((world * B, n_out), np.int32)
 
     replay = plan.capture(t_d, s_d, n_d) if args.graph else None
 
@@ -268,13 +293,16 @@ def run_b200(args):
             logits = plan.logits
         else:
             logits, _, _ = plan.forward_device(t_d, s_d, n_d)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, logits)
+        if comm is not None:
+            comm.all_gather(logits, gathered)
 
     def barrier():
-        if world > 1:
+        if comm is not None:
+            comm.wait(120.0)
+        D.synchronize()
+        if dist is not None:
             dist.barrier()
-        torch.cuda.synchronize()
+            D.synchronize()
 
     for _ in range(args.warmup):
         step()
@@ -282,34 +310,27 @@ def run_b200(args):
     plan.profile_read(reset=True)
     if replay is None:
         plan.set_profiling(True)   # kernel times recorded live inside the timed region
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    start, stop = D.Event(timing=True), D.Event(timing=True)
+    with ClockSampler(D.current_device()) as clocks:
         barrier()
         start.record()
         for _ in range(args.steps):
             step()
         stop.record()
-        torch.cuda.synchronize()
         barrier()
     if replay is not None:   # graph replays record no per-kernel events: an eager profiled pass
         plan.set_profiling(True)
         for _ in range(min(args.steps, 20)):
             plan.forward_device(t_d, s_d, n_d)
-        torch.cuda.synchronize()
+        D.synchronize()
     plan.set_profiling(False)
     fused_ms, layer_ms, fused_n = plan.profile_read(reset=True)
     launches_per_step = plan.last_launch_count()
-    ms = start.elapsed_time(stop) / args.steps
+    ms = start.elapsed_ms(stop) / args.steps
     # the last forward's results, for the parity check against the oracle (rank 0, N = 1)
-    gpu_results = (plan.logits.cpu().numpy(), plan.stats[0].cpu().numpy(),
-                   plan.fits.cpu().numpy())
-    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    ev_all = torch.tensor([events_rank], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        dist.all_reduce(ev_all, op=dist.ReduceOp.SUM)
-    ms_max = float(t_max.item())
-    events_step = float(ev_all.item())
+    gpu_results = (plan.logits.numpy(), plan.stats[0].numpy(), plan.fits.numpy())
+    ms_max = _reduce(dist, ms, "max")
+    events_step = _reduce(dist, events_rank, "sum")
     value = events_step / (ms_max / 1000.0)
 
     # ---- end to end through the public API with host buffers (pinned), per step: the
@@ -317,19 +338,18 @@ def run_b200(args):
     # sub-batch computes, and returns the logits and fits to the host; N > 1 also all-gathers
     # the logits.
     from salt_b200.plan import PipelinedForward
-    t_h = torch.from_numpy(wl.times).pin_memory()
-    s_h = torch.from_numpy(wl.src).pin_memory()
-    n_h = torch.from_numpy(wl.n_real).pin_memory()
+    t_h, s_h = D.pinned_copy(wl.times, np.float32), D.pinned_copy(wl.src, np.int32)
+    n_h = D.pinned_copy(wl.n_real, np.int32)
     chunks = 4 if B % 4 == 0 else 1
     pf = PipelinedForward(layers, params, B, E, chunks=chunks)
-    logits_d = torch.empty((B, n_out), dtype=torch.int32, device="cuda")
+    logits_d = D.empty((B, n_out), np.int32)
     e2e_steps = max(1, min(args.steps, 20))
 
     def e2e_step():
         logits_h, _ = pf(t_h, s_h, n_h)
-        if world > 1:
-            logits_d.copy_(logits_h, non_blocking=True)
-            dist.all_gather_into_tensor(gathered, logits_d)
+        if comm is not None:
+            logits_d.copy_from(logits_h)
+            comm.all_gather(logits_d, gathered)
 
     e2e_step()
     barrier()
@@ -337,15 +357,11 @@ def run_b200(args):
     for _ in range(e2e_steps):
         e2e_step()
     stop.record()
-    torch.cuda.synchronize()
     barrier()
-    e2e_ms = torch.tensor([start.elapsed_time(stop) / e2e_steps], dtype=torch.float64,
-                          device="cuda")
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = events_step / (float(e2e_ms.item()) / 1000.0)
+    e2e_ms = _reduce(dist, start.elapsed_ms(stop) / e2e_steps, "max")
+    e2e_value = events_step / (e2e_ms / 1000.0)
     h2d = pf.h2d_bytes(wl.n_real)
-    d2h = int(pf.logits.numel() * 4 + pf.fits.numel() * 4)
+    d2h = int(pf.logits.nbytes + pf.fits.nbytes)
     pf.close()
 
     # ---- roofline: the dominant kernel (the fused bucket+scan kernel of the busiest conv layer;
@@ -367,14 +383,11 @@ def run_b200(args):
         alg_bytes = float(8 * v["E"] + 24 * v["S"] + 4 * v["N"])
         kernel_name = f"fc_scan + compaction (layer {layers[dom].name})"
         traffic = None
-    net_bytes = torch.tensor([sum(layer_bytes(l, v, np.size(p.decay_table_int))
-                                  for l, v, p in zip(layers, vol, params))],
-                             dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(net_bytes, op=dist.ReduceOp.SUM)
+    net_bytes = _reduce(dist, sum(layer_bytes(l, v, np.size(p.decay_table_int))
+                                  for l, v, p in zip(layers, vol, params)), "sum")
     peak, peak_kind = peak_hbm()
     achieved = alg_bytes / (avg_ms / 1000.0) / 1e9
-    net_achieved = float(net_bytes.item()) / (ms_max / 1000.0) / 1e9
+    net_achieved = net_bytes / (ms_max / 1000.0) / 1e9
 
     if rank == 0:
         line = {
@@ -386,7 +399,9 @@ def run_b200(args):
             "layout": {"per_rank_batch": B, "events_rank0": int(events_rank),
                        "parallelism": f"dp{world} (" + ("one batch per rank" if args.scaling ==
                                                         "weak" else "event-balanced shards of "
-                                                        "one batch") + ")"},
+                                                        "one batch") + ")",
+                       "collective": "ncclAllGather of the int32 logits (salt_b200.comm)"
+                                     if world > 1 else None},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_source": ("ncu DRAM bytes per input event of the captured "
@@ -396,7 +411,7 @@ def run_b200(args):
                          "kernel_ms": avg_ms, "algorithmic_bytes": alg_bytes,
                          "network": {"achieved": net_achieved, "frac": net_achieved / peak,
                                      "frac_of_8tbs": net_achieved / 8000.0,
-                                     "bytes_per_step": float(net_bytes.item()),
+                                     "bytes_per_step": net_bytes,
                                      "model": "sum over layers and ranks of the conv/FC layer "
                                               "byte model (8E + 16C + 16S + 8S_out + 4N; FC "
                                               "8E + 24S + 4N; weights and LUT once) / step"},
@@ -424,7 +439,9 @@ def run_b200(args):
             line["parity"] = line["cpu_baseline"].pop("parity")
         print(json.dumps(line), flush=True)
     plan.close()
-    if world > 1:
+    if comm is not None:
+        comm.close()
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
@@ -536,33 +553,29 @@ def run_reference_float(args):
 
 
 def run_b200_float(args):
-    import torch
-    import torch.distributed as dist
     rank, world, local = rank_info()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    dist, comm = _init_ranks(world, local)
     import salt_b200 as S
     from salt_b200 import _lib
+    from salt_b200 import device as D
     from salt_b200 import float_backend as F
     from salt_b200 import workloads as W
-    from salt_b200.device import DeviceStream
     be = S.FloatB200Backend()
     wl = W.size_float_capacity(W.config5(seed=args.seed + rank), be)
     layer = wl.layer
     B, E = wl.batch, wl.times.shape[1]
     plan = be.compile(layer, wl.w, B, E, tau=wl.tau)
-    t_d = torch.from_numpy(wl.times).cuda()
-    s_d = torch.from_numpy(wl.src).cuda()
-    n_d = torch.from_numpy(wl.n_real).cuda()
-    ds = DeviceStream(t_d, s_d, n_d, False)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB of L2
+    t_d = D.to_device(wl.times, np.float32)
+    s_d = D.to_device(wl.src, np.int32)
+    n_d = D.to_device(wl.n_real, np.int32)
+    ds = D.DeviceStream(t_d, s_d, n_d, False)
+    flush = D.empty((256 << 20,), np.uint8)  # > 126 MB of L2
 
     def barrier():
-        if world > 1:
+        D.synchronize()
+        if dist is not None:
             dist.barrier()
-        torch.cuda.synchronize()
+            D.synchronize()
 
     for _ in range(args.warmup):
         plan.forward_device(ds)
@@ -574,56 +587,47 @@ def run_b200_float(args):
     barrier()
     F.profile_read(reset=True)
     F.set_profiling(True)
-    with ClockSampler(torch.cuda.current_device()) as clocks:
+    with ClockSampler(D.current_device()) as clocks:
         for _ in range(args.steps):
-            flush.zero_()  # outside the layer's timed events
+            flush.fill_bytes(0)  # outside the layer's timed events
             plan.forward_device(ds)
-        torch.cuda.synchronize()
+        D.synchronize()
     F.set_profiling(False)
     seg_ms, layer_ms, n_timed = F.profile_read(reset=True)
     barrier()
     ms = layer_ms / max(n_timed, 1)
-    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    ev_all = torch.tensor([wl.events], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        dist.all_reduce(ev_all, op=dist.ReduceOp.SUM)
-    ms_max, events_step = float(t_max.item()), float(ev_all.item())
+    ms_max = _reduce(dist, ms, "max")
+    events_step = _reduce(dist, wl.events, "sum")
     value = events_step / (ms_max / 1000.0)
-    spikes = int(plan.stats[0].sum().item())
+    spikes = int(plan.stats[0].numpy().sum())
 
     # end to end through the public plan: H2D of the stream, the layer, D2H of v_final + stats
-    t_h = torch.from_numpy(wl.times).pin_memory()
-    s_h = torch.from_numpy(wl.src).pin_memory()
-    n_h = torch.from_numpy(wl.n_real).pin_memory()
-    v_h = torch.empty(plan.v_final.shape, dtype=torch.float32).pin_memory()
-    st_h = torch.empty(plan.stats.shape, dtype=torch.int32).pin_memory()
+    t_h, s_h = D.pinned_copy(wl.times, np.float32), D.pinned_copy(wl.src, np.int32)
+    n_h = D.pinned_copy(wl.n_real, np.int32)
+    v_h = D.pinned_empty(plan.v_final.shape, np.float32)
+    st_h = D.pinned_empty(plan.stats.shape, np.int32)
     e2e_steps = max(1, min(args.steps, 20))
 
     def e2e_step():
-        t_d.copy_(t_h, non_blocking=True)
-        s_d.copy_(s_h, non_blocking=True)
-        n_d.copy_(n_h, non_blocking=True)
+        t_d.copy_from(t_h)
+        s_d.copy_from(s_h)
+        n_d.copy_from(n_h)
         run = plan.forward_device(ds)
-        v_h.copy_(run.v_final, non_blocking=True)
-        st_h.copy_(run.stats, non_blocking=True)
+        run.v_final.copy_to(v_h, sync=False)
+        run.stats.copy_to(st_h, sync=False)
 
     e2e_step()
     barrier()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start, stop = D.Event(timing=True), D.Event(timing=True)
     start.record()
     for _ in range(e2e_steps):
         e2e_step()
     stop.record()
-    torch.cuda.synchronize()
     barrier()
-    e2e_ms = torch.tensor([start.elapsed_time(stop) / e2e_steps], dtype=torch.float64,
-                          device="cuda")
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = events_step / (float(e2e_ms.item()) / 1000.0)
-    h2d = int(t_h.numel() * 4 + s_h.numel() * 4 + n_h.numel() * 4)
-    d2h = int(v_h.numel() * 4 + st_h.numel() * 4)
+    e2e_ms = _reduce(dist, start.elapsed_ms(stop) / e2e_steps, "max")
+    e2e_value = events_step / (e2e_ms / 1000.0)
+    h2d = int(t_h.nbytes + s_h.nbytes + n_h.nbytes)
+    d2h = int(v_h.nbytes + st_h.nbytes)
 
     seg_avg = seg_ms / max(n_timed, 1)
     G = (layer.n_out + 31) // 32
@@ -661,7 +665,9 @@ def run_b200_float(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_float(wl, args.cpu_seconds)
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if comm is not None:
+        comm.close()
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 

@@ -414,6 +414,8 @@ salt_status salt_event_create(int32_t timing, void **event);
 salt_status salt_event_destroy(void *event);
 salt_status salt_event_record(void *event, void *stream);
 salt_status salt_event_synchronize(void *event);
+/* *done = 1 when the work before the event's last record has finished, else 0 (no waiting). */
+salt_status salt_event_query(void *event, int32_t *done);
 salt_status salt_event_elapsed_ms(void *start, void *stop, float *ms);
 salt_status salt_graph_begin_capture(void *stream);
 salt_status salt_graph_end_capture(void *stream, void **graph_exec);

@@ -7,7 +7,7 @@ import sys
 
 _REAL = "spiking-affine-lazy-training_b200"
 _SUBMODULES = ("stream", "quant", "capacity", "layers", "network", "_lib", "device", "backend",
-               "plan", "workloads", "float_backend", "sharding", "io", "quant_run", "trace", "build", "calibrate")
+               "plan", "workloads", "float_backend", "sharding", "io", "quant_run", "trace", "build", "calibrate", "comm")
 
 _root = os.path.dirname(os.path.abspath(__file__))
 if _root not in sys.path:

@@ -134,6 +134,7 @@ _SIGS = {
     "salt_event_destroy": (_i32, [_vp]),
     "salt_event_record": (_i32, [_vp, _vp]),
     "salt_event_synchronize": (_i32, [_vp]),
+    "salt_event_query": (_i32, [_vp, _vp]),
     "salt_event_elapsed_ms": (_i32, [_vp, _vp, _vp]),
     "salt_graph_begin_capture": (_i32, [_vp]),
     "salt_graph_end_capture": (_i32, [_vp, _vp]),

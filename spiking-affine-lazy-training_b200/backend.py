@@ -21,17 +21,12 @@ import numpy as np
 
 from . import _lib
 from .capacity import LayerDiag
-from .device import DeviceStream, current_stream, ptr, require_cuda, to_device, workspace
+from .device import (DeviceArray, DeviceStream, empty, ptr, require_cuda, stream_handle,
+                     to_device, workspace, zeros)
 from .layers import LayerOutput, is_conv
 from .quant import (OverflowMode, RoundMode, apply_decay_table_int, check_bit_widths,
                     check_weight_codes, weight_bits)
 from .stream import EventStream
-
-try:
-    import torch
-except ImportError:  # pragma: no cover
-    torch = None
-
 
 class QuantLayerResult(NamedTuple):
     """Per-layer integer result (salt_core/quant/scan.py:55-62), batched.
@@ -134,8 +129,8 @@ def fc_desc(layer) -> _lib.FCDesc:
 
 class _LayerRun(NamedTuple):
     out: DeviceStream
-    v_final: "torch.Tensor"
-    stats: "torch.Tensor"   # (6, B): spike_count, needed_queue, overflowed, vmin, vmax, fits
+    v_final: DeviceArray
+    stats: DeviceArray      # (6, B): spike_count, needed_queue, overflowed, vmin, vmax, fits
 
 
 @dataclass(frozen=True)
@@ -156,15 +151,15 @@ class QuantB200Backend:
                             np.int32) if qd.lut_len else None
         vth_dev = to_device(vth, np.int32) if vth is not None else None
         M = int(layer.max_out_spikes)
-        out_t = torch.empty((B, M), dtype=torch.float32, device="cuda")
-        out_s = torch.empty((B, M), dtype=torch.int32, device="cuda")
-        out_n = torch.empty((B,), dtype=torch.int32, device="cuda")
-        v_final = torch.empty((B, n), dtype=torch.int32, device="cuda")
-        stats = torch.zeros((6, B), dtype=torch.int32, device="cuda")
+        out_t = empty((B, M), np.float32)
+        out_s = empty((B, M), np.int32)
+        out_n = empty((B,), np.int32)
+        v_final = empty((B, n), np.int32)
+        stats = zeros((6, B), np.int32)
         sin = _lib.StreamIn(ptr(dstream.times), ptr(dstream.src), ptr(dstream.n_real), E,
                             int(dstream.virtual_pads))
         sout = _lib.StreamOut(ptr(out_t), ptr(out_s), ptr(out_n))
-        st = _lib.LayerStats(*[ctypes.c_void_p(stats[i].data_ptr()) for i in range(6)])
+        st = _lib.LayerStats(*[ptr(stats[i]) for i in range(6)])
         nbytes = ctypes.c_size_t(0)
         if is_conv(layer):
             d = conv_desc(layer)
@@ -174,7 +169,7 @@ class QuantB200Backend:
             _lib.check(lib.salt_conv_layer_forward(
                 _lib.byref(d), _lib.byref(qd), ptr(q_dev), ptr(lut_dev), ptr(vth_dev), B,
                 _lib.byref(sin), _lib.byref(sout), ptr(v_final), _lib.byref(st), ptr(ws),
-                nbytes.value, current_stream()))
+                nbytes.value, stream_handle()))
         else:
             d = fc_desc(layer)
             _lib.check(lib.salt_fc_layer_workspace_size(_lib.byref(d), _lib.byref(qd), B, E,
@@ -183,16 +178,16 @@ class QuantB200Backend:
             _lib.check(lib.salt_fc_layer_forward(
                 _lib.byref(d), _lib.byref(qd), ptr(q_dev), ptr(lut_dev), ptr(vth_dev), B,
                 _lib.byref(sin), _lib.byref(sout), ptr(v_final), _lib.byref(st), ptr(ws),
-                nbytes.value, current_stream()))
-        # Temporaries (weights, workspace) may be released now: torch's caching allocator only
-        # hands their memory to later work on this same stream, which runs after these kernels.
+                nbytes.value, stream_handle()))
+        # Temporaries (weights, workspace) may be released now: their memory is freed in stream
+        # order on this stream, after these kernels.
         return _LayerRun(DeviceStream(out_t, out_s, out_n, True), v_final, stats)
 
     def trace_layer_device(self, layer, params, dstream: DeviceStream, *, dense: bool = True,
                            per_neuron: bool = True) -> dict:
         """Per-column trace of one layer over a device stream (salt_conv_layer_trace /
         salt_fc_layer_trace): dense (B, n, L) v_steps / spike_mask / event_ms and per-neuron
-        first-overflow records, as torch tensors keyed by field name."""
+        first-overflow records, as device arrays keyed by field name."""
         require_cuda()
         lib = _lib.lib()
         B, E = dstream.batch, dstream.capacity
@@ -206,15 +201,14 @@ class QuantB200Backend:
         vth_dev = to_device(vth, np.int32) if vth is not None else None
         out = {}
         if dense:
-            out["v_steps"] = torch.empty((B, n, L), dtype=torch.int32, device="cuda")
-            out["spike_mask"] = torch.empty((B, n, L), dtype=torch.uint8, device="cuda")
-            out["event_ms"] = torch.empty((B, n, L), dtype=torch.float32, device="cuda")
+            out["v_steps"] = empty((B, n, L), np.int32)
+            out["spike_mask"] = empty((B, n, L), np.uint8)
+            out["event_ms"] = empty((B, n, L), np.float32)
         rec = None
         if per_neuron:
             names = [f for f, _ in _lib.NeuronTrace._fields_]
             for f in names:
-                out[f] = torch.empty((B, n), dtype=torch.float32 if f == "time_ms" else
-                                     torch.int32, device="cuda")
+                out[f] = empty((B, n), np.float32 if f == "time_ms" else np.int32)
             rec = _lib.NeuronTrace(*[ptr(out[f]) for f in names])
         sin = _lib.StreamIn(ptr(dstream.times), ptr(dstream.src), ptr(dstream.n_real), E,
                             int(dstream.virtual_pads))
@@ -223,21 +217,21 @@ class QuantB200Backend:
         _lib.check(fn(_lib.byref(desc), _lib.byref(qd), ptr(q_dev), ptr(lut_dev), ptr(vth_dev), B,
                       _lib.byref(sin), ptr(out.get("v_steps")), ptr(out.get("spike_mask")),
                       ptr(out.get("event_ms")), _lib.byref(rec) if rec is not None else None,
-                      current_stream()))
+                      stream_handle()))
         return out
 
     @staticmethod
     def _layer_trace(tr: dict):
         from .trace import LayerForwardTrace
-        return LayerForwardTrace(spike_mask=tr["spike_mask"].cpu().numpy().astype(bool),
-                                 v_steps=tr["v_steps"].cpu().numpy(),
-                                 event_ms=tr["event_ms"].cpu().numpy())
+        return LayerForwardTrace(spike_mask=tr["spike_mask"].numpy().astype(bool),
+                                 v_steps=tr["v_steps"].numpy(),
+                                 event_ms=tr["event_ms"].numpy())
 
     # ------------------------------------------------------------ host-level API
     @staticmethod
     def _host_layer(layer, run: _LayerRun, n_in: np.ndarray) -> tuple:
-        stats = run.stats.cpu().numpy()
-        v_final = run.v_final.cpu().numpy()
+        stats = run.stats.numpy()
+        v_final = run.v_final.numpy()
         S = stats[0].astype(np.int32)
         result = QuantLayerResult(v_final=v_final, spike_count=S, overflowed=stats[2] != 0,
                                   v_unfitted_min=stats[3].copy(), v_unfitted_max=stats[4].copy())
@@ -353,25 +347,24 @@ class QuantB200Backend:
         id_d = to_device(np.asarray(is_identity, dtype=np.uint8), np.uint8)
         q_d = to_device(np.asarray(q_int), np.int32)
         vth_d = to_device(vth, np.int32) if vth is not None else None
-        mask = torch.empty((n, L), dtype=torch.uint8, device="cuda")
-        ovf = torch.empty((n, L), dtype=torch.uint8, device="cuda")
-        vf, lo, hi = (torch.empty((n,), dtype=torch.int32, device="cuda") for _ in range(3))
+        mask = empty((n, L), np.uint8)
+        ovf = empty((n, L), np.uint8)
+        vf, lo, hi = (empty((n,), np.int32) for _ in range(3))
         args = (_lib.byref(qd), n, L, ptr(a_d), ptr(id_d), ptr(q_d), ptr(vth_d), ptr(mask),
                 ptr(ovf), ptr(vf), ptr(lo), ptr(hi))
         steps = None
         if trace:
-            steps = torch.empty((n, L), dtype=torch.int32, device="cuda")
+            steps = empty((n, L), np.int32)
             _lib.check(_lib.lib().salt_quant_scan_dense_trace(*args, ptr(steps),
-                                                              current_stream()))
+                                                              stream_handle()))
         else:
-            _lib.check(_lib.lib().salt_quant_scan_dense(*args, current_stream()))
-        m = mask.cpu().numpy().astype(bool)
+            _lib.check(_lib.lib().salt_quant_scan_dense(*args, stream_handle()))
+        m = mask.numpy().astype(bool)
         res = DenseQuantLayerResult(spike_mask=m,
                                     spike_event_idx=np.broadcast_to(np.arange(L), (n, L)),
-                                    v_final=vf.cpu().numpy(), overflowed=ovf.cpu().numpy() != 0,
-                                    v_unfitted_min=lo.cpu().numpy(),
-                                    v_unfitted_max=hi.cpu().numpy())
-        return (res, steps.cpu().numpy()) if trace else res
+                                    v_final=vf.numpy(), overflowed=ovf.numpy() != 0,
+                                    v_unfitted_min=lo.numpy(), v_unfitted_max=hi.numpy())
+        return (res, steps.numpy()) if trace else res
 
     # ------------------------------------------------------------ compiled network
     def compile(self, layers, weights, batch: int, in_capacity: int):

@@ -159,15 +159,15 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
     int32_t sb_spk = 0;
 #pragma unroll
     for (int r = 0; r < R; ++r) mybits[r] = 0;
-    auto step = [&](int e) {
-      const int2 ev = ev_s[e];
-      int32_t qv;
-      // lanes past n_out read the row's tail (or the zero row's padding); their results are
-      // dropped
-      if (WT) qv = (int32_t)q_s[ev.y + gl];
-      else qv = (ev.y >= 0 && active) ? __ldg(&P.qT[ev.y + gl]) : 0;
+    // lanes past n_out read the row's tail (or the zero row's padding); their results are
+    // dropped
+    auto load_q = [&](int32_t row) -> int32_t {
+      if (WT) return (int32_t)q_s[row + gl];
+      return (row >= 0 && active) ? __ldg(&P.qT[row + gl]) : 0;
+    };
+    auto step_with = [&](int e, int32_t a, int32_t qv) {
       int32_t u;
-      const int32_t w = sc.step<SAT, FORM != kStepSplit, FORM != kStepWideNoFit>(V, ev.x, qv, u);
+      const int32_t w = sc.step<SAT, FORM != kStepSplit, FORM != kStepWideNoFit>(V, a, qv, u);
       vmin = min(vmin, u);
       vmax = max(vmax, u);
       if (FIRES) {
@@ -183,12 +183,27 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
       }
     };
     if (cntw == SB) {
+      // blocks of kFcStepBlock steps: a block's (decay code, weight row) pairs and weight codes
+      // are loaded together ahead of its dependent register chain, so the shared-memory
+      // latencies overlap one another and the previous block's chain
 #pragma unroll
-      for (int e = 0; e < SB; ++e) step(e);
+      for (int e0 = 0; e0 < SB; e0 += kFcStepBlock) {
+        int2 evb[kFcStepBlock];
+        int32_t qb[kFcStepBlock];
+#pragma unroll
+        for (int k = 0; k < kFcStepBlock; ++k) evb[k] = ev_s[e0 + k];
+#pragma unroll
+        for (int k = 0; k < kFcStepBlock; ++k) qb[k] = load_q(evb[k].y);
+#pragma unroll
+        for (int k = 0; k < kFcStepBlock; ++k) step_with(e0 + k, evb[k].x, qb[k]);
+      }
     } else {
 #pragma unroll
       for (int e = 0; e < SB; ++e)
-        if (e < cntw) step(e);
+        if (e < cntw) {
+          const int2 ev = ev_s[e];
+          step_with(e, ev.x, load_q(ev.y));
+        }
     }
     if (FIRES) {
 #pragma unroll

@@ -272,21 +272,39 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   // position count has few events per position whatever the tiling, and its blocks' fixed work
   // (weight staging, register init, catch-up) dominates: it takes tiles of up to 256 positions
   // (configuration 4's conv2, 36 events over 1024 positions: 0.50 -> 0.36 ms at 128).
+  //
+  // A small batch would leave SMs idle behind a few long blocks (one heavy sample's whole plane
+  // in one block): while batch x tiles stays below kConvFillBlocks, the tiles shrink (to no
+  // fewer than 16 positions), so each sample is spread over more blocks.  The workspace sizes
+  // take the finest tiling into account (conv_scratch_bytes), so a plan made for a batch also
+  // serves its row slices.
   const size_t budget = 100 * 1024;
   int npm_cap = E < p.n_sp ? 256 : 64;
   while (npm_cap > 1 && fused_smem(d, q, p, 1, npm_cap, 2) > budget) npm_cap >>= 1;
-  if (p.n_sp <= npm_cap) {
-    p.tile_h = p.h_out;
-    p.tile_w = p.w_out;
-  } else {
-    p.tile_w = std::min(p.w_out, std::max(16, p.ncand));
-    p.tile_h = std::max(1, npm_cap / p.tile_w);
-    p.tile_h = std::min(p.h_out, std::max(p.tile_h, std::min(p.ncand, p.h_out)));
-    if (p.tile_w < p.w_out && p.tile_w < p.ncand) p.tile_w = std::min(p.w_out, p.ncand);
+  auto tile_for = [&](int cap) {
+    if (p.n_sp <= cap) {
+      p.tile_h = p.h_out;
+      p.tile_w = p.w_out;
+    } else {
+      p.tile_w = std::min(p.w_out, std::max(16, p.ncand));
+      p.tile_h = std::max(1, cap / p.tile_w);
+      p.tile_h = std::min(p.h_out, std::max(p.tile_h, std::min(p.ncand, p.h_out)));
+      if (p.tile_w < p.w_out && p.tile_w < p.ncand) p.tile_w = std::min(p.w_out, p.ncand);
+    }
+    p.tiles_x = (p.w_out + p.tile_w - 1) / p.tile_w;
+    p.tiles_y = (p.h_out + p.tile_h - 1) / p.tile_h;
+    p.T = p.tiles_x * p.tiles_y;
+  };
+  tile_for(npm_cap);
+  while ((int64_t)std::max(batch, 1) * p.T < kConvFillBlocks && npm_cap > 16) {
+    const int prev = npm_cap;
+    npm_cap >>= 1;
+    tile_for(npm_cap);
+    if (p.T > 1 && conv_scatter_smem(p.T) > 227 * 1024) {  // past the partition's tile limit
+      tile_for(prev);
+      break;
+    }
   }
-  p.tiles_x = (p.w_out + p.tile_w - 1) / p.tile_w;
-  p.tiles_y = (p.h_out + p.tile_h - 1) / p.tile_h;
-  p.T = p.tiles_x * p.tiles_y;
   const int per_y = p.tiles_y > 1 ? (p.ncand - 1 + p.tile_h - 1) / p.tile_h + 1 : 1;
   const int per_x = p.tiles_x > 1 ? (p.ncand - 1 + p.tile_w - 1) / p.tile_w + 1 : 1;
   p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
@@ -299,7 +317,6 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   if (p.smem > 227 * 1024)
     return fail(SALT_BAD_ARG, "conv layer weights do not fit in shared memory (ic*k*k*oc too "
                               "large for the chosen weight width)");
-  (void)batch;
   return SALT_OK;
 }
 
@@ -339,6 +356,20 @@ static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, 
   s.hist = c.take<int32_t>((size_t)B * 2 * p.n_sp);
   s.order = c.take<int32_t>((size_t)B);
   return c.size();
+}
+
+// Scratch bytes of a conv layer on B samples: enough for the batch's own tiling and for the
+// finest one a slice of the batch may take (plan_conv shrinks tiles for small batches; every
+// scratch term grows with the tile count and the batch).
+static salt_status conv_scratch_bytes(const salt_conv_desc* d, const salt_quant_desc* q, int32_t B,
+                                      int32_t E, size_t& bytes) {
+  ConvPlan p, fine;
+  salt_status rc = plan_conv(d, q, B, E, p);
+  if (rc) return rc;
+  if ((rc = plan_conv(d, q, 1, E, fine))) return rc;
+  ConvScratch s;
+  bytes = std::max(conv_carve(d, p, B, E, nullptr, s), conv_carve(d, fine, B, E, nullptr, s));
+  return SALT_OK;
 }
 
 // Optional CUDA-event pair recorded around the fused kernel (network profiling).
@@ -906,6 +937,18 @@ salt_status salt_event_synchronize(void* event) {
   return SALT_OK;
 }
 
+salt_status salt_event_query(void* event, int32_t* done) {
+  if (!done) return fail(SALT_BAD_ARG, "salt_event_query: NULL");
+  const cudaError_t e = cudaEventQuery((cudaEvent_t)event);
+  if (e == cudaErrorNotReady) {
+    *done = 0;
+    return SALT_OK;
+  }
+  SALT_CUDA(e);
+  *done = 1;
+  return SALT_OK;
+}
+
 salt_status salt_event_elapsed_ms(void* start, void* stop, float* ms) {
   SALT_CUDA(cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)stop));
   return SALT_OK;
@@ -952,11 +995,7 @@ salt_status salt_conv_layer_workspace_size(const salt_conv_desc* layer, const sa
   salt_status rc = check_quant(quant);
   if (rc) return rc;
   if (!bytes || batch < 1 || in_capacity < 1) return fail(SALT_BAD_ARG, "bad batch/capacity");
-  ConvPlan p;
-  if ((rc = plan_conv(layer, quant, batch, in_capacity, p))) return rc;
-  ConvScratch s;
-  *bytes = conv_carve(layer, p, batch, in_capacity, nullptr, s);
-  return SALT_OK;
+  return conv_scratch_bytes(layer, quant, batch, in_capacity, *bytes);
 }
 
 salt_status salt_conv_layer_forward(const salt_conv_desc* layer, const salt_quant_desc* quant,
@@ -1502,11 +1541,8 @@ static salt_status net_layout(const salt_network* net, int32_t B, int32_t E0, vo
     const LayerRec& r = net->layers[l];
     size_t b = 0;
     if (r.spec.kind == 0) {
-      ConvPlan p;
-      salt_status rc = plan_conv(&r.spec.conv, &r.spec.quant, B, E, p);
+      salt_status rc = conv_scratch_bytes(&r.spec.conv, &r.spec.quant, B, E, b);
       if (rc) return rc;
-      ConvScratch s;
-      b = conv_carve(&r.spec.conv, p, B, E, nullptr, s);
     } else {
       FCScratch s;
       b = fc_carve(&r.spec.fc, &r.spec.quant, B, E, false, nullptr, s);

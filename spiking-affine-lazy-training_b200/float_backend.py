@@ -24,15 +24,12 @@ import numpy as np
 
 from . import _lib
 from .capacity import LayerDiag
-from .device import DeviceStream, current_stream, ptr, require_cuda, to_device, workspace
+from .device import (DeviceArray, DeviceStream, empty, ptr, require_cuda, stream_handle, to_device,
+                     workspace, zeros)
 from .layers import LayerOutput, is_conv
 from .stream import EventStream
 from .trace import LayerForwardTrace
 
-try:
-    import torch
-except ImportError:  # pragma: no cover
-    torch = None
 
 
 class FloatLayerResult(NamedTuple):
@@ -62,10 +59,10 @@ class NetworkOutput(NamedTuple):
 
 class _FloatRun(NamedTuple):
     out: DeviceStream
-    v_final: "torch.Tensor"
+    v_final: DeviceArray
     # FC (3, B): spike_count, needed_extra_steps, fits;
     # conv (4, B): spike_count, needed_queue, needed_extra_steps, fits
-    stats: "torch.Tensor"
+    stats: DeviceArray
     trace: tuple | None = None    # (spike_mask, v_steps, event_ms), each (B, n, max_steps)
     v_range: tuple | None = None  # (v_max, v_min), each (B, channels)
 
@@ -125,11 +122,11 @@ class _TraceBuffers:
         self.trace = trace
         self.v_range = v_range
         z = None
-        self.spike_mask = torch.empty((B, n, steps), dtype=torch.uint8, device="cuda") if trace else z
-        self.v_steps = torch.empty((B, n, steps), dtype=torch.float32, device="cuda") if trace else z
-        self.event_ms = torch.empty((B, n, steps), dtype=torch.float32, device="cuda") if trace else z
-        self.v_max = torch.empty((B, channels), dtype=torch.float32, device="cuda") if v_range else z
-        self.v_min = torch.empty((B, channels), dtype=torch.float32, device="cuda") if v_range else z
+        self.spike_mask = empty((B, n, steps), np.uint8) if trace else z
+        self.v_steps = empty((B, n, steps), np.float32) if trace else z
+        self.event_ms = empty((B, n, steps), np.float32) if trace else z
+        self.v_max = empty((B, channels), np.float32) if v_range else z
+        self.v_min = empty((B, channels), np.float32) if v_range else z
         self.struct = _lib.FloatTrace(ptr(self.v_steps), ptr(self.event_ms), ptr(self.spike_mask),
                                       ptr(self.v_max), ptr(self.v_min))
 
@@ -158,11 +155,11 @@ class FloatLayerPlan:
         self.w = to_device(np.asarray(w, dtype=np.float32).reshape(n, int(layer.n_in)), np.float32)
         self.base = to_device(decay_base(layer.tau if tau is None else tau, n), np.float32)
         B, M = self.batch, int(layer.max_out_spikes)
-        self.out_t = torch.empty((B, M), dtype=torch.float32, device="cuda")
-        self.out_s = torch.empty((B, M), dtype=torch.int32, device="cuda")
-        self.out_n = torch.empty((B,), dtype=torch.int32, device="cuda")
-        self.v_final = torch.empty((B, n), dtype=torch.float32, device="cuda")
-        self.stats = torch.zeros((3, B), dtype=torch.int32, device="cuda")
+        self.out_t = empty((B, M), np.float32)
+        self.out_s = empty((B, M), np.int32)
+        self.out_n = empty((B,), np.int32)
+        self.v_final = empty((B, n), np.float32)
+        self.stats = zeros((3, B), np.int32)
         self._st = _lib.FloatLayerStats(*[ptr(self.stats[i]) for i in range(3)])
         self._sout = _lib.StreamOut(ptr(self.out_t), ptr(self.out_s), ptr(self.out_n))
         self._tb = _TraceBuffers(B, n, max_steps(layer, self.capacity), n, trace, v_range)
@@ -172,7 +169,7 @@ class FloatLayerPlan:
         self.ws_bytes = nbytes.value
         self.ws = workspace(self.ws_bytes)
 
-    def forward_device(self, dstream: DeviceStream, gain: "torch.Tensor | None" = None
+    def forward_device(self, dstream: DeviceStream, gain: "DeviceArray | None" = None
                        ) -> _FloatRun:
         if (dstream.batch, dstream.capacity) != (self.batch, self.capacity):
             raise ValueError(f"stream shape {(dstream.batch, dstream.capacity)} does not match the "
@@ -185,11 +182,11 @@ class FloatLayerPlan:
         _lib.check(lib.salt_float_fc_layer_forward(
             _lib.byref(self.desc), ptr(self.w), ptr(self.base), self.batch, _lib.byref(sin),
             ptr(gain), _lib.byref(self._sout), ptr(self.v_final), _lib.byref(self._st),
-            ptr(self.ws), self.ws_bytes, current_stream()))
+            ptr(self.ws), self.ws_bytes, stream_handle()))
         if self._tb.any:
             _lib.check(lib.salt_float_fc_layer_trace(
                 _lib.byref(self.desc), ptr(self.w), ptr(self.base), self.batch, _lib.byref(sin),
-                ptr(gain), None, _lib.byref(self._tb.struct), current_stream()))
+                ptr(gain), None, _lib.byref(self._tb.struct), stream_handle()))
         tr, vr = self._tb.outputs()
         return _FloatRun(DeviceStream(self.out_t, self.out_s, self.out_n, True), self.v_final,
                          self.stats, tr, vr)
@@ -208,11 +205,11 @@ class FloatConvPlan:
         self.w = to_device(np.asarray(w, dtype=np.float32).reshape(layer.weight_shape), np.float32)
         self.base = float(decay_base(layer.tau, 1)[0])
         B, M = self.batch, int(layer.max_out_spikes)
-        self.out_t = torch.empty((B, M), dtype=torch.float32, device="cuda")
-        self.out_s = torch.empty((B, M), dtype=torch.int32, device="cuda")
-        self.out_n = torch.empty((B,), dtype=torch.int32, device="cuda")
-        self.v_final = torch.empty((B, n), dtype=torch.float32, device="cuda")
-        self.stats = torch.zeros((4, B), dtype=torch.int32, device="cuda")
+        self.out_t = empty((B, M), np.float32)
+        self.out_s = empty((B, M), np.int32)
+        self.out_n = empty((B,), np.int32)
+        self.v_final = empty((B, n), np.float32)
+        self.stats = zeros((4, B), np.int32)
         self._st = _lib.FloatConvStats(*[ptr(self.stats[i]) for i in range(4)])
         self._sout = _lib.StreamOut(ptr(self.out_t), ptr(self.out_s), ptr(self.out_n))
         self._tb = _TraceBuffers(B, n, max_steps(layer, self.capacity), int(layer.oc), trace,
@@ -223,7 +220,7 @@ class FloatConvPlan:
         self.ws_bytes = nbytes.value
         self.ws = workspace(self.ws_bytes)
 
-    def forward_device(self, dstream: DeviceStream, gain: "torch.Tensor | None" = None
+    def forward_device(self, dstream: DeviceStream, gain: "DeviceArray | None" = None
                        ) -> _FloatRun:
         if (dstream.batch, dstream.capacity) != (self.batch, self.capacity):
             raise ValueError(f"stream shape {(dstream.batch, dstream.capacity)} does not match the "
@@ -236,7 +233,7 @@ class FloatConvPlan:
             _lib.byref(self.desc), ptr(self.w), ctypes.c_float(self.base), self.batch,
             _lib.byref(sin), ptr(gain), _lib.byref(self._sout), ptr(self.v_final),
             _lib.byref(self._st), _lib.byref(self._tb.struct) if self._tb.any else None,
-            ptr(self.ws), self.ws_bytes, current_stream()))
+            ptr(self.ws), self.ws_bytes, stream_handle()))
         tr, vr = self._tb.outputs()
         return _FloatRun(DeviceStream(self.out_t, self.out_s, self.out_n, True), self.v_final,
                          self.stats, tr, vr)
@@ -274,7 +271,7 @@ class FloatB200Backend:
                               v_range=v_range)
 
     def forward_layer_device(self, layer, w, dstream: DeviceStream, *, tau=None,
-                             gain: "torch.Tensor | None" = None, trace: bool = False,
+                             gain: "DeviceArray | None" = None, trace: bool = False,
                              v_range: bool = False) -> _FloatRun:
         """One batched layer on device-resident streams; gain (B, capacity) or None (ones)."""
         plan = self.compile(layer, w, dstream.batch, dstream.capacity, tau=tau,
@@ -283,9 +280,9 @@ class FloatB200Backend:
 
     @staticmethod
     def _host_layer(layer, run: _FloatRun, n_in: np.ndarray):
-        stats = run.stats.cpu().numpy()
+        stats = run.stats.numpy()
         S = stats[0].astype(np.int32)
-        result = FloatLayerResult(v_final=run.v_final.cpu().numpy(), spike_count=S)
+        result = FloatLayerResult(v_final=run.v_final.numpy(), spike_count=S)
         n = int(layer.n_neurons) if is_conv(layer) else int(layer.n_out)
         denom = np.float32(n) * np.maximum(n_in, 1).astype(np.float32)
         if is_conv(layer):
@@ -302,7 +299,7 @@ class FloatB200Backend:
     def _host_trace(run: _FloatRun):
         if run.trace is None:
             return None
-        mask, v, ms = (t.cpu().numpy() for t in run.trace)
+        mask, v, ms = (t.numpy() for t in run.trace)
         return LayerForwardTrace(spike_mask=mask.astype(bool), v_steps=v, event_ms=ms)
 
     @staticmethod
@@ -363,7 +360,7 @@ class FloatB200Backend:
             prev = r.spike_count.astype(np.int64)
             tr = self._host_trace(run)
             st = run.out.to_host() if keep_streams else None
-            vr = tuple(t.cpu().numpy() for t in run.v_range) if v_range else None
+            vr = tuple(t.numpy() for t in run.v_range) if v_range else None
             if single:
                 r, d, st, tr = self._single(r, d, st, tr)
                 f = f[0]

@@ -1,17 +1,19 @@
-"""Network descriptions and weights, float or quantised, saved with the network as npz.
+"""Model files: network descriptions, float weights and quantised models as npz archives.
 
-The file formats are the reference's (salt_core/io.py:16-180), so that models quantised by the
-reference's tooling load here unchanged and the other way round:
+The layouts are the reference's (salt_core/io.py), byte-compatible so that a model quantised by
+either implementation loads in the other:
 
-* ``"__network__"``: a JSON string ``{"format": 1, "input_shape": [...], "layers": [{"type":
-  "conv" | "fc", <every layer field>}, ...]}`` (``network_to_dict``, io.py:39-48).
-* float weights: one array per layer, keyed by layer name (io.py:80-118).
-* quantised models: arrays ``"<layer>/q"``, ``"<layer>/decay_table_int"``, ``"<layer>/v_th_int"``
-  (absent when the layer does not fire) and ``"<layer>/scale"``, plus ``"__quant__"``, a JSON
-  string ``{"format": 1, "round_mode": ..., "layers": {name: {"f_a", "f_V", "i_V",
-  "overflow_mode"}}, "metadata": {...}}`` (io.py:129-180).
+  ``__network__``  0-d string array holding the JSON ``{"format": 1, "input_shape": [...],
+                   "layers": [{"type": "conv" | "fc", <every layer field>}, ...]}``
+  ``<layer>``      float weights, one array per layer (weight files)
+  ``<layer>/<a>``  quantised arrays, ``a`` from ``QUANT_ARRAYS`` (quantised models)
+  ``__quant__``    0-d string array holding the JSON ``{"format": 1, "round_mode": ...,
+                   "layers": {<layer>: {"f_a", "f_V", "i_V", "overflow_mode"}},
+                   "metadata": {...}}`` (quantised models)
 
-Arrays are returned as numpy arrays (the reference returns JAX arrays); the values are the same.
+Every read and write goes through one schema: the tag table of layer classes, the table of
+per-layer quantised arrays and the table of per-layer quantised settings.  Arrays come back as
+numpy arrays.
 """
 from __future__ import annotations
 
@@ -30,79 +32,130 @@ from .quant import OverflowMode, QuantizedLayerParams, RoundMode
 FORMAT_VERSION = 1
 NETWORK_KEY = "__network__"
 QUANT_KEY = "__quant__"
-_LAYER_TYPES = {"conv": ConvLayer, "fc": FCLayer}
+RESERVED_KEYS = (NETWORK_KEY, QUANT_KEY)
+
+# type tag of each serialisable layer class
+LAYER_TAGS = {"conv": ConvLayer, "fc": FCLayer}
+
+# quantised arrays stored per layer as "<layer>/<name>": (name, may be absent).  An absent
+# optional array stands for None (v_th_int of a layer that never fires).
+QUANT_ARRAYS = (("q", False), ("decay_table_int", False), ("v_th_int", True), ("scale", False))
+
+# quantised settings stored per layer in the __quant__ document: name -> (encode, decode)
+QUANT_SETTINGS = {
+    "f_a": (int, int),
+    "f_V": (int, int),
+    "i_V": (int, int),
+    "overflow_mode": (lambda m: OverflowMode(m).value, OverflowMode),
+}
 
 
-def _layer_type(layer) -> str:
-    for name, cls in _LAYER_TYPES.items():
-        if type(layer) is cls:
-            return name
-    raise ValueError(f"{layer.name}: layer type {type(layer).__name__} cannot be serialised")
+# ---------------------------------------------------------------- network descriptions
+
+def _tag_of(layer) -> str:
+    tags = [tag for tag, cls in LAYER_TAGS.items() if type(layer) is cls]
+    if not tags:
+        raise ValueError(f"{layer.name}: layer type {type(layer).__name__} cannot be serialised")
+    return tags[0]
+
+
+def _require_format(doc: Mapping, what: str) -> None:
+    if doc.get("format") != FORMAT_VERSION:
+        raise ValueError(f"{what} format must be {FORMAT_VERSION}, got {doc.get('format')!r}")
 
 
 def network_to_dict(network: Network) -> dict:
-    """io.py:39-48: the input grid and every field of every layer (capacities included)."""
-    return {"format": FORMAT_VERSION, "input_shape": list(network.input_shape),
-            "layers": [{"type": _layer_type(l), **dataclasses.asdict(l)} for l in network.layers]}
+    """The JSON-ready description: the input grid and every field of every layer, capacities
+    included (salt_core/io.py:40-48)."""
+    layers = [dict(type=_tag_of(layer), **dataclasses.asdict(layer)) for layer in network.layers]
+    return {"format": FORMAT_VERSION, "input_shape": list(network.input_shape), "layers": layers}
 
 
 def network_from_dict(description: Mapping) -> Network:
-    """io.py:51-66; ValueError on another format or an unknown layer type."""
-    if description.get("format") != FORMAT_VERSION:
-        raise ValueError(f"network description format must be {FORMAT_VERSION}, got "
-                         f"{description.get('format')!r}")
+    """Inverse of network_to_dict; ValueError on another format or an unknown layer type
+    (salt_core/io.py:51-63)."""
+    _require_format(description, "network description")
     layers = []
     for entry in description["layers"]:
-        fields = dict(entry)
-        kind = fields.pop("type")
-        if kind not in _LAYER_TYPES:
-            raise ValueError(f"unknown layer type {kind!r} (known: {list(_LAYER_TYPES)})")
-        layers.append(_LAYER_TYPES[kind](**fields))
+        fields = {k: v for k, v in entry.items() if k != "type"}
+        cls = LAYER_TAGS.get(entry.get("type"))
+        if cls is None:
+            raise ValueError(f"unknown layer type {entry.get('type')!r} (known: "
+                             f"{sorted(LAYER_TAGS)})")
+        layers.append(cls(**fields))
     return Network(tuple(description["input_shape"]), tuple(layers))
 
 
-def _checked_layer_names(network: Network, n_per_layer: int, what: str) -> list[str]:
-    names = [l.name for l in network.layers]
-    if n_per_layer != len(names):
-        raise ValueError(f"{n_per_layer} {what} for a network of {len(names)} layers")
-    if len(set(names)) != len(names) or NETWORK_KEY in names or QUANT_KEY in names:
-        raise ValueError(f"layer names must be distinct and not {NETWORK_KEY!r}: {names}")
-    return names
+# ---------------------------------------------------------------- the archive
+
+class _Archive:
+    """A flat name -> array mapping with the two JSON documents and per-layer keys."""
+
+    def __init__(self, arrays: Mapping[str, np.ndarray] | None = None):
+        self.arrays = dict(arrays or {})
+
+    @staticmethod
+    def for_network(network: Network, per_layer: int, what: str) -> "_Archive":
+        names = [layer.name for layer in network.layers]
+        if per_layer != len(names):
+            raise ValueError(f"{per_layer} {what} for a network of {len(names)} layers")
+        clash = len(set(names)) != len(names) or any(n in RESERVED_KEYS for n in names)
+        if clash:
+            raise ValueError(f"layer names must be distinct and not in {RESERVED_KEYS}: {names}")
+        archive = _Archive()
+        archive.put_doc(NETWORK_KEY, network_to_dict(network))
+        return archive
+
+    def put_doc(self, key: str, doc: Mapping) -> None:
+        self.arrays[key] = np.asarray(json.dumps(doc))
+
+    def doc(self, key: str, what: str) -> dict:
+        if key not in self.arrays:
+            raise ValueError(f"no {what} ({key!r})")
+        return json.loads(str(self.arrays[key]))
+
+    def network(self) -> Network:
+        return network_from_dict(self.doc(NETWORK_KEY, "network description"))
+
+    def save(self, path: str | os.PathLike) -> None:
+        np.savez(path, **self.arrays)
+
+    @staticmethod
+    def load(path: str | os.PathLike) -> "_Archive":
+        with np.load(path) as z:
+            return _Archive({k: z[k] for k in z.files})
 
 
-def _network_json(network: Network) -> np.ndarray:
-    return np.asarray(json.dumps(network_to_dict(network)))
-
-
-def _read_network(arrays: Mapping[str, np.ndarray]) -> Network:
-    if NETWORK_KEY not in arrays:
-        raise ValueError(f"no network description ({NETWORK_KEY!r})")
-    return network_from_dict(json.loads(str(arrays[NETWORK_KEY])))
-
+# ---------------------------------------------------------------- float weights
 
 def weights_to_arrays(network: Network, weights: Sequence) -> dict[str, np.ndarray]:
-    names = _checked_layer_names(network, len(weights), "weight arrays")
-    arrays = {n: np.asarray(w) for n, w in zip(names, weights)}
-    arrays[NETWORK_KEY] = _network_json(network)
-    return arrays
+    """The weight-file mapping: one array per layer name plus the network description
+    (salt_core/io.py:87-97)."""
+    archive = _Archive.for_network(network, len(weights), "weight arrays")
+    for layer, w in zip(network.layers, weights):
+        archive.arrays[layer.name] = np.asarray(w)
+    return archive.arrays
 
 
 def weights_from_arrays(arrays: Mapping[str, np.ndarray]) -> tuple[Network, tuple]:
-    network = _read_network(arrays)
-    return network, tuple(np.asarray(arrays[l.name]) for l in network.layers)
+    """(network, weights in layer order) from a weight-file mapping (salt_core/io.py:100-106)."""
+    archive = _Archive(arrays)
+    network = archive.network()
+    return network, tuple(np.asarray(archive.arrays[layer.name]) for layer in network.layers)
 
 
 def save_weights(path: str | os.PathLike, network: Network, weights: Sequence) -> None:
-    np.savez(path, **weights_to_arrays(network, weights))
+    _Archive(weights_to_arrays(network, weights)).save(path)
 
 
 def load_weights(path: str | os.PathLike) -> tuple[Network, tuple]:
-    with np.load(path) as arrays:
-        return weights_from_arrays(arrays)
+    return weights_from_arrays(_Archive.load(path).arrays)
 
+
+# ---------------------------------------------------------------- quantised models
 
 class QuantizedModel(NamedTuple):
-    """io.py:121-126"""
+    """A loaded quantised model (salt_core/io.py:121-126)."""
     network: Network
     params: tuple
     round_mode: RoundMode
@@ -111,45 +164,40 @@ class QuantizedModel(NamedTuple):
 
 def save_quantized(path: str | os.PathLike, network: Network, params: Sequence,
                    round_mode, metadata: Mapping[str, Any]) -> None:
-    """io.py:129-155.  metadata must be JSON-serialisable (TypeError otherwise)."""
-    names = _checked_layer_names(network, len(params), "parameter sets")
-    arrays = {NETWORK_KEY: _network_json(network)}
-    info = {}
-    for name, p in zip(names, params):
-        arrays[f"{name}/q"] = np.asarray(p.q)
-        arrays[f"{name}/decay_table_int"] = np.asarray(p.decay_table_int)
-        if p.v_th_int is not None:
-            arrays[f"{name}/v_th_int"] = np.asarray(p.v_th_int)
-        arrays[f"{name}/scale"] = np.asarray(p.scale)
-        info[name] = {"f_a": int(p.f_a), "f_V": int(p.f_V), "i_V": int(p.i_V),
-                      "overflow_mode": OverflowMode(getattr(p, "overflow_mode", "wrap")).value}
-    arrays[QUANT_KEY] = np.asarray(json.dumps({
-        "format": FORMAT_VERSION, "round_mode": RoundMode(round_mode).value, "layers": info,
-        "metadata": dict(metadata)}))
-    np.savez(path, **arrays)
+    """Writes a quantised model (salt_core/io.py:129-153); metadata must be JSON-serialisable
+    (TypeError otherwise)."""
+    archive = _Archive.for_network(network, len(params), "parameter sets")
+    settings = {}
+    for layer, p in zip(network.layers, params):
+        for name, optional in QUANT_ARRAYS:
+            value = getattr(p, name)
+            if value is None and optional:
+                continue
+            archive.arrays[f"{layer.name}/{name}"] = np.asarray(value)
+        settings[layer.name] = {name: enc(getattr(p, name))
+                                for name, (enc, _) in QUANT_SETTINGS.items()}
+    archive.put_doc(QUANT_KEY, {"format": FORMAT_VERSION,
+                                "round_mode": RoundMode(round_mode).value,
+                                "layers": settings, "metadata": dict(metadata)})
+    archive.save(path)
 
 
 def load_quantized(path: str | os.PathLike) -> QuantizedModel:
-    """io.py:158-180; ValueError without the network or quantisation entries or on another
-    format."""
-    with np.load(path) as arrays:
-        network = _read_network(arrays)
-        if QUANT_KEY not in arrays:
-            raise ValueError(f"no quantisation settings ({QUANT_KEY!r})")
-        quant = json.loads(str(arrays[QUANT_KEY]))
-        if quant.get("format") != FORMAT_VERSION:
-            raise ValueError(f"quantisation format must be {FORMAT_VERSION}, got "
-                             f"{quant.get('format')!r}")
-        params = []
-        for layer in network.layers:
-            name, li = layer.name, quant["layers"][layer.name]
-            vkey = f"{name}/v_th_int"
-            params.append(QuantizedLayerParams(
-                q=np.asarray(arrays[f"{name}/q"]),
-                decay_table_int=np.asarray(arrays[f"{name}/decay_table_int"]),
-                v_th_int=np.asarray(arrays[vkey]) if vkey in arrays else None,
-                scale=np.asarray(arrays[f"{name}/scale"]),
-                f_a=li["f_a"], f_V=li["f_V"], i_V=li["i_V"],
-                overflow_mode=OverflowMode(li["overflow_mode"])))
+    """Reads a quantised model (salt_core/io.py:156-180); ValueError when the network or the
+    quantisation document is missing or has another format."""
+    archive = _Archive.load(path)
+    network = archive.network()
+    quant = archive.doc(QUANT_KEY, "quantisation settings")
+    _require_format(quant, "quantisation")
+    params = []
+    for layer in network.layers:
+        fields = {}
+        for name, optional in QUANT_ARRAYS:
+            key = f"{layer.name}/{name}"
+            fields[name] = np.asarray(archive.arrays[key]) if (key in archive.arrays
+                                                                or not optional) else None
+        stored = quant["layers"][layer.name]
+        fields.update({name: dec(stored[name]) for name, (_, dec) in QUANT_SETTINGS.items()})
+        params.append(QuantizedLayerParams(**fields))
     return QuantizedModel(network, tuple(params), RoundMode(quant["round_mode"]),
                           quant["metadata"])

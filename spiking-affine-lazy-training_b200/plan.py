@@ -12,13 +12,9 @@ import numpy as np
 
 from . import _lib
 from .backend import conv_desc, fc_desc, quant_desc
-from .device import current_stream, ptr, require_cuda, to_device, workspace
+from .device import (Event, Graph, Stream, current_stream, empty, pinned_empty, ptr, require_cuda,
+                     stream_handle, to_device, use_stream, workspace)
 from .layers import is_conv
-
-try:
-    import torch
-except ImportError:  # pragma: no cover
-    torch = None
 
 
 class NetworkPlan:
@@ -51,13 +47,14 @@ class NetworkPlan:
         self._ws = workspace(self.workspace_bytes)
         nl, B = len(self.layers), self.batch
         self.n_out = self.layers[-1].n_neurons
-        self.logits = torch.empty((B, self.n_out), dtype=torch.int32, device="cuda")
-        self.stats = torch.empty((5, nl, B), dtype=torch.int32, device="cuda")
-        self.fits = torch.empty((B,), dtype=torch.int32, device="cuda")
+        self.logits = empty((B, self.n_out), np.int32)
+        self.stats = empty((5, nl, B), np.int32)
+        self.fits = empty((B,), np.int32)
+        self._graph = None
 
     def forward_device(self, times, src, n_real, virtual_pads: bool = False):
         """Enqueue one batched forward on the current stream (inputs already on the device).
-        Returns (logits, stats, fits) device tensors; stats rows are spike_count, overflowed,
+        Returns (logits, stats, fits) device arrays; stats rows are spike_count, overflowed,
         vmin, vmax, needed_queue, each (n_layers, B)."""
         sin = _lib.StreamIn(ptr(times), ptr(src), ptr(n_real), int(times.shape[1]),
                             int(virtual_pads))
@@ -65,7 +62,7 @@ class NetworkPlan:
         _lib.check(_lib.lib().salt_network_forward(
             self._net, self.batch, _lib.byref(sin), ptr(self.logits), ptr(s[0]), ptr(s[1]),
             ptr(s[2]), ptr(s[3]), ptr(s[4]), ptr(self.fits), ptr(self._ws),
-            self.workspace_bytes, current_stream()))
+            self.workspace_bytes, stream_handle()))
         return self.logits, self.stats, self.fits
 
     def forward_part(self, times, src, n_real, row0: int, rows: int, layer_begin: int,
@@ -84,24 +81,23 @@ class NetworkPlan:
             self._net, self.batch, self.in_capacity, int(row0), int(rows), int(layer_begin),
             int(layer_end), _lib.byref(sin) if sin is not None else None, ptr(self.logits),
             ptr(s[0]), ptr(s[1]), ptr(s[2]), ptr(s[3]), ptr(s[4]), ptr(self.fits), ptr(self._ws),
-            self.workspace_bytes, current_stream()))
+            self.workspace_bytes, stream_handle()))
         return self.logits, self.stats, self.fits
 
     def capture(self, times, src, n_real, virtual_pads: bool = False):
         """Records forward_device on these device buffers as a CUDA graph and returns its replay
         function: one launch per forward instead of one per kernel (launch-bound batches gain,
         large ones do not).  Refill the same buffers between replays; the results appear in the
-        tensors forward_device returns.  Profiling must be off while capturing."""
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):   # first call outside the capture: kernel attributes set
+        arrays forward_device returns.  Profiling must be off while capturing."""
+        side = Stream()
+        side.wait_stream(current_stream())
+        with use_stream(side):   # first call outside the capture: kernel attributes set
             self.forward_device(times, src, n_real, virtual_pads)
-        torch.cuda.current_stream().wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        current_stream().wait_stream(side)
+        with Graph.capture(side) as graph:
             self.forward_device(times, src, n_real, virtual_pads)
-        self._graph = graph   # kept alive with the plan
-        return graph.replay
+        self._graph = (graph, side)   # kept alive with the plan
+        return lambda: graph.replay(current_stream())
 
     def set_profiling(self, enable: bool) -> None:
         _lib.check(_lib.lib().salt_network_set_profiling(self._net, int(bool(enable))))
@@ -126,7 +122,7 @@ class NetworkPlan:
         s = to_device(np.asarray(raw.source_idx), np.int32)
         n = to_device(np.asarray(raw.n_real_events), np.int32)
         logits, stats, fits = self.forward_device(t, s, n)
-        return logits.cpu().numpy(), stats[0].cpu().numpy().T, fits.cpu().numpy() != 0
+        return logits.numpy(), stats[0].numpy().T, fits.numpy() != 0
 
     def close(self) -> None:
         if self._net:
@@ -148,10 +144,11 @@ class PipelinedForward:
     n_real (salt_stream_h2d_real) unless the first layer may fire on pad entries (needs_tail), in
     which case whole rows are copied.
 
-    Host arrays must be pinned torch tensors: times (B, E) float32, src (B, E) int32, n_real
-    (B,) int32.  Returns pinned (logits (B, n_out) int32, fits (B,) int32) filled in place; with
-    sync=False the call returns once everything is enqueued, and the buffers hold the results
-    when the current stream reaches the end of the call (the next call reuses them)."""
+    Host arrays should be pinned numpy arrays (device.pinned_empty / pinned_copy): times (B, E)
+    float32, src (B, E) int32, n_real (B,) int32; the real-event gather requires pinned rows.
+    Returns pinned (logits (B, n_out) int32, fits (B,) int32) filled in place; with sync=False
+    the call returns once everything is enqueued, and the buffers hold the results when the
+    current stream reaches the end of the call (the next call reuses them)."""
 
     def __init__(self, layers, weights, batch: int, in_capacity: int, chunks: int = 4,
                  round_mode="round", slice_layers: int = 1):
@@ -167,15 +164,15 @@ class PipelinedForward:
         qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
         self.full_rows = bool(qd.needs_tail)
         E, sub = self.capacity, self.sub
-        self._t = [torch.empty((sub, E), dtype=torch.float32, device="cuda") for _ in range(2)]
-        self._s = [torch.empty((sub, E), dtype=torch.int32, device="cuda") for _ in range(2)]
-        self._n = [torch.empty((sub,), dtype=torch.int32, device="cuda") for _ in range(2)]
-        self._copy = torch.cuda.Stream()
-        self._ready = [torch.cuda.Event() for _ in range(2)]
-        self._free = [torch.cuda.Event() for _ in range(2)]
+        self._t = [empty((sub, E), np.float32) for _ in range(2)]
+        self._s = [empty((sub, E), np.int32) for _ in range(2)]
+        self._n = [empty((sub,), np.int32) for _ in range(2)]
+        self._copy = Stream()
+        self._ready = [Event() for _ in range(2)]
+        self._free = [Event() for _ in range(2)]
         self._used = [False, False]   # buffer i was handed to a forward (this or an earlier call)
-        self.logits = torch.empty((batch, self.plan.n_out), dtype=torch.int32).pin_memory()
-        self.fits = torch.empty((batch,), dtype=torch.int32).pin_memory()
+        self.logits = pinned_empty((batch, self.plan.n_out), np.int32)
+        self.fits = pinned_empty((batch,), np.int32)
 
     def h2d_bytes(self, n_real_host) -> int:
         """Bytes one call moves host -> device for these event counts."""
@@ -185,25 +182,24 @@ class PipelinedForward:
 
     def __call__(self, times_h, src_h, n_real_h, sync: bool = True):
         lib = _lib.lib()
-        compute = torch.cuda.current_stream()
+        compute = current_stream()
         sub, E = self.sub, self.capacity
         per_slice = self.slice_layers
         for k in range(self.chunks):
             i = k % 2
             rows = slice(k * sub, (k + 1) * sub)
-            with torch.cuda.stream(self._copy):
-                if self._used[i]:   # the forward that last read buffer i, in any call
-                    self._copy.wait_event(self._free[i])
-                self._n[i].copy_(n_real_h[rows], non_blocking=True)
-                if self.full_rows:
-                    self._t[i].copy_(times_h[rows], non_blocking=True)
-                    self._s[i].copy_(src_h[rows], non_blocking=True)
-                else:
-                    _lib.check(lib.salt_stream_h2d_real(
-                        ptr(times_h[rows]), ptr(src_h[rows]), ctypes.c_int64(times_h.shape[1]),
-                        ptr(self._n[i]), sub, E, ptr(self._t[i]), ptr(self._s[i]),
-                        ctypes.c_void_p(self._copy.cuda_stream)))
-                self._ready[i].record(self._copy)
+            copy = self._copy
+            if self._used[i]:   # the forward that last read buffer i, in any call
+                copy.wait_event(self._free[i])
+            self._n[i].copy_from(n_real_h[rows], stream=copy)
+            if self.full_rows:
+                self._t[i].copy_from(times_h[rows], stream=copy)
+                self._s[i].copy_from(src_h[rows], stream=copy)
+            else:
+                _lib.check(lib.salt_stream_h2d_real(
+                    ptr(times_h[rows]), ptr(src_h[rows]), ctypes.c_int64(times_h.shape[1]),
+                    ptr(self._n[i]), sub, E, ptr(self._t[i]), ptr(self._s[i]), copy.ptr))
+            self._ready[i].record(copy)
             compute.wait_event(self._ready[i])
             self.plan.forward_part(self._t[i], self._s[i], self._n[i], k * sub, sub, 0,
                                    per_slice)
@@ -211,11 +207,13 @@ class PipelinedForward:
             self._used[i] = True
         if per_slice < self.n_layers:
             self.plan.forward_part(None, None, None, 0, self.batch, per_slice, self.n_layers)
-        self.logits.copy_(self.plan.logits, non_blocking=True)
-        self.fits.copy_(self.plan.fits, non_blocking=True)
+        self.plan.logits.copy_to(self.logits, sync=False, stream=compute)
+        self.plan.fits.copy_to(self.fits, sync=False, stream=compute)
         if sync:
             compute.synchronize()
         return self.logits, self.fits
 
     def close(self) -> None:
+        self._copy.synchronize()   # no copy still writes into the buffers about to be freed
+        current_stream().synchronize()
         self.plan.close()

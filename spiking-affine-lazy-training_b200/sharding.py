@@ -76,13 +76,16 @@ def unshard(gathered: np.ndarray, shards: Shards) -> np.ndarray:
     return out
 
 
-def gather_rows(local, group=None):
-    """All-gather equally shaped (per_rank, ...) tensors from every rank into (world * per_rank,
-    ...) in rank order (NCCL on GPUs, gloo on CPU)."""
-    import torch
-    import torch.distributed as dist
-    world = dist.get_world_size(group)
-    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
-                      device=local.device)
-    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+def gather_rows(local, comm):
+    """All-gather equally shaped (per_rank, ...) rows from every rank into (world * per_rank,
+    ...) in rank order.  `comm` provides ``world`` and ``all_gather(send, recv)``: an
+    ``comm.NcclComm`` for device arrays (the all-gather is then enqueued on the current stream;
+    ``comm.wait()`` bounds the wait), or any object with the same two members for host arrays."""
+    shape = (comm.world * local.shape[0],) + tuple(local.shape[1:])
+    if isinstance(local, np.ndarray):
+        out = np.empty(shape, local.dtype)
+    else:
+        from .device import DeviceArray
+        out = DeviceArray.empty(shape, local.dtype)
+    comm.all_gather(local, out)
     return out

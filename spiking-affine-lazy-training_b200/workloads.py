@@ -225,7 +225,7 @@ def size_float_capacity(wl: FloatWorkload, backend, factor: float = 1.5) -> Floa
     ds = DeviceStream(to_device(wl.times, np.float32), to_device(wl.src, np.int32),
                       to_device(wl.n_real, np.int32), False)
     run = backend.forward_layer_device(wl.layer, wl.w, ds, tau=wl.tau)
-    need = int(run.stats[0].max().item())
+    need = int(run.stats[0].numpy().max())
     return replace(wl, layer=replace(wl.layer, max_out_spikes=max(1, math.ceil(need * factor))))
 
 

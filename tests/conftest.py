@@ -15,8 +15,8 @@ def pytest_configure(config):
 
 def pytest_collection_modifyitems(config, items):
     try:
-        import torch
-        has_gpu = torch.cuda.is_available()
+        from salt_b200.device import device_count
+        has_gpu = device_count() > 0
     except Exception:
         has_gpu = False
     if has_gpu:

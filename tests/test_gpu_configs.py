@@ -69,14 +69,14 @@ def _check_layerwise(wl, refs, rows):
 
 def _plan_rows(wl, rows=None):
     """The benchmark's timed path (NetworkPlan.forward_device) on rows of the workload."""
-    import torch
+    from salt_b200.device import to_device
     sub = wl if rows is None else wl.subset(rows)
     plan = S.QuantB200Backend("round").compile(list(wl.network.layers), wl.params,
                                                batch=sub.batch, in_capacity=sub.times.shape[1])
-    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-    logits, stats, fits = plan.forward_device(dev(sub.times), dev(sub.src),
-                                              dev(sub.n_real.astype(np.int32)))
-    res = (logits.cpu().numpy().copy(), stats.cpu().numpy().copy(), fits.cpu().numpy().copy())
+    logits, stats, fits = plan.forward_device(to_device(sub.times, np.float32),
+                                              to_device(sub.src, np.int32),
+                                              to_device(sub.n_real, np.int32))
+    res = (logits.numpy(), stats.numpy(), fits.numpy())
     plan.close()
     return res
 

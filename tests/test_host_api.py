@@ -222,3 +222,26 @@ def test_workloads_are_deterministic_and_shaped_like_the_configs():
     assert np.all(np.diff(np.where(real, c3.times, np.inf), axis=1)[real[:, 1:]] >= 0)
     t, s = W.burst_events(np.random.default_rng(0), 5000, 2 * 128 * 128)
     assert np.all(np.diff(t) >= 0) and np.all(t == np.floor(t))
+
+
+_NO_TORCH_IMPORTS = """
+import sys
+sys.path.insert(0, {root!r})
+import salt_b200
+from salt_b200 import (backend, plan, device, float_backend, sharding, comm, quant_run, io,
+                       calibrate, workloads, trace)
+assert 'torch' not in sys.modules, 'the package imported torch'
+print('ok')
+"""
+
+
+def test_package_never_imports_torch():
+    """The product path is numpy + the C ABI: importing every module of the package leaves torch
+    unimported (device memory, streams, events, graphs and NCCL go through libsalt_b200 and
+    libnccl)."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _NO_TORCH_IMPORTS.format(root=root)],
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stderr[-2000:]

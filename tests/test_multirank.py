@@ -40,6 +40,19 @@ def _free_port():
         return s.getsockname()[1]
 
 
+class _GlooComm:
+    """The communicator interface gather_rows takes (world, all_gather), over torch's gloo
+    process group on host arrays: the CPU stand-in for comm.NcclComm."""
+
+    def __init__(self, world):
+        self.world = world
+
+    def all_gather(self, send, recv):
+        import torch
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(torch.from_numpy(recv), torch.from_numpy(send))
+
+
 def _rank_main(rank, world, port, mode, q):
     """One gloo rank: run the CPU oracle network on this rank's shard, gather the logits."""
     try:
@@ -65,8 +78,8 @@ def _rank_main(rank, world, port, mode, q):
         t, s, n = take_shard([times, src, nr], sh, rank)
         n = np.where(sh.of(rank) == sh.pad_index, 0, n)
         logits, _, _ = O.network_batch(net.layers, params, t, s, n, threads=1)
-        full = gather_rows(torch.from_numpy(logits.astype(np.int32)))
-        got = unshard(full.numpy(), sh)
+        full = gather_rows(np.ascontiguousarray(logits, dtype=np.int32), _GlooComm(world))
+        got = unshard(full, sh)
         ref, _, _ = O.network_batch(net.layers, params, times, src, nr, threads=1)
         q.put((rank, "ok", bool(np.array_equal(got, ref))))
         dist.destroy_process_group()

@@ -32,28 +32,27 @@ def _layer(geom, L=96, M=2000):
 
 def _run(layer, params, times, src, nr, noalloc):
     """One conv layer forward through the C ABI; returns host copies of every output."""
-    import torch
+    from salt_b200 import device as D
 
     lib = _lib.lib()
     B, E = times.shape
     qd, vth = quant_desc(params, "round", layer.n_neurons)
     d = conv_desc(layer)
-    dev = lambda a, t: torch.from_numpy(np.array(a, dtype=t, copy=True, order="C")).cuda()
-    q = dev(np.asarray(params.q).reshape(layer.weight_shape), np.int32)
-    lut = dev(params.decay_table_int, np.int32)
-    vt = dev(vth, np.int32)
-    t_d, s_d, n_d = dev(times, np.float32), dev(src, np.int32), dev(nr, np.int32)
+    q = D.to_device(np.asarray(params.q).reshape(layer.weight_shape), np.int32)
+    lut = D.to_device(params.decay_table_int, np.int32)
+    vt = D.to_device(vth, np.int32)
+    t_d, s_d, n_d = D.to_device(times, np.float32), D.to_device(src, np.int32), D.to_device(nr, np.int32)
     M = layer.max_out_spikes
-    out_t = torch.full((B, M), -1.0, dtype=torch.float32, device="cuda")
-    out_s = torch.full((B, M), -1, dtype=torch.int32, device="cuda")
-    out_n = torch.full((B,), -1, dtype=torch.int32, device="cuda")
-    v_final = torch.full((B, layer.n_neurons), -7, dtype=torch.int32, device="cuda")
-    stats = torch.full((6, B), -7, dtype=torch.int32, device="cuda")
-    p = lambda x: ctypes.c_void_p(x.data_ptr())
+    out_t = D.DeviceArray.full((B, M), -1.0, np.float32)
+    out_s = D.DeviceArray.full((B, M), -1, np.int32)
+    out_n = D.DeviceArray.full((B,), -1, np.int32)
+    v_final = D.DeviceArray.full((B, layer.n_neurons), -7, np.int32)
+    stats = D.DeviceArray.full((6, B), -7, np.int32)
+    p = D.ptr
     sin = _lib.StreamIn(p(t_d), p(s_d), p(n_d), E, 1)
     sout = _lib.StreamOut(p(out_t), p(out_s), p(out_n))
-    st = _lib.LayerStats(*[ctypes.c_void_p(stats[i].data_ptr()) for i in range(6)])
-    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    st = _lib.LayerStats(*[p(stats[i]) for i in range(6)])
+    stream = D.stream_handle()
     args = (_lib.byref(d), _lib.byref(qd), p(q), p(lut), p(vt), B, _lib.byref(sin),
             _lib.byref(sout), p(v_final), _lib.byref(st))
     if noalloc:
@@ -63,14 +62,13 @@ def _run(layer, params, times, src, nr, noalloc):
         _lib.check(lib.salt_conv_layer_workspace_size(_lib.byref(d), _lib.byref(qd), B, E,
                                                       _lib.byref(nbytes)))
         assert nbytes.value <= NOALLOC_SCRATCH_BYTES
-        buf = torch.empty(nbytes.value + 256, dtype=torch.uint8, device="cuda")
-        ws = buf[(-buf.data_ptr()) % 256:]
+        ws = D.workspace(nbytes.value)
         _lib.check(lib.salt_conv_layer_forward(*args, p(ws), nbytes.value, stream))
-    torch.cuda.synchronize()
-    n = out_n.cpu().numpy()
+    D.current_stream().synchronize()
+    n = out_n.numpy()
     k = np.minimum(n, M)
-    ot, os_ = out_t.cpu().numpy(), out_s.cpu().numpy()
-    return dict(n_real=n, v_final=v_final.cpu().numpy(), stats=stats.cpu().numpy(),
+    ot, os_ = out_t.numpy(), out_s.numpy()
+    return dict(n_real=n, v_final=v_final.numpy(), stats=stats.numpy(),
                 times=[ot[b, :k[b]] for b in range(B)], src=[os_[b, :k[b]] for b in range(B)])
 
 
