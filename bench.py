@@ -333,35 +333,43 @@ def run_b200(args):
     events_step = _reduce(dist, events_rank, "sum")
     value = events_step / (ms_max / 1000.0)
 
-    # ---- end to end through the public API with host buffers (pinned), per step: the
-    # pipelined plan copies each sub-batch's real events host -> device while the previous
-    # sub-batch computes, and returns the logits and fits to the host; N > 1 also all-gathers
-    # the logits.
+    # ---- end to end through the public API with host buffers (pinned).  Every step copies its
+    # inputs host -> device (each sample's real events, a sub-batch at a time on a copy stream,
+    # overlapping the forward of the previous sub-batch and, across steps, the previous step's
+    # later layers) and its results device -> host into that step's own pinned slot; N > 1 also
+    # all-gathers the logits on the device and copies the gathered rows back.  Steps are
+    # enqueued back to back (a streaming server's throughput); the region ends when the last
+    # step's results are on the host, and every step's results are checked afterwards.
     from salt_b200.plan import PipelinedForward
     t_h, s_h = D.pinned_copy(wl.times, np.float32), D.pinned_copy(wl.src, np.int32)
     n_h = D.pinned_copy(wl.n_real, np.int32)
     chunks = 4 if B % 4 == 0 else 1
     pf = PipelinedForward(layers, params, B, E, chunks=chunks)
-    logits_d = D.empty((B, n_out), np.int32)
     e2e_steps = max(1, min(args.steps, 20))
+    ring = [(D.pinned_empty((B, n_out), np.int32), D.pinned_empty((B,), np.int32),
+             D.pinned_empty((world * B, n_out), np.int32) if comm is not None else None)
+            for _ in range(e2e_steps)]
 
-    def e2e_step():
-        logits_h, _ = pf(t_h, s_h, n_h)
+    def e2e_step(k):
+        pf(t_h, s_h, n_h, sync=False, out=ring[k][:2])
         if comm is not None:
-            logits_d.copy_from(logits_h)
-            comm.all_gather(logits_d, gathered)
+            comm.all_gather(pf.plan.logits, gathered)
+            gathered.copy_to(ring[k][2], sync=False)
 
-    e2e_step()
+    e2e_step(0)
     barrier()
     start.record()
-    for _ in range(e2e_steps):
-        e2e_step()
+    pf.wait_for(start)
+    for k in range(e2e_steps):
+        e2e_step(k)
     stop.record()
     barrier()
     e2e_ms = _reduce(dist, start.elapsed_ms(stop) / e2e_steps, "max")
     e2e_value = events_step / (e2e_ms / 1000.0)
+    e2e_ok = all(np.array_equal(r[0], gpu_results[0]) and np.array_equal(r[1], gpu_results[2])
+                 for r in ring)
     h2d = pf.h2d_bytes(wl.n_real)
-    d2h = int(pf.logits.nbytes + pf.fits.nbytes)
+    d2h = int(ring[0][0].nbytes + ring[0][1].nbytes + (ring[0][2].nbytes if comm else 0))
     pf.close()
 
     # ---- roofline: the dominant kernel (the fused bucket+scan kernel of the busiest conv layer;
@@ -427,8 +435,10 @@ def run_b200(args):
                                  "integer-pipe utilisation"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "results_match_device_run": bool(e2e_ok),
                     "path": f"PipelinedForward, {chunks} sub-batches, real events only"
-                            + (" (whole rows)" if pf.full_rows else "")},
+                            + (" (whole rows)" if pf.full_rows else "")
+                            + ", steps enqueued back to back, per-step result slots"},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks.summary(),
         }

@@ -311,9 +311,20 @@ conv_fused(ConvLaunch P) {
   const int th = min(P.tile_h, P.h_out - oy0), tw = min(P.tile_w, P.w_out - ox0);
 
   const int zero_row = P.ic * KK * OCP;
-  for (int i = tid; i < zero_row + OCP; i += blockDim.x) {
-    const int tap = i / OCP, oc = i - tap * OCP;
-    w_s[i] = (oc < P.oc && i < zero_row) ? (WT)P.q[(int64_t)oc * P.ic * KK + tap] : (WT)0;
+  // the weight table's loads are issued kConvStageLoads at a time before they are stored
+  for (int i0 = tid; i0 < zero_row + OCP; i0 += blockDim.x * kConvStageLoads) {
+    int32_t v[kConvStageLoads];
+#pragma unroll
+    for (int u = 0; u < kConvStageLoads; ++u) {
+      const int i = i0 + u * (int)blockDim.x;
+      const int tap = i / OCP, oc = i - tap * OCP;
+      v[u] = (oc < P.oc && i < zero_row) ? __ldg(&P.q[(int64_t)oc * P.ic * KK + tap]) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kConvStageLoads; ++u) {
+      const int i = i0 + u * (int)blockDim.x;
+      if (i < zero_row + OCP) w_s[i] = (WT)v[u];
+    }
   }
   if (P.lut_in_smem)
     for (int i = tid; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];

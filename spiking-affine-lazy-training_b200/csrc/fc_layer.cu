@@ -74,12 +74,28 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   if (lut_words)
     for (int i = threadIdx.x; i < P.qc.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
   if (WT) {
-    if (P.G == 1) {  // the whole table, as laid out in global memory
-      for (int32_t i = threadIdx.x; i < zero_row; i += blockDim.x) q_s[i] = (QT)__ldg(&P.qT[i]);
-    } else {         // this group's LPU columns
-      for (int32_t i = threadIdx.x; i < zero_row; i += blockDim.x) {
-        const int32_t row = i / LPU, col = g * LPU + (i - row * LPU);
-        q_s[i] = col < P.n_out ? (QT)__ldg(&P.qT[(int64_t)row * P.n_out + col]) : (QT)0;
+    // kStageLoads loads per thread are issued before any is stored, so the staging costs a few
+    // global latencies instead of one per code (a block of a narrow layer stages its whole table
+    // and the sample chains start only after it)
+    for (int32_t i0 = threadIdx.x; i0 < zero_row; i0 += blockDim.x * kStageLoads) {
+      int32_t v[kStageLoads];
+#pragma unroll
+      for (int u = 0; u < kStageLoads; ++u) {
+        const int32_t i = i0 + u * (int32_t)blockDim.x;
+        v[u] = 0;
+        if (i < zero_row) {
+          if (P.G == 1) {  // the whole table, as laid out in global memory
+            v[u] = __ldg(&P.qT[i]);
+          } else {         // this group's LPU columns
+            const int32_t row = i / LPU, col = g * LPU + (i - row * LPU);
+            if (col < P.n_out) v[u] = __ldg(&P.qT[(int64_t)row * P.n_out + col]);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kStageLoads; ++u) {
+        const int32_t i = i0 + u * (int32_t)blockDim.x;
+        if (i < zero_row) q_s[i] = (QT)v[u];
       }
     }
     for (int32_t i = threadIdx.x; i < LPU; i += blockDim.x) q_s[zero_row + i] = 0;
@@ -108,21 +124,24 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
   int32_t* chunk_b = FIRES ? P.chunk_spikes + (int64_t)b * P.n_spk_chunks : nullptr;
   const int32_t nmax = __reduce_max_sync(kAll, nproc);
 
-  float tn[R];
-  int32_t sn[R];
-  auto load = [&](int32_t base) {
+  // the input stream is read two super-batches ahead: a super-batch's chain is shorter than a
+  // global load's latency at the occupancy of a narrow layer (one warp per scheduler)
+  float tn[R], tn2[R];
+  int32_t sn[R], sn2[R];
+  auto load = [&](int32_t base, float (&t)[R], int32_t (&sv)[R]) {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int32_t j = base + r * LPU + gl;
-      tn[r] = 0.0f;
-      sn[r] = 0;
+      t[r] = 0.0f;
+      sv[r] = 0;
       if (j < nproc) {
-        tn[r] = P.in.time(b, j, n_eff);
-        sn[r] = P.in.source(b, j, n_eff);
+        t[r] = P.in.time(b, j, n_eff);
+        sv[r] = P.in.source(b, j, n_eff);
       }
     }
   };
-  load(0);
+  load(0, tn, sn);
+  load(SB, tn2, sn2);
   int32_t V = 0, vmin = 0, vmax = 0, nspk = 0;
   float tcarry = 0.0f;
   for (int32_t base = 0; base < nmax; base += SB) {
@@ -132,8 +151,10 @@ __global__ void __launch_bounds__(kFcThreads) fc_scan(FCLaunch P) {
     for (int r = 0; r < R; ++r) {
       tc[r] = tn[r];
       scur[r] = sn[r];
+      tn[r] = tn2[r];
+      sn[r] = sn2[r];
     }
-    if (base + SB < nmax) load(base + SB);  // in flight while this super-batch runs
+    if (base + 2 * SB < nmax) load(base + 2 * SB, tn2, sn2);  // in flight for two super-batches
     // lane-parallel: Δt against the previous entry (connectivity/fc.py:26-29: the first
     // against t = 0, pads masked to Δt = 0 and weight 0), decay code and weight-row offset
 #pragma unroll

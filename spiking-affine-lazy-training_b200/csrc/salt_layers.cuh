@@ -8,7 +8,7 @@ namespace salt {
 constexpr int kFusedThreads = 256;   // conv_fused block size (8 warps)
 constexpr int kFusedChunk = 512;     // events bucketed per shared-memory chunk
 constexpr int kPartChunk = 1024;     // events per tile-partition block
-constexpr int kConvFillBlocks = 148 * 8;  // conv_fused blocks a launch should reach (tiling)
+constexpr int kConvFillBlocks = 148 * 16;  // conv_fused blocks a launch should reach (tiling)
 constexpr int kPartThreads = 256;    // tile-partition block size
 constexpr int kPartPer = kPartChunk / kPartThreads;  // events per partition thread
 constexpr int kCompactThreads = 256; // compaction block size == events per spike chunk
@@ -319,6 +319,8 @@ cudaError_t float_fc_trace_launch(const FTraceArgs& T, cudaStream_t stream);
 constexpr int kFcThreads = 128;
 constexpr int kFcRing = 4;            // events per lane per fc_scan super-batch (smem codes)
 constexpr int kFcStepBlock = 8;       // fc_scan steps whose loads are issued together
+constexpr int kStageLoads = 8;        // weight-table staging: global loads in flight per thread
+constexpr int kConvStageLoads = 4;    // the same for conv_fused (held to its register budget)
 constexpr size_t kFcQSmemMax = 96 * 1024;  // largest staged weight table of fc_scan
 
 }  // namespace salt

@@ -180,7 +180,14 @@ class PipelinedForward:
         rows = n.size * self.capacity if self.full_rows else int(n.sum())
         return int(rows * 8 + n.size * 4)
 
-    def __call__(self, times_h, src_h, n_real_h, sync: bool = True):
+    def wait_for(self, event) -> None:
+        """Orders this object's transfers after `event` (e.g. the start of a timed region)."""
+        self._copy.wait_event(event)
+
+    def __call__(self, times_h, src_h, n_real_h, sync: bool = True, out=None):
+        """out = (logits (B, n_out) int32, fits (B,) int32) pinned host arrays to receive this
+        call's results instead of the object's own buffers (calls enqueued back to back with
+        sync=False then keep their results apart)."""
         lib = _lib.lib()
         compute = current_stream()
         sub, E = self.sub, self.capacity
@@ -207,11 +214,12 @@ class PipelinedForward:
             self._used[i] = True
         if per_slice < self.n_layers:
             self.plan.forward_part(None, None, None, 0, self.batch, per_slice, self.n_layers)
-        self.plan.logits.copy_to(self.logits, sync=False, stream=compute)
-        self.plan.fits.copy_to(self.fits, sync=False, stream=compute)
+        logits_h, fits_h = out if out is not None else (self.logits, self.fits)
+        self.plan.logits.copy_to(logits_h, sync=False, stream=compute)
+        self.plan.fits.copy_to(fits_h, sync=False, stream=compute)
         if sync:
             compute.synchronize()
-        return self.logits, self.fits
+        return logits_h, fits_h
 
     def close(self) -> None:
         self._copy.synchronize()   # no copy still writes into the buffers about to be freed
