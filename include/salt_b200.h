@@ -127,7 +127,9 @@ salt_status salt_conv_layer_forward(const salt_conv_desc *layer, const salt_quan
  *   - Nothing has to start at zero: every call clears the counters it uses, on `stream`.
  *   - The first call on a device does a one-time setup (it looks up the scratch's device
  *     address, which loads the module holding it); make that first call before any stream
- *     capture.
+ *     capture.  The address is kept for the life of the process: a context reset
+ *     (cudaDeviceReset) reloads the library's device code and leaves the kept address stale, so
+ *     do not call this entry point on a device after resetting it.
  *   - All calls on one device share the one scratch: calls that may overlap in time (other
  *     streams, other host threads) race and corrupt each other's results.  Order them on one
  *     stream, or with events. */
@@ -147,7 +149,7 @@ salt_status salt_conv_layer_forward_noalloc(const salt_conv_desc *layer,
  * event_ms are (batch, n_neurons, L) or NULL.  per_neuron (optional, each pointer optional,
  * (batch, n_neurons) each) gives the first overflowing column (-1: none) with the register before
  * and after it, whether that column fired and its event time — the fields example/quant_run.py
- * (overflow_events, :191-223) reports — plus the unfitted extremes, v_final and the spike count.
+ * (overflow_events, :189-214) reports — plus the unfitted extremes, v_final and the spike count.
  * An analysis path: one thread per neuron rebuilds its queue from the stream. */
 typedef struct {
   int32_t *first_overflow;
@@ -205,7 +207,7 @@ salt_status salt_quant_scan_dense_trace(const salt_quant_desc *quant, int32_t n,
 
 /* ---------------------------------------------------------------- network plan
  * A native runtime object that chains layers on the device (salt_core/network.py:93-122
- * run_network, vmapped over the batch as Network.apply_batched :279-283) with every
+ * run_network, vmapped over the batch as Network.apply_batched :179-183) with every
  * intermediate stream kept in the workspace, optionally replayed as one CUDA graph.
  * Layer parameters are HOST pointers copied to the device at creation. */
 typedef struct {

@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import sys
 import time
 
 import numpy as np
@@ -34,17 +35,27 @@ class CommError(RuntimeError):
 class _UniqueId(ctypes.Structure):
     _fields_ = [("internal", ctypes.c_char * 128)]
 
+    @staticmethod
+    def from_bytes(raw: bytes) -> "_UniqueId":
+        if len(raw) != 128:
+            raise ValueError("an NCCL unique id has 128 bytes")
+        uid = _UniqueId()
+        ctypes.memmove(ctypes.addressof(uid), raw, 128)   # (the field itself reads as a copy)
+        return uid
+
+    def to_bytes(self) -> bytes:
+        return ctypes.string_at(ctypes.addressof(self), 128)
+
 
 def nccl():
     """libnccl.so.2 (the copy already in the process if another library loaded one)."""
     global _nccl
     if _nccl is None:
+        # by soname first: a process that already loaded an NCCL (another library's) shares it
         names = [os.environ.get("SALT_NCCL_LIBRARY") or "libnccl.so.2"]
-        try:
-            import nvidia.nccl  # a pip-installed NCCL, when present
-            names.append(os.path.join(list(nvidia.nccl.__path__)[0], "lib", "libnccl.so.2"))
-        except ImportError:
-            pass
+        names += [os.path.join(p, "nvidia", "nccl", "lib", "libnccl.so.2") for p in sys.path
+                  if p and os.path.exists(os.path.join(p, "nvidia", "nccl", "lib",
+                                                       "libnccl.so.2"))]
         err = None
         for name in names:
             try:
@@ -84,18 +95,15 @@ def nccl_version() -> int:
 def new_unique_id() -> bytes:
     uid = _UniqueId()
     _check(nccl().ncclGetUniqueId(ctypes.byref(uid)), "ncclGetUniqueId")
-    return ctypes.string_at(ctypes.addressof(uid), 128)
+    return uid.to_bytes()
 
 
 class NcclComm:
     """One rank of an NCCL communicator on the current device."""
 
     def __init__(self, rank: int, world: int, unique_id: bytes):
-        if len(unique_id) != 128:
-            raise ValueError("an NCCL unique id has 128 bytes")
         self.rank, self.world = int(rank), int(world)
-        uid = _UniqueId()
-        ctypes.memmove(uid.internal, unique_id, 128)
+        uid = _UniqueId.from_bytes(bytes(unique_id))
         comm = ctypes.c_void_p()
         _check(nccl().ncclCommInitRank(ctypes.byref(comm), self.world, uid, self.rank),
                "ncclCommInitRank")

@@ -11,7 +11,8 @@ namespace salt {
 static __device__ __align__(256) unsigned char g_fixed_scratch[SALT_NOALLOC_SCRATCH_BYTES];
 
 // Device address of g_fixed_scratch on the current device.  The first call on a device looks
-// the address up (cudaGetSymbolAddress, which loads the module); later calls read a cache.
+// the address up (cudaGetSymbolAddress, which loads the module); later calls read a cache.  A
+// context reset (cudaDeviceReset) reloads the module, and the cached address is then stale.
 cudaError_t fixed_scratch_address(void** ptr) {
   constexpr int kMaxDevices = 64;
   static std::mutex mu;

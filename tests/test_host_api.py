@@ -245,3 +245,12 @@ def test_package_never_imports_torch():
     r = subprocess.run([sys.executable, "-c", _NO_TORCH_IMPORTS.format(root=root)],
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip() == "ok", r.stderr[-2000:]
+
+
+def test_nccl_unique_id_survives_the_round_trip():
+    """The 128-byte NCCL unique id (with its zero bytes) reaches ncclCommInitRank unchanged."""
+    from salt_b200.comm import _UniqueId
+    raw = bytes(range(128))[::-1]
+    assert _UniqueId.from_bytes(raw).to_bytes() == raw
+    with pytest.raises(ValueError):
+        _UniqueId.from_bytes(b"short")
