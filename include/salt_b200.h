@@ -409,6 +409,9 @@ salt_status salt_set_device(int32_t device);
 salt_status salt_get_device(int32_t *device);
 salt_status salt_device_synchronize(void);
 salt_status salt_stream_create(void **stream);
+/* A non-blocking stream whose blocks the scheduler prefers (the device's greatest priority):
+ * for transfers that must overlap a kernel already filling the GPU. */
+salt_status salt_stream_create_high_priority(void **stream);
 salt_status salt_stream_destroy(void *stream);
 salt_status salt_stream_synchronize(void *stream);
 salt_status salt_stream_wait_event(void *stream, void *event);

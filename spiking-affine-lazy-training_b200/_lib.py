@@ -127,6 +127,7 @@ _SIGS = {
     "salt_get_device": (_i32, [_vp]),
     "salt_device_synchronize": (_i32, []),
     "salt_stream_create": (_i32, [_vp]),
+    "salt_stream_create_high_priority": (_i32, [_vp]),
     "salt_stream_destroy": (_i32, [_vp]),
     "salt_stream_synchronize": (_i32, [_vp]),
     "salt_stream_wait_event": (_i32, [_vp, _vp]),

@@ -900,6 +900,15 @@ salt_status salt_stream_create(void** stream) {
   return SALT_OK;
 }
 
+salt_status salt_stream_create_high_priority(void** stream) {
+  int least = 0, greatest = 0;
+  SALT_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  cudaStream_t s;
+  SALT_CUDA(cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, greatest));
+  *stream = (void*)s;
+  return SALT_OK;
+}
+
 salt_status salt_stream_destroy(void* stream) {
   if (stream) SALT_CUDA(cudaStreamDestroy((cudaStream_t)stream));
   return SALT_OK;

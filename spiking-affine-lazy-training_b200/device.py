@@ -63,13 +63,16 @@ def synchronize() -> None:
 # ---------------------------------------------------------------- streams and events
 
 class Stream:
-    """A CUDA stream.  Stream() creates a non-blocking stream; Stream.default() is the legacy
-    default stream (handle NULL)."""
+    """A CUDA stream.  Stream() creates a non-blocking stream (high_priority=True: one whose
+    blocks the scheduler prefers); Stream.default() is the legacy default stream (handle NULL)."""
 
-    def __init__(self, _handle: int | None = None, _owned: bool = True):
+    def __init__(self, _handle: int | None = None, _owned: bool = True,
+                 high_priority: bool = False):
         if _handle is None and _owned:
             h = ctypes.c_void_p()
-            _lib.check(_lib.lib().salt_stream_create(ctypes.byref(h)))
+            make = (_lib.lib().salt_stream_create_high_priority if high_priority
+                    else _lib.lib().salt_stream_create)
+            _lib.check(make(ctypes.byref(h)))
             _handle = h.value
         self.handle = _handle or 0
         self._owned = bool(_owned and self.handle)

@@ -167,7 +167,8 @@ class PipelinedForward:
         self._t = [empty((sub, E), np.float32) for _ in range(2)]
         self._s = [empty((sub, E), np.int32) for _ in range(2)]
         self._n = [empty((sub,), np.int32) for _ in range(2)]
-        self._copy = Stream()
+        # the gather kernel of the copy stream must get SM slots while a layer fills the GPU
+        self._copy = Stream(high_priority=True)
         self._ready = [Event() for _ in range(2)]
         self._free = [Event() for _ in range(2)]
         self._used = [False, False]   # buffer i was handed to a forward (this or an earlier call)
