@@ -233,9 +233,9 @@ def run_reference(args):
 
 
 # DRAM bytes (read + write) per input event of conv1's conv_fused launch, measured by ncu on the
-# 1024-sample configuration-3 case of the current kernel (profiles/conv_fused_config3.md, "v17"
-# rows: 185.0 + 143.4 MB for 7.77 M input events); reported scaled by the launch's input events.
-CONV_FUSED_DRAM_BYTES_PER_EVENT = (185.0e6 + 143.4e6) / 7.772496e6
+# 1024-sample configuration-3 case of the current kernel (profiles/conv_fused_config3.md, "v21"
+# rows: 183.6 + 140.3 MB for 7.77 M input events); reported scaled by the launch's input events.
+CONV_FUSED_DRAM_BYTES_PER_EVENT = (183.586e6 + 140.337e6) / 7.772496e6
 
 
 def _init_ranks(world, local):

@@ -139,10 +139,12 @@ class NetworkPlan:
 class PipelinedForward:
     """Host in, host out, with the transfer overlapped: the batch's first `slice_layers` layers
     run as `chunks` row slices, each starting as soon as its rows are on the device, while the
-    next slice is copied on a second stream into the other of two device buffers; the remaining
-    layers then run on the whole batch (salt_network_forward_part).  Each sample's row is copied only up to its
-    n_real (salt_stream_h2d_real) unless the first layer may fire on pad entries (needs_tail), in
-    which case whole rows are copied.
+    next slice is copied on a second (high-priority) stream into its own device buffer; the
+    remaining layers then run on the whole batch (salt_network_forward_part).  Calls enqueued
+    back to back overlap too: a slice's copy waits only for that slice's first layer of the
+    previous call.  Each sample's row is copied only up to its n_real (salt_stream_h2d_real)
+    unless the first layer may fire on pad entries (needs_tail), in which case whole rows are
+    copied.
 
     Host arrays should be pinned numpy arrays (device.pinned_empty / pinned_copy): times (B, E)
     float32, src (B, E) int32, n_real (B,) int32; the real-event gather requires pinned rows.
@@ -164,14 +166,17 @@ class PipelinedForward:
         qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
         self.full_rows = bool(qd.needs_tail)
         E, sub = self.capacity, self.sub
-        self._t = [empty((sub, E), np.float32) for _ in range(2)]
-        self._s = [empty((sub, E), np.int32) for _ in range(2)]
-        self._n = [empty((sub,), np.int32) for _ in range(2)]
+        # one device buffer per slice: a slice's copy waits only for the same slice's forward of
+        # the previous call, so consecutive calls keep the copy stream busy
+        nbuf = self.chunks
+        self._t = [empty((sub, E), np.float32) for _ in range(nbuf)]
+        self._s = [empty((sub, E), np.int32) for _ in range(nbuf)]
+        self._n = [empty((sub,), np.int32) for _ in range(nbuf)]
         # the gather kernel of the copy stream must get SM slots while a layer fills the GPU
         self._copy = Stream(high_priority=True)
-        self._ready = [Event() for _ in range(2)]
-        self._free = [Event() for _ in range(2)]
-        self._used = [False, False]   # buffer i was handed to a forward (this or an earlier call)
+        self._ready = [Event() for _ in range(nbuf)]
+        self._free = [Event() for _ in range(nbuf)]
+        self._used = [False] * nbuf   # buffer i was handed to a forward (this or an earlier call)
         self.logits = pinned_empty((batch, self.plan.n_out), np.int32)
         self.fits = pinned_empty((batch,), np.int32)
 
@@ -194,7 +199,7 @@ class PipelinedForward:
         sub, E = self.sub, self.capacity
         per_slice = self.slice_layers
         for k in range(self.chunks):
-            i = k % 2
+            i = k
             rows = slice(k * sub, (k + 1) * sub)
             copy = self._copy
             if self._used[i]:   # the forward that last read buffer i, in any call
