@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--graph", action="store_true",
                     help="time CUDA-graph replays of the forward (NetworkPlan.capture); kernel "
                          "times then come from an eager profiled pass after the timed region")
+    ap.add_argument("--e2e-chunks", type=int, default=1,
+                    help="row slices of the end-to-end pipelined forward")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target duration of the bounded CPU-baseline sample")
     args = ap.parse_args()
@@ -343,7 +345,7 @@ def run_b200(args):
     from salt_b200.plan import PipelinedForward
     t_h, s_h = D.pinned_copy(wl.times, np.float32), D.pinned_copy(wl.src, np.int32)
     n_h = D.pinned_copy(wl.n_real, np.int32)
-    chunks = 4 if B % 4 == 0 else 1
+    chunks = args.e2e_chunks if B % args.e2e_chunks == 0 else 1
     pf = PipelinedForward(layers, params, B, E, chunks=chunks)
     e2e_steps = max(1, min(args.steps, 20))
     ring = [(D.pinned_empty((B, n_out), np.int32), D.pinned_empty((B,), np.int32),

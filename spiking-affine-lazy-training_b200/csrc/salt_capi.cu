@@ -275,7 +275,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   //
   // A small batch would leave SMs idle behind a few long blocks (one heavy sample's whole plane
   // in one block): while batch x tiles stays below kConvFillBlocks, the tiles shrink (to no
-  // fewer than 16 positions), so each sample is spread over more blocks.  The workspace sizes
+  // fewer than 8 positions), so each sample is spread over more blocks.  The workspace sizes
   // take the finest tiling into account (conv_scratch_bytes), so a plan made for a batch also
   // serves its row slices.
   const size_t budget = 100 * 1024;
@@ -286,7 +286,9 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
       p.tile_h = p.h_out;
       p.tile_w = p.w_out;
     } else {
-      p.tile_w = std::min(p.w_out, std::max(16, p.ncand));
+      // 16 positions wide (8 below a 32-position cap, 4 below 16), never narrower than one
+      // candidate window
+      p.tile_w = std::min(p.w_out, std::max(p.ncand, std::min(16, cap / 2)));
       p.tile_h = std::max(1, cap / p.tile_w);
       p.tile_h = std::min(p.h_out, std::max(p.tile_h, std::min(p.ncand, p.h_out)));
       if (p.tile_w < p.w_out && p.tile_w < p.ncand) p.tile_w = std::min(p.w_out, p.ncand);
@@ -296,7 +298,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
     p.T = p.tiles_x * p.tiles_y;
   };
   tile_for(npm_cap);
-  while ((int64_t)std::max(batch, 1) * p.T < kConvFillBlocks && npm_cap > 16) {
+  while ((int64_t)std::max(batch, 1) * p.T < kConvFillBlocks && npm_cap > 8) {
     const int prev = npm_cap;
     npm_cap >>= 1;
     tile_for(npm_cap);

@@ -264,7 +264,7 @@ size_t fc_scan_q_bytes(int32_t n_in, int32_t n_out, int wt, int lpu);
 cudaError_t fixed_scratch_address(void** ptr);
 
 // Real-event rows of pinned host streams into device streams (stream_io.cu).
-constexpr int kGatherBlocks = 32, kGatherThreads = 512;
+constexpr int kGatherBlocks = 16, kGatherThreads = 256;
 cudaError_t gather_rows_launch(const float* ht, const int32_t* hs, const int32_t* n_real_dev,
                                int32_t batch, int32_t capacity, int64_t host_pitch, float* dt,
                                int32_t* ds, cudaStream_t st);

@@ -12,9 +12,11 @@
 
 namespace salt {
 
-// A few persistent blocks loop over the rows (16-byte loads where both rows allow them): the
-// host link is saturated by a small share of the GPU, so a layer running on the compute stream
-// keeps the rest of the SMs while the next rows arrive.
+// A few persistent blocks loop over the rows (16-byte loads where both rows allow them).  The
+// host reads in flight slow a layer running beside the gather, in proportion to their number
+// (measured against configuration 3's forward, 5.63 ms alone: 32 x 512 threads 7.68 ms per
+// overlapped step, 148 x 128 8.42, 32 x 128 6.23, 16 x 256 5.98, the gather alone 5.1-5.8 ms),
+// so the kernel keeps just enough of them to stay near the host link's rate.
 __global__ void __launch_bounds__(kGatherThreads)
 gather_rows_kernel(const float* __restrict__ ht, const int32_t* __restrict__ hs,
                    const int32_t* __restrict__ n_real, int32_t batch, int32_t capacity,

@@ -141,8 +141,8 @@ class PipelinedForward:
     run as `chunks` row slices, each starting as soon as its rows are on the device, while the
     next slice is copied on a second (high-priority) stream into its own device buffer; the
     remaining layers then run on the whole batch (salt_network_forward_part).  Calls enqueued
-    back to back overlap too: a slice's copy waits only for that slice's first layer of the
-    previous call.  Each sample's row is copied only up to its n_real (salt_stream_h2d_real)
+    back to back overlap too: the buffers form a ring of two per slice, so a slice's copy waits
+    only for the first layer that read its buffer two calls earlier.  Each sample's row is copied only up to its n_real (salt_stream_h2d_real)
     unless the first layer may fire on pad entries (needs_tail), in which case whole rows are
     copied.
 
@@ -166,9 +166,11 @@ class PipelinedForward:
         qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
         self.full_rows = bool(qd.needs_tail)
         E, sub = self.capacity, self.sub
-        # one device buffer per slice: a slice's copy waits only for the same slice's forward of
-        # the previous call, so consecutive calls keep the copy stream busy
-        nbuf = self.chunks
+        # a ring of two device buffers per slice: a slice's copy waits only for the first layer
+        # that read its buffer two calls earlier, so calls enqueued back to back keep the copy
+        # stream busy (a one-slice call's copy overlaps the previous call's whole forward)
+        nbuf = 2 * self.chunks
+        self._calls = 0
         self._t = [empty((sub, E), np.float32) for _ in range(nbuf)]
         self._s = [empty((sub, E), np.int32) for _ in range(nbuf)]
         self._n = [empty((sub,), np.int32) for _ in range(nbuf)]
@@ -198,8 +200,10 @@ class PipelinedForward:
         compute = current_stream()
         sub, E = self.sub, self.capacity
         per_slice = self.slice_layers
+        base = (self._calls % 2) * self.chunks
+        self._calls += 1
         for k in range(self.chunks):
-            i = k
+            i = base + k
             rows = slice(k * sub, (k + 1) * sub)
             copy = self._copy
             if self._used[i]:   # the forward that last read buffer i, in any call
