@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--graph", action="store_true",
                     help="time CUDA-graph replays of the forward (NetworkPlan.capture); kernel "
                          "times then come from an eager profiled pass after the timed region")
+    ap.add_argument("--overlap", action=argparse.BooleanOptionalAction, default=True,
+                    help="two batches in flight (two plans on two streams): step k+1 starts "
+                         "while step k's last layer runs")
     ap.add_argument("--e2e-chunks", type=int, default=1,
                     help="row slices of the end-to-end pipelined forward")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -288,15 +291,38 @@ def run_b200(args):
     gathered = D.empty((world * B, n_out), np.int32)
 
     replay = plan.capture(t_d, s_d, n_d) if args.graph else None
+    # consecutive steps with two batches in flight: a second plan (own workspace) on its own
+    # stream starts step k+1 while step k's last layer is still running
+    ov = None
+    if replay is None and args.overlap and len(layers) > 1:
+        from salt_b200.plan import OverlappedForward
+        ov = OverlappedForward(layers, params, B, E)
+        comm_stream = D.Stream() if comm is not None else None
+    last = {}
 
     def step():
+        if ov is not None:
+            logits, stats, fits, done = ov.submit(t_d, s_d, n_d)
+            last.update(logits=logits, stats=stats, fits=fits)
+            if comm is not None:   # the gather reads this plan's logits: its next batch waits
+                comm_stream.wait_event(done)
+                comm.all_gather(logits, gathered, stream=comm_stream)
+                ov.hold(D.Event().record(comm_stream))
+            return
         if replay is not None:
             replay()
             logits = plan.logits
         else:
             logits, _, _ = plan.forward_device(t_d, s_d, n_d)
+        last.update(logits=logits, stats=plan.stats, fits=plan.fits)
         if comm is not None:
             comm.all_gather(logits, gathered)
+
+    def join():
+        if ov is not None:
+            ov.join()
+            if comm is not None:
+                D.current_stream().wait_stream(comm_stream)
 
     def barrier():
         if comm is not None:
@@ -306,18 +332,21 @@ def run_b200(args):
             dist.barrier()
             D.synchronize()
 
+    prof = ov if ov is not None else plan
     for _ in range(args.warmup):
         step()
+    join()
     barrier()
-    plan.profile_read(reset=True)
+    prof.profile_read(reset=True)
     if replay is None:
-        plan.set_profiling(True)   # kernel times recorded live inside the timed region
+        prof.set_profiling(True)   # kernel times recorded live inside the timed region
     start, stop = D.Event(timing=True), D.Event(timing=True)
     with ClockSampler(D.current_device()) as clocks:
         barrier()
         start.record()
         for _ in range(args.steps):
             step()
+        join()
         stop.record()
         barrier()
     if replay is not None:   # graph replays record no per-kernel events: an eager profiled pass
@@ -325,12 +354,12 @@ def run_b200(args):
         for _ in range(min(args.steps, 20)):
             plan.forward_device(t_d, s_d, n_d)
         D.synchronize()
-    plan.set_profiling(False)
-    fused_ms, layer_ms, fused_n = plan.profile_read(reset=True)
-    launches_per_step = plan.last_launch_count()
+    prof.set_profiling(False)
+    fused_ms, layer_ms, fused_n = prof.profile_read(reset=True)
+    launches_per_step = prof.last_launch_count()
     ms = start.elapsed_ms(stop) / args.steps
     # the last forward's results, for the parity check against the oracle (rank 0, N = 1)
-    gpu_results = (plan.logits.numpy(), plan.stats[0].numpy(), plan.fits.numpy())
+    gpu_results = (last["logits"].numpy(), last["stats"][0].numpy(), last["fits"].numpy())
     ms_max = _reduce(dist, ms, "max")
     events_step = _reduce(dist, events_rank, "sum")
     value = events_step / (ms_max / 1000.0)
@@ -346,24 +375,38 @@ def run_b200(args):
     t_h, s_h = D.pinned_copy(wl.times, np.float32), D.pinned_copy(wl.src, np.int32)
     n_h = D.pinned_copy(wl.n_real, np.int32)
     chunks = args.e2e_chunks if B % args.e2e_chunks == 0 else 1
-    pf = PipelinedForward(layers, params, B, E, chunks=chunks)
+    overlap = bool(args.overlap and len(layers) > 1)
+    pf = PipelinedForward(layers, params, B, E, chunks=chunks, overlap=overlap)
     e2e_steps = max(1, min(args.steps, 20))
     ring = [(D.pinned_empty((B, n_out), np.int32), D.pinned_empty((B,), np.int32),
              D.pinned_empty((world * B, n_out), np.int32) if comm is not None else None)
             for _ in range(e2e_steps)]
+    gather_stream = D.Stream() if (comm is not None and overlap) else None
 
     def e2e_step(k):
         pf(t_h, s_h, n_h, sync=False, out=ring[k][:2])
-        if comm is not None:
+        if comm is not None and overlap:   # one stream for every gather, in call order
+            gather_stream.wait_event(pf.done)
+            comm.all_gather(pf.plan.logits, gathered, stream=gather_stream)
+            gathered.copy_to(ring[k][2], sync=False, stream=gather_stream)
+            pf.hold(D.Event().record(gather_stream))
+        elif comm is not None:
             comm.all_gather(pf.plan.logits, gathered)
             gathered.copy_to(ring[k][2], sync=False)
 
+    def e2e_join():
+        pf.join()
+        if gather_stream is not None:
+            D.current_stream().wait_stream(gather_stream)
+
     e2e_step(0)
+    e2e_join()
     barrier()
     start.record()
     pf.wait_for(start)
     for k in range(e2e_steps):
         e2e_step(k)
+    e2e_join()
     stop.record()
     barrier()
     e2e_ms = _reduce(dist, start.elapsed_ms(stop) / e2e_steps, "max")
@@ -440,17 +483,23 @@ def run_b200(args):
                     "results_match_device_run": bool(e2e_ok),
                     "path": f"PipelinedForward, {chunks} sub-batches, real events only"
                             + (" (whole rows)" if pf.full_rows else "")
-                            + ", steps enqueued back to back, per-step result slots"},
+                            + ", steps enqueued back to back, per-step result slots"
+                            + (", two steps in flight (two plans)" if overlap else "")},
             "gpu_launches": int(launches_per_step * args.steps),
             "clocks": clocks.summary(),
         }
         if replay is not None:
             line["layout"]["launch"] = "CUDA graph replay of the forward"
+        elif ov is not None:
+            line["layout"]["launch"] = ("two batches in flight: two plans on two streams, step "
+                                        "k+1's first layers beside step k's last layer")
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds, gpu=gpu_results)
             line["parity"] = line["cpu_baseline"].pop("parity")
         print(json.dumps(line), flush=True)
     plan.close()
+    if ov is not None:
+        ov.close()
     if comm is not None:
         comm.close()
     if dist is not None:

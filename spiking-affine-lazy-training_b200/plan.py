@@ -136,6 +136,87 @@ class NetworkPlan:
             pass
 
 
+class OverlappedForward:
+    """Consecutive batches with two in flight: two network plans (each with its own workspace)
+    on two streams take the batches in turn, and batch k+1's layers start as soon as batch k's
+    second-to-last layer is done, so batch k's last layer — a membrane readout whose time is one
+    sample's chain, with most of the GPU idle — runs beside batch k+1's first layers.  Every batch
+    is computed in full; only the idle tail of one overlaps the head of the next.
+
+    submit() enqueues one batch (device inputs, read-only) after the work already on the caller's
+    current stream and returns (logits, stats, fits, done): the outputs of the plan that took it
+    and an event recorded when they are final.  A plan's outputs are overwritten two submissions
+    later; pass `wait` events (e.g. a collective that reads the logits) that its next batch must
+    wait for.  join() makes the current stream wait for everything submitted."""
+
+    def __init__(self, layers, weights, batch: int, in_capacity: int, round_mode="round"):
+        require_cuda()
+        self.plans = [NetworkPlan(layers, weights, batch, in_capacity, round_mode) for _ in range(2)]
+        self.streams = [Stream(), Stream()]
+        self.entry = [Event(), Event()]       # the caller's stream reached the submission
+        self.head_done = [Event(), Event()]   # a batch's layers but the last are done
+        self.done = [Event(), Event()]
+        self.n_layers = len(self.plans[0].layers)
+        self.batch = int(batch)
+        self._waits = [[], []]
+        self._k = 0
+        self._launches = 0
+
+    def submit(self, times, src, n_real, wait=()):
+        i = self._k % 2
+        plan, st = self.plans[i], self.streams[i]
+        st.wait_event(self.entry[i].record(current_stream()))   # inputs ready
+        for ev in list(self._waits[i]) + list(wait):
+            st.wait_event(ev)
+        self._waits[i] = []
+        if self._k > 0:
+            st.wait_event(self.head_done[1 - i])             # the previous batch's head is done
+        nl, B = self.n_layers, self.batch
+        with use_stream(st):
+            if nl > 1:
+                plan.forward_part(times, src, n_real, 0, B, 0, nl - 1)
+                launches = plan.last_launch_count()
+                self.head_done[i].record(st)
+                plan.forward_part(None, None, None, 0, B, nl - 1, nl)
+                launches += plan.last_launch_count()
+            else:
+                plan.forward_device(times, src, n_real)
+                launches = plan.last_launch_count()
+                self.head_done[i].record(st)
+        self._launches = launches
+        self.done[i].record(st)
+        self._k += 1
+        return plan.logits, plan.stats, plan.fits, self.done[i]
+
+    def hold(self, event) -> None:
+        """The plan that took the last batch starts its next batch only after `event` (a reader of
+        its outputs, e.g. the logits all-gather)."""
+        self._waits[(self._k - 1) % 2].append(event)
+
+    def join(self) -> None:
+        for ev in self.done:
+            current_stream().wait_event(ev)
+
+    def set_profiling(self, enable: bool) -> None:
+        for p in self.plans:
+            p.set_profiling(enable)
+
+    def profile_read(self, reset: bool = True):
+        """Per-layer fused-kernel ms, whole-layer ms and timed forwards, summed over both plans."""
+        parts = [p.profile_read(reset) for p in self.plans]
+        return tuple(sum(x[j] for x in parts) for j in range(3))
+
+    def last_launch_count(self) -> int:
+        """Kernel launches of the last submission."""
+        return self._launches
+
+    def close(self) -> None:
+        for st in self.streams:
+            st.synchronize()
+        for p in self.plans:
+            p.close()
+
+
 class PipelinedForward:
     """Host in, host out, with the transfer overlapped: the batch's first `slice_layers` layers
     run as `chunks` row slices, each starting as soon as its rows are on the device, while the
@@ -150,17 +231,35 @@ class PipelinedForward:
     float32, src (B, E) int32, n_real (B,) int32; the real-event gather requires pinned rows.
     Returns pinned (logits (B, n_out) int32, fits (B,) int32) filled in place; with sync=False
     the call returns once everything is enqueued, and the buffers hold the results when the
-    current stream reaches the end of the call (the next call reuses them)."""
+    current stream reaches the end of the call (the next call reuses them).
+
+    overlap=True keeps two calls in flight: two plans on two streams of this object take the
+    calls in turn, and a call's layers start once the previous call's layers but the last are
+    done (the last layer, a readout with most of the GPU idle, runs beside the next call's first
+    layers).  The caller's current stream then does not wait for a call: `done` is the event
+    recorded when the last call's results are on the host, `plan` the plan that computed them
+    (its device outputs stay valid until two calls later, or longer with hold()), and join()
+    makes the current stream wait for every call."""
 
     def __init__(self, layers, weights, batch: int, in_capacity: int, chunks: int = 4,
-                 round_mode="round", slice_layers: int = 1):
+                 round_mode="round", slice_layers: int = 1, overlap: bool = False):
         require_cuda()
         if batch % chunks:
             raise ValueError(f"batch {batch} is not a multiple of chunks {chunks}")
         self.batch, self.chunks, self.sub = int(batch), int(chunks), int(batch) // int(chunks)
         self.capacity = int(in_capacity)
-        self.plan = NetworkPlan(layers, weights, self.batch, self.capacity, round_mode)
+        self.overlap = bool(overlap)
+        self.plans = [NetworkPlan(layers, weights, self.batch, self.capacity, round_mode)
+                      for _ in range(2 if self.overlap else 1)]
+        self.plan = self.plans[0]
         self.n_layers = len(self.plan.layers)
+        if self.overlap:
+            self._streams = [Stream(), Stream()]
+            self._entry = [Event(), Event()]
+            self._head_done = [Event(), Event()]
+            self._done = [Event(), Event()]
+            self._waits = [[], []]
+        self.done = None
         # layers run per slice as the slice arrives; the rest run once on the whole batch
         self.slice_layers = max(1, min(int(slice_layers), self.n_layers))
         qd, _ = quant_desc(weights[0], round_mode, layers[0].n_neurons)
@@ -192,16 +291,48 @@ class PipelinedForward:
         """Orders this object's transfers after `event` (e.g. the start of a timed region)."""
         self._copy.wait_event(event)
 
+    def hold(self, event) -> None:
+        """overlap=True: the plan of the last call takes its next call only after `event` (a
+        reader of its device outputs, e.g. a logits all-gather)."""
+        self._waits[(self._calls - 1) % 2].append(event)
+
+    def join(self) -> None:
+        """Makes the current stream wait for every call enqueued so far."""
+        if self.overlap:
+            for ev in self._done:
+                current_stream().wait_event(ev)
+
     def __call__(self, times_h, src_h, n_real_h, sync: bool = True, out=None):
         """out = (logits (B, n_out) int32, fits (B,) int32) pinned host arrays to receive this
         call's results instead of the object's own buffers (calls enqueued back to back with
         sync=False then keep their results apart)."""
         lib = _lib.lib()
-        compute = current_stream()
-        sub, E = self.sub, self.capacity
-        per_slice = self.slice_layers
-        base = (self._calls % 2) * self.chunks
+        call = self._calls
         self._calls += 1
+        if self.overlap:
+            j = call % 2
+            plan, compute = self.plans[j], self._streams[j]
+            compute.wait_event(self._entry[j].record(current_stream()))
+            for ev in self._waits[j]:
+                compute.wait_event(ev)
+            self._waits[j] = []
+            if call > 0:   # the previous call's layers but its last are done
+                compute.wait_event(self._head_done[1 - j])
+        else:
+            plan, compute = self.plans[0], current_stream()
+        self.plan = plan
+        with use_stream(compute):
+            out = self._enqueue(lib, plan, compute, call, times_h, src_h, n_real_h, out)
+        if self.overlap:
+            self.done = self._done[call % 2].record(compute)
+        if sync:
+            compute.synchronize()
+        return out
+
+    def _enqueue(self, lib, plan, compute, call, times_h, src_h, n_real_h, out):
+        sub, E = self.sub, self.capacity
+        per_slice, nl = self.slice_layers, self.n_layers
+        base = (call % 2) * self.chunks
         for k in range(self.chunks):
             i = base + k
             rows = slice(k * sub, (k + 1) * sub)
@@ -218,20 +349,26 @@ class PipelinedForward:
                     ptr(self._n[i]), sub, E, ptr(self._t[i]), ptr(self._s[i]), copy.ptr))
             self._ready[i].record(copy)
             compute.wait_event(self._ready[i])
-            self.plan.forward_part(self._t[i], self._s[i], self._n[i], k * sub, sub, 0,
-                                   per_slice)
+            plan.forward_part(self._t[i], self._s[i], self._n[i], k * sub, sub, 0, per_slice)
             self._free[i].record(compute)
             self._used[i] = True
-        if per_slice < self.n_layers:
-            self.plan.forward_part(None, None, None, 0, self.batch, per_slice, self.n_layers)
+        # the remaining layers on the whole batch; with overlap, the last one after head_done
+        head_end = max(per_slice, nl - 1) if self.overlap else nl
+        if per_slice < head_end:
+            plan.forward_part(None, None, None, 0, self.batch, per_slice, head_end)
+        if self.overlap:
+            self._head_done[call % 2].record(compute)
+        if head_end < nl:
+            plan.forward_part(None, None, None, 0, self.batch, head_end, nl)
         logits_h, fits_h = out if out is not None else (self.logits, self.fits)
-        self.plan.logits.copy_to(logits_h, sync=False, stream=compute)
-        self.plan.fits.copy_to(fits_h, sync=False, stream=compute)
-        if sync:
-            compute.synchronize()
+        plan.logits.copy_to(logits_h, sync=False, stream=compute)
+        plan.fits.copy_to(fits_h, sync=False, stream=compute)
         return logits_h, fits_h
 
     def close(self) -> None:
         self._copy.synchronize()   # no copy still writes into the buffers about to be freed
+        for st in (self._streams if self.overlap else []):
+            st.synchronize()
         current_stream().synchronize()
-        self.plan.close()
+        for plan in self.plans:
+            plan.close()

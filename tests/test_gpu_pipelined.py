@@ -152,3 +152,84 @@ def test_network_whose_last_layer_fires():
             refs = O.network_forward(net.layers, params, times[b], src[b], nr[b])
             np.testing.assert_array_equal(logits[b], refs[-1].v_final)
             assert [int(v) for v in stats[0, :, b]] == [r.n_real_events for r in refs]
+
+
+def test_overlapped_batches_equal_the_batched_plan():
+    """Two batches in flight (two plans on two streams): every submission's logits, stats and
+    fits equal a single plan's forward of the same batch, with the outputs read on a stream that
+    waits only for that submission's done event, and a held event delaying a plan's reuse."""
+    from salt_b200.plan import OverlappedForward
+    rng = np.random.default_rng(13)
+    net, params = _net(rng, (60, 160))
+    B, E = 32, 600
+    sets = []
+    for _ in range(3):
+        times, src, nr = make_events(rng, B, E, 2 * 12 * 12)
+        sets.append((D.to_device(times, np.float32), D.to_device(src, np.int32),
+                     D.to_device(nr, np.int32)))
+    plan = NetworkPlan(net.layers, params, B, E)
+    refs = []
+    for t, s, n in sets:
+        logits, stats, fits = plan.forward_device(t, s, n)
+        refs.append((logits.numpy(), stats.numpy(), fits.numpy()))
+    ov = OverlappedForward(net.layers, params, B, E)
+    reader = D.Stream()
+    out_l = D.empty((7, B, plan.n_out), np.int32)
+    out_s = D.empty((7,) + tuple(plan.stats.shape), np.int32)
+    out_f = D.empty((7, B), np.int32)
+    for r in range(7):
+        logits, stats, fits, done = ov.submit(*sets[r % 3])
+        reader.wait_event(done)
+        out_l[r].copy_from_device(logits, stream=reader)
+        out_s[r].copy_from_device(stats, stream=reader)
+        out_f[r].copy_from_device(fits, stream=reader)
+        ov.hold(D.Event().record(reader))
+    ov.join()
+    D.synchronize()
+    assert ov.last_launch_count() > 0
+    for r in range(7):
+        ref = refs[r % 3]
+        np.testing.assert_array_equal(out_l[r].numpy(), ref[0])
+        np.testing.assert_array_equal(out_s[r].numpy(), ref[1])
+        np.testing.assert_array_equal(out_f[r].numpy(), ref[2])
+    ov.close()
+    plan.close()
+
+
+@pytest.mark.parametrize("chunks", [1, 4])
+def test_overlapped_pipelined_calls(chunks):
+    """overlap=True: calls enqueued back to back on two plans, each into its own pinned result
+    slot, with a device reader of each call's logits holding that plan; all equal the batched
+    plan."""
+    rng = np.random.default_rng(17)
+    net, params = _net(rng, (60, 160))
+    B, E = 32, 600
+    sets = []
+    for _ in range(3):
+        times, src, nr = make_events(rng, B, E, 2 * 12 * 12)
+        sets.append((D.pinned_copy(times), D.pinned_copy(src), D.pinned_copy(nr, np.int32)))
+    plan = NetworkPlan(net.layers, params, B, E)
+    refs = []
+    for t, s, n in sets:
+        logits, _, fits = plan.forward_device(D.to_device(t, np.float32), D.to_device(s, np.int32),
+                                              D.to_device(n, np.int32))
+        refs.append((logits.numpy(), fits.numpy()))
+    pf = PipelinedForward(net.layers, params, B, E, chunks=chunks, overlap=True)
+    reader = D.Stream()
+    dev = D.empty((7, B, plan.n_out), np.int32)
+    slots = [(D.pinned_empty((B, plan.n_out), np.int32), D.pinned_empty((B,), np.int32))
+             for _ in range(7)]
+    for r in range(7):
+        pf(*sets[r % 3], sync=False, out=slots[r])
+        reader.wait_event(pf.done)
+        dev[r].copy_from_device(pf.plan.logits, stream=reader)
+        pf.hold(D.Event().record(reader))
+    pf.join()
+    D.synchronize()
+    got = dev.numpy()
+    for r in range(7):
+        np.testing.assert_array_equal(slots[r][0], refs[r % 3][0])
+        np.testing.assert_array_equal(slots[r][1], refs[r % 3][1])
+        np.testing.assert_array_equal(got[r], refs[r % 3][0])
+    pf.close()
+    plan.close()
