@@ -26,21 +26,6 @@
 
 namespace salt {
 
-// Valid candidate ranges of one event (both axes).
-struct EvCand {
-  int32_t oy_min, oy_lo, oy_hi, ox_min, ox_lo, ox_hi;
-  __device__ __forceinline__ bool empty() const { return oy_lo > oy_hi || ox_lo > ox_hi; }
-};
-
-__device__ __forceinline__ EvCand event_cand(const ConvLaunch& P, int32_t src, int32_t& c,
-                                             int32_t& y, int32_t& x) {
-  EvCand r;
-  P.decode(src, c, y, x);
-  P.axis(y, P.h_out, r.oy_min, r.oy_lo, r.oy_hi);
-  P.axis(x, P.w_out, r.ox_min, r.ox_lo, r.ox_hi);
-  return r;
-}
-
 // ------------------------------------------------------------------ schedule
 
 // Samples by decreasing event count: a stable-enough counting sort over 1024 bins of

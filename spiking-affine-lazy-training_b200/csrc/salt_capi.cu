@@ -2,6 +2,7 @@
 // include/salt_b200.h and the native network plan.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -206,6 +207,10 @@ struct ConvPlan {
   int32_t tile_h, tile_w, tiles_x, tiles_y, T, n_part_chunks, n_spk_chunks, tail_mode;
   int64_t list_stride;
   size_t smem;
+  // queue form (conv_queue): whole-sample position queues instead of per-chunk walks
+  bool queue;
+  int32_t grp_in_smem;
+  int64_t queue_stride;       // queue entries per sample
 };
 
 // A launch block carrying only what the shared-memory layout depends on.
@@ -224,7 +229,22 @@ static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, cons
   L.T = T;
   L.lut_in_smem = q->lut_len <= kLutSmemMax;
   L.qc.lut_len = q->lut_len;
-  return conv_fused_smem_bytes(L, p.wt_bytes);
+  L.n_spk_chunks = p.n_spk_chunks;
+  L.grp_in_smem = p.grp_in_smem;
+  return p.queue ? conv_queue_smem_bytes(L, p.wt_bytes) : conv_fused_smem_bytes(L, p.wt_bytes);
+}
+
+// The queue form serves layers whose catch-up/identity columns cannot fire (no needs_tail: decay
+// codes and the identity code 2^f_a fit 16 bits) and whose weight rows, zero row included, have
+// 16-bit offsets.  SALT_CONV_FORM=chunked in the environment selects conv_fused for every layer
+// (a comparison switch; both forms give identical results).
+static bool queue_form(const salt_conv_desc* d, const salt_quant_desc* q, int ocp) {
+  static const bool chunked = [] {
+    const char* v = getenv("SALT_CONV_FORM");
+    return v && strcmp(v, "chunked") == 0;
+  }();
+  if (chunked || q->needs_tail) return false;
+  return (int64_t)(d->ic * d->k * d->k + 1) * ocp <= 65536;
 }
 
 // Step form of a layer's hot loop (salt_common.cuh).  Without needs_tail every decay code lies
@@ -264,6 +284,9 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.ocp = p.G * lpu;
   p.wt_bytes = q->q_bits <= 8 ? 1 : (q->q_bits <= 16 ? 2 : 4);
   p.tail_mode = q->needs_tail ? 1 : 0;
+  p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
+  p.queue = queue_form(d, q, p.ocp);
+  p.grp_in_smem = (int64_t)p.n_spk_chunks * 4 <= 32 * 1024;
   // Positions per block: at most 64 (fewer positions per block means more of each position's
   // events per 512-event chunk, so the per-position setup of the recurrence is shared by more
   // events, and more, smaller blocks), within a ~100 KB shared-memory budget, never fewer than
@@ -278,8 +301,11 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   // fewer than 8 positions), so each sample is spread over more blocks.  The workspace sizes
   // take the finest tiling into account (conv_scratch_bytes), so a plan made for a batch also
   // serves its row slices.
+  //
+  // The queue form has no per-chunk walk to amortise: its blocks take up to 256 positions (one
+  // thread per position in its count and scan phases), and a whole plane needs no partition.
   const size_t budget = 100 * 1024;
-  int npm_cap = E < p.n_sp ? 256 : 64;
+  int npm_cap = (p.queue || E < p.n_sp) ? 256 : 64;
   while (npm_cap > 1 && fused_smem(d, q, p, 1, npm_cap, 2) > budget) npm_cap >>= 1;
   auto tile_for = [&](int cap) {
     if (p.n_sp <= cap) {
@@ -311,7 +337,10 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   const int per_x = p.tiles_x > 1 ? (p.ncand - 1 + p.tile_w - 1) / p.tile_w + 1 : 1;
   p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
   p.n_part_chunks = (E + kPartChunk - 1) / kPartChunk;
-  p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
+  // a tile's queues hold at most nslots entries per tile event
+  p.queue_stride = p.queue ? (int64_t)p.nslots * (p.T > 1 ? p.list_stride : E) : 0;
+  if (p.queue && p.tile_h * p.tile_w > kFusedThreads)
+    return fail(SALT_BAD_ARG, "queue form: tile larger than a block");
   if (p.T > 1 && conv_scatter_smem(p.T) > 227 * 1024)
     return fail(SALT_BAD_ARG, "conv output plane too large: its tile partition needs more shared "
                               "memory than a block has (at most 894 tiles)");
@@ -327,6 +356,7 @@ struct ConvScratch {
   size_t stats_bytes;
   uint32_t* sw;
   int32_t *tail_cnt, *counts, *tile_len, *tile_off, *lists, *hist, *order;
+  int2* queues;
 };
 
 static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, int32_t E,
@@ -357,6 +387,7 @@ static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, 
   }
   s.hist = c.take<int32_t>((size_t)B * 2 * p.n_sp);
   s.order = c.take<int32_t>((size_t)B);
+  s.queues = p.queue ? c.take<int2>((size_t)B * p.queue_stride) : nullptr;
   return c.size();
 }
 
@@ -428,6 +459,10 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.tail_mode = p.tail_mode; L.tail_cnt = s.tail_cnt;
   L.tile_len = s.tile_len; L.tile_off = s.tile_off; L.tile_lists = s.lists;
   L.order = B >= kOrderMinBatch ? s.order : nullptr;  // small batches: launch-bound anyway
+  L.queues = s.queues;
+  L.queue_stride = p.queue_stride;
+  L.fd_sww = FastDiv((uint32_t)(p.nslots * p.G));
+  L.grp_in_smem = p.grp_in_smem;
 
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
   if (L.order) {
@@ -450,8 +485,10 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     SALT_LAUNCHED("conv_tile_scatter");
   }
   // a neuron sees at most max_queue_len weighted steps
-  void* fn = conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE,
-                               step_form(q, d->max_queue_len));
+  const int form = step_form(q, d->max_queue_len);
+  void* fn = p.queue ? conv_queue_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form)
+                     : conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form);
+  if (!fn) return fail(SALT_BAD_ARG, "conv layer: no kernel for this step form");
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
   void* args[] = {&L};
   if (timer) SALT_CUDA(cudaEventRecord(timer->start, st));

@@ -66,6 +66,12 @@ struct ConvLaunch {
   const int32_t* tile_len;    // [B][T] events per tile
   const int32_t* tile_off;    // [B][T] start of each tile's list in the sample's region
   const int32_t* tile_lists;  // [B][list_stride] event indices, tile-major, arrival order
+  // queue form (conv_queue): per (sample, tile) the kept candidates of every position, position
+  // by position in arrival order, as (weight row << 16 | decay code, spike-word index) pairs
+  int2* queues;               // [B][queue_stride]
+  int64_t queue_stride;
+  FastDiv fd_sww;             // spike words per event (nslots * G)
+  int32_t grp_in_smem;        // per-group spike counts gathered in shared memory
 
   __device__ __forceinline__ int32_t n_eff(int b) const {
     int32_t n = in_nreal[b];
@@ -98,6 +104,21 @@ struct ConvLaunch {
     hi = min(min(upper, o_min + ncand - 1), O - 1);
   }
 };
+
+// Valid candidate ranges of one event (both axes).
+struct EvCand {
+  int32_t oy_min, oy_lo, oy_hi, ox_min, ox_lo, ox_hi;
+  __device__ __forceinline__ bool empty() const { return oy_lo > oy_hi || ox_lo > ox_hi; }
+};
+
+__device__ __forceinline__ EvCand event_cand(const ConvLaunch& P, int32_t src, int32_t& c,
+                                             int32_t& y, int32_t& x) {
+  EvCand r;
+  P.decode(src, c, y, x);
+  P.axis(y, P.h_out, r.oy_min, r.oy_lo, r.oy_hi);
+  P.axis(x, P.w_out, r.ox_min, r.ox_lo, r.ox_hi);
+  return r;
+}
 
 struct FCLaunch {
   int32_t n_in, n_out, G;
@@ -252,6 +273,12 @@ inline size_t conv_scatter_smem(int T) {
 }
 // Dynamic shared memory conv_fused needs for a launch configuration (same layout as the kernel).
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
+// The queue form of the fused kernel (conv_queue.cu), for layers without needs_tail: form
+// kStepWide or kStepWideNoFit (null otherwise); its dynamic shared memory.
+constexpr int kQueueChunk = 256;     // events bucketed per chunk: one per conv_queue thread
+static_assert(kQueueChunk == kFusedThreads, "conv_queue buckets one event per thread");
+void* conv_queue_kernel(int wt_bytes, int lpu, bool saturate, int form);
+size_t conv_queue_smem_bytes(const ConvLaunch& P, int wt_bytes);
 // lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons;
 // wt: bytes per weight code staged in shared memory (1, 2, 4), 0 to read them from global.
 void* fc_scan_kernel(bool fires, bool saturate, int lpu, int wt, int form);
