@@ -13,16 +13,17 @@
 //               buckets), so that lane groups sharing a warp walk queues of similar length and
 //               the longest queues start first.
 //   2. queue    256-event chunks in arrival order are bucketed by position into one bitmask word
-//               per warp (match_any); a column scan per position turns the words into ranks and
-//               predecessors, and every candidate writes its queue entry at (position offset +
-//               entries already queued + rank): the weight row of its tap and the decay code of
-//               its Δt to the position's previous event — the (position, arrival) order of
-//               conv.py:71 — or, past max_queue_len, a zero spike word (a dropped column never
-//               fires).
+//               per warp (match_any); a column scan per position turns the words into ranks, and
+//               every candidate writes its queue entry at (position offset + entries already
+//               queued + rank) — the (position, arrival) order of conv.py:71 — holding its event
+//               time, the weight row of its tap and its spike-word index; past max_queue_len it
+//               writes a zero spike word instead (a dropped column never fires).
 //   3. walk     lane groups (one lane per output channel) take the positions in that order and
-//               run each whole queue with the membrane register in a register, then the catch-up
-//               column (conv.py:102-125 regimes).  Spike words go straight to the event's slot;
-//               spikes per 32-event group are counted in shared memory.
+//               run each whole queue with the membrane register in a register: per batch of
+//               entries the lanes form each Δt to the previous entry and its decay code, then the
+//               recurrence walks the batch; then the catch-up column (conv.py:102-125 regimes).
+//               Spike words go straight to the event's slot; spikes per 32-event group are
+//               counted in shared memory.
 //
 // The queues live in global memory (8 bytes per kept candidate); a block reads back only what it
 // wrote moments before, so they are served from L2.
@@ -49,9 +50,9 @@ struct QueueSmem {
     run = o;    o += align16(npm * 4);           // entries queued so far per position
     lastt = o;  o += align16(npm * 4);           // time of the position's latest event so far
     order = o;  o += align16(npm * 4);           // positions by decreasing kept length
-    mask = o;   o += align16(chw * npm * 4);     // [warp word][position] chunk bitmasks
-    pre = o;    o += align16(chw * npm * 4);     // [warp word][position] rank | predecessor
-    evt = o;    o += align16((size_t)kQueueChunk * 4);
+    mask = o;   o += align16(2 * chw * npm * 4); // [chunk parity][warp word][position] bitmasks
+    pre = o;    o += align16(chw * npm * 4);     // [warp word][position] entries before the word
+    evt = o;    o += align16(2 * (size_t)kQueueChunk * 4);  // [chunk parity] event times
     grp = o;    o += align16((size_t)(P.grp_in_smem ? P.n_spk_chunks : 0) * 4);
     bucket = o; o += align16((size_t)kQBuckets * 4);
     // 32-lane groups park each batch's (decay code, weight row) pairs and step ballots per warp
@@ -150,7 +151,7 @@ conv_queue(ConvLaunch P) {
     run_s[i] = 0;
     lastt_s[i] = 0.0f;  // a queue's first Δt is measured from time 0
   }
-  for (int i = tid; i < CHW * NPM; i += blockDim.x) mask_s[i] = 0u;
+  for (int i = tid; i < 2 * CHW * NPM; i += blockDim.x) mask_s[i] = 0u;
   const int32_t n_eff = P.n_eff(b);
   const int32_t n_groups = (n_eff + kConvGroup - 1) >> kConvGroupShift;
   if (P.grp_in_smem)
@@ -248,15 +249,22 @@ conv_queue(ConvLaunch P) {
     if (real) order_s[bucket_s[bk] + rk] = tid;
   }
 
-  // -------- 2. queue entries, 256 events (one per thread) at a time in arrival order
+  // -------- 2. queue entries, 256 events (one per thread) at a time in arrival order.  The
+  // chunk bitmasks and event times are double-buffered, so a chunk needs two block barriers:
+  // after bucketing and after the column scan; the scan also retires the previous chunk
+  // (queued counts, latest event time, clearing its masks).
   const uint32_t lt_mask = (1u << lane) - 1u;
+  int32_t prev_col = 0, prev_last = -1;
+  int par = 0;
 #pragma unroll 1
-  for (int32_t base = 0; base < nev; base += kQueueChunk) {  // block-uniform trip count
+  for (int32_t base = 0; base < nev; base += kQueueChunk, par ^= 1) {  // block-uniform
+    uint32_t* mask_c = mask_s + par * CHW * NPM;
+    float* evt_c = evt_s + par * kQueueChunk;
     int32_t j = 0, c = 0, y = 0, x = 0;
     const int32_t e = base + tid;
     const EvCand k = candidates(e, j, c, y, x);
     const float t = e < nev ? P.in.times[row * P.in.capacity + j] : 0.0f;
-    evt_s[tid] = t;
+    evt_c[tid] = t;
     // bucket: one word per warp and position; the group's first lane ORs the group's lanes in
     if (P.ncand == 2) {
       const uint32_t vb = window_bits(k);
@@ -264,7 +272,7 @@ conv_queue(ConvLaunch P) {
       const int32_t key = vb ? (((ly + 2) << 13) | ((lx + 2) << 4) | (int32_t)vb) : -1;
       const uint32_t same = __match_any_sync(kAll, key);
       if (vb && (__ffs(same) - 1) == lane) {
-        uint32_t* m0 = mask_s + warp * NPM + ly * P.tile_w + lx;  // slot (0, 0)
+        uint32_t* m0 = mask_c + warp * NPM + ly * P.tile_w + lx;  // slot (0, 0)
         if (vb & 1u) atomicOr(m0, same);
         if (vb & 2u) atomicOr(m0 + 1, same);
         if (vb & 4u) atomicOr(m0 + P.tile_w, same);
@@ -277,53 +285,53 @@ conv_queue(ConvLaunch P) {
           const bool ok = oy >= k.oy_lo && oy <= k.oy_hi && ox >= k.ox_lo && ox <= k.ox_hi;
           const int pl = ok ? (oy - oy0) * P.tile_w + (ox - ox0) : -1;
           const uint32_t same = __match_any_sync(kAll, pl);
-          if (ok && (__ffs(same) - 1) == lane) atomicOr(&mask_s[warp * NPM + pl], same);
+          if (ok && (__ffs(same) - 1) == lane) atomicOr(&mask_c[warp * NPM + pl], same);
         }
     }
     __syncthreads();
-    // column scan per position: entries before each word, and the chunk event before it
-    int32_t col = 0, last = -1;
     if (tid < NPM) {
+      // retire the previous chunk of this position
+      if (base > 0) {
+        uint32_t* mask_p = mask_s + (par ^ 1) * CHW * NPM;
+        run_s[tid] += prev_col;
+        if (prev_last >= 0) lastt_s[tid] = evt_s[(par ^ 1) * kQueueChunk + prev_last];
+#pragma unroll
+        for (int w = 0; w < CHW; ++w) mask_p[w * NPM + tid] = 0u;
+      }
+      // column scan: entries of this position before each warp's word
+      int32_t col = 0, last = -1;
 #pragma unroll
       for (int w = 0; w < CHW; ++w) {
-        const uint32_t m = mask_s[w * NPM + tid];
-        pre_s[w * NPM + tid] = (uint32_t)col | ((uint32_t)(last + 1) << 16);
+        const uint32_t m = mask_c[w * NPM + tid];
+        pre_s[w * NPM + tid] = (uint32_t)col;
         col += __popc(m);
         if (m) last = w * 32 + 31 - __clz(m);
       }
+      prev_col = col;
+      prev_last = last;
     }
     __syncthreads();
     if (e < nev) {
       const int32_t ckk = c * KK, yp = y + P.p, xp = x + P.p;
+      const int32_t tb = __float_as_int(t);
       for (int oy = k.oy_lo; oy <= k.oy_hi; ++oy)
         for (int ox = k.ox_lo; ox <= k.ox_hi; ++ox) {
           const int pl = (oy - oy0) * P.tile_w + (ox - ox0);
-          const uint32_t before = mask_s[warp * NPM + pl] & lt_mask;
-          const uint32_t pr = pre_s[warp * NPM + pl];
-          const int32_t qi = run_s[pl] + (int32_t)(pr & 0xffffu) + __popc(before);
+          const uint32_t before = mask_c[warp * NPM + pl] & lt_mask;
+          const int32_t qi = run_s[pl] + (int32_t)pre_s[warp * NPM + pl] + __popc(before);
           const int slot = (oy - k.oy_min) * P.ncand + (ox - k.ox_min);
-          const int32_t widx = j * SWW + slot * P.G;
+          const uint32_t widx = (uint32_t)(j * SWW + slot * P.G);
           if (qi < P.L) {
-            const int pred = before ? warp * 32 + 31 - __clz(before) : (int)(pr >> 16) - 1;
-            const float tprev = pred >= 0 ? evt_s[pred] : lastt_s[pl];
-            const int32_t dt = dt_from_times(t, tprev);
-            const int32_t a = dt == 0 ? sc.ident_a : decay_code(dt, lut, P.qc.lut_len);
             const uint32_t T = (uint32_t)((ckk + (yp - oy * P.s) * P.k + (xp - ox * P.s)) * OCP);
-            q_b[off_s[pl] + qi] = make_int2((int32_t)((T << 16) | (uint32_t)a), widx);
+            q_b[off_s[pl] + qi] = make_int2(tb, (int32_t)((T << P.q_shift) | widx));
           } else {
             for (int g = 0; g < P.G; ++g) sw_b[widx + g] = 0u;
           }
         }
     }
-    __syncthreads();
-    if (tid < NPM) {
-      run_s[tid] += col;
-      if (last >= 0) lastt_s[tid] = evt_s[last];
-#pragma unroll
-      for (int w = 0; w < CHW; ++w) mask_s[w * NPM + tid] = 0u;
-    }
-    __syncthreads();
   }
+  if (tid < NPM && prev_last >= 0)  // the last chunk's latest event per position
+    lastt_s[tid] = evt_s[(par ^ 1) * kQueueChunk + prev_last];
   __syncthreads();
 
   // -------- 3. walk: lane groups run whole queues, longest first, then the catch-up column
@@ -357,7 +365,9 @@ conv_queue(ConvLaunch P) {
     int32_t vth = INT32_MAX;
     if (lane_ok && P.has_vth) vth = __ldg(&P.vth[(int64_t)oc * P.n_sp + oy * P.w_out + ox]);
     int32_t V = 0;
+    float tp = 0.0f;  // time of the unit's previous queue entry (a queue starts at time 0)
     const int32_t nmax = __reduce_max_sync(kAll, nk);
+    const uint32_t widx_mask = (1u << P.q_shift) - 1u;
     // each batch's entries are loaded one batch ahead (they come from L2)
     int2 ahead = glane < nk ? qp[glane] : make_int2(0, 0);
     for (int32_t b0 = 0; b0 < nmax; b0 += LPU) {
@@ -365,13 +375,22 @@ conv_queue(ConvLaunch P) {
       const bool has = idx < nk;
       const int2 en = ahead;
       if (idx + LPU < nk) ahead = qp[idx + LPU];
+      // Δt to the previous entry of the same queue (the batch's first lane: the carry)
+      const float te = __int_as_float(en.x);
+      float tprev = __shfl_up_sync(kAll, te, 1, LPU);
+      if (glane == 0) tprev = tp;
+      const int32_t nb = min(nk - b0, LPU);
+      const float tlast = __shfl_sync(kAll, te, nb > 0 ? nb - 1 : 0, LPU);
+      if (nb > 0) tp = tlast;
       // lanes without an entry take an identity step on the zero row in the no-fit form (it
       // changes nothing: V stays inside the tracked range and below every threshold), else -1
-      int32_t a = sc.ident_a, T = kPadIdentity ? zero_row : -1, widx = 0;
+      int32_t a = sc.ident_a, T = kPadIdentity ? zero_row : -1;
+      uint32_t widx = 0;
       if (has) {
-        a = en.x & 0xffff;
-        T = (int32_t)((uint32_t)en.x >> 16);
-        widx = en.y;
+        const int32_t dt = dt_from_times(te, tprev);
+        if (dt != 0) a = decay_code(dt, lut, P.qc.lut_len);
+        T = (int32_t)((uint32_t)en.y >> P.q_shift);
+        widx = (uint32_t)en.y & widx_mask;
       }
       const int32_t nbw = min(nmax - b0, LPU);  // warp-uniform batch length
       uint32_t myvote = 0;  // the warp's spike ballot of this lane's step
@@ -429,7 +448,7 @@ conv_queue(ConvLaunch P) {
         const uint32_t word = (myvote >> (gi * LPU)) & gmask_bits;
         sw_b[widx + g] = word;
         if (word) {
-          const int32_t grp = (int32_t)(P.fd_sww.div((uint32_t)widx) >> kConvGroupShift);
+          const int32_t grp = (int32_t)(P.fd_sww.div(widx) >> kConvGroupShift);
           if (P.grp_in_smem) atomicAdd(&grp_s[grp], __popc(word));
           else atomicAdd(&chunk_spk_b[grp], __popc(word));
         }

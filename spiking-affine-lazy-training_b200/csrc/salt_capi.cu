@@ -234,17 +234,28 @@ static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, cons
   return p.queue ? conv_queue_smem_bytes(L, p.wt_bytes) : conv_fused_smem_bytes(L, p.wt_bytes);
 }
 
-// The queue form serves layers whose catch-up/identity columns cannot fire (no needs_tail: decay
-// codes and the identity code 2^f_a fit 16 bits) and whose weight rows, zero row included, have
-// 16-bit offsets.  SALT_CONV_FORM=chunked in the environment selects conv_fused for every layer
-// (a comparison switch; both forms give identical results).
-static bool queue_form(const salt_conv_desc* d, const salt_quant_desc* q, int ocp) {
+// Bits of a conv_queue entry's spike-word index: enough for every (event, slot, group) word of a
+// sample.
+static int queue_shift(int64_t words_per_sample) {
+  int b = 1;
+  while ((int64_t(1) << b) < words_per_sample) ++b;
+  return b;
+}
+
+// The queue form serves layers whose catch-up/identity columns cannot fire (no needs_tail) and
+// whose queue entries can pack a tap's weight row beside the spike-word index in 32 bits.
+// SALT_CONV_FORM=chunked in the environment selects conv_fused for every layer (a comparison
+// switch; both forms give identical results).
+static bool queue_form(const salt_conv_desc* d, const salt_quant_desc* q, int ocp, int nslots,
+                       int G, int32_t E) {
   static const bool chunked = [] {
     const char* v = getenv("SALT_CONV_FORM");
     return v && strcmp(v, "chunked") == 0;
   }();
   if (chunked || q->needs_tail) return false;
-  return (int64_t)(d->ic * d->k * d->k + 1) * ocp <= 65536;
+  const int shift = queue_shift((int64_t)E * nslots * G);
+  const int64_t max_row = (int64_t)(d->ic * d->k * d->k - 1) * ocp;
+  return shift < 32 && max_row < (int64_t(1) << (32 - shift));
 }
 
 // Step form of a layer's hot loop (salt_common.cuh).  Without needs_tail every decay code lies
@@ -285,7 +296,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.wt_bytes = q->q_bits <= 8 ? 1 : (q->q_bits <= 16 ? 2 : 4);
   p.tail_mode = q->needs_tail ? 1 : 0;
   p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
-  p.queue = queue_form(d, q, p.ocp);
+  p.queue = queue_form(d, q, p.ocp, p.nslots, p.G, E);
   p.grp_in_smem = (int64_t)p.n_spk_chunks * 4 <= 32 * 1024;
   // Positions per block: at most 64 (fewer positions per block means more of each position's
   // events per 512-event chunk, so the per-position setup of the recurrence is shared by more
@@ -462,6 +473,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.queues = s.queues;
   L.queue_stride = p.queue_stride;
   L.fd_sww = FastDiv((uint32_t)(p.nslots * p.G));
+  L.q_shift = queue_shift((int64_t)E * p.nslots * p.G);
   L.grp_in_smem = p.grp_in_smem;
 
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));

@@ -67,9 +67,10 @@ struct ConvLaunch {
   const int32_t* tile_off;    // [B][T] start of each tile's list in the sample's region
   const int32_t* tile_lists;  // [B][list_stride] event indices, tile-major, arrival order
   // queue form (conv_queue): per (sample, tile) the kept candidates of every position, position
-  // by position in arrival order, as (weight row << 16 | decay code, spike-word index) pairs
+  // by position in arrival order, as (event time bits, weight row << q_shift | spike-word index)
   int2* queues;               // [B][queue_stride]
   int64_t queue_stride;
+  int32_t q_shift;            // bits of the spike-word index in a queue entry
   FastDiv fd_sww;             // spike words per event (nslots * G)
   int32_t grp_in_smem;        // per-group spike counts gathered in shared memory
 
