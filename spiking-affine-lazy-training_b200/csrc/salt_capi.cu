@@ -209,6 +209,7 @@ struct ConvPlan {
   size_t smem;
   // queue form (conv_queue): whole-sample position queues instead of per-chunk walks
   bool queue;
+  bool win;                   // 2x2 windows read from an address table (conv_addr_table)
   int32_t grp_in_smem;
   int64_t queue_stride;       // queue entries per sample
 };
@@ -297,6 +298,9 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.tail_mode = q->needs_tail ? 1 : 0;
   p.n_spk_chunks = (E + kConvGroup - 1) / kConvGroup;  // conv: per 32-event group
   p.queue = queue_form(d, q, p.ocp, p.nslots, p.G, E);
+  // the address table packs the window origin + 1 into 8 bits per axis and the tap into 12
+  p.win = p.queue && p.ncand == 2 && p.h_out <= 254 && p.w_out <= 254 &&
+          d->ic * d->k * d->k <= 4096;
   p.grp_in_smem = (int64_t)p.n_spk_chunks * 4 <= 32 * 1024;
   // Positions per block: at most 64 (fewer positions per block means more of each position's
   // events per 512-event chunk, so the per-position setup of the recurrence is shared by more
@@ -368,6 +372,7 @@ struct ConvScratch {
   uint32_t* sw;
   int32_t *tail_cnt, *counts, *tile_len, *tile_off, *lists, *hist, *order;
   int2* queues;
+  uint32_t* addr_table;
 };
 
 static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, int32_t E,
@@ -399,6 +404,7 @@ static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, 
   s.hist = c.take<int32_t>((size_t)B * 2 * p.n_sp);
   s.order = c.take<int32_t>((size_t)B);
   s.queues = p.queue ? c.take<int2>((size_t)B * p.queue_stride) : nullptr;
+  s.addr_table = p.win ? c.take<uint32_t>((size_t)d->ic * d->h_in * d->w_in) : nullptr;
   return c.size();
 }
 
@@ -474,6 +480,8 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.queue_stride = p.queue_stride;
   L.fd_sww = FastDiv((uint32_t)(p.nslots * p.G));
   L.q_shift = queue_shift((int64_t)E * p.nslots * p.G);
+  L.addr_table = s.addr_table;
+  L.n_addr = d->ic * d->h_in * d->w_in;
   L.grp_in_smem = p.grp_in_smem;
 
   SALT_CUDA(cudaMemsetAsync(s.stats, 0, s.stats_bytes, st));
@@ -497,8 +505,13 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     SALT_LAUNCHED("conv_tile_scatter");
   }
   // a neuron sees at most max_queue_len weighted steps
+  if (p.win) {
+    conv_addr_table<<<(L.n_addr + 255) / 256, 256, 0, st>>>(L, s.addr_table);
+    SALT_LAUNCHED("conv_addr_table");
+  }
   const int form = step_form(q, d->max_queue_len);
-  void* fn = p.queue ? conv_queue_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form)
+  void* fn = p.queue ? conv_queue_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form,
+                                         p.win)
                      : conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form);
   if (!fn) return fail(SALT_BAD_ARG, "conv layer: no kernel for this step form");
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));

@@ -71,6 +71,8 @@ struct ConvLaunch {
   int2* queues;               // [B][queue_stride]
   int64_t queue_stride;
   int32_t q_shift;            // bits of the spike-word index in a queue entry
+  const uint32_t* addr_table; // 2x2-window layers: per input address its window (conv_addr_table)
+  int32_t n_addr;             // input addresses ic * h_in * w_in
   FastDiv fd_sww;             // spike words per event (nslots * G)
   int32_t grp_in_smem;        // per-group spike counts gathered in shared memory
 
@@ -278,7 +280,11 @@ size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 // kStepWide or kStepWideNoFit (null otherwise); its dynamic shared memory.
 constexpr int kQueueChunk = 256;     // events bucketed per chunk: one per conv_queue thread
 static_assert(kQueueChunk == kFusedThreads, "conv_queue buckets one event per thread");
-void* conv_queue_kernel(int wt_bytes, int lpu, bool saturate, int form);
+// win: the variant that reads 2x2 windows from the layer's address table (conv_addr_table).
+void* conv_queue_kernel(int wt_bytes, int lpu, bool saturate, int form, bool win);
+void* conv_queue_kernel_win(int wt_bytes, int lpu, bool saturate, int form);
+// Fills the address table of a layer with 2x2 windows (one thread per input address).
+__global__ void conv_addr_table(ConvLaunch P, uint32_t* table);
 size_t conv_queue_smem_bytes(const ConvLaunch& P, int wt_bytes);
 // lpu: lanes per (sample, neuron group) unit, 8 / 16 for layers of at most that many neurons;
 // wt: bytes per weight code staged in shared memory (1, 2, 4), 0 to read them from global.
