@@ -766,7 +766,9 @@ __device__ __forceinline__ void count_channels(const ConvLaunch& P, int b) {
   }
 }
 
-template <bool FOUR>
+// TAB (2x2 windows with an address table): the window comes from the table and the event's four
+// slot words from one 16-byte load, masked by the slots valid in the plane.
+template <bool FOUR, bool TAB>
 __global__ void __launch_bounds__(kCompactThreads, 6)
 conv_compact(ConvLaunch P, salt_stream_out out) {
   constexpr uint32_t kAll = 0xffffffffu;
@@ -789,7 +791,38 @@ conv_compact(ConvLaunch P, salt_stream_out out) {
     int32_t cnt = 0;
     uint32_t om = 0, rg = 0, w0 = 0, w1 = 0, w2 = 0, w3 = 0;
     float t = 0.0f;
-    if (j < n_eff) {
+    if (TAB && j < n_eff) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(sw_b + (int64_t)j * 4);
+      const int32_t sv = P.in.src[(int64_t)b * P.in.capacity + j];
+      uint32_t vb;
+      int32_t oym, oxm;
+      if ((uint32_t)sv < (uint32_t)P.n_addr) {
+        const uint32_t en = __ldg(&P.addr_table[sv]);
+        vb = en & 15u;
+        oym = (int32_t)((en >> 4) & 255u) - 1;
+        oxm = (int32_t)((en >> 12) & 255u) - 1;
+      } else {  // a source index outside the input plane: decoded as the reference does
+        int32_t cc, y, x;
+        const EvCand k = event_cand(P, sv, cc, y, x);
+        const bool y0 = k.oy_min >= k.oy_lo && k.oy_min <= k.oy_hi;
+        const bool y1 = k.oy_min + 1 >= k.oy_lo && k.oy_min + 1 <= k.oy_hi;
+        const bool x0 = k.ox_min >= k.ox_lo && k.ox_min <= k.ox_hi;
+        const bool x1 = k.ox_min + 1 >= k.ox_lo && k.ox_min + 1 <= k.ox_hi;
+        vb = (uint32_t)(y0 && x0) | ((uint32_t)(y0 && x1) << 1) | ((uint32_t)(y1 && x0) << 2) |
+             ((uint32_t)(y1 && x1) << 3);
+        oym = k.oy_min;
+        oxm = k.ox_min;
+      }
+      w0 = (vb & 1u) ? wv.x : 0u;
+      w1 = (vb & 2u) ? wv.y : 0u;
+      w2 = (vb & 4u) ? wv.z : 0u;
+      w3 = (vb & 8u) ? wv.w : 0u;
+      cnt = __popc(w0) + __popc(w1) + __popc(w2) + __popc(w3);
+      if (cnt) {
+        om = ((uint32_t)(oym + 32768) << 16) | (uint32_t)(oxm + 32768);
+        t = P.in.time(b, j, n_eff);
+      }
+    } else if (!TAB && j < n_eff) {
       int32_t cc, y, x;
       const EvCand k = event_cand(P, P.in.src[(int64_t)b * P.in.capacity + j], cc, y, x);
       const uint32_t* sw_j = sw_b + (int64_t)j * SWW;
@@ -883,8 +916,10 @@ conv_compact(ConvLaunch P, salt_stream_out out) {
   }
 }
 
-void* conv_compact_kernel(int ncand, int G) {
-  return (ncand <= 2 && G == 1) ? (void*)conv_compact<true> : (void*)conv_compact<false>;
+void* conv_compact_kernel(int ncand, int G, bool table) {
+  if (table && ncand == 2 && G == 1) return (void*)conv_compact<true, true>;
+  return (ncand <= 2 && G == 1) ? (void*)conv_compact<true, false>
+                                : (void*)conv_compact<false, false>;
 }
 
 // Spikes on catch-up / identity columns (tail mode only): they map to the empty queue entry

@@ -527,7 +527,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   {
     salt_stream_out so = *out;
     void* cargs[] = {&L, &so};
-    SALT_CUDA(cudaLaunchKernel(conv_compact_kernel(p.ncand, p.G),
+    SALT_CUDA(cudaLaunchKernel(conv_compact_kernel(p.ncand, p.G, L.addr_table != nullptr),
                                dim3(conv_compact_blocks(p.n_spk_chunks, B), B),
                                dim3(kCompactThreads), cargs, 0, st));
   }
@@ -1357,7 +1357,7 @@ salt_status salt_float_conv_layer_forward(const salt_float_conv_desc* d, const f
   {
     salt_stream_out so = *out;
     void* cargs[] = {&L, &so};
-    SALT_CUDA(cudaLaunchKernel(conv_compact_kernel(p.ncand, p.G),
+    SALT_CUDA(cudaLaunchKernel(conv_compact_kernel(p.ncand, p.G, L.addr_table != nullptr),
                                dim3(conv_compact_blocks(p.n_spk_chunks, B), B),
                                dim3(kCompactThreads), cargs, 0, st));
   }

@@ -261,7 +261,8 @@ __global__ void sample_order_desc(const int32_t* __restrict__ n_real, int32_t ca
 constexpr int kOrderThreads = 1024;
 constexpr int kOrderMinBatch = 128;  // below this the sort costs more than the schedule gains
 // conv_compact specialised for the geometry (ncand <= 2 and one channel group, or the rest).
-void* conv_compact_kernel(int ncand, int G);
+// table: the layer's address table is filled (conv_addr_table) and L.addr_table points at it.
+void* conv_compact_kernel(int ncand, int G, bool table);
 __global__ void conv_tail_append(ConvLaunch P, salt_stream_out out);
 __global__ void conv_truncated(ConvLaunch P, salt_stream_out out, int32_t* scratch_hist);
 __global__ void fc_compact(FCLaunch P, salt_stream_out out);
