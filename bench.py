@@ -237,10 +237,19 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) per input event of conv1's conv_fused launch, measured by ncu on the
-# 1024-sample configuration-3 case of the current kernel (profiles/conv_fused_config3.md, "v21"
-# rows: 183.6 + 140.3 MB for 7.77 M input events); reported scaled by the launch's input events.
-CONV_FUSED_DRAM_BYTES_PER_EVENT = (183.586e6 + 140.337e6) / 7.772496e6
+# DRAM bytes (read + write) per input event of conv1's fused layer kernel on configuration 3 at
+# 4096 samples, measured by ncu on the full-size launch (one-pass DRAM metrics): the queue form
+# conv_queue moves 1830.8 + 1983.5 MB for 31.73 M input events; the chunked form conv_fused
+# (SALT_CONV_FORM=chunked) 183.6 + 140.3 MB per 7.77 M events at 1024 samples (the ncu summaries
+# under profiles/).  Reported times the launch's input events.
+CONV_DRAM_BYTES_PER_EVENT = {"queue": (1830.800e6 + 1983.544e6) / 31725760,
+                             "chunked": (183.586e6 + 140.337e6) / 7.772496e6}
+
+
+def conv_form() -> str:
+    """The fused conv kernel the library launches for the benchmark layers: the queue form unless
+    the environment selects the chunked one."""
+    return "chunked" if os.environ.get("SALT_CONV_FORM") == "chunked" else "queue"
 
 
 def _init_ranks(world, local):
@@ -427,8 +436,10 @@ def run_b200(args):
         avg_ms = float(fused_ms[dom] / max(int(fused_n[dom]), 1))
         v = vol[dom]
         alg_bytes = float(8 * v["E"] + 16 * v["C"] + 4 * v["N"])
-        kernel_name = f"conv_fused (layer {layers[dom].name})"
-        traffic = CONV_FUSED_DRAM_BYTES_PER_EVENT * v["E"] if dom == 0 else None
+        form = conv_form()
+        kernel_name = (f"{'conv_queue' if form == 'queue' else 'conv_fused'} "
+                       f"(layer {layers[dom].name})")
+        traffic = CONV_DRAM_BYTES_PER_EVENT[form] * v["E"] if dom == 0 else None
     else:
         dom = int(np.argmax(layer_ms))
         avg_ms = float(layer_ms[dom] / max(int(fused_n[dom]), 1))
@@ -458,7 +469,7 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_source": ("ncu DRAM bytes per input event of the captured "
-                                            "1024-sample case, scaled by this launch's events"
+                                            "configuration-3 launch, times this launch's events"
                                             if traffic is not None else None),
                          "kernel": kernel_name,
                          "kernel_ms": avg_ms, "algorithmic_bytes": alg_bytes,
