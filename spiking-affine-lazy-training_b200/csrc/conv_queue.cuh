@@ -167,8 +167,11 @@ conv_queue(ConvLaunch P) {
   if (tid < 8) misc_s[tid] = 0;
   const int32_t* lut = P.lut_in_smem ? lut_s : P.lut;
 
-  const int32_t nev = P.T == 1 ? n_eff : P.tile_len[(int64_t)b * P.T + tile];
-  const int32_t* list = P.T == 1 ? nullptr
+  // tiles come with event lists from the partition kernels, or (few tiles) read the whole stream
+  // and keep their own candidates
+  const bool part = P.T > 1 && P.tile_lists != nullptr;
+  const int32_t nev = !part ? n_eff : P.tile_len[(int64_t)b * P.T + tile];
+  const int32_t* list = !part ? nullptr
                                  : P.tile_lists + (int64_t)b * P.list_stride +
                                        P.tile_off[(int64_t)b * P.T + tile];
   const int64_t row = b;
@@ -176,7 +179,8 @@ conv_queue(ConvLaunch P) {
   int32_t* chunk_spk_b = P.chunk_spikes + (int64_t)b * P.n_spk_chunks;
   // this tile's queues: at most nslots entries per tile event
   int2* q_b = P.queues + (int64_t)b * P.queue_stride +
-              (P.T == 1 ? 0 : (int64_t)P.nslots * P.tile_off[(int64_t)b * P.T + tile]);
+              (part ? (int64_t)P.nslots * P.tile_off[(int64_t)b * P.T + tile]
+                    : (int64_t)tile * P.nslots * P.in.capacity);
   const StepConsts sc(P.qc);
 
   // Tile-clipped candidates of tile event e (an empty range past the tile's events).

@@ -210,6 +210,7 @@ struct ConvPlan {
   // queue form (conv_queue): whole-sample position queues instead of per-chunk walks
   bool queue;
   bool win;                   // 2x2 windows read from an address table (conv_addr_table)
+  bool part;                  // tiles get event lists from the partition kernels
   int32_t grp_in_smem;
   int64_t queue_stride;       // queue entries per sample
 };
@@ -319,6 +320,11 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   //
   // The queue form has no per-chunk walk to amortise: its blocks take up to 256 positions (one
   // thread per position in its count and scan phases), and a whole plane needs no partition.
+  // Its tiles shrink while batch x tiles stays below kQueueFillBlocks, and up to
+  // kQueueNoPartTiles tiles each block reads the sample's whole stream and keeps its own
+  // candidates instead of waiting for the partition kernels (configuration 3, G events/s:
+  // 2048 samples 6.03 partitioned in two tiles, 6.93 in one block; 1024 samples 5.25 in four
+  // partitioned tiles, 5.71 in two unpartitioned; 512 samples 4.23 and 4.25 in four).
   const size_t budget = 100 * 1024;
   int npm_cap = (p.queue || E < p.n_sp) ? 256 : 64;
   while (npm_cap > 1 && fused_smem(d, q, p, 1, npm_cap, 2) > budget) npm_cap >>= 1;
@@ -339,7 +345,8 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
     p.T = p.tiles_x * p.tiles_y;
   };
   tile_for(npm_cap);
-  while ((int64_t)std::max(batch, 1) * p.T < kConvFillBlocks && npm_cap > 8) {
+  const int fill = p.queue ? kQueueFillBlocks : kConvFillBlocks;
+  while ((int64_t)std::max(batch, 1) * p.T < fill && npm_cap > 8) {
     const int prev = npm_cap;
     npm_cap >>= 1;
     tile_for(npm_cap);
@@ -353,7 +360,9 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.list_stride = (int64_t)E * std::min(per_y * per_x, p.T);
   p.n_part_chunks = (E + kPartChunk - 1) / kPartChunk;
   // a tile's queues hold at most nslots entries per tile event
-  p.queue_stride = p.queue ? (int64_t)p.nslots * (p.T > 1 ? p.list_stride : E) : 0;
+  p.part = p.T > 1 && !(p.queue && p.T <= kQueueNoPartTiles);
+  // an unpartitioned tile's queues hold at most nslots entries per sample event
+  p.queue_stride = p.queue ? (int64_t)p.nslots * (p.part ? p.list_stride : (int64_t)p.T * E) : 0;
   if (p.queue && p.tile_h * p.tile_w > kFusedThreads)
     return fail(SALT_BAD_ARG, "queue form: tile larger than a block");
   if (p.T > 1 && conv_scatter_smem(p.T) > 227 * 1024)
@@ -393,7 +402,7 @@ static size_t conv_carve(const salt_conv_desc* d, const ConvPlan& p, int32_t B, 
   }
   s.sw = c.take<uint32_t>((size_t)B * E * p.nslots * p.G);
   s.tail_cnt = p.tail_mode ? c.take<int32_t>((size_t)B * p.n_neurons) : nullptr;
-  if (p.T > 1) {
+  if (p.part) {
     s.counts = c.take<int32_t>((size_t)B * p.n_part_chunks * p.T);
     s.tile_len = c.take<int32_t>((size_t)B * p.T);
     s.tile_off = c.take<int32_t>((size_t)B * p.T);
@@ -419,6 +428,13 @@ static salt_status conv_scratch_bytes(const salt_conv_desc* d, const salt_quant_
   if ((rc = plan_conv(d, q, 1, E, fine))) return rc;
   ConvScratch s;
   bytes = std::max(conv_carve(d, p, B, E, nullptr, s), conv_carve(d, fine, B, E, nullptr, s));
+  if (p.queue) {  // the widest unpartitioned tiling a row slice of the queue form may take
+    ConvPlan wide = p;
+    wide.T = kQueueNoPartTiles;
+    wide.part = false;
+    wide.queue_stride = (int64_t)p.nslots * kQueueNoPartTiles * E;
+    bytes = std::max(bytes, conv_carve(d, wide, B, E, nullptr, s));
+  }
   return SALT_OK;
 }
 
@@ -489,7 +505,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
     sample_order_desc<<<1, kOrderThreads, 0, st>>>(in->n_real, E, B, s.order);
     SALT_LAUNCHED("sample_order_desc");
   }
-  if (p.T > 1) {
+  if (p.part) {
     // a few blocks per sample loop over its chunks (chunks past its events are skipped)
     dim3 gp(std::min(p.n_part_chunks, std::max(2, (4 * 1184 + B - 1) / B)), B);
     conv_tile_count<<<gp, kPartThreads, p.T * sizeof(int32_t), st>>>(L, s.counts);

@@ -9,6 +9,8 @@ constexpr int kFusedThreads = 256;   // conv_fused block size (8 warps)
 constexpr int kFusedChunk = 512;     // events bucketed per shared-memory chunk
 constexpr int kPartChunk = 1024;     // events per tile-partition block
 constexpr int kConvFillBlocks = 148 * 16;  // conv_fused blocks a launch should reach (tiling)
+constexpr int kQueueFillBlocks = 2048;     // the same for conv_queue
+constexpr int kQueueNoPartTiles = 4;       // conv_queue tiles per sample read without a partition
 constexpr int kPartThreads = 256;    // tile-partition block size
 constexpr int kPartPer = kPartChunk / kPartThreads;  // events per partition thread
 constexpr int kCompactThreads = 256; // compaction block size == events per spike chunk
