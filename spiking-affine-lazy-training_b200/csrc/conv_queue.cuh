@@ -39,9 +39,9 @@ constexpr int kQBuckets = 64;   // quarter-octave buckets of the kept queue leng
 // Shared-memory layout of conv_queue; the host sizes it with the same function.
 struct QueueSmem {
   size_t w, lut, cnt, off, run, lastt, order, mask, pre, evt, grp, bucket, park, vote, misc, total;
-  __host__ __device__ QueueSmem(const ConvLaunch& P, int wt_bytes) {
+  __host__ __device__ QueueSmem(const ConvLaunch& P, int wt_bytes, int threads) {
     const size_t npm = (size_t)P.tile_h * P.tile_w;
-    constexpr size_t chw = kQueueChunk / 32;
+    const size_t chw = (size_t)threads / 32;
     size_t o = 0;
     // weights [ic*k*k][ocp], then one zero row (the padding steps of the no-fit walk)
     w = o;      o += align16((size_t)(P.ic * P.k * P.k + 1) * P.ocp * wt_bytes);
@@ -53,12 +53,12 @@ struct QueueSmem {
     order = o;  o += align16(npm * 4);           // positions by decreasing kept length
     mask = o;   o += align16(2 * chw * npm * 4); // [chunk parity][warp word][position] bitmasks
     pre = o;    o += align16(chw * npm * 4);     // [warp word][position] entries before the word
-    evt = o;    o += align16(2 * (size_t)kQueueChunk * 4);  // [chunk parity] event times
+    evt = o;    o += align16(2 * (size_t)threads * 4);  // [chunk parity] event times
     grp = o;    o += align16((size_t)(P.grp_in_smem ? P.n_spk_chunks : 0) * 4);
     bucket = o; o += align16((size_t)kQBuckets * 4);
     // 32-lane groups park each batch's (decay code, weight row) pairs and step ballots per warp
-    park = o;   o += align16((size_t)(P.lpu == 32 ? kFusedThreads : 0) * sizeof(int2));
-    vote = o;   o += align16((size_t)(P.lpu == 32 ? kFusedThreads : 0) * 4);
+    park = o;   o += align16((size_t)(P.lpu == 32 ? threads : 0) * sizeof(int2));
+    vote = o;   o += align16((size_t)(P.lpu == 32 ? threads : 0) * 4);
     misc = o;   o += 64;
     total = o;
   }
@@ -96,15 +96,19 @@ struct Win {
 // phases wait at block barriers, so the kernel needs the warps to hide them (40 registers).
 // WIN: 2x2 windows read from the layer's address table (conv_addr_table) instead of decoding
 // every source index twice.
-template <typename WT, int LPU, bool SAT, int FORM, bool WIN>
-__global__ void __launch_bounds__(kFusedThreads, 6)
+// THREADS: 256 (six blocks per SM) or 512 (three), the events a chunk buckets.  512-thread
+// blocks halve the block barriers per event and the tiles a small batch needs (configuration 3,
+// G events/s, 256 -> 512: 4096 samples 7.16 -> 7.68, 1024 samples 5.61 -> 6.50, 512 samples
+// 4.19 -> 4.93).
+template <typename WT, int LPU, bool SAT, int FORM, bool WIN, int THREADS>
+__global__ void __launch_bounds__(THREADS, THREADS == 256 ? 6 : 3)
 conv_queue(ConvLaunch P) {
   static_assert(FORM != kStepSplit, "the queue form serves layers without needs_tail only");
   constexpr int UPW = 32 / LPU;  // units (position x channel group) per warp
-  constexpr int CHW = kQueueChunk / 32;
+  constexpr int CHW = THREADS / 32;
   constexpr uint32_t kAll = 0xffffffffu;
   extern __shared__ __align__(16) uint8_t smem[];
-  const QueueSmem L(P, sizeof(WT));
+  const QueueSmem L(P, sizeof(WT), THREADS);
   WT* w_s = reinterpret_cast<WT*>(smem + L.w);
   int32_t* lut_s = reinterpret_cast<int32_t*>(smem + L.lut);
   int32_t* cnt_s = reinterpret_cast<int32_t*>(smem + L.cnt);
@@ -233,7 +237,7 @@ conv_queue(ConvLaunch P) {
   // -------- 1. count each position's events.  Lanes whose 2x2 windows start at the same
   // position with the same valid slots add together (one atomic per group and slot).
 #pragma unroll 1
-  for (int32_t base = 0; base < nev; base += kQueueChunk) {  // block-uniform trip count
+  for (int32_t base = 0; base < nev; base += THREADS) {  // block-uniform trip count
     int32_t j = 0, c = 0, y = 0, x = 0;
     if constexpr (WIN) {
       const Win w = window(base + tid, j);
@@ -314,9 +318,9 @@ conv_queue(ConvLaunch P) {
   int32_t prev_col = 0, prev_last = -1;
   int par = 0;
 #pragma unroll 1
-  for (int32_t base = 0; base < nev; base += kQueueChunk, par ^= 1) {  // block-uniform
+  for (int32_t base = 0; base < nev; base += THREADS, par ^= 1) {  // block-uniform
     uint32_t* mask_c = mask_s + par * CHW * NPM;
-    float* evt_c = evt_s + par * kQueueChunk;
+    float* evt_c = evt_s + par * THREADS;
     int32_t j = 0, c = 0, y = 0, x = 0;
     const int32_t e = base + tid;
     EvCand k{0, 1, 0, 0, 1, 0};
@@ -364,7 +368,7 @@ conv_queue(ConvLaunch P) {
       if (base > 0) {
         uint32_t* mask_p = mask_s + (par ^ 1) * CHW * NPM;
         run_s[tid] += prev_col;
-        if (prev_last >= 0) lastt_s[tid] = evt_s[(par ^ 1) * kQueueChunk + prev_last];
+        if (prev_last >= 0) lastt_s[tid] = evt_s[(par ^ 1) * THREADS + prev_last];
 #pragma unroll
         for (int w = 0; w < CHW; ++w) mask_p[w * NPM + tid] = 0u;
       }
@@ -418,7 +422,7 @@ conv_queue(ConvLaunch P) {
     }
   }
   if (tid < NPM && prev_last >= 0)  // the last chunk's latest event per position
-    lastt_s[tid] = evt_s[(par ^ 1) * kQueueChunk + prev_last];
+    lastt_s[tid] = evt_s[(par ^ 1) * THREADS + prev_last];
   __syncthreads();
 
   // -------- 3. walk: lane groups run whole queues, longest first, then the catch-up column

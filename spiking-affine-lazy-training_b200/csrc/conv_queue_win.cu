@@ -6,31 +6,35 @@ namespace salt {
 
 // Host-side dispatch over the (weight width, lanes per channel group, overflow mode, step form)
 // instantiations; the no-fit form ignores the overflow mode.
+// 16- and 32-lane groups run 512-thread blocks, narrower ones 256 (conv_queue_threads); a
+// block size other than that one has no kernel.
 template <typename WT, bool SAT, int FORM, bool WIN>
-static void* queue_for_lpu(int lpu) {
+static void* queue_for_lpu(int lpu, int threads) {
+  if (threads != conv_queue_threads(lpu)) return nullptr;
   switch (lpu) {
-    case 1: return (void*)conv_queue<WT, 1, SAT, FORM, WIN>;
-    case 2: return (void*)conv_queue<WT, 2, SAT, FORM, WIN>;
-    case 4: return (void*)conv_queue<WT, 4, SAT, FORM, WIN>;
-    case 8: return (void*)conv_queue<WT, 8, SAT, FORM, WIN>;
-    case 16: return (void*)conv_queue<WT, 16, SAT, FORM, WIN>;
-    default: return (void*)conv_queue<WT, 32, SAT, FORM, WIN>;
+    case 1: return (void*)conv_queue<WT, 1, SAT, FORM, WIN, 256>;
+    case 2: return (void*)conv_queue<WT, 2, SAT, FORM, WIN, 256>;
+    case 4: return (void*)conv_queue<WT, 4, SAT, FORM, WIN, 256>;
+    case 8: return (void*)conv_queue<WT, 8, SAT, FORM, WIN, 256>;
+    case 16: return (void*)conv_queue<WT, 16, SAT, FORM, WIN, 512>;
+    default: return (void*)conv_queue<WT, 32, SAT, FORM, WIN, 512>;
   }
 }
 
 template <bool SAT, int FORM, bool WIN>
-static void* queue_for_wt(int wt_bytes, int lpu) {
-  if (wt_bytes == 1) return queue_for_lpu<int8_t, SAT, FORM, WIN>(lpu);
-  if (wt_bytes == 2) return queue_for_lpu<int16_t, SAT, FORM, WIN>(lpu);
-  return queue_for_lpu<int32_t, SAT, FORM, WIN>(lpu);
+static void* queue_for_wt(int wt_bytes, int lpu, int threads) {
+  if (wt_bytes == 1) return queue_for_lpu<int8_t, SAT, FORM, WIN>(lpu, threads);
+  if (wt_bytes == 2) return queue_for_lpu<int16_t, SAT, FORM, WIN>(lpu, threads);
+  return queue_for_lpu<int32_t, SAT, FORM, WIN>(lpu, threads);
 }
 
 template <bool WIN>
-static void* queue_kernel(int wt_bytes, int lpu, bool saturate, int form) {
-  if (form == kStepWideNoFit) return queue_for_wt<false, kStepWideNoFit, WIN>(wt_bytes, lpu);
+static void* queue_kernel(int wt_bytes, int lpu, bool saturate, int form, int threads) {
+  if (form == kStepWideNoFit)
+    return queue_for_wt<false, kStepWideNoFit, WIN>(wt_bytes, lpu, threads);
   if (form != kStepWide) return nullptr;
-  return saturate ? queue_for_wt<true, kStepWide, WIN>(wt_bytes, lpu)
-                  : queue_for_wt<false, kStepWide, WIN>(wt_bytes, lpu);
+  return saturate ? queue_for_wt<true, kStepWide, WIN>(wt_bytes, lpu, threads)
+                  : queue_for_wt<false, kStepWide, WIN>(wt_bytes, lpu, threads);
 }
 
 // The address table of a layer with 2x2 windows: per input address (channel, y, x) its
@@ -47,8 +51,8 @@ __global__ void conv_addr_table(ConvLaunch P, uint32_t* __restrict__ table) {
              ((uint32_t)(k.ox_min + 1) << 12) | ((uint32_t)tap0 << 20);
 }
 
-void* conv_queue_kernel_win(int wt_bytes, int lpu, bool saturate, int form) {
-  return queue_kernel<true>(wt_bytes, lpu, saturate, form);
+void* conv_queue_kernel_win(int wt_bytes, int lpu, bool saturate, int form, int threads) {
+  return queue_kernel<true>(wt_bytes, lpu, saturate, form, threads);
 }
 
 }  // namespace salt

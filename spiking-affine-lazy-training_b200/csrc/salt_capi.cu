@@ -211,6 +211,7 @@ struct ConvPlan {
   bool queue;
   bool win;                   // 2x2 windows read from an address table (conv_addr_table)
   bool part;                  // tiles get event lists from the partition kernels
+  int32_t q_threads;          // conv_queue block size
   int32_t grp_in_smem;
   int64_t queue_stride;       // queue entries per sample
 };
@@ -233,6 +234,7 @@ static size_t fused_smem(const salt_conv_desc* d, const salt_quant_desc* q, cons
   L.qc.lut_len = q->lut_len;
   L.n_spk_chunks = p.n_spk_chunks;
   L.grp_in_smem = p.grp_in_smem;
+  L.q_threads = p.q_threads;
   return p.queue ? conv_queue_smem_bytes(L, p.wt_bytes) : conv_fused_smem_bytes(L, p.wt_bytes);
 }
 
@@ -303,6 +305,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.win = p.queue && p.ncand == 2 && p.h_out <= 254 && p.w_out <= 254 &&
           d->ic * d->k * d->k <= 4096;
   p.grp_in_smem = (int64_t)p.n_spk_chunks * 4 <= 32 * 1024;
+  p.q_threads = p.queue ? conv_queue_threads(p.lpu) : kFusedThreads;
   // Positions per block: at most 64 (fewer positions per block means more of each position's
   // events per 512-event chunk, so the per-position setup of the recurrence is shared by more
   // events, and more, smaller blocks), within a ~100 KB shared-memory budget, never fewer than
@@ -345,7 +348,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
     p.T = p.tiles_x * p.tiles_y;
   };
   tile_for(npm_cap);
-  const int fill = p.queue ? kQueueFillBlocks : kConvFillBlocks;
+  const int fill = p.queue ? kQueueFillBlocks * 256 / p.q_threads : kConvFillBlocks;
   while ((int64_t)std::max(batch, 1) * p.T < fill && npm_cap > 8) {
     const int prev = npm_cap;
     npm_cap >>= 1;
@@ -363,7 +366,7 @@ static salt_status plan_conv(const salt_conv_desc* d, const salt_quant_desc* q, 
   p.part = p.T > 1 && !(p.queue && p.T <= kQueueNoPartTiles);
   // an unpartitioned tile's queues hold at most nslots entries per sample event
   p.queue_stride = p.queue ? (int64_t)p.nslots * (p.part ? p.list_stride : (int64_t)p.T * E) : 0;
-  if (p.queue && p.tile_h * p.tile_w > kFusedThreads)
+  if (p.queue && p.tile_h * p.tile_w > p.q_threads)
     return fail(SALT_BAD_ARG, "queue form: tile larger than a block");
   if (p.T > 1 && conv_scatter_smem(p.T) > 227 * 1024)
     return fail(SALT_BAD_ARG, "conv output plane too large: its tile partition needs more shared "
@@ -496,6 +499,7 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   L.queue_stride = p.queue_stride;
   L.fd_sww = FastDiv((uint32_t)(p.nslots * p.G));
   L.q_shift = queue_shift((int64_t)E * p.nslots * p.G);
+  L.q_threads = p.q_threads;
   L.addr_table = s.addr_table;
   L.n_addr = d->ic * d->h_in * d->w_in;
   L.grp_in_smem = p.grp_in_smem;
@@ -527,13 +531,13 @@ static salt_status conv_forward_impl(const salt_conv_desc* d, const salt_quant_d
   }
   const int form = step_form(q, d->max_queue_len);
   void* fn = p.queue ? conv_queue_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form,
-                                         p.win)
+                                         p.win, p.q_threads)
                      : conv_fused_kernel(p.wt_bytes, p.lpu, q->overflow_mode == SALT_SATURATE, form);
   if (!fn) return fail(SALT_BAD_ARG, "conv layer: no kernel for this step form");
   SALT_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
   void* args[] = {&L};
   if (timer) SALT_CUDA(cudaEventRecord(timer->start, st));
-  SALT_CUDA(cudaLaunchKernel(fn, dim3(p.T, B), dim3(kFusedThreads), args, p.smem, st));
+  SALT_CUDA(cudaLaunchKernel(fn, dim3(p.T, B), dim3(p.q_threads), args, p.smem, st));
   SALT_LAUNCHED("conv_fused");
   if (timer) SALT_CUDA(cudaEventRecord(timer->stop, st));
   // conv_fused counts only catch-up/identity spikes into s_total: the spike words' count is the

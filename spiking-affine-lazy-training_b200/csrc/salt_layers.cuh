@@ -75,6 +75,7 @@ struct ConvLaunch {
   int32_t q_shift;            // bits of the spike-word index in a queue entry
   const uint32_t* addr_table; // 2x2-window layers: per input address its window (conv_addr_table)
   int32_t n_addr;             // input addresses ic * h_in * w_in
+  int32_t q_threads;          // conv_queue block size = events per chunk
   FastDiv fd_sww;             // spike words per event (nslots * G)
   int32_t grp_in_smem;        // per-group spike counts gathered in shared memory
 
@@ -281,11 +282,11 @@ inline size_t conv_scatter_smem(int T) {
 size_t conv_fused_smem_bytes(const ConvLaunch& P, int wt_bytes);
 // The queue form of the fused kernel (conv_queue.cu), for layers without needs_tail: form
 // kStepWide or kStepWideNoFit (null otherwise); its dynamic shared memory.
-constexpr int kQueueChunk = 256;     // events bucketed per chunk: one per conv_queue thread
-static_assert(kQueueChunk == kFusedThreads, "conv_queue buckets one event per thread");
 // win: the variant that reads 2x2 windows from the layer's address table (conv_addr_table).
-void* conv_queue_kernel(int wt_bytes, int lpu, bool saturate, int form, bool win);
-void* conv_queue_kernel_win(int wt_bytes, int lpu, bool saturate, int form);
+// threads: the block size, conv_queue_threads(lpu): 512 for 16- and 32-lane groups, else 256.
+void* conv_queue_kernel(int wt_bytes, int lpu, bool saturate, int form, bool win, int threads);
+void* conv_queue_kernel_win(int wt_bytes, int lpu, bool saturate, int form, int threads);
+int conv_queue_threads(int lpu);
 // Fills the address table of a layer with 2x2 windows (one thread per input address).
 __global__ void conv_addr_table(ConvLaunch P, uint32_t* table);
 size_t conv_queue_smem_bytes(const ConvLaunch& P, int wt_bytes);
