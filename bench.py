@@ -239,10 +239,10 @@ def run_reference(args):
 
 # DRAM bytes (read + write) per input event of conv1's fused layer kernel on configuration 3 at
 # 4096 samples, measured by ncu on the full-size launch (one-pass DRAM metrics): the queue form
-# conv_queue moves 1830.8 + 1983.5 MB for 31.73 M input events; the chunked form conv_fused
+# conv_queue moves 1266.3 + 1578.7 MB for 31.73 M input events; the chunked form conv_fused
 # (SALT_CONV_FORM=chunked) 183.6 + 140.3 MB per 7.77 M events at 1024 samples (the ncu summaries
 # under profiles/).  Reported times the launch's input events.
-CONV_DRAM_BYTES_PER_EVENT = {"queue": (1830.800e6 + 1983.544e6) / 31725760,
+CONV_DRAM_BYTES_PER_EVENT = {"queue": (1266.301e6 + 1578.716e6) / 31725760,
                              "chunked": (183.586e6 + 140.337e6) / 7.772496e6}
 
 
